@@ -1,0 +1,315 @@
+#!/usr/bin/env python
+"""Headline benchmark: Qwen2.5-0.5B-shape int8 greedy decode, batch 1 per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    (N > 1: launched by torch.distributed.run, one rank per GPU)
+
+Workload (BASELINE.json config 3's model at the north star's batch-1 decode):
+a seeded random-init Qwen2.5-0.5B-shape int8 .ecm (24 layers, E 896, 14/2
+heads, I 4864, V 151936, tied fp16 lm_head), a 64-token uniform-random prompt
+prefilled once, then greedy decode.  A step is one decode token of the stream.
+Positions cycle through [64, 64+256): every 256 steps a new 256-token
+continuation of the cached prompt starts, so the context stays that of a
+64-prompt / 256-decode run however many steps are timed.
+
+Our arm: `value` times K steps of the device-resident decode loop (CUDA-graph
+step, greedy argmax on the device) with CUDA events on the model stream, max
+over ranks; `e2e` times the reference-facing call gpt2_forward with host
+token/position arrays and host logits (608 KB per step) -- the same contract
+the reference runtime times for its tokens_per_sec (decode forward only,
+sampling excluded).  Independent replicas per GPU: weak scaling, no collective
+on the data path.
+
+Reference arm (--impl reference): the reference's own C implementation
+(oracle/_ref/libecref.so, built from its sources) on the host cores, rank 0
+only, same model, prompt and metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from edgecore_b200 import synth  # noqa: E402
+
+METRIC = "Qwen2.5-0.5B-shape int8 decode tok/s @1/2/4/8 B200; GEMV % of HBM peak"
+CONFIG_KEY = "c3_qwen05b_int8"
+PROMPT = 64
+PERIOD = 256
+PROFILE_STEPS = 24
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=4096)
+    ap.add_argument("--warmup", type=int, default=32)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=512)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    return ap.parse_args()
+
+
+def host_cores() -> int:
+    return len(os.sched_getaffinity(0))
+
+
+def config_dict(world: int) -> dict:
+    spec = synth.CONFIGS[CONFIG_KEY]
+    return {"workload": "qwen2.5-0.5b-shape int8 (W8A8 linears, fp16 tied lm_head) batch-1 greedy decode, "
+                        "64-token prompt, positions cycling 64..319",
+            "config": CONFIG_KEY, "n_layer": spec.n_layer, "n_embd": spec.n_embd, "n_head": spec.n_head,
+            "n_kv_head": spec.n_kv_head, "intermediate": spec.intermediate, "vocab": spec.vocab,
+            "prompt": PROMPT, "decode_period": PERIOD, "streams_per_gpu": 1,
+            "global_batch": world, "parallelism": f"replicas{world}",
+            "l2": "inputs larger than L2 (631.6 MB of weights streamed per step vs 126 MB L2)"}
+
+
+# ---- clocks -------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                       "-i", str(gpu_index), "-lms", "100"], stdout=self.tmp,
+                                      stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.tmp.flush()
+        rows = [r.split(",") for r in Path(self.tmp.name).read_text().splitlines() if r.count(",") >= 8]
+        os.unlink(self.tmp.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm = [float(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if "Active" in v and "Not" not in v})
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows)}
+
+
+# ---- CPU reference ------------------------------------------------------------
+
+def run_reference_decode(path: Path, steps: int, warmup: int, budget_s: float, threads: int):
+    """Reference CPU decode (oracle/_ref, built from the reference sources;
+    the restatement if that is absent).  Returns (tok/s, steps timed, kind)."""
+    from oracle import oracle
+    try:
+        R = oracle.Reference(threads=threads)
+        kind = "reference"
+    except FileNotFoundError:
+        R = oracle.Restatement()
+        kind = "port"
+    spec = synth.CONFIGS[CONFIG_KEY]
+    m = R.open(path, batch_cap=1, max_ctx=PROMPT + PERIOD)
+    m.reset()
+    toks = synth.prompt_ids(spec.vocab, PROMPT)
+    lg = m.forward(toks, np.arange(PROMPT, dtype=np.int32), np.zeros(PROMPT, np.int32))
+    cur = int(np.argmax(lg[-1]))
+    pos = PROMPT
+    total, done = 0.0, 0
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        lg = m.forward(np.array([cur], np.int32), np.array([pos], np.int32))
+        dt = time.perf_counter() - t0
+        cur = int(np.argmax(lg[0]))
+        pos = pos + 1 if pos + 1 < PROMPT + PERIOD else PROMPT
+        if i >= warmup:
+            total += dt
+            done += 1
+            if total >= budget_s:
+                break
+    m.close()
+    return done / total, done, kind
+
+
+def reference_arm(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    path = synth.ensure_model(synth.CONFIGS[CONFIG_KEY])
+    threads = host_cores()
+    tps, done, kind = run_reference_decode(path, args.steps, min(args.warmup, 3), 120.0, threads)
+    sample = (f"{done} timed decode steps (of --steps {args.steps}, capped at 120 s) after a {PROMPT}-token "
+              f"prefill, {threads} threads, gpt2_forward per step as the reference runtime times it")
+    line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": world,
+            "steps": done, "warmup": min(args.warmup, 3), "ms_per_step": 1000.0 / tps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded random-init weights)",
+            "config": config_dict(1),
+            "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": kind, "sample": sample},
+            "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---- our arm ------------------------------------------------------------------
+
+def measured_peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def committed_traffic() -> dict:
+    p = ROOT / "profiles" / "traffic.json"
+    return json.loads(p.read_text()) if p.exists() else {}
+
+
+def ours_arm(args, rank: int, world: int, local: int) -> None:
+    import torch
+    import torch.distributed as dist
+
+    import edgecore_b200 as ec
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
+                                device_id=torch.device("cuda", local))
+    spec = synth.CONFIGS[CONFIG_KEY]
+    if rank == 0:
+        path = synth.ensure_model(spec)
+    if world > 1:
+        dist.barrier()
+    path = synth.ensure_model(spec)
+
+    max_ctx = PROMPT + PERIOD
+    m = ec.Model(path, batch_cap=1, max_ctx=max_ctx)
+    stream = torch.cuda.Stream()
+    m.set_stream(stream.cuda_stream)
+    toks = synth.prompt_ids(spec.vocab, PROMPT)
+    lg = m.forward(toks, np.arange(PROMPT), np.zeros(PROMPT, np.int32))
+    first = int(np.argmax(lg[-1]))
+    d_tok = torch.tensor([first], dtype=torch.int32, device="cuda")
+
+    # warm-up: W steps of the same cycling loop (captures the graph)
+    m.decode_greedy_cycle(d_tok, PROMPT, PERIOD, max(args.warmup, 3))
+    torch.cuda.synchronize()
+
+    # timed region: exactly K steps, barrier + synchronize on both sides
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local) if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start.record(stream)
+    m.decode_greedy_cycle(d_tok, PROMPT, PERIOD, args.steps)
+    end.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop() if clocks else None
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * args.steps / (ms_max / 1000.0)
+
+    # e2e: the reference-facing gpt2_forward, host arrays in and host logits out
+    e2e_steps = min(args.e2e_steps, args.steps)
+    m.set_stream(None)
+    cur = first
+    lg = m.forward(toks, np.arange(PROMPT), np.zeros(PROMPT, np.int32))
+    pos = PROMPT
+    tok_h = np.empty(1, np.int32)
+    pos_h = np.empty(1, np.int32)
+    for _ in range(3):
+        tok_h[0], pos_h[0] = cur, pos
+        m.forward(tok_h, pos_h)
+    if world > 1:
+        dist.barrier()
+    e2e_s = 0.0
+    for i in range(e2e_steps):
+        tok_h[0], pos_h[0] = cur, pos
+        t0 = time.perf_counter()
+        out = m.forward(tok_h, pos_h)
+        e2e_s += time.perf_counter() - t0
+        cur = int(np.argmax(out[0]))
+        pos = pos + 1 if pos + 1 < PROMPT + PERIOD else PROMPT
+    te = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = world * e2e_steps / float(te.item())
+
+    # roofline: per-launch CUDA events over instrumented decode steps
+    m.set_stream(stream.cuda_stream)
+    prof = m.decode_profile(d_tok, PROMPT, PROFILE_STEPS)
+    torch.cuda.synchronize()
+    classes = {k: v for k, v in prof.items() if k != "steps"}
+    dom = max(classes, key=lambda k: classes[k]["ms"])
+    launches_per_step = sum(v["launches"] for v in classes.values()) / prof["steps"]
+    peak, peak_kind = measured_peaks()
+    c = classes[dom]
+    achieved = (c["bytes"] / c["launches"]) / (c["ms"] / c["launches"] / 1e3) / 1e9 if c["ms"] else 0.0
+    step_bytes = sum(v["bytes"] for v in classes.values()) / prof["steps"]
+    traffic = committed_traffic().get(dom)
+    roofline = {"bound": "hbm", "kernel": {"layer_gemv": "k_gemv<int8>", "lm_head_gemv": "k_gemv<fp16>"}.get(dom, dom),
+                "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured" else "fallback",
+                "traffic": traffic,
+                "bytes_per_launch": c["bytes"] / c["launches"], "us_per_launch": 1e3 * c["ms"] / c["launches"],
+                "method": f"CUDA events around every launch on the model stream over {prof['steps']} "
+                          f"instrumented decode steps run after the timed region",
+                "step_algorithmic_bytes": step_bytes,
+                "step_frac_of_peak": step_bytes / (ms_max / args.steps / 1e3) / 1e9 / peak,
+                "classes_us_per_step": {k: 1e3 * v["ms"] / prof["steps"] for k, v in classes.items()}}
+
+    cpu = None
+    if rank == 0 and world == 1:
+        tps, done, kind = run_reference_decode(path, 10_000, 2, args.cpu_seconds, host_cores())
+        cpu = {"value": tps, "unit": "tok/s", "cores": host_cores(), "kind": kind,
+               "sample": f"{done} decode steps (~{args.cpu_seconds:.0f} s) of the same workload after a "
+                         f"{PROMPT}-token prefill, reference C compiled from its sources"}
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+                "warmup": max(args.warmup, 3), "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+                "data": "synthetic (seeded random-init weights, uniform-random prompt ids)",
+                "config": config_dict(world), "clocks": clk,
+                "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 12,
+                        "d2h_bytes_per_step": 4 * spec.vocab, "steps": e2e_steps,
+                        "api": "gpt2_forward (host tokens/positions, host logits [1][151936])"},
+                "gpu_launches": int(round(launches_per_step * args.steps)),
+                "roofline": roofline, "cpu_baseline": cpu}
+        print(json.dumps(line), flush=True)
+    m.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        reference_arm(args, rank, world)
+    else:
+        ours_arm(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    main()

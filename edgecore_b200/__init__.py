@@ -1,0 +1,285 @@
+"""edgecore_b200 -- B200 (sm_100a) implementation of EdgeCore's inference hot path.
+
+The product is the C library ``libedgecore_b200.so`` (include/edgecore.h and
+include/edgecore_b200.h).  This package builds it (``build.py``), loads it with
+ctypes, and mirrors the reference entry points for Python callers:
+
+* ``gemm_int8``, ``gemm_fp16_fp32``, ``gemm_bf16_fp32`` -- reference
+  src/kernels.c:129-168, on the GPU;
+* ``Model`` -- ``gpt2_load`` / ``gpt2_forward`` / ``gpt2_free`` (reference
+  src/gpt2.c:161-805) plus the greedy/device-resident extensions.
+
+Arrays may be numpy arrays (host) or objects exposing ``data_ptr()`` (device
+tensors); the library classifies each pointer.  There is no CPU fallback: if
+the shared library is missing or fails to load, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+from typing import Any
+
+import numpy as np
+
+__all__ = ["load_library", "Model", "gemm_int8", "gemm_fp16_fp32", "gemm_bf16_fp32",
+           "quantize_rows", "linear_int8", "argmax_key", "argmax_key_decode", "LIB_PATH"]
+
+LIB_PATH = Path(__file__).resolve().parent / "libedgecore_b200.so"
+_LIB: C.CDLL | None = None
+
+_vp, _i, _f = C.c_void_p, C.c_int, C.c_float
+
+
+def _declare(lib: C.CDLL) -> None:
+    sig = {
+        "ec_last_error": (C.c_char_p, []),
+        "ec_version": (C.c_char_p, []),
+        "ec_model_open": (_vp, [C.c_char_p, _i, _i]),
+        "ec_model_close": (None, [_vp]),
+        "ec_model_info": (_i, [_vp, _vp]),
+        "ec_model_set_stream": (_i, [_vp, _vp]),
+        "ec_forward_device": (_i, [_vp, _vp, _vp, _vp, _i, _vp]),
+        "ec_forward_argmax": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp]),
+        "ec_forward_shard_argmax": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp]),
+        "ec_decode_greedy": (_i, [_vp, _vp, _i, _i, _vp]),
+        "ec_decode_profile": (_i, [_vp, _vp, _i, _i, _vp]),
+        "ec_decode_greedy_cycle": (_i, [_vp, _vp, _i, _i, _i, _vp]),
+        "ec_model_set_taps": (_i, [_vp, _i]),
+        "ec_model_get_taps": (_i, [_vp, _vp, _i]),
+        "ec_model_set_vocab_shard": (_i, [_vp, _i, _i]),
+        "ec_argmax_key": (C.c_uint64, [_f, _i]),
+        "ec_argmax_key_decode": (None, [C.c_uint64, _vp, _vp]),
+        "ec_quantize_rows": (_i, [_vp, _vp, _vp, _i, _i]),
+        "ec_linear_int8": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i]),
+        "gemm_fp16_fp32": (None, [_vp, _vp, _vp, _i, _i, _i]),
+        "gemm_bf16_fp32": (None, [_vp, _vp, _vp, _i, _i, _i]),
+        "gemm_int8": (None, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i]),
+        "gpt2_forward": (None, [_vp, _vp, _vp, _vp, _i, _vp]),
+        "ecm_parse": (_i, [_vp, C.c_size_t, _vp, _i, _vp]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+
+
+def load_library(path: str | os.PathLike | None = None) -> C.CDLL:
+    """Load (once) and return the shared library; raise if it is not built."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    p = Path(path) if path else LIB_PATH
+    if not p.exists():
+        raise RuntimeError(f"{p} is not built; run `python -m edgecore_b200.build` "
+                           "(there is no CPU fallback)")
+    lib = C.CDLL(str(p))
+    _declare(lib)
+    _LIB = lib
+    return lib
+
+
+def last_error() -> str:
+    return (load_library().ec_last_error() or b"").decode(errors="replace")
+
+
+def _ptr(a: Any) -> int | None:
+    """Address of a numpy array / device tensor / raw int (None stays None)."""
+    if a is None:
+        return None
+    if isinstance(a, int):
+        return a
+    if hasattr(a, "data_ptr"):
+        return int(a.data_ptr())
+    if isinstance(a, np.ndarray):
+        if not a.flags["C_CONTIGUOUS"]:
+            raise ValueError("arrays passed to the C ABI must be C-contiguous")
+        return a.ctypes.data
+    raise TypeError(f"cannot pass {type(a)} to the C ABI")
+
+
+def _np(a, dtype) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+def _is_dev(a) -> bool:
+    return hasattr(a, "data_ptr")
+
+
+# ---- standalone GEMMs (reference src/kernels.c:129-168) ----------------------
+
+def gemm_int8(A, a_scale, B, b_scale=None, bias=None, out=None):
+    """C[m][n] = bias[n] + ((float)sum_k A[m][k]*B[n][k]) * a_scale[m] * b_scale[n]."""
+    lib = load_library()
+    if not _is_dev(A):
+        A, a_scale = _np(A, np.int8), _np(a_scale, np.float32)
+    if not _is_dev(B):
+        B = _np(B, np.int8)
+        b_scale = None if b_scale is None else _np(b_scale, np.float32)
+        bias = None if bias is None else _np(bias, np.float32)
+    M, K = A.shape
+    N = B.shape[0]
+    if out is None:
+        out = np.empty((M, N), np.float32)
+    lib.gemm_int8(_ptr(out), _ptr(A), _ptr(a_scale), _ptr(B), _ptr(b_scale), _ptr(bias), M, K, N)
+    return out
+
+
+def _gemm16(fn, A, B16, out):
+    lib = load_library()
+    if not _is_dev(A):
+        A = _np(A, np.float32)
+    if not _is_dev(B16):
+        B16 = np.ascontiguousarray(B16).view(np.uint16)
+    M, K = A.shape
+    N = B16.shape[0]
+    if out is None:
+        out = np.empty((M, N), np.float32)
+    getattr(lib, fn)(_ptr(out), _ptr(A), _ptr(B16), M, K, N)
+    return out
+
+
+def gemm_fp16_fp32(A, B16, out=None):
+    """C[m][n] = sum_k A[m][k] * fp16(B[n][k]) with fp32 accumulation."""
+    return _gemm16("gemm_fp16_fp32", A, B16, out)
+
+
+def gemm_bf16_fp32(A, B16, out=None):
+    """Same as gemm_fp16_fp32 with bfloat16 weights (uint16 bit patterns)."""
+    return _gemm16("gemm_bf16_fp32", A, B16, out)
+
+
+def quantize_rows(X):
+    """Per-row int8 activation quantisation (reference src/gpt2.c:446-461)."""
+    lib = load_library()
+    X = _np(X, np.float32)
+    M, K = X.shape
+    q = np.empty((M, K), np.int8)
+    s = np.empty(M, np.float32)
+    if lib.ec_quantize_rows(_ptr(q), _ptr(s), _ptr(X), M, K):
+        raise RuntimeError(last_error())
+    return q, s
+
+
+def linear_int8(X, W, w_scale, bias=None, out=None):
+    """The W8A8 linear of reference linear() (src/gpt2.c:437-462)."""
+    lib = load_library()
+    if not _is_dev(X):
+        X = _np(X, np.float32)
+    if not _is_dev(W):
+        W, w_scale = _np(W, np.int8), _np(w_scale, np.float32)
+        bias = None if bias is None else _np(bias, np.float32)
+    M, K = X.shape
+    N = W.shape[0]
+    if out is None:
+        out = np.empty((M, N), np.float32)
+    if lib.ec_linear_int8(_ptr(out), _ptr(X), _ptr(W), _ptr(w_scale), _ptr(bias), M, K, N):
+        raise RuntimeError(last_error())
+    return out
+
+
+def argmax_key(maxv: float, idx: int) -> int:
+    return int(load_library().ec_argmax_key(float(maxv), int(idx)))
+
+
+def argmax_key_decode(key: int) -> tuple[float, int]:
+    v, i = C.c_float(), C.c_int()
+    load_library().ec_argmax_key_decode(C.c_uint64(key), C.byref(v), C.byref(i))
+    return v.value, i.value
+
+
+# ---- model -------------------------------------------------------------------
+
+class Model:
+    """A model loaded on the current CUDA device (gpt2_load on a heap GPT2)."""
+
+    INFO = ("arch", "precision", "n_layer", "n_head", "n_kv_head", "n_embd", "head_dim",
+            "intermediate", "vocab", "n_ctx", "eff_ctx", "batch_cap", "n_kv_embd", "tie", "device")
+
+    def __init__(self, path: str | os.PathLike, batch_cap: int = 1, max_ctx: int = 0):
+        self.lib = load_library()
+        self.h = self.lib.ec_model_open(str(path).encode(), int(batch_cap), int(max_ctx))
+        if not self.h:
+            raise RuntimeError(f"gpt2_load({path}) failed: {last_error()}")
+        info = np.zeros(16, np.int32)
+        self._check(self.lib.ec_model_info(self.h, info.ctypes.data))
+        for k, v in zip(self.INFO, info):
+            setattr(self, k, int(v))
+
+    def _check(self, rc: int) -> None:
+        if rc:
+            raise RuntimeError(last_error())
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.lib.ec_model_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def forward(self, tokens, positions, seqs=None) -> np.ndarray:
+        """gpt2_forward with host arrays: logits [M][vocab] fp32."""
+        t, p = _np(tokens, np.int32), _np(positions, np.int32)
+        s = None if seqs is None else _np(seqs, np.int32)
+        M = len(t)
+        logits = np.empty((M, self.vocab), np.float32)
+        self.lib.gpt2_forward(self.h, _ptr(t), _ptr(p), _ptr(s), M, _ptr(logits))
+        return logits
+
+    def forward_argmax(self, tokens, positions, seqs=None, shard: bool = False):
+        t, p = _np(tokens, np.int32), _np(positions, np.int32)
+        s = None if seqs is None else _np(seqs, np.int32)
+        M = len(t)
+        ids = np.empty(M, np.int32)
+        mx = np.empty(M, np.float32)
+        fn = self.lib.ec_forward_shard_argmax if shard else self.lib.ec_forward_argmax
+        self._check(fn(self.h, _ptr(t), _ptr(p), _ptr(s), M, _ptr(ids), _ptr(mx)))
+        return ids, mx
+
+    def forward_taps(self, tokens, positions, seqs=None):
+        """Logits plus residual taps [n_layer+1][M][n_embd]."""
+        M = len(tokens)
+        self._check(self.lib.ec_model_set_taps(self.h, M))
+        try:
+            logits = self.forward(tokens, positions, seqs)
+            taps = np.empty((self.n_layer + 1, M, self.n_embd), np.float32)
+            self._check(self.lib.ec_model_get_taps(self.h, _ptr(taps), M))
+        finally:
+            self.lib.ec_model_set_taps(self.h, 0)
+        return logits, taps
+
+    def forward_device(self, d_tokens, d_positions, d_seqs, M: int, d_logits) -> None:
+        self._check(self.lib.ec_forward_device(self.h, _ptr(d_tokens), _ptr(d_positions), _ptr(d_seqs),
+                                               int(M), _ptr(d_logits)))
+
+    def decode_greedy(self, d_tokens, start_pos: int, n_steps: int, d_out_ids=None) -> None:
+        self._check(self.lib.ec_decode_greedy(self.h, _ptr(d_tokens), int(start_pos), int(n_steps),
+                                              _ptr(d_out_ids)))
+
+    def decode_greedy_cycle(self, d_tokens, start_pos: int, period: int, n_steps: int, d_out_ids=None) -> None:
+        self._check(self.lib.ec_decode_greedy_cycle(self.h, _ptr(d_tokens), int(start_pos), int(period),
+                                                    int(n_steps), _ptr(d_out_ids)))
+
+    def decode_profile(self, d_tokens, start_pos: int, n_steps: int) -> dict:
+        """Per-kernel-class event timings of an instrumented decode."""
+        out = np.zeros(16, np.float64)
+        self._check(self.lib.ec_decode_profile(self.h, _ptr(d_tokens), int(start_pos), int(n_steps), _ptr(out)))
+        names = ("layer_gemv", "lm_head_gemv", "attention", "norm", "other")
+        return {n: {"ms": out[3 * i], "bytes": out[3 * i + 1], "launches": int(out[3 * i + 2])}
+                for i, n in enumerate(names)} | {"steps": int(out[15])}
+
+    def set_stream(self, stream_ptr: int | None) -> None:
+        self._check(self.lib.ec_model_set_stream(self.h, stream_ptr))
+
+    def set_vocab_shard(self, v0: int, v1: int) -> None:
+        self._check(self.lib.ec_model_set_vocab_shard(self.h, int(v0), int(v1)))

@@ -1,0 +1,907 @@
+// ec_kernels.cu -- the sm_100a kernels of the decode/prefill path.
+//
+//   k_gemv        weight-streaming GEMV for M <= 8 token rows.  Each CTA owns
+//                 row blocks of the [N][Kp] weight matrix and stages them into
+//                 shared memory with bulk TMA copies (cp.async.bulk) issued
+//                 before it quantises the activations, so HBM streaming and the
+//                 activation prologue overlap.  int8 weights: exact int32 dp4a
+//                 dot + the reference epilogue (bias + ((float)dot*as)*ws).
+//   k_gemm_simt   generic tiled GEMM for any M (prefill until the tcgen05 path
+//                 takes over), same numerics.
+//   k_quant       per-row activation quantisation (reference gpt2.c:446-461).
+//   k_embed, k_norm, k_rope_kv, k_swiglu, k_gelu, k_attn_part/k_attn_combine,
+//   k_argmax*, k_step_advance.
+//
+// Every index that comes from the caller (token ids, positions, slots) is
+// bounds-checked on the device; a bad one is skipped and recorded in the
+// library error word instead of being dereferenced.
+#include "ec_common.cuh"
+#include "ec_launch.h"
+
+#include <float.h>
+
+__device__ int g_ec_err;
+
+#define GEMV_THREADS 256
+#define GEMV_WARPS (GEMV_THREADS / 32)
+#define GEMV_MT 8          // max token rows per GEMV launch
+#define GEMV_MAX_ROWS 128  // max staged rows per block (val[] size)
+
+// ---------------------------------------------------------------------------
+// GEMV
+// ---------------------------------------------------------------------------
+
+struct GemvSmem {
+    // Layout of the dynamic shared memory, computed identically on host and
+    // device: [stages][stage_bytes] | x region | val[GEMV_MAX_ROWS][MT] (4 B) |
+    // part[8][MT] | ascale[MT] | red[8][MT] | mbarriers[stages]
+    uint32_t stage_bytes, x_off, val_off, part_off, asc_off, red_off, bar_off, total;
+};
+
+__host__ __device__ inline uint32_t ec_align16(uint32_t v) { return (v + 15u) & ~15u; }
+
+__host__ __device__ inline GemvSmem gemv_layout(int wt, int M, int Kp, int block_rows, int stages) {
+    GemvSmem s;
+    const uint32_t elt = wt == EC_W_I8 ? 1u : 2u;
+    s.stage_bytes = ec_align16((uint32_t)block_rows * (uint32_t)Kp * elt);
+    uint32_t off = s.stage_bytes * (uint32_t)stages;
+    s.x_off = off;
+    off += ec_align16((uint32_t)M * (uint32_t)Kp * (wt == EC_W_I8 ? 1u : 4u));
+    s.val_off = off;
+    off += GEMV_MAX_ROWS * GEMV_MT * 4;
+    s.part_off = off;
+    off += GEMV_WARPS * GEMV_MT * 4;
+    s.asc_off = off;
+    off += GEMV_MT * 4;
+    s.red_off = off;
+    off += GEMV_WARPS * GEMV_MT * 4;
+    s.bar_off = ec_align16(off);
+    s.total = s.bar_off + 8u * (uint32_t)stages;
+    return s;
+}
+
+template <int WT>
+struct GemvAcc;
+template <> struct GemvAcc<EC_W_I8> { typedef int T; };
+template <> struct GemvAcc<EC_W_F16> { typedef float T; };
+template <> struct GemvAcc<EC_W_BF16> { typedef float T; };
+
+EC_DEV void ec_bf16x8_to_f32(const uint4 w, float f[8]) {
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        f[2 * i] = __uint_as_float(u[i] << 16);
+        f[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+    }
+}
+
+EC_DEV void ec_f16x8_to_f32(const uint4 w, float f[8]) {
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float2 t = __half22float2(*reinterpret_cast<const __half2 *>(&u[i]));
+        f[2 * i] = t.x;
+        f[2 * i + 1] = t.y;
+    }
+}
+
+// Apply the epilogue of one (row value, token) pair set.  `v_lo` is the value
+// of staged row r (global row n_lo); for pair blocks `v_hi` is the partner row.
+EC_DEV void gemv_store_kv(const ec_kvgeo &g, uint16_t *cache, int slot, int pos, int col, float v) {
+    cache[((size_t)slot * g.C + pos) * g.kv + col] = ec_f2h(v);
+}
+
+template <int WT>
+__global__ void __launch_bounds__(GEMV_THREADS)
+k_gemv(const ec_gemv_args a, const int stages) {
+    typedef typename GemvAcc<WT>::T Acc;
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int M = a.M;
+    const GemvSmem L = gemv_layout(WT, M, a.Kp, a.block_rows, stages);
+    unsigned char *stage0 = smem;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bar_off);
+    Acc *val = reinterpret_cast<Acc *>(smem + L.val_off);
+    Acc *part = reinterpret_cast<Acc *>(smem + L.part_off);
+    float *asc = reinterpret_cast<float *>(smem + L.asc_off);
+    float *red = reinterpret_cast<float *>(smem + L.red_off);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t elt = WT == EC_W_I8 ? 1u : 2u;
+    const uint32_t row_bytes = (uint32_t)a.Kp * elt;
+    const int nch = (int)(row_bytes / 16u);            // 16-byte chunks per row
+    const int nmine = (a.nblocks - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    if (nmine <= 0) return;
+
+    auto desc = [&](int i) -> ec_block {
+        const int b = (int)blockIdx.x + i * (int)gridDim.x;
+        if (a.blocks) return a.blocks[b];
+        ec_block d;
+        d.row0 = b * a.block_rows;
+        d.nrows = min(a.block_rows, a.N - d.row0);
+        d.pair = 0;
+        d.kind = 0;
+        return d;
+    };
+    auto issue = [&](int i) {
+        const ec_block d = desc(i);
+        const int s = i % stages;
+        unsigned char *dst = stage0 + (size_t)s * L.stage_bytes;
+        const uint32_t b1 = (uint32_t)d.nrows * row_bytes;
+        const uint32_t tot = d.pair ? 2u * b1 : b1;
+        ec_mbar_expect_tx(&bars[s], tot);
+        const unsigned char *W = static_cast<const unsigned char *>(a.W);
+        ec_bulk_g2s(dst, W + (size_t)d.row0 * row_bytes, b1, &bars[s]);
+        if (d.pair) ec_bulk_g2s(dst + b1, W + (size_t)(d.row0 + d.pair) * row_bytes, b1, &bars[s]);
+    };
+
+    if (tid == 0) {
+        for (int s = 0; s < stages; ++s) ec_mbar_init(&bars[s], 1);
+        ec_fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+        const int pre = nmine < stages ? nmine : stages;
+        for (int i = 0; i < pre; ++i) issue(i);
+    }
+
+    // ---- activation prologue (overlaps the weight fetch) -------------------
+    if (WT == EC_W_I8 && a.Xq) {
+        int8_t *xs = reinterpret_cast<int8_t *>(smem + L.x_off);
+        if (tid < M) asc[tid] = a.xscale[tid];
+        for (int m = 0; m < M; ++m)
+            for (int k = tid; k < a.Kp; k += GEMV_THREADS)
+                xs[(size_t)m * a.Kp + k] = k < a.K ? a.Xq[(size_t)m * a.ldx + k] : (int8_t)0;
+    } else if (WT == EC_W_I8) {
+        int8_t *xs = reinterpret_cast<int8_t *>(smem + L.x_off);
+        float mx[GEMV_MT];
+#pragma unroll
+        for (int m = 0; m < GEMV_MT; ++m) mx[m] = 0.0f;
+        for (int k = tid; k < a.K; k += GEMV_THREADS) {
+#pragma unroll
+            for (int m = 0; m < GEMV_MT; ++m)
+                if (m < M) mx[m] = ec_max_keep(mx[m], fabsf(a.X[(size_t)m * a.ldx + k]));
+        }
+#pragma unroll
+        for (int m = 0; m < GEMV_MT; ++m) {
+            float w = ec_warp_max(mx[m]);
+            if (lane == 0 && m < M) red[warp * GEMV_MT + m] = w;
+        }
+        __syncthreads();
+        if (tid < M) {
+            float w = 0.0f;
+            for (int i = 0; i < GEMV_WARPS; ++i) w = ec_max_keep(w, red[i * GEMV_MT + tid]);
+            asc[tid] = w > 0.0f ? __fdiv_rn(w, 127.0f) : 1.0f;
+        }
+        __syncthreads();
+        for (int m = 0; m < M; ++m) {
+            const float s = asc[m];
+            const float *xr = a.X + (size_t)m * a.ldx;
+            for (int k = tid; k < a.Kp; k += GEMV_THREADS)
+                xs[(size_t)m * a.Kp + k] = (int8_t)(k < a.K ? ec_quant1(xr[k], s) : 0);
+        }
+    } else {
+        // fp32 activations, stored as two planes per row (elements 0-3 and
+        // 4-7 of every 8-element chunk) so that 16-byte reads are conflict-free.
+        float *xs = reinterpret_cast<float *>(smem + L.x_off);
+        for (int m = 0; m < M; ++m) {
+            const float *xr = a.X + (size_t)m * a.ldx;
+            float *xm = xs + (size_t)m * a.Kp;
+            for (int k = tid; k < a.Kp; k += GEMV_THREADS) {
+                const float v = k < a.K ? xr[k] : 0.0f;
+                const int c = k >> 3, e = k & 7;
+                xm[(e >> 2) * (a.Kp >> 1) + c * 4 + (e & 3)] = v;
+            }
+        }
+    }
+    __syncthreads();
+
+    for (int i = 0; i < nmine; ++i) {
+        const int s = i % stages;
+        const ec_block d = desc(i);
+        const int rows = d.pair ? 2 * d.nrows : d.nrows;
+        const bool ok = ec_mbar_wait(&bars[s], (uint32_t)((i / stages) & 1), &g_ec_err);
+        if (__syncthreads_or(!ok)) return;
+        const unsigned char *st = stage0 + (size_t)s * L.stage_bytes;
+
+        const int wpr = rows >= 8 ? 1 : (rows >= 4 ? 2 : (rows >= 2 ? 4 : 8));
+        const int conc = GEMV_WARPS / wpr;
+        for (int r0 = 0; r0 < rows; r0 += conc) {
+            const int r = r0 + warp / wpr, sub = warp % wpr;
+            if (r < rows) {
+                Acc acc[GEMV_MT];
+#pragma unroll
+                for (int m = 0; m < GEMV_MT; ++m) acc[m] = 0;
+                const uint4 *wrow = reinterpret_cast<const uint4 *>(st + (size_t)r * row_bytes);
+                for (int c = sub * 32 + lane; c < nch; c += wpr * 32) {
+                    const uint4 w = wrow[c];
+                    if (WT == EC_W_I8) {
+                        const int8_t *xs = reinterpret_cast<const int8_t *>(smem + L.x_off);
+#pragma unroll
+                        for (int m = 0; m < GEMV_MT; ++m) {
+                            if (m < M) {
+                                const uint4 x = reinterpret_cast<const uint4 *>(xs + (size_t)m * a.Kp)[c];
+                                int t = (int)acc[m];
+                                t = __dp4a((int)w.x, (int)x.x, t);
+                                t = __dp4a((int)w.y, (int)x.y, t);
+                                t = __dp4a((int)w.z, (int)x.z, t);
+                                t = __dp4a((int)w.w, (int)x.w, t);
+                                acc[m] = t;
+                            }
+                        }
+                    } else {
+                        float f[8];
+                        if (WT == EC_W_F16) ec_f16x8_to_f32(w, f); else ec_bf16x8_to_f32(w, f);
+                        const float *xs = reinterpret_cast<const float *>(smem + L.x_off);
+#pragma unroll
+                        for (int m = 0; m < GEMV_MT; ++m) {
+                            if (m < M) {
+                                const float *xm = xs + (size_t)m * a.Kp;
+                                const float4 x0 = reinterpret_cast<const float4 *>(xm)[c];
+                                const float4 x1 = reinterpret_cast<const float4 *>(xm + (a.Kp >> 1))[c];
+                                float t = (float)acc[m];
+                                t = fmaf(f[0], x0.x, t); t = fmaf(f[1], x0.y, t);
+                                t = fmaf(f[2], x0.z, t); t = fmaf(f[3], x0.w, t);
+                                t = fmaf(f[4], x1.x, t); t = fmaf(f[5], x1.y, t);
+                                t = fmaf(f[6], x1.z, t); t = fmaf(f[7], x1.w, t);
+                                acc[m] = t;
+                            }
+                        }
+                    }
+                }
+#pragma unroll
+                for (int m = 0; m < GEMV_MT; ++m) {
+                    if (WT == EC_W_I8) acc[m] = ec_warp_sum_i((int)acc[m]);
+                    else acc[m] = ec_warp_sum((float)acc[m]);
+                }
+                if (lane == 0) {
+                    for (int m = 0; m < M; ++m) {
+                        if (wpr == 1) val[r * GEMV_MT + m] = acc[m];
+                        else part[warp * GEMV_MT + m] = acc[m];
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        if (wpr > 1) {
+            for (int idx = tid; idx < rows * M; idx += GEMV_THREADS) {
+                const int r = idx / M, m = idx % M;
+                Acc t = 0;
+                for (int q = 0; q < wpr; ++q) t = t + part[(r * wpr + q) * GEMV_MT + m];
+                val[r * GEMV_MT + m] = t;
+            }
+            __syncthreads();
+        }
+        // The stage has been consumed: refill it with block i + stages.
+        if (tid == 0 && i + stages < nmine) issue(i + stages);
+
+        // ---- epilogue ------------------------------------------------------
+        const int nout = d.nrows;
+        for (int idx = tid; idx < nout * M; idx += GEMV_THREADS) {
+            const int r = idx / M, m = idx % M;
+            const int n_lo = d.row0 + r;
+            float v_lo, v_hi = 0.0f;
+            int n_hi = n_lo + d.pair;
+            if (WT == EC_W_I8) {
+                const float as = asc[m];
+                float t = __fmul_rn(__fmul_rn(__int2float_rn((int)val[r * GEMV_MT + m]), as),
+                                    a.wscale ? a.wscale[n_lo] : 1.0f);
+                v_lo = __fadd_rn(a.bias ? a.bias[n_lo] : 0.0f, t);
+                if (d.pair) {
+                    float u = __fmul_rn(__fmul_rn(__int2float_rn((int)val[(d.nrows + r) * GEMV_MT + m]), as),
+                                        a.wscale ? a.wscale[n_hi] : 1.0f);
+                    v_hi = __fadd_rn(a.bias ? a.bias[n_hi] : 0.0f, u);
+                }
+            } else {
+                v_lo = (float)val[r * GEMV_MT + m];
+                if (a.bias) v_lo = __fadd_rn(v_lo, a.bias[n_lo]);
+                if (d.pair) {
+                    v_hi = (float)val[(d.nrows + r) * GEMV_MT + m];
+                    if (a.bias) v_hi = __fadd_rn(v_hi, a.bias[n_hi]);
+                }
+            }
+            float *orow = a.out + (size_t)m * a.ldo;
+            switch (a.epi) {
+            case EC_EPI_STORE: orow[n_lo] = v_lo; if (d.pair) orow[n_hi] = v_hi; break;
+            case EC_EPI_RESID:
+                orow[n_lo] = __fadd_rn(orow[n_lo], v_lo);
+                if (d.pair) orow[n_hi] = __fadd_rn(orow[n_hi], v_hi);
+                break;
+            case EC_EPI_GELU:
+                orow[n_lo] = ec_gelu(v_lo);
+                if (d.pair) orow[n_hi] = ec_gelu(v_hi);
+                break;
+            case EC_EPI_SWIGLU: orow[n_lo] = __fmul_rn(ec_silu(v_lo), v_hi); break;
+            case EC_EPI_QKV: {
+                const ec_kvgeo &g = a.geo;
+                const int pos = a.tk.pos[m], slot = a.tk.slot[m];
+                if (pos < 0 || pos >= g.C || slot < 0 || slot >= g.B) {
+                    atomicCAS(&g_ec_err, 0, EC_KERR_BAD_INDEX);
+                    break;
+                }
+                if (d.kind == EC_BK_ROPE) {
+                    const int half = g.hd >> 1;
+                    const int i2 = (n_lo % g.hd);   // < half by construction
+                    const double c = g.rope_cos[(size_t)pos * half + i2];
+                    const double sn = g.rope_sin[(size_t)pos * half + i2];
+                    const double av = (double)v_lo, bv = (double)v_hi;
+                    const float lo = (float)__dsub_rn(__dmul_rn(av, c), __dmul_rn(bv, sn));
+                    const float hi = (float)__dadd_rn(__dmul_rn(av, sn), __dmul_rn(bv, c));
+                    v_lo = lo;
+                    v_hi = hi;
+                }
+                const int nn[2] = {n_lo, n_hi};
+                const float vv[2] = {v_lo, v_hi};
+                for (int h = 0; h < (d.pair ? 2 : 1); ++h) {
+                    const int n = nn[h];
+                    if (n < g.E) orow[n] = vv[h];
+                    else if (n < g.E + g.kv) gemv_store_kv(g, g.kc, slot, pos, n - g.E, vv[h]);
+                    else gemv_store_kv(g, g.vc, slot, pos, n - g.E - g.kv, vv[h]);
+                }
+                break;
+            }
+            default: break;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+static int g_ec_max_optin_smem = 0;
+
+extern "C" int ec_kernels_init(void) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    e = cudaDeviceGetAttribute(&g_ec_max_optin_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return (int)e;
+    e = cudaFuncSetAttribute(k_gemv<EC_W_I8>, cudaFuncAttributeMaxDynamicSharedMemorySize, g_ec_max_optin_smem);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_gemv<EC_W_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, g_ec_max_optin_smem);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_gemv<EC_W_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, g_ec_max_optin_smem);
+    return (int)e;
+}
+
+extern "C" int ec_launch_gemv(const ec_gemv_args *a, int num_sms, cudaStream_t stream) {
+    if (a->M <= 0 || a->nblocks <= 0) return 0;
+    if (a->M > GEMV_MT || a->block_rows > GEMV_MAX_ROWS || (a->Kp % 16) != 0) return (int)cudaErrorInvalidValue;
+    if (g_ec_max_optin_smem == 0) {
+        const int e = ec_kernels_init();
+        if (e) return e;
+    }
+    // A CTA owning several blocks keeps up to 3 of them in flight.
+    const int per_sm_target = 2;
+    int grid = a->nblocks;
+    const int cap = num_sms * per_sm_target;
+    int stages = 1;
+    if (grid > cap) { grid = cap; stages = 3; }
+    GemvSmem L = gemv_layout(a->wt, a->M, a->Kp, a->block_rows, stages);
+    while (stages > 1 && (int)L.total > g_ec_max_optin_smem / per_sm_target) {
+        --stages;
+        L = gemv_layout(a->wt, a->M, a->Kp, a->block_rows, stages);
+    }
+    if ((int)L.total > g_ec_max_optin_smem) return (int)cudaErrorInvalidValue;
+    switch (a->wt) {
+    case EC_W_I8: k_gemv<EC_W_I8><<<grid, GEMV_THREADS, L.total, stream>>>(*a, stages); break;
+    case EC_W_F16: k_gemv<EC_W_F16><<<grid, GEMV_THREADS, L.total, stream>>>(*a, stages); break;
+    default: k_gemv<EC_W_BF16><<<grid, GEMV_THREADS, L.total, stream>>>(*a, stages); break;
+    }
+    return (int)cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Generic tiled GEMM (any M).  C[m][n] over a 64x64 tile per CTA, 256 threads,
+// each thread a 4x4 micro-tile.  int8: exact int32 dp4a accumulation and the
+// reference epilogue; 16-bit weights: fp32 FMA accumulation.
+// ---------------------------------------------------------------------------
+
+#define GT_BM 64
+#define GT_BN 64
+#define GT_BK 64
+
+EC_DEV float gemm_finish(const ec_gemm_args &a, int m, int n, float acc_f, int acc_i) {
+    float v;
+    if (a.wt == EC_W_I8) {
+        float t = __fmul_rn(__fmul_rn(__int2float_rn(acc_i), a.a_scale[m]), a.wscale ? a.wscale[n] : 1.0f);
+        v = __fadd_rn(a.bias ? a.bias[n] : 0.0f, t);
+    } else {
+        v = acc_f;
+        if (a.bias) v = __fadd_rn(v, a.bias[n]);
+    }
+    return v;
+}
+
+EC_DEV void gemm_apply(const ec_gemm_args &a, int m, int n, float v) {
+    float *o = a.out + (size_t)m * a.ldo + n;
+    if (a.epi == EC_EPI_RESID) *o = __fadd_rn(*o, v);
+    else if (a.epi == EC_EPI_GELU) *o = ec_gelu(v);
+    else *o = v;
+}
+
+__global__ void __launch_bounds__(256) k_gemm_i8(const ec_gemm_args a) {
+    __shared__ __align__(16) int8_t As[GT_BM][GT_BK + 16];
+    __shared__ __align__(16) int8_t Ws[GT_BN][GT_BK + 16];
+    const int tid = threadIdx.x;
+    const int m0 = blockIdx.y * GT_BM, n0 = blockIdx.x * GT_BN;
+    const int tm = (tid / 16) * 4, tn = (tid % 16) * 4;
+    int acc[4][4] = {};
+    for (int k0 = 0; k0 < a.Kp; k0 += GT_BK) {
+        // 64 rows x 64 bytes per operand = 256 x 16 B
+        {
+            const int r = tid / 4, c = (tid % 4) * 16;
+            uint4 va = make_uint4(0, 0, 0, 0), vw = make_uint4(0, 0, 0, 0);
+            if (m0 + r < a.M && k0 + c < a.Kp)
+                va = *reinterpret_cast<const uint4 *>(a.Aq + (size_t)(m0 + r) * a.Kp + k0 + c);
+            if (n0 + r < a.N && k0 + c < a.Kp)
+                vw = *reinterpret_cast<const uint4 *>(static_cast<const int8_t *>(a.W) + (size_t)(n0 + r) * a.Kp + k0 + c);
+            *reinterpret_cast<uint4 *>(&As[r][c]) = va;
+            *reinterpret_cast<uint4 *>(&Ws[r][c]) = vw;
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int kk = 0; kk < GT_BK; kk += 4) {
+            int av[4], wv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) av[i] = *reinterpret_cast<const int *>(&As[tm + i][kk]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) wv[j] = *reinterpret_cast<const int *>(&Ws[tn + j][kk]);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = __dp4a(av[i], wv[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int m = m0 + tm + i, n = n0 + tn + j;
+            if (m < a.M && n < a.N) gemm_apply(a, m, n, gemm_finish(a, m, n, 0.0f, acc[i][j]));
+        }
+}
+
+template <int WT>
+__global__ void __launch_bounds__(256) k_gemm_f(const ec_gemm_args a) {
+    __shared__ float As[GT_BK / 2][GT_BM + 4];   // [k][m]
+    __shared__ float Ws[GT_BK / 2][GT_BN + 4];   // [k][n]
+    const int tid = threadIdx.x;
+    const int m0 = blockIdx.y * GT_BM, n0 = blockIdx.x * GT_BN;
+    const int tm = (tid / 16) * 4, tn = (tid % 16) * 4;
+    const int BK = GT_BK / 2;
+    float acc[4][4] = {};
+    const uint16_t *W = static_cast<const uint16_t *>(a.W);
+    for (int k0 = 0; k0 < a.Kp; k0 += BK) {
+        for (int e = tid; e < GT_BM * BK; e += 256) {
+            const int r = e / BK, c = e % BK;
+            const int k = k0 + c;
+            As[c][r] = (m0 + r < a.M && k < a.K) ? a.X[(size_t)(m0 + r) * a.ldx + k] : 0.0f;
+            Ws[c][r] = (n0 + r < a.N && k < a.Kp) ? ec_h2f(W[(size_t)(n0 + r) * a.Kp + k], WT == EC_W_BF16) : 0.0f;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int kk = 0; kk < BK; ++kk) {
+            float av[4], wv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) av[i] = As[kk][tm + i];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) wv[j] = Ws[kk][tn + j];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], wv[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int m = m0 + tm + i, n = n0 + tn + j;
+            if (m < a.M && n < a.N) gemm_apply(a, m, n, gemm_finish(a, m, n, acc[i][j], 0));
+        }
+}
+
+extern "C" int ec_launch_gemm(const ec_gemm_args *a, cudaStream_t stream) {
+    if (a->M <= 0 || a->N <= 0) return 0;
+    if (a->Kp % 16) return (int)cudaErrorInvalidValue;
+    dim3 grid((a->N + GT_BN - 1) / GT_BN, (a->M + GT_BM - 1) / GT_BM);
+    if (grid.y > 65535) return (int)cudaErrorInvalidValue;
+    if (a->wt == EC_W_I8) k_gemm_i8<<<grid, 256, 0, stream>>>(*a);
+    else if (a->wt == EC_W_F16) k_gemm_f<EC_W_F16><<<grid, 256, 0, stream>>>(*a);
+    else k_gemm_f<EC_W_BF16><<<grid, 256, 0, stream>>>(*a);
+    return (int)cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Row-wise ops
+// ---------------------------------------------------------------------------
+
+template <typename T>
+EC_DEV T block_reduce_sum(T v, T *sh) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();
+    if (lane == 0) sh[warp] = v;
+    __syncthreads();
+    T t = 0;
+    for (int i = 0; i < nw; ++i) t += sh[i];   // fixed order: deterministic
+    return t;
+}
+
+EC_DEV float block_reduce_max(float v, float *sh) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = ec_warp_max(v);
+    __syncthreads();
+    if (lane == 0) sh[warp] = v;
+    __syncthreads();
+    float t = 0.0f;
+    for (int i = 0; i < nw; ++i) t = ec_max_keep(t, sh[i]);
+    return t;
+}
+
+// Per-row activation quantisation: q[m][k] (k < Kp, zero padding), scale[m].
+__global__ void __launch_bounds__(256) k_quant(int8_t *q, float *scale, const float *X, int ldx, int K, int Kp) {
+    __shared__ float sh[32];
+    const int m = blockIdx.x;
+    const float *xr = X + (size_t)m * ldx;
+    float mx = 0.0f;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) mx = ec_max_keep(mx, fabsf(xr[k]));
+    mx = block_reduce_max(mx, sh);
+    const float s = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 1.0f;
+    if (threadIdx.x == 0) scale[m] = s;
+    for (int k = threadIdx.x; k < Kp; k += blockDim.x)
+        q[(size_t)m * Kp + k] = (int8_t)(k < K ? ec_quant1(xr[k], s) : 0);
+}
+
+extern "C" int ec_launch_quant(int8_t *q, float *scale, const float *X, int ldx, int M, int K, int Kp,
+                               cudaStream_t stream) {
+    if (M <= 0) return 0;
+    k_quant<<<M, 256, 0, stream>>>(q, scale, X, ldx, K, Kp);
+    return (int)cudaGetLastError();
+}
+
+__global__ void __launch_bounds__(256) k_embed(float *x, const uint16_t *wte, const uint16_t *wpe, int ld,
+                                               int bf16, ec_tokens tk, int E, int V, int C) {
+    const int m = blockIdx.x;
+    const int t = tk.tok[m];
+    const int p = tk.pos ? tk.pos[m] : 0;
+    if (t < 0 || t >= V || (wpe && (p < 0 || p >= C))) {
+        if (threadIdx.x == 0) atomicCAS(&g_ec_err, 0, EC_KERR_BAD_INDEX);
+        return;
+    }
+    for (int d = threadIdx.x; d < E; d += blockDim.x) {
+        float e = ec_h2f(wte[(size_t)t * ld + d], bf16);
+        if (wpe) e = __fadd_rn(e, ec_h2f(wpe[(size_t)p * ld + d], bf16));
+        x[(size_t)m * E + d] = e;
+    }
+}
+
+extern "C" int ec_launch_embed(float *x, const uint16_t *wte, const uint16_t *wpe, int ld, int is_bf16,
+                               ec_tokens tk, int M, int E, int V, int C, cudaStream_t stream) {
+    if (M <= 0) return 0;
+    k_embed<<<M, 256, 0, stream>>>(x, wte, wpe, ld, is_bf16, tk, E, V, C);
+    return (int)cudaGetLastError();
+}
+
+// LayerNorm (beta != NULL) / RMSNorm (beta == NULL) with fp64 statistics,
+// products rounded separately as in the reference's -ffp-contract=off build.
+__global__ void __launch_bounds__(256) k_norm(float *out, const float *x, const float *g, const float *b,
+                                              int E, double eps) {
+    __shared__ double sh[32];
+    const int m = blockIdx.x;
+    const float *xr = x + (size_t)m * E;
+    float *orow = out + (size_t)m * E;
+    if (b) {
+        double s = 0.0;
+        for (int i = threadIdx.x; i < E; i += blockDim.x) s = __dadd_rn(s, (double)xr[i]);
+        const double mean = __ddiv_rn(block_reduce_sum(s, sh), (double)E);
+        double v = 0.0;
+        for (int i = threadIdx.x; i < E; i += blockDim.x) {
+            const double d = __dsub_rn((double)xr[i], mean);
+            v = __dadd_rn(v, __dmul_rn(d, d));
+        }
+        const double var = __ddiv_rn(block_reduce_sum(v, sh), (double)E);
+        const double rstd = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(var, eps)));
+        for (int i = threadIdx.x; i < E; i += blockDim.x) {
+            const float t = (float)__dmul_rn(__dsub_rn((double)xr[i], mean), rstd);
+            orow[i] = __fadd_rn(__fmul_rn(t, g[i]), b[i]);
+        }
+    } else {
+        double s = 0.0;
+        for (int i = threadIdx.x; i < E; i += blockDim.x) {
+            const double d = (double)xr[i];
+            s = __dadd_rn(s, __dmul_rn(d, d));
+        }
+        const double ms = block_reduce_sum(s, sh);
+        const double rstd = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ms, (double)E), eps)));
+        for (int i = threadIdx.x; i < E; i += blockDim.x)
+            orow[i] = __fmul_rn((float)__dmul_rn((double)xr[i], rstd), g[i]);
+    }
+}
+
+extern "C" int ec_launch_norm(float *out, const float *x, const float *gamma, const float *beta,
+                              int M, int E, double eps, cudaStream_t stream) {
+    if (M <= 0) return 0;
+    k_norm<<<M, 256, 0, stream>>>(out, x, gamma, beta, E, eps);
+    return (int)cudaGetLastError();
+}
+
+// RoPE + KV store from a [M][ldq] buffer whose columns are q | k | v.
+__global__ void __launch_bounds__(256) k_rope_kv(float *qkv, int ldq, ec_tokens tk, ec_kvgeo g, int H, int KVH) {
+    const int m = blockIdx.x;
+    const int pos = tk.pos[m], slot = tk.slot[m];
+    if (pos < 0 || pos >= g.C || slot < 0 || slot >= g.B) {
+        if (threadIdx.x == 0) atomicCAS(&g_ec_err, 0, EC_KERR_BAD_INDEX);
+        return;
+    }
+    float *row = qkv + (size_t)m * ldq;
+    const int half = g.hd >> 1;
+    if (g.rope_cos) {
+        const int npairs = (H + KVH) * half;
+        for (int idx = threadIdx.x; idx < npairs; idx += blockDim.x) {
+            const int h = idx / half, i = idx % half;
+            float *v = row + (h < H ? h * g.hd : g.E + (h - H) * g.hd);
+            const double c = g.rope_cos[(size_t)pos * half + i], s = g.rope_sin[(size_t)pos * half + i];
+            const double av = (double)v[i], bv = (double)v[i + half];
+            v[i] = (float)__dsub_rn(__dmul_rn(av, c), __dmul_rn(bv, s));
+            v[i + half] = (float)__dadd_rn(__dmul_rn(av, s), __dmul_rn(bv, c));
+        }
+        __syncthreads();
+    }
+    uint16_t *kr = g.kc + ((size_t)slot * g.C + pos) * g.kv;
+    uint16_t *vr = g.vc + ((size_t)slot * g.C + pos) * g.kv;
+    for (int d = threadIdx.x; d < g.kv; d += blockDim.x) {
+        kr[d] = ec_f2h(row[g.E + d]);
+        vr[d] = ec_f2h(row[g.E + g.kv + d]);
+    }
+}
+
+extern "C" int ec_launch_rope_kv(float *qkv, int ldq, ec_tokens tk, ec_kvgeo geo, int H, int KVH, int M,
+                                 cudaStream_t stream) {
+    if (M <= 0) return 0;
+    k_rope_kv<<<M, 256, 0, stream>>>(qkv, ldq, tk, geo, H, KVH);
+    return (int)cudaGetLastError();
+}
+
+__global__ void k_swiglu(float *out, int ldo, const float *gu, int ldg, int I, int M) {
+    const size_t n = (size_t)M * I;
+    for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < n; idx += (size_t)gridDim.x * blockDim.x) {
+        const size_t m = idx / I, j = idx % I;
+        const float g = gu[m * ldg + j], u = gu[m * ldg + I + j];
+        out[m * ldo + j] = __fmul_rn(ec_silu(g), u);
+    }
+}
+
+extern "C" int ec_launch_swiglu(float *out, int ldo, const float *gu, int ldg, int I, int M, cudaStream_t stream) {
+    if (M <= 0) return 0;
+    const size_t n = (size_t)M * I;
+    const int grid = (int)((n + 255) / 256 > 65535 ? 65535 : (n + 255) / 256);
+    k_swiglu<<<grid, 256, 0, stream>>>(out, ldo, gu, ldg, I, M);
+    return (int)cudaGetLastError();
+}
+
+__global__ void k_gelu(float *x, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        x[i] = ec_gelu(x[i]);
+}
+
+extern "C" int ec_launch_gelu_inplace(float *x, size_t n, cudaStream_t stream) {
+    if (!n) return 0;
+    const int grid = (int)((n + 255) / 256 > 65535 ? 65535 : (n + 255) / 256);
+    k_gelu<<<grid, 256, 0, stream>>>(x, n);
+    return (int)cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Attention: split over key positions (flash-decoding), then combine.
+// Part layout: [M][H][nsplit][hd + 2] = partial output (unnormalised), max, sum.
+// ---------------------------------------------------------------------------
+
+#define ATT_THREADS 128
+#define ATT_MAX_CHUNK 1024
+
+extern "C" size_t ec_attention_scratch_floats(int M, int H, int hd, int nsplit) {
+    return (size_t)M * H * nsplit * (hd + 2);
+}
+
+__global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const ec_attn_args a) {
+    __shared__ float qs[256];
+    __shared__ float sc[ATT_MAX_CHUNK];
+    __shared__ float red[ATT_THREADS / 32];
+    __shared__ double redd[ATT_THREADS / 32];
+    const int s = blockIdx.x, h = blockIdx.y, m = blockIdx.z;
+    const ec_kvgeo &g = a.geo;
+    const int hd = g.hd;
+    const int pos = a.tk.pos[m], slot = a.tk.slot[m];
+    float *part = a.part + (((size_t)m * a.H + h) * a.nsplit + s) * (hd + 2);
+    if (pos < 0 || pos >= g.C || slot < 0 || slot >= g.B) {
+        if (threadIdx.x == 0) atomicCAS(&g_ec_err, 0, EC_KERR_BAD_INDEX);
+        return;
+    }
+    int lo = 0;
+    if (a.window > 0) { lo = pos - a.window + 1; if (lo < 0) lo = 0; }
+    const int len = pos + 1 - lo;
+    const int chunk = (len + a.nsplit - 1) / a.nsplit;
+    const int p0 = lo + s * chunk;
+    const int p1 = min(pos + 1, p0 + chunk);
+    if (p0 >= p1 || chunk > ATT_MAX_CHUNK) {
+        if (chunk > ATT_MAX_CHUNK && threadIdx.x == 0) atomicCAS(&g_ec_err, 0, EC_KERR_BAD_INDEX);
+        if (threadIdx.x == 0) { part[hd] = -FLT_MAX; part[hd + 1] = 0.0f; }
+        for (int d = threadIdx.x; d < hd; d += blockDim.x) part[d] = 0.0f;
+        return;
+    }
+    const int kvh = h * a.KVH / a.H;
+    const uint16_t *kb = g.kc + (size_t)slot * g.C * g.kv + (size_t)kvh * hd;
+    const uint16_t *vb = g.vc + (size_t)slot * g.C * g.kv + (size_t)kvh * hd;
+    const float *q = a.q + (size_t)m * a.ldq + (size_t)h * hd;
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) qs[d] = q[d];
+    __syncthreads();
+    const double inv_hd = 1.0 / sqrt((double)hd);
+    // scores: one position per thread, the reference's sequential fp32 dot
+    float mx = -FLT_MAX;
+    for (int p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
+        const uint16_t *kp = kb + (size_t)p * g.kv;
+        float acc = 0.0f;
+        for (int d = 0; d < hd; d += 8) {
+            const uint4 w = *reinterpret_cast<const uint4 *>(kp + d);
+            float f[8];
+            ec_f16x8_to_f32(w, f);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc = __fadd_rn(acc, __fmul_rn(qs[d + e], f[e]));
+        }
+        const float sv = (float)__dmul_rn((double)acc, inv_hd);
+        sc[p - p0] = sv;
+        mx = ec_max_keep(mx, sv);
+    }
+    {
+        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+        float w = mx;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) { float t = __shfl_xor_sync(0xffffffffu, w, o); w = t > w ? t : w; }
+        if (lane == 0) red[warp] = w;
+        __syncthreads();
+        mx = red[0];
+        for (int i = 1; i < ATT_THREADS / 32; ++i) mx = red[i] > mx ? red[i] : mx;
+    }
+    double sum = 0.0;
+    for (int p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
+        const float e = expf(sc[p - p0] - mx);
+        sc[p - p0] = e;
+        sum += (double)e;
+    }
+    {
+        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+        sum = ec_warp_sum_d(sum);
+        if (lane == 0) redd[warp] = sum;
+        __syncthreads();
+        sum = 0.0;
+        for (int i = 0; i < ATT_THREADS / 32; ++i) sum += redd[i];
+    }
+    // unnormalised P.V: one output dim per thread, sequential over positions
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float o = 0.0f;
+        for (int p = p0; p < p1; ++p)
+            o = __fadd_rn(o, __fmul_rn(sc[p - p0], __half2float(__ushort_as_half(vb[(size_t)p * g.kv + d]))));
+        part[d] = o;
+    }
+    if (threadIdx.x == 0) { part[hd] = mx; part[hd + 1] = (float)sum; }
+}
+
+__global__ void k_attn_combine(const ec_attn_args a) {
+    const int h = blockIdx.x, m = blockIdx.y;
+    const int hd = a.geo.hd;
+    const float *part = a.part + ((size_t)m * a.H + h) * a.nsplit * (hd + 2);
+    float M = -FLT_MAX;
+    for (int s = 0; s < a.nsplit; ++s) M = ec_max_keep(M, part[s * (hd + 2) + hd]);
+    double L = 0.0;
+    for (int s = 0; s < a.nsplit; ++s) {
+        const float ls = part[s * (hd + 2) + hd + 1];
+        if (ls > 0.0f) L += (double)ls * exp((double)part[s * (hd + 2) + hd] - (double)M);
+    }
+    const double invL = L > 0.0 ? 1.0 / L : 0.0;
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        double o = 0.0;
+        for (int s = 0; s < a.nsplit; ++s) {
+            const float ls = part[s * (hd + 2) + hd + 1];
+            if (ls > 0.0f) o += (double)part[s * (hd + 2) + d] * exp((double)part[s * (hd + 2) + hd] - (double)M);
+        }
+        a.out[(size_t)m * a.ldo + (size_t)h * hd + d] = (float)(o * invL);
+    }
+}
+
+extern "C" int ec_launch_attention(const ec_attn_args *a, cudaStream_t stream) {
+    if (a->M <= 0) return 0;
+    if (a->geo.hd > 256 || a->geo.hd % 8 || a->nsplit < 1) return (int)cudaErrorInvalidValue;
+    dim3 g1(a->nsplit, a->H, a->M);
+    k_attn_part<<<g1, ATT_THREADS, 0, stream>>>(*a);
+    dim3 g2(a->H, a->M);
+    k_attn_combine<<<g2, 128, 0, stream>>>(*a);
+    return (int)cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Argmax (lowest index among equal maxima) and decode bookkeeping
+// ---------------------------------------------------------------------------
+
+EC_DEV void argmax_merge(float &bv, int &bi, float v, int i) {
+    if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+}
+
+__global__ void __launch_bounds__(256) k_argmax_part(const float *logits, int ld, int N, int nchunk, float2 *part) {
+    __shared__ float sv[8];
+    __shared__ int si[8];
+    const int c = blockIdx.x, m = blockIdx.y;
+    const int per = (N + nchunk - 1) / nchunk;
+    const int b = c * per, e = min(N, b + per);
+    const float *row = logits + (size_t)m * ld;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = b + threadIdx.x; i < e; i += blockDim.x) argmax_merge(bv, bi, row[i], i);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        argmax_merge(bv, bi, ov, oi);
+    }
+    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        bv = sv[0]; bi = si[0];
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) argmax_merge(bv, bi, sv[w], si[w]);
+        part[(size_t)m * nchunk + c] = make_float2(bv, __int_as_float(bi));
+    }
+}
+
+__global__ void k_argmax_final(const float2 *part, int nchunk, int M, int id_base, int *ids, float *maxv) {
+    const int m = blockIdx.x * blockDim.x + threadIdx.x;
+    if (m >= M) return;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int c = 0; c < nchunk; ++c) {
+        const float2 p = part[(size_t)m * nchunk + c];
+        argmax_merge(bv, bi, p.x, __float_as_int(p.y));
+    }
+    if (bi == 0x7fffffff) bi = 0;   // all NaN / empty: the reference keeps index 0
+    if (ids) ids[m] = bi + id_base;
+    if (maxv) maxv[m] = bv;
+}
+
+extern "C" int ec_launch_argmax(int *ids, float *maxv, const float *logits, int ld, int N, int M,
+                                int id_base, void *part, int nchunk, cudaStream_t stream) {
+    if (M <= 0) return 0;
+    dim3 g(nchunk, M);
+    k_argmax_part<<<g, 256, 0, stream>>>(logits, ld, N, nchunk, static_cast<float2 *>(part));
+    k_argmax_final<<<(M + 127) / 128, 128, 0, stream>>>(static_cast<const float2 *>(part), nchunk, M, id_base, ids, maxv);
+    return (int)cudaGetLastError();
+}
+
+__global__ void k_step_advance(int *tok, int *pos, const int *ids, int M, int *hist, int *counter,
+                               int wrap_lo, int wrap_hi) {
+    const int step = counter ? *counter : 0;
+    for (int m = threadIdx.x; m < M; m += blockDim.x) {
+        tok[m] = ids[m];
+        const int np = pos[m] + 1;
+        pos[m] = (wrap_hi > 0 && np >= wrap_hi) ? wrap_lo : np;
+        if (hist) hist[(size_t)step * M + m] = ids[m];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && counter) *counter = step + 1;
+}
+
+extern "C" int ec_launch_step_advance(int *tok, int *pos, const int *ids, int M, int *hist, int *counter,
+                                      int wrap_lo, int wrap_hi, cudaStream_t stream) {
+    k_step_advance<<<1, 256, 0, stream>>>(tok, pos, ids, M, hist, counter, wrap_lo, wrap_hi);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int ec_kernel_error_take(cudaStream_t stream, int *code) {
+    int zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbolAsync(code, g_ec_err, sizeof(int), 0, cudaMemcpyDeviceToHost, stream);
+    if (e != cudaSuccess) return (int)e;
+    e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return (int)e;
+    if (*code) e = cudaMemcpyToSymbolAsync(g_ec_err, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    return (int)e;
+}

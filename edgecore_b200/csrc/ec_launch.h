@@ -1,0 +1,150 @@
+/*
+ * ec_launch.h -- internal C interface between the host code (ec_model.c,
+ * ec_abi.c; plain C11) and the sm_100a kernels (*.cu).  Every launcher
+ * enqueues on `stream` and returns a cudaError_t-compatible int (0 = ok).
+ */
+#ifndef EC_LAUNCH_H
+#define EC_LAUNCH_H
+
+#include <stdint.h>
+#include <stddef.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Weight element types. */
+enum { EC_W_I8 = 0, EC_W_F16 = 1, EC_W_BF16 = 2 };
+
+/* GEMV / GEMM epilogues. */
+enum {
+    EC_EPI_STORE = 0,   /* out[m][n] = v                                     */
+    EC_EPI_RESID = 1,   /* out[m][n] = out[m][n] + v   (residual add)        */
+    EC_EPI_GELU = 2,    /* out[m][n] = gelu_new(v)                           */
+    EC_EPI_SWIGLU = 3,  /* pair blocks: out[m][j] = silu(v_j) * v_{j+P}      */
+    EC_EPI_QKV = 4      /* q -> out, k/v -> fp16 KV cache (+RoPE on pairs)   */
+};
+
+/* One row block of a weight matrix: rows [row0, row0+nrows) and, when pair>0,
+ * also [row0+pair, row0+pair+nrows) (staged right after the first range). */
+typedef struct { int row0, nrows, pair, kind; } ec_block;
+
+/* Block kinds for EC_EPI_QKV. */
+enum { EC_BK_PLAIN = 0, EC_BK_ROPE = 1 };
+
+/* Per-step token inputs, all device arrays of length M. */
+typedef struct {
+    const int *tok;     /* token ids                      */
+    const int *pos;     /* absolute positions             */
+    const int *slot;    /* KV slot (already clamped)      */
+} ec_tokens;
+
+/* KV-cache / attention geometry for the QKV epilogue and attention. */
+typedef struct {
+    uint16_t *kc, *vc;        /* this layer's [B][C][kv] fp16 caches          */
+    int B;                    /* batch_cap (slots)                             */
+    int C;                    /* eff_ctx                                       */
+    int kv;                   /* n_kv_embd                                     */
+    int E;                    /* n_embd (q rows of the fused qkv)              */
+    int hd;                   /* head_dim                                      */
+    const double *rope_cos;   /* [C][hd/2] scaled cos (NULL: no RoPE)          */
+    const double *rope_sin;
+} ec_kvgeo;
+
+typedef struct {
+    const void *W;            /* [N][Kp] weights (type wt), row-major          */
+    const float *wscale;      /* [N] per-row scale (int8 only)                 */
+    const float *bias;        /* [N] or NULL                                   */
+    int wt, N, K, Kp;
+    const ec_block *blocks;   /* device table                                   */
+    int nblocks;
+    int block_rows;           /* max staged rows per block (nrows * (pair?2:1)) */
+    const float *X;           /* [M][ldx] fp32 activations                     */
+    const int8_t *Xq;         /* or pre-quantised int8 [M][ldx] ...            */
+    const float *xscale;      /* ... with per-row scales (int8 weights only)   */
+    int ldx, M;
+    float *out;               /* epilogue target                                */
+    int ldo;
+    int epi;
+    ec_tokens tk;             /* EC_EPI_QKV only                               */
+    ec_kvgeo geo;             /* EC_EPI_QKV only                               */
+} ec_gemv_args;
+
+/* Decode-shaped (M <= 8) weight-streaming GEMV with fused activation
+ * quantisation (int8) and epilogue. */
+int ec_launch_gemv(const ec_gemv_args *a, int num_sms, cudaStream_t stream);
+
+/* Generic GEMM for any M: A int8 [M][Kp] + a_scale[M] (int8 weights) or
+ * A fp32 [M][ldx] (16-bit weights); plain/resid/gelu epilogues only. */
+typedef struct {
+    const void *W; const float *wscale; const float *bias;
+    int wt, N, K, Kp;
+    const int8_t *Aq; const float *a_scale;   /* int8 weights */
+    const float *X; int ldx;                  /* 16-bit weights */
+    int M;
+    float *out; int ldo; int epi;
+} ec_gemm_args;
+int ec_launch_gemm(const ec_gemm_args *a, cudaStream_t stream);
+
+/* Per-row symmetric int8 quantisation of X [M][ldx] (K used, Kp written). */
+int ec_launch_quant(int8_t *q, float *scale, const float *X, int ldx, int M, int K, int Kp,
+                    cudaStream_t stream);
+
+/* x[m][:E] = h2f(wte[tok[m]]) (+ h2f(wpe[pos[m]])); table rows have stride ld. */
+int ec_launch_embed(float *x, const uint16_t *wte, const uint16_t *wpe, int ld, int is_bf16,
+                    ec_tokens tk, int M, int E, int V, int C, cudaStream_t stream);
+
+/* LayerNorm (beta != NULL) or RMSNorm (beta == NULL) rows, fp64 statistics. */
+int ec_launch_norm(float *out, const float *x, const float *gamma, const float *beta,
+                   int M, int E, double eps, cudaStream_t stream);
+
+/* Split q/k/v rows of a [M][E+2kv] buffer: RoPE q (in place) and k, store
+ * k/v as fp16 into the cache.  q ends up in qkv's first E columns. */
+int ec_launch_rope_kv(float *qkv, int ldq, ec_tokens tk, ec_kvgeo geo, int H, int KVH, int M,
+                      cudaStream_t stream);
+
+/* out[m][j] = silu(gu[m][j]) * gu[m][I + j] (gate/up side by side). */
+int ec_launch_swiglu(float *out, int ldo, const float *gu, int ldg, int I, int M,
+                     cudaStream_t stream);
+
+/* x[i] = gelu_new(x[i]) */
+int ec_launch_gelu_inplace(float *x, size_t n, cudaStream_t stream);
+
+/* Attention for M query rows against the fp16 KV cache (GQA / MHA).
+ * q [M][ldq] (head h at column h*hd), out [M][E]; split over positions. */
+typedef struct {
+    const float *q; int ldq;
+    float *out; int ldo;
+    ec_tokens tk; ec_kvgeo geo;
+    int H, KVH, M, window;        /* window > 0: sliding window */
+    float *part;                  /* scratch: [M][H][nsplit][hd + 2] */
+    int nsplit;
+} ec_attn_args;
+int ec_launch_attention(const ec_attn_args *a, cudaStream_t stream);
+size_t ec_attention_scratch_floats(int M, int H, int hd, int nsplit);
+
+/* Row-wise argmax (lowest index on ties) of logits [M][ld] over [0, N),
+ * reporting ids offset by id_base.  part is scratch of 2*M*nchunk words. */
+int ec_launch_argmax(int *ids, float *maxv, const float *logits, int ld, int N, int M,
+                     int id_base, void *part, int nchunk, cudaStream_t stream);
+
+/* Device-side decode bookkeeping for a captured step: tok[m] = ids[m];
+ * pos[m] += 1, wrapping to wrap_lo when it reaches wrap_hi (wrap_hi <= 0: no
+ * wrap); optionally record ids into hist[step][M] with step read from and
+ * incremented in *counter. */
+int ec_launch_step_advance(int *tok, int *pos, const int *ids, int M, int *hist, int *counter,
+                           int wrap_lo, int wrap_hi, cudaStream_t stream);
+
+/* The library-wide device error word (bounded waits that gave up, bad
+ * indices skipped).  Read and cleared by ec_kernel_error_take. */
+int ec_kernel_error_take(cudaStream_t stream, int *code);
+
+/* One-time per-device kernel attribute setup (dynamic shared memory limits). */
+int ec_kernels_init(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EC_LAUNCH_H */

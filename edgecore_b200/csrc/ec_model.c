@@ -1,0 +1,1564 @@
+/*
+ * ec_model.c -- host side of the drop-in replacement for EdgeCore's
+ * src/gpt2.c: .ecm parsing, gpt2_load / gpt2_free / gpt2_forward /
+ * qwen2_forward, and the edgecore_b200.h extensions built on them.
+ *
+ * A loaded model keeps the reference's host-visible state (the mmap'd file,
+ * the bound host weight pointers, full-size host KV buffers, the tokenizer)
+ * and adds device state, found through a registry keyed by the GPT2 address:
+ *   - every linear weight uploaded once, rows padded to a multiple of 16
+ *     elements; Qwen2 q|k|v and gate|up are fused into one matrix each (the
+ *     reference quantises the same input once per projection, so fusing is
+ *     exact), GPT-2 keeps its fused attn matrix;
+ *   - a device KV arena [n_layer][batch_cap][eff_ctx][n_kv_embd] fp16, the
+ *     reference cache layout (src/gpt2.c:312-317);
+ *   - RoPE cos/sin tables in fp64, computed on the host with the reference
+ *     formula so the rotation is bit-exact;
+ *   - workspaces and, for decode-shaped calls, captured CUDA graphs.
+ */
+#define _GNU_SOURCE
+#include "edgecore.h"
+#include "edgecore_b200.h"
+#include "ec_launch.h"
+
+#include <cuda_runtime_api.h>
+#include <errno.h>
+#include <fcntl.h>
+#include <pthread.h>
+#include <stdarg.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+/* The tokenizer is the reference's src/tokenizer.c, present when this library
+ * is linked into the reference runtime; absent (NULL) in other processes. */
+#pragma weak tokenizer_load
+#pragma weak tokenizer_free
+
+#define EC_EXPORT __attribute__((visibility("default")))
+
+/* ------------------------------------------------------------------ */
+/* errors                                                              */
+/* ------------------------------------------------------------------ */
+
+static __thread char g_err[512];
+
+static void ec_seterr(const char *fmt, ...)
+{
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+}
+
+EC_EXPORT const char *ec_last_error(void) { return g_err; }
+EC_EXPORT const char *ec_version(void) { return "edgecore_b200 0.1 sm_100a"; }
+
+#define CK(call)                                                                   \
+    do {                                                                           \
+        cudaError_t e_ = (cudaError_t)(call);                                      \
+        if (e_ != cudaSuccess) {                                                   \
+            ec_seterr("%s:%d: %s: %s", __FILE__, __LINE__, #call, cudaGetErrorString(e_)); \
+            return -1;                                                             \
+        }                                                                          \
+    } while (0)
+
+/* For the void reference entry points: report and abort, as the reference
+ * exits on an unrecoverable forward error (src/gpt2.c:442-445). */
+static void ec_fatal(const char *where)
+{
+    fprintf(stderr, "edgecore_b200: %s: %s\n", where, g_err[0] ? g_err : "error");
+    abort();
+}
+
+/* ------------------------------------------------------------------ */
+/* .ecm parsing (format of reference src/gpt2.c:34-136)                 */
+/* ------------------------------------------------------------------ */
+
+static const char *ec_readline(const char *p, const char *end, char *line, size_t cap)
+{
+    size_t n = 0;
+    if (p >= end) return NULL;
+    while (p < end && *p != '\n') {
+        if (*p != '\r' && n + 1 < cap) line[n++] = *p;
+        p++;
+    }
+    line[n] = '\0';
+    if (p < end) p++;
+    return p;
+}
+
+static size_t ec_dtype_bytes(int dt)
+{
+    switch (dt) {
+    case 0: return 4;
+    case 1: return 2;
+    case 2: return 1;
+    case 4: return 2;
+    default: return 0;
+    }
+}
+
+EC_EXPORT int ecm_parse(const void *data, size_t size, EcmTensor *out, int max, GPT2 *meta)
+{
+    const char *p = (const char *)data, *end = p + size;
+    char line[1024];
+    if (size < 5 || memcmp(p, ECM_MAGIC, 5) != 0) {
+        fprintf(stderr, "ecm: bad magic\n");
+        return -1;
+    }
+    p += 5;
+    for (;;) {
+        p = ec_readline(p, end, line, sizeof line);
+        if (!p) return -1;
+        if (!strcmp(line, "END_META")) break;
+        char *eq = strchr(line, '=');
+        if (!eq) continue;
+        *eq = '\0';
+        const char *k = line, *v = eq + 1;
+        if (!strcmp(k, "model_name")) snprintf(meta->model_name, sizeof meta->model_name, "%s", v);
+        else if (!strcmp(k, "n_layer")) meta->n_layer = atoi(v);
+        else if (!strcmp(k, "n_head")) meta->n_head = atoi(v);
+        else if (!strcmp(k, "n_kv_head")) meta->n_kv_head = atoi(v);
+        else if (!strcmp(k, "intermediate")) meta->intermediate = atoi(v);
+        else if (!strcmp(k, "n_embd")) meta->n_embd = atoi(v);
+        else if (!strcmp(k, "n_ctx")) meta->n_ctx = atoi(v);
+        else if (!strcmp(k, "vocab")) meta->vocab = atoi(v);
+        else if (!strcmp(k, "n_params")) meta->n_params = (size_t)strtoull(v, NULL, 10);
+        else if (!strcmp(k, "eps")) meta->eps = atof(v);
+        else if (!strcmp(k, "rope_theta")) meta->rope_theta = atof(v);
+        else if (!strcmp(k, "rope_type")) meta->rope_type = !strcmp(v, "yarn") ? ROPE_YARN : ROPE_DEFAULT;
+        else if (!strcmp(k, "yarn_factor")) meta->yarn_factor = atof(v);
+        else if (!strcmp(k, "yarn_attention_factor")) meta->yarn_attention_factor = atof(v);
+        else if (!strcmp(k, "yarn_orig_max")) meta->yarn_orig_max = atof(v);
+        else if (!strcmp(k, "sliding_window")) meta->sliding_window = atoi(v);
+        else if (!strcmp(k, "tie_word_embeddings")) meta->tie_word_embeddings = atoi(v);
+        else if (!strcmp(k, "eos_token_id")) meta->eos_token_id = atoi(v);
+        else if (!strcmp(k, "arch"))
+            meta->arch = (!strcmp(v, "qwen2") || !strcmp(v, "olmo3")) ? ARCH_QWEN2 : ARCH_GPT2;
+    }
+    int nt = 0;
+    for (;;) {
+        p = ec_readline(p, end, line, sizeof line);
+        if (!p) return -1;
+        if (!strcmp(line, "END_TENSORS")) break;
+        EcmTensor *t = &out[nt];
+        memset(t, 0, sizeof *t);
+        char name[128], ds[16];
+        if (sscanf(line, "%127s %15s", name, ds) < 2) continue;
+        if (!strcmp(ds, "fp32")) t->dtype = 0;
+        else if (!strcmp(ds, "fp16")) t->dtype = 1;
+        else if (!strcmp(ds, "int8")) t->dtype = 2;
+        else if (!strcmp(ds, "text")) t->dtype = 3;
+        else if (!strcmp(ds, "bf16")) t->dtype = 4;
+        else continue;
+        snprintf(t->name, sizeof t->name, "%s", name);
+        const char *q = line;
+        for (int w = 0; w < 2; w++) {
+            while (*q == ' ') q++;
+            while (*q && *q != ' ') q++;
+        }
+        if (t->dtype == 3) {
+            t->ndims = 1;
+            t->dims[0] = (size_t)strtoull(q, NULL, 10);
+            t->nelems = t->bytes = t->dims[0];
+        } else {
+            t->nelems = 1;
+            while (*q) {
+                while (*q == ' ') q++;
+                if (!*q) break;
+                char *e2;
+                size_t d = (size_t)strtoull(q, &e2, 10);
+                if (e2 == q) break;
+                if (t->ndims < 4) t->dims[t->ndims++] = d;
+                t->nelems *= d;
+                q = e2;
+            }
+            t->bytes = t->nelems * ec_dtype_bytes(t->dtype);
+        }
+        if (++nt >= max) return -1;
+    }
+    size_t off = (size_t)(p - (const char *)data);
+    for (int i = 0; i < nt; i++) {
+        out[i].offset = off;
+        off += out[i].bytes;
+    }
+    return nt;
+}
+
+static const EcmTensor *ec_find(const EcmTensor *t, int n, const char *name)
+{
+    for (int i = 0; i < n; i++)
+        if (!strcmp(t[i].name, name)) return &t[i];
+    return NULL;
+}
+
+/* ------------------------------------------------------------------ */
+/* device state                                                         */
+/* ------------------------------------------------------------------ */
+
+typedef struct {
+    void *w;            /* [N][Kp] */
+    float *s, *b;       /* [N] scales (int8), bias or NULL */
+    int N, K, Kp, wt;
+    ec_block *blocks;   /* device table */
+    int nblocks, block_rows;
+} ec_lin;
+
+typedef struct {
+    float *n1g, *n1b, *n2g, *n2b;
+    ec_lin qkv, o, up, down;   /* up = gate|up (qwen2) or fc (gpt2); down = down / fc2 */
+} ec_dlayer;
+
+#define EC_MAX_GRAPHS 16
+#define EC_PROF_MAX 1024
+
+/* Kernel classes reported by ec_decode_profile. */
+enum { EC_PC_GEMV = 0, EC_PC_LMHEAD = 1, EC_PC_ATTN = 2, EC_PC_NORM = 3, EC_PC_OTHER = 4, EC_PC_N = 5 };
+
+typedef struct {
+    int M, nsplit, kind;       /* kind 0: logits forward, 1: argmax forward, 2/3: decode step */
+    int wrap_lo, wrap_hi;      /* decode position cycle (wrap_hi <= 0: none) */
+    cudaGraphExec_t exec;
+} ec_graph;
+
+typedef struct ec_dev {
+    GPT2 *owner;
+    int device, num_sms;
+    cudaStream_t stream, own_stream;
+    int arch, prec, wt, L, E, Ep, H, KVH, hd, kv, I, V, C, B, window;
+    double eps;
+    /* weights */
+    uint16_t *wte, *wpe, *lm;
+    float *nfg, *nfb;
+    ec_dlayer *lw;
+    ec_lin lm_lin;             /* lm_head as a linear over the current vocab shard */
+    int v0, v1;                /* vocab shard [v0, v1) */
+    /* KV arena */
+    uint16_t *kc, *vc;
+    size_t layer_kv;           /* elements per layer: B*C*kv */
+    double *rope_cos, *rope_sin;
+    /* workspaces */
+    int cap;                   /* rows */
+    float *x, *h, *qkv, *att, *act, *big;
+    int8_t *aq;
+    float *as;
+    float *attn_part;
+    size_t attn_part_floats;
+    float *logits;
+    int logit_rows;
+    void *amax_part;
+    int amax_chunks;
+    int *d_tok, *d_pos, *d_slot, *d_ids;
+    float *d_max;
+    int *d_counter, *d_hist;
+    int hist_cap;
+    int *h_in;                 /* pinned: tok | pos | slot */
+    int *h_ids;
+    float *h_max;
+    float *h_logits;
+    size_t h_logits_cap;
+    /* graphs */
+    ec_graph graphs[EC_MAX_GRAPHS];
+    int ngraphs;
+    /* taps */
+    int taps_on;
+    float *taps;
+    int taps_rows;
+    /* decode position cycle used by the step being enqueued */
+    int wrap_lo, wrap_hi;
+    /* per-launch event profiling (ec_decode_profile) */
+    int prof_on, prof_n;
+    cudaEvent_t prof_ev[2 * EC_PROF_MAX];
+    int prof_cls[EC_PROF_MAX];
+    double prof_bytes[EC_PROF_MAX];
+    int prof_ready;
+} ec_dev;
+
+/* ---- registry: GPT2 address -> device state ---- */
+
+static pthread_mutex_t g_reg_mu = PTHREAD_MUTEX_INITIALIZER;
+static struct { GPT2 *g; ec_dev *d; } g_reg[256];
+
+static ec_dev *ec_lookup(const GPT2 *g)
+{
+    ec_dev *d = NULL;
+    pthread_mutex_lock(&g_reg_mu);
+    for (int i = 0; i < 256; i++)
+        if (g_reg[i].g == g) { d = g_reg[i].d; break; }
+    pthread_mutex_unlock(&g_reg_mu);
+    return d;
+}
+
+static int ec_register(GPT2 *g, ec_dev *d)
+{
+    int ok = -1;
+    pthread_mutex_lock(&g_reg_mu);
+    for (int i = 0; i < 256; i++)
+        if (!g_reg[i].g) { g_reg[i].g = g; g_reg[i].d = d; ok = 0; break; }
+    pthread_mutex_unlock(&g_reg_mu);
+    if (ok) ec_seterr("too many loaded models (256)");
+    return ok;
+}
+
+static void ec_unregister(GPT2 *g)
+{
+    pthread_mutex_lock(&g_reg_mu);
+    for (int i = 0; i < 256; i++)
+        if (g_reg[i].g == g) { g_reg[i].g = NULL; g_reg[i].d = NULL; }
+    pthread_mutex_unlock(&g_reg_mu);
+}
+
+static int round16(int k) { return (k + 15) & ~15; }
+
+/* ---- uploads ---- */
+
+static int ec_upload(void **dst, const void *src, size_t bytes)
+{
+    CK(cudaMalloc(dst, bytes ? bytes : 16));
+    if (bytes) CK(cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice));
+    return 0;
+}
+
+/* Copy `rows` rows of `k` elements (elt bytes) into a device matrix with row
+ * stride kp elements at row offset r0; padding was zeroed beforehand. */
+static int ec_upload_rows(void *dev, int r0, const void *src, int rows, int k, int kp, int elt)
+{
+    if (rows <= 0) return 0;
+    CK(cudaMemcpy2D((char *)dev + (size_t)r0 * kp * elt, (size_t)kp * elt, src, (size_t)k * elt,
+                    (size_t)k * elt, (size_t)rows, cudaMemcpyHostToDevice));
+    return 0;
+}
+
+/* Row-block tables.  Plain blocks of R rows; pair blocks (pair offset P) of R
+ * rows from [j, j+R) and [j+P, j+P+R). */
+static int ec_pick_rows(int units, int row_bytes, int num_sms, int pair)
+{
+    /* enough blocks for ~2 CTAs per SM; staged bytes per block <= 48 KB */
+    int target = 2 * num_sms;
+    int r = units / target;
+    if (r < 1) r = 1;
+    int maxr = (48 * 1024) / (row_bytes * (pair ? 2 : 1));
+    if (maxr < 1) maxr = 1;
+    if (r > maxr) r = maxr;
+    int cap = pair ? 64 : 128;
+    if (r > cap) r = cap;
+    /* prefer a power of two */
+    int p2 = 1;
+    while (p2 * 2 <= r) p2 *= 2;
+    return p2;
+}
+
+static int ec_set_blocks(ec_lin *l, const ec_block *hb, int n, int block_rows)
+{
+    if (l->blocks) cudaFree(l->blocks);
+    l->blocks = NULL;
+    if (ec_upload((void **)&l->blocks, hb, (size_t)n * sizeof(ec_block))) return -1;
+    l->nblocks = n;
+    l->block_rows = block_rows;
+    return 0;
+}
+
+static int ec_plain_blocks(ec_lin *l, int row_begin, int row_end, int num_sms)
+{
+    int units = row_end - row_begin;
+    int R = ec_pick_rows(units, l->Kp * (l->wt == EC_W_I8 ? 1 : 2), num_sms, 0);
+    int n = (units + R - 1) / R;
+    ec_block *hb = calloc((size_t)n, sizeof *hb);
+    for (int i = 0; i < n; i++) {
+        hb[i].row0 = row_begin + i * R;
+        hb[i].nrows = (row_begin + (i + 1) * R <= row_end) ? R : row_end - hb[i].row0;
+    }
+    int rc = ec_set_blocks(l, hb, n, R);
+    free(hb);
+    return rc;
+}
+
+/* gate|up: pair blocks over the I gate rows with pair offset I. */
+static int ec_swiglu_blocks(ec_lin *l, int I, int num_sms)
+{
+    int R = ec_pick_rows(I, l->Kp * (l->wt == EC_W_I8 ? 1 : 2), num_sms, 1);
+    int n = (I + R - 1) / R;
+    ec_block *hb = calloc((size_t)n, sizeof *hb);
+    for (int i = 0; i < n; i++) {
+        hb[i].row0 = i * R;
+        hb[i].nrows = ((i + 1) * R <= I) ? R : I - i * R;
+        hb[i].pair = I;
+    }
+    int rc = ec_set_blocks(l, hb, n, 2 * R);
+    free(hb);
+    return rc;
+}
+
+/* qwen2 q|k|v: RoPE pair blocks inside every q and k head, plain blocks for v. */
+static int ec_qkv_rope_blocks(ec_lin *l, int E, int kv, int hd, int H, int KVH, int num_sms)
+{
+    int half = hd / 2;
+    int heads = H + KVH;
+    int R = ec_pick_rows(heads * half + kv / 2, l->Kp * (l->wt == EC_W_I8 ? 1 : 2), num_sms, 1);
+    while (half % R) R /= 2;
+    int per_head = half / R;
+    int nv = (kv + 2 * R - 1) / (2 * R);
+    int n = heads * per_head + nv;
+    ec_block *hb = calloc((size_t)n, sizeof *hb);
+    int i = 0;
+    for (int h = 0; h < heads; h++) {
+        int base = h < H ? h * hd : E + (h - H) * hd;
+        for (int j = 0; j < per_head; j++, i++) {
+            hb[i].row0 = base + j * R;
+            hb[i].nrows = R;
+            hb[i].pair = half;
+            hb[i].kind = EC_BK_ROPE;
+        }
+    }
+    for (int j = 0; j < nv; j++, i++) {
+        int r0 = E + kv + j * 2 * R;
+        hb[i].row0 = r0;
+        hb[i].nrows = (r0 + 2 * R <= E + 2 * kv) ? 2 * R : E + 2 * kv - r0;
+    }
+    int rc = ec_set_blocks(l, hb, n, 2 * R);
+    free(hb);
+    return rc;
+}
+
+/* Build a device linear from up to three stacked host matrices (same K). */
+static int ec_make_lin(ec_lin *l, int wt, int K, int nparts, const void *const *w, const float *const *s,
+                       const float *const *b, const int *rows)
+{
+    memset(l, 0, sizeof *l);
+    int N = 0;
+    for (int i = 0; i < nparts; i++) N += rows[i];
+    int elt = wt == EC_W_I8 ? 1 : 2;
+    l->N = N;
+    l->K = K;
+    l->Kp = round16(K);
+    l->wt = wt;
+    CK(cudaMalloc(&l->w, (size_t)N * l->Kp * elt));
+    CK(cudaMemset(l->w, 0, (size_t)N * l->Kp * elt));
+    int r = 0;
+    for (int i = 0; i < nparts; i++) {
+        if (ec_upload_rows(l->w, r, w[i], rows[i], K, l->Kp, elt)) return -1;
+        r += rows[i];
+    }
+    int have_s = 0, have_b = 0;
+    for (int i = 0; i < nparts; i++) {
+        have_s |= s && s[i] != NULL;
+        have_b |= b && b[i] != NULL;
+    }
+    if (have_s || have_b) {
+        float *tmp = malloc((size_t)N * sizeof(float));
+        for (int pass = 0; pass < 2; pass++) {
+            if (pass == 0 && !have_s) continue;
+            if (pass == 1 && !have_b) continue;
+            const float *const *src = pass == 0 ? s : b;
+            r = 0;
+            for (int i = 0; i < nparts; i++) {
+                for (int j = 0; j < rows[i]; j++) {
+                    float v = pass == 0 ? 1.0f : 0.0f;
+                    if (src[i]) memcpy(&v, (const char *)src[i] + (size_t)j * 4, 4);  /* may be unaligned */
+                    tmp[r + j] = v;
+                }
+                r += rows[i];
+            }
+            if (ec_upload((void **)(pass == 0 ? &l->s : &l->b), tmp, (size_t)N * sizeof(float))) {
+                free(tmp);
+                return -1;
+            }
+        }
+        free(tmp);
+    }
+    return 0;
+}
+
+static void ec_free_lin(ec_lin *l)
+{
+    cudaFree(l->w);
+    cudaFree(l->s);
+    cudaFree(l->b);
+    cudaFree(l->blocks);
+    memset(l, 0, sizeof *l);
+}
+
+static int ec_upload_f32(float **dst, const float *src, int n)
+{
+    if (!src) { *dst = NULL; return 0; }
+    return ec_upload((void **)dst, src, (size_t)n * sizeof(float));
+}
+
+/* RoPE tables: inverse frequencies with the YaRN ramp and cos/sin per position
+ * scaled by the attention factor, in fp64 (reference src/gpt2.c:608-654). */
+static int ec_rope_tables(ec_dev *d, const GPT2 *g)
+{
+    int half = d->hd / 2;
+    double *inv = malloc((size_t)half * sizeof(double));
+    int dim = 2 * half;
+    for (int i = 0; i < half; i++) inv[i] = pow(1.0 / g->rope_theta, (double)(2 * i) / (double)dim);
+    if (g->rope_type == ROPE_YARN) {
+        const double two_pi = 6.28318530717958647692;
+        double lb = log(g->rope_theta);
+        double lo = floor((double)dim * log(g->yarn_orig_max / (32.0 * two_pi)) / (2.0 * lb));
+        double hi = ceil((double)dim * log(g->yarn_orig_max / (1.0 * two_pi)) / (2.0 * lb));
+        if (lo < 0.0) lo = 0.0;
+        if (hi > (double)(dim - 1)) hi = (double)(dim - 1);
+        double span = hi - lo < 1.0 ? 1.0 : hi - lo;
+        for (int i = 0; i < half; i++) {
+            double ramp = ((double)i - lo) / span;
+            ramp = ramp < 0.0 ? 0.0 : (ramp > 1.0 ? 1.0 : ramp);
+            double e = inv[i];
+            inv[i] = (e / g->yarn_factor) * ramp + e * (1.0 - ramp);
+        }
+    }
+    size_t n = (size_t)d->C * half;
+    double *c = malloc(n * sizeof(double)), *s = malloc(n * sizeof(double));
+    double scale = g->yarn_attention_factor;
+    for (int p = 0; p < d->C; p++)
+        for (int i = 0; i < half; i++) {
+            double f = (double)p * inv[i];
+            c[(size_t)p * half + i] = cos(f) * scale;
+            s[(size_t)p * half + i] = sin(f) * scale;
+        }
+    int rc = ec_upload((void **)&d->rope_cos, c, n * sizeof(double));
+    if (!rc) rc = ec_upload((void **)&d->rope_sin, s, n * sizeof(double));
+    free(inv);
+    free(c);
+    free(s);
+    return rc;
+}
+
+static void ec_free_graphs(ec_dev *d)
+{
+    for (int i = 0; i < d->ngraphs; i++) cudaGraphExecDestroy(d->graphs[i].exec);
+    d->ngraphs = 0;
+}
+
+static void ec_free_work(ec_dev *d)
+{
+    cudaFree(d->x); cudaFree(d->h); cudaFree(d->qkv); cudaFree(d->att); cudaFree(d->act); cudaFree(d->big);
+    cudaFree(d->aq); cudaFree(d->as); cudaFree(d->d_tok); cudaFree(d->d_pos); cudaFree(d->d_slot);
+    cudaFree(d->d_ids); cudaFree(d->d_max);
+    cudaFreeHost(d->h_in); cudaFreeHost(d->h_ids); cudaFreeHost(d->h_max);
+    d->x = d->h = d->qkv = d->att = d->act = d->big = NULL;
+    d->aq = NULL; d->as = NULL;
+    d->d_tok = d->d_pos = d->d_slot = d->d_ids = NULL;
+    d->d_max = NULL;
+    d->h_in = d->h_ids = NULL;
+    d->h_max = NULL;
+    d->cap = 0;
+}
+
+/* Grow the row-indexed workspaces to at least M rows.  Graphs captured with
+ * the old buffers are dropped. */
+static int ec_ensure(ec_dev *d, int M)
+{
+    if (M <= d->cap) return 0;
+    int cap = d->cap ? d->cap : 8;
+    while (cap < M) cap *= 2;
+    ec_free_graphs(d);
+    ec_free_work(d);
+    int act = d->arch == ARCH_QWEN2 ? d->I : 4 * d->E;
+    int big = d->arch == ARCH_QWEN2 ? 2 * d->I : 1;
+    int kmax = d->E > d->I ? d->E : d->I;
+    if (d->arch == ARCH_GPT2) kmax = 4 * d->E;
+    kmax = round16(kmax);
+    CK(cudaMalloc((void **)&d->x, (size_t)cap * d->E * 4));
+    CK(cudaMalloc((void **)&d->h, (size_t)cap * d->E * 4));
+    CK(cudaMalloc((void **)&d->qkv, (size_t)cap * (d->E + 2 * d->kv) * 4));
+    CK(cudaMalloc((void **)&d->att, (size_t)cap * d->E * 4));
+    CK(cudaMalloc((void **)&d->act, (size_t)cap * act * 4));
+    CK(cudaMalloc((void **)&d->big, (size_t)cap * big * 4));
+    CK(cudaMalloc((void **)&d->aq, (size_t)cap * kmax));
+    CK(cudaMalloc((void **)&d->as, (size_t)cap * 4));
+    CK(cudaMalloc((void **)&d->d_tok, (size_t)cap * 4));
+    CK(cudaMalloc((void **)&d->d_pos, (size_t)cap * 4));
+    CK(cudaMalloc((void **)&d->d_slot, (size_t)cap * 4));
+    CK(cudaMalloc((void **)&d->d_ids, (size_t)cap * 4));
+    CK(cudaMalloc((void **)&d->d_max, (size_t)cap * 4));
+    CK(cudaMallocHost((void **)&d->h_in, (size_t)cap * 3 * 4));
+    CK(cudaMallocHost((void **)&d->h_ids, (size_t)cap * 4));
+    CK(cudaMallocHost((void **)&d->h_max, (size_t)cap * 4));
+    d->cap = cap;
+    return 0;
+}
+
+static int ec_ensure_attn(ec_dev *d, int M, int nsplit)
+{
+    size_t need = ec_attention_scratch_floats(M, d->H, d->hd, nsplit);
+    if (need <= d->attn_part_floats) return 0;
+    ec_free_graphs(d);
+    cudaFree(d->attn_part);
+    d->attn_part = NULL;
+    CK(cudaMalloc((void **)&d->attn_part, need * 4));
+    d->attn_part_floats = need;
+    return 0;
+}
+
+/* Device logits buffer of `rows` rows of the shard width. */
+static int ec_ensure_logits(ec_dev *d, int rows)
+{
+    if (rows <= d->logit_rows) return 0;
+    ec_free_graphs(d);
+    cudaFree(d->logits);
+    d->logits = NULL;
+    CK(cudaMalloc((void **)&d->logits, (size_t)rows * (d->v1 - d->v0) * 4));
+    d->logit_rows = rows;
+    return 0;
+}
+
+static int ec_ensure_amax(ec_dev *d, int M)
+{
+    int chunks = 2 * d->num_sms;
+    if (d->amax_part && d->amax_chunks >= chunks && d->cap >= M) return 0;
+    ec_free_graphs(d);
+    cudaFree(d->amax_part);
+    d->amax_part = NULL;
+    int rows = d->cap > M ? d->cap : M;
+    CK(cudaMalloc(&d->amax_part, (size_t)rows * chunks * 8));
+    d->amax_chunks = chunks;
+    return 0;
+}
+
+static void ec_dev_free(ec_dev *d)
+{
+    if (!d) return;
+    int cur = 0;
+    cudaGetDevice(&cur);
+    cudaSetDevice(d->device);
+    cudaStreamSynchronize(d->stream);
+    ec_free_graphs(d);
+    ec_free_work(d);
+    if (d->lw) {
+        for (int l = 0; l < d->L; l++) {
+            ec_dlayer *W = &d->lw[l];
+            cudaFree(W->n1g); cudaFree(W->n1b); cudaFree(W->n2g); cudaFree(W->n2b);
+            ec_free_lin(&W->qkv); ec_free_lin(&W->o); ec_free_lin(&W->up); ec_free_lin(&W->down);
+        }
+        free(d->lw);
+    }
+    cudaFree(d->lm_lin.blocks);
+    if (d->lm != d->wte) cudaFree(d->lm);
+    cudaFree(d->wte); cudaFree(d->wpe); cudaFree(d->nfg); cudaFree(d->nfb);
+    cudaFree(d->kc); cudaFree(d->vc); cudaFree(d->rope_cos); cudaFree(d->rope_sin);
+    cudaFree(d->attn_part); cudaFree(d->logits); cudaFree(d->amax_part);
+    cudaFree(d->d_counter); cudaFree(d->d_hist); cudaFree(d->taps);
+    cudaFreeHost(d->h_logits);
+    if (d->prof_ready)
+        for (int i = 0; i < 2 * EC_PROF_MAX; i++) cudaEventDestroy(d->prof_ev[i]);
+    if (d->own_stream) cudaStreamDestroy(d->own_stream);
+    free(d);
+    cudaSetDevice(cur);
+}
+
+/* 16-bit [rows][E] table -> device with row stride Ep. */
+static int ec_upload_table(uint16_t **dst, const uint16_t *src, int rows, int E, int Ep)
+{
+    CK(cudaMalloc((void **)dst, (size_t)rows * Ep * 2));
+    if (Ep != E) CK(cudaMemset(*dst, 0, (size_t)rows * Ep * 2));
+    return ec_upload_rows(*dst, 0, src, rows, E, Ep, 2);
+}
+
+static int ec_set_lm_shard(ec_dev *d, int v0, int v1)
+{
+    d->v0 = v0;
+    d->v1 = v1;
+    ec_lin *l = &d->lm_lin;
+    l->w = (char *)d->lm + (size_t)v0 * d->Ep * 2;
+    l->s = l->b = NULL;
+    l->N = v1 - v0;
+    l->K = d->E;
+    l->Kp = d->Ep;
+    l->wt = d->prec == 2 ? EC_W_BF16 : EC_W_F16;
+    d->logit_rows = 0;
+    cudaFree(d->logits);
+    d->logits = NULL;
+    ec_free_graphs(d);
+    return ec_plain_blocks(l, 0, l->N, d->num_sms);
+}
+
+static int ec_dev_build(GPT2 *g, ec_dev *d)
+{
+    d->owner = g;
+    CK(cudaGetDevice(&d->device));
+    CK(cudaDeviceGetAttribute(&d->num_sms, cudaDevAttrMultiProcessorCount, d->device));
+    CK(cudaStreamCreateWithFlags(&d->own_stream, cudaStreamNonBlocking));
+    d->stream = d->own_stream;
+    if (ec_kernels_init()) { ec_seterr("kernel init failed: %s", cudaGetErrorString(cudaGetLastError())); return -1; }
+    d->arch = g->arch;
+    d->prec = g->precision;
+    d->wt = g->precision == 0 ? EC_W_I8 : (g->precision == 1 ? EC_W_F16 : EC_W_BF16);
+    d->L = g->n_layer;
+    d->E = g->n_embd;
+    d->Ep = round16(g->n_embd);
+    d->H = g->n_head;
+    d->KVH = g->n_kv_head;
+    d->hd = g->head_dim;
+    d->kv = g->n_kv_embd;
+    d->I = g->intermediate;
+    d->V = g->vocab;
+    d->C = gpt2_eff_ctx(g);
+    d->B = g->batch_cap;
+    d->eps = g->eps;
+    d->window = g->arch == ARCH_QWEN2 ? g->sliding_window : 0;
+    if (d->hd % 8 || d->hd > 256 || d->hd < 8) { ec_seterr("unsupported head_dim %d", d->hd); return -1; }
+
+    if (ec_upload_table(&d->wte, g->wte, d->V, d->E, d->Ep)) return -1;
+    if (g->wpe && ec_upload_table(&d->wpe, g->wpe, g->n_ctx, d->E, d->Ep)) return -1;
+    if (g->lm_head) {
+        if (ec_upload_table(&d->lm, g->lm_head, d->V, d->E, d->Ep)) return -1;
+    } else {
+        d->lm = d->wte;
+    }
+    if (ec_upload_f32(&d->nfg, g->lnf_g, d->E) || ec_upload_f32(&d->nfb, g->lnf_b, d->E)) return -1;
+
+    d->lw = calloc((size_t)d->L, sizeof *d->lw);
+    for (int l = 0; l < d->L; l++) {
+        const struct LayerW *S = &g->lw[l];
+        ec_dlayer *W = &d->lw[l];
+        if (ec_upload_f32(&W->n1g, S->ln1_g, d->E) || ec_upload_f32(&W->n2g, S->ln2_g, d->E)) return -1;
+        if (d->arch == ARCH_GPT2) {
+            if (ec_upload_f32(&W->n1b, S->ln1_b, d->E) || ec_upload_f32(&W->n2b, S->ln2_b, d->E)) return -1;
+            int E = d->E;
+            { const void *w[1] = {S->attn_w}; const float *s[1] = {S->attn_s}; const float *b[1] = {S->attn_b}; int r[1] = {3 * E};
+              if (ec_make_lin(&W->qkv, d->wt, E, 1, w, s, b, r) || ec_plain_blocks(&W->qkv, 0, 3 * E, d->num_sms)) return -1; }
+            { const void *w[1] = {S->proj_w}; const float *s[1] = {S->proj_s}; const float *b[1] = {S->proj_b}; int r[1] = {E};
+              if (ec_make_lin(&W->o, d->wt, E, 1, w, s, b, r) || ec_plain_blocks(&W->o, 0, E, d->num_sms)) return -1; }
+            { const void *w[1] = {S->fc_w}; const float *s[1] = {S->fc_s}; const float *b[1] = {S->fc_b}; int r[1] = {4 * E};
+              if (ec_make_lin(&W->up, d->wt, E, 1, w, s, b, r) || ec_plain_blocks(&W->up, 0, 4 * E, d->num_sms)) return -1; }
+            { const void *w[1] = {S->fc2_w}; const float *s[1] = {S->fc2_s}; const float *b[1] = {S->fc2_b}; int r[1] = {E};
+              if (ec_make_lin(&W->down, d->wt, 4 * E, 1, w, s, b, r) || ec_plain_blocks(&W->down, 0, E, d->num_sms)) return -1; }
+        } else {
+            int E = d->E, kv = d->kv, I = d->I;
+            /* The reference passes NULL bias to every Qwen2 projection
+             * (src/gpt2.c:709-711, :781, :788-792): stored biases are unused. */
+            { const void *w[3] = {S->q_w, S->k_w, S->v_w}; const float *s[3] = {S->q_s, S->k_s, S->v_s}; int r[3] = {E, kv, kv};
+              if (ec_make_lin(&W->qkv, d->wt, E, 3, w, s, NULL, r) ||
+                  ec_qkv_rope_blocks(&W->qkv, E, kv, d->hd, d->H, d->KVH, d->num_sms)) return -1; }
+            { const void *w[1] = {S->o_w}; const float *s[1] = {S->o_s}; int r[1] = {E};
+              if (ec_make_lin(&W->o, d->wt, E, 1, w, s, NULL, r) || ec_plain_blocks(&W->o, 0, E, d->num_sms)) return -1; }
+            { const void *w[2] = {S->gate_w, S->up_w}; const float *s[2] = {S->gate_s, S->up_s}; int r[2] = {I, I};
+              if (ec_make_lin(&W->up, d->wt, E, 2, w, s, NULL, r) || ec_swiglu_blocks(&W->up, I, d->num_sms)) return -1; }
+            { const void *w[1] = {S->down_w}; const float *s[1] = {S->down_s}; int r[1] = {E};
+              if (ec_make_lin(&W->down, d->wt, I, 1, w, s, NULL, r) || ec_plain_blocks(&W->down, 0, E, d->num_sms)) return -1; }
+        }
+    }
+    if (ec_set_lm_shard(d, 0, d->V)) return -1;
+
+    d->layer_kv = (size_t)d->B * d->C * d->kv;
+    CK(cudaMalloc((void **)&d->kc, d->layer_kv * d->L * 2));
+    CK(cudaMalloc((void **)&d->vc, d->layer_kv * d->L * 2));
+    CK(cudaMemset(d->kc, 0, d->layer_kv * d->L * 2));
+    CK(cudaMemset(d->vc, 0, d->layer_kv * d->L * 2));
+    if (d->arch == ARCH_QWEN2 && ec_rope_tables(d, g)) return -1;
+    CK(cudaMalloc((void **)&d->d_counter, 4));
+    if (ec_ensure(d, d->B > 8 ? d->B : 8)) return -1;
+    CK(cudaDeviceSynchronize());
+    return 0;
+}
+
+/* ------------------------------------------------------------------ */
+/* load / free (reference src/gpt2.c:161-387)                          */
+/* ------------------------------------------------------------------ */
+
+static void *ec_shadow_alloc(size_t bytes)
+{
+    void *p = mmap(NULL, bytes ? bytes : 4096, PROT_READ | PROT_WRITE,
+                   MAP_PRIVATE | MAP_ANONYMOUS | MAP_NORESERVE, -1, 0);
+    return p == MAP_FAILED ? NULL : p;
+}
+
+static size_t ec_shadow_bytes(const GPT2 *g)
+{
+    return (size_t)g->n_layer * g->batch_cap * gpt2_eff_ctx(g) * g->n_kv_embd * sizeof(uint16_t);
+}
+
+static void ec_host_free(GPT2 *g)
+{
+    if (g->tok.id_to_token && tokenizer_free) tokenizer_free(&g->tok);
+    free(g->lw);
+    size_t kvb = ec_shadow_bytes(g);
+    if (g->k_cache) munmap(g->k_cache, kvb ? kvb : 4096);
+    if (g->v_cache) munmap(g->v_cache, kvb ? kvb : 4096);
+    if (g->file_data) {
+        if (g->file_mapped) munmap(g->file_data, g->file_size);
+        else free(g->file_data);
+    }
+}
+
+static void ec_defaults_qwen2(GPT2 *g)
+{
+    if (g->n_kv_head <= 0) g->n_kv_head = g->n_head;
+    g->head_dim = g->n_embd / (g->n_head > 0 ? g->n_head : 1);
+    g->n_kv_embd = g->n_kv_head * g->head_dim;
+    if (g->intermediate <= 0) g->intermediate = 4 * g->n_embd;
+    if (g->rope_theta <= 0) g->rope_theta = 10000.0;
+    if (g->yarn_orig_max <= 0) g->yarn_orig_max = g->n_ctx;
+    if (g->yarn_factor <= 0) g->yarn_factor = 1.0;
+    if (g->yarn_attention_factor <= 0) g->yarn_attention_factor = 1.0;
+}
+
+static int ec_load_host(GPT2 *g, const char *path, int batch_cap, int max_ctx)
+{
+    memset(g, 0, sizeof *g);
+    g->batch_cap = batch_cap < 1 ? 1 : batch_cap;
+    g->max_ctx = max_ctx > 0 ? max_ctx : 0;
+    g->eps = 1e-5;
+    int fd = open(path, O_RDONLY);
+    if (fd < 0) { perror("open model"); ec_seterr("cannot open %s", path); return -1; }
+    struct stat st;
+    if (fstat(fd, &st) != 0 || st.st_size <= 0) { close(fd); ec_seterr("empty model file"); return -1; }
+    void *map = mmap(NULL, (size_t)st.st_size, PROT_READ, MAP_PRIVATE, fd, 0);
+    close(fd);
+    if (map == MAP_FAILED) { perror("mmap model"); ec_seterr("mmap failed"); return -1; }
+    g->file_data = map;
+    g->file_size = (size_t)st.st_size;
+    g->file_mapped = 1;
+
+    EcmTensor *t = calloc(512, sizeof *t);
+    int n = ecm_parse(g->file_data, g->file_size, t, 512, g);
+    if (n < 0) { free(t); ec_seterr("ecm: parse failed"); return -1; }
+    const char *base = g->file_data;
+    for (int i = 0; i < n; i++)
+        if (t[i].offset + t[i].bytes > g->file_size) {
+            ec_seterr("ecm: tensor %s past end of file", t[i].name);
+            free(t);
+            return -1;
+        }
+    const EcmTensor *wte = ec_find(t, n, "wte"), *lnf = ec_find(t, n, "ln_f.g");
+    if (!wte || !lnf) { free(t); fprintf(stderr, "ecm: missing core tensors (wte, ln_f.g)\n"); ec_seterr("ecm: missing wte/ln_f.g"); return -1; }
+    g->wte = (const uint16_t *)(base + wte->offset);
+    g->lnf_g = (const float *)(base + lnf->offset);
+    const char *lin0 = g->arch == ARCH_QWEN2 ? "blocks.0.q.w" : "blocks.0.attn.w";
+    const EcmTensor *t0 = ec_find(t, n, lin0);
+    if (!t0) { free(t); fprintf(stderr, "ecm: missing %s\n", lin0); ec_seterr("ecm: missing %s", lin0); return -1; }
+    if (t0->dtype == 1) g->precision = 1;
+    else if (t0->dtype == 2) g->precision = 0;
+    else if (t0->dtype == 4) g->precision = 2;
+    else { free(t); fprintf(stderr, "ecm: unexpected linear weight dtype\n"); ec_seterr("ecm: linear dtype"); return -1; }
+    if (g->arch == ARCH_QWEN2) ec_defaults_qwen2(g);
+    if (g->arch == ARCH_GPT2) {
+        const EcmTensor *wpe = ec_find(t, n, "wpe"), *lnb = ec_find(t, n, "ln_f.b");
+        if (!wpe || !lnb) { free(t); fprintf(stderr, "ecm: missing wpe / ln_f.b\n"); ec_seterr("ecm: missing wpe/ln_f.b"); return -1; }
+        g->wpe = (const uint16_t *)(base + wpe->offset);
+        g->lnf_b = (const float *)(base + lnb->offset);
+        g->n_kv_embd = g->n_embd;
+        g->n_kv_head = g->n_head;
+        g->intermediate = 4 * g->n_embd;
+        g->head_dim = g->n_embd / g->n_head;
+    } else {
+        const EcmTensor *lmh = ec_find(t, n, "lm_head.w");
+        if (lmh && !g->tie_word_embeddings) g->lm_head = (const uint16_t *)(base + lmh->offset);
+        if (g->tie_word_embeddings || !lmh) g->tie_word_embeddings = 1;
+    }
+    g->lw = calloc((size_t)g->n_layer, sizeof *g->lw);
+    char nm[256];
+    for (int l = 0; l < g->n_layer; l++) {
+        struct LayerW *W = &g->lw[l];
+#define EC_BIND(field, fmt)                                                   \
+        do {                                                                  \
+            snprintf(nm, sizeof nm, fmt, l);                                  \
+            const EcmTensor *x_ = ec_find(t, n, nm);                          \
+            if (x_) W->field = (const float *)(base + x_->offset);            \
+        } while (0)
+        EC_BIND(ln1_g, "blocks.%d.ln_1.g");
+        EC_BIND(ln1_b, "blocks.%d.ln_1.b");
+        EC_BIND(ln2_g, "blocks.%d.ln_2.g");
+        EC_BIND(ln2_b, "blocks.%d.ln_2.b");
+#undef EC_BIND
+        if (!W->ln1_g || !W->ln2_g || (g->arch == ARCH_GPT2 && (!W->ln1_b || !W->ln2_b))) {
+            free(t);
+            ec_seterr("ecm: missing norm tensors of layer %d", l);
+            fprintf(stderr, "%s\n", g_err);
+            return -1;
+        }
+        const char *qn[7] = {"q", "k", "v", "o", "gate", "up", "down"};
+        const void **qw[7] = {&W->q_w, &W->k_w, &W->v_w, &W->o_w, &W->gate_w, &W->up_w, &W->down_w};
+        const float **qs[7] = {&W->q_s, &W->k_s, &W->v_s, &W->o_s, &W->gate_s, &W->up_s, &W->down_s};
+        const float **qb[7] = {&W->q_b, &W->k_b, &W->v_b, &W->o_b, &W->gate_b, &W->up_b, &W->down_b};
+        const char *gn[4] = {"attn", "proj", "fc", "fc2"};
+        const void **gw[4] = {&W->attn_w, &W->proj_w, &W->fc_w, &W->fc2_w};
+        const float **gs[4] = {&W->attn_s, &W->proj_s, &W->fc_s, &W->fc2_s};
+        const float **gb[4] = {&W->attn_b, &W->proj_b, &W->fc_b, &W->fc2_b};
+        int cnt = g->arch == ARCH_QWEN2 ? 7 : 4;
+        for (int s = 0; s < cnt; s++) {
+            const char *sf = g->arch == ARCH_QWEN2 ? qn[s] : gn[s];
+            snprintf(nm, sizeof nm, "blocks.%d.%s.w", l, sf);
+            const EcmTensor *tw = ec_find(t, n, nm);
+            snprintf(nm, sizeof nm, "blocks.%d.%s.s", l, sf);
+            const EcmTensor *ts = ec_find(t, n, nm);
+            snprintf(nm, sizeof nm, "blocks.%d.%s.b", l, sf);
+            const EcmTensor *tb = ec_find(t, n, nm);
+            if (!tw || (g->arch == ARCH_GPT2 && !tb) || (g->arch == ARCH_GPT2 && g->precision == 0 && !ts)) {
+                free(t);
+                fprintf(stderr, "ecm: missing %s tensors\n", nm);
+                ec_seterr("ecm: missing %s", nm);
+                return -1;
+            }
+            const void *wp = base + tw->offset;
+            const float *sp = (g->precision == 0 && ts) ? (const float *)(base + ts->offset) : NULL;
+            const float *bp = tb ? (const float *)(base + tb->offset) : NULL;
+            if (g->arch == ARCH_QWEN2) { *qw[s] = wp; *qs[s] = sp; *qb[s] = bp; }
+            else { *gw[s] = wp; *gs[s] = sp; *gb[s] = bp; }
+        }
+    }
+    int V = g->vocab;
+    if (V <= 0 || g->n_layer <= 0 || g->n_embd <= 0 || g->n_head <= 0 || g->n_ctx <= 0) {
+        free(t); ec_seterr("ecm: bad dimensions"); return -1;
+    }
+    if (wte->bytes < (size_t)V * g->n_embd * 2) { free(t); ec_seterr("ecm: wte smaller than vocab x n_embd"); return -1; }
+    size_t kvb = ec_shadow_bytes(g);
+    g->k_cache = ec_shadow_alloc(kvb);
+    g->v_cache = ec_shadow_alloc(kvb);
+    if (!g->k_cache || !g->v_cache) { free(t); ec_seterr("host KV shadow allocation failed"); return -1; }
+    if (tokenizer_load) {
+        const EcmTensor *tv = ec_find(t, n, "tokenizer.vocab"), *tm = ec_find(t, n, "tokenizer.merges");
+        if (!tv || !tm) { free(t); fprintf(stderr, "ecm: tokenizer blobs missing\n"); ec_seterr("ecm: tokenizer blobs missing"); return -1; }
+        if (tokenizer_load(&g->tok, base + tv->offset, tv->bytes, base + tm->offset, tm->bytes, g->vocab,
+                           g->arch == ARCH_QWEN2 ? 1 : 0) != 0) {
+            free(t); ec_seterr("tokenizer_load failed"); return -1;
+        }
+    }
+    free(t);
+    return 0;
+}
+
+EC_EXPORT int gpt2_load(GPT2 *g, const char *path, int batch_cap, int max_ctx)
+{
+    g_err[0] = 0;
+    if (ec_load_host(g, path, batch_cap, max_ctx)) {
+        if (!g_err[0]) ec_seterr("load failed");
+        fprintf(stderr, "edgecore_b200: %s\n", g_err);
+        ec_host_free(g);
+        memset(g, 0, sizeof *g);
+        return -1;
+    }
+    ec_dev *d = calloc(1, sizeof *d);
+    if (ec_dev_build(g, d) || ec_register(g, d)) {
+        fprintf(stderr, "edgecore_b200: device setup failed: %s\n", g_err);
+        ec_dev_free(d);
+        ec_host_free(g);
+        memset(g, 0, sizeof *g);
+        return -1;
+    }
+    return 0;
+}
+
+EC_EXPORT void gpt2_free(GPT2 *g)
+{
+    if (!g) return;
+    ec_dev *d = ec_lookup(g);
+    if (d) {
+        ec_unregister(g);
+        ec_dev_free(d);
+    }
+    ec_host_free(g);
+    memset(g, 0, sizeof *g);
+}
+
+/* ------------------------------------------------------------------ */
+/* forward                                                              */
+/* ------------------------------------------------------------------ */
+
+static int ec_pick_nsplit(const ec_dev *d, int max_len)
+{
+    /* ~64 positions per split, power of two, each split <= 1024 positions */
+    int need = (max_len + 63) / 64;
+    int ns = 1;
+    while (ns < need && ns < 64) ns *= 2;
+    while ((max_len + ns - 1) / ns > 1024) ns *= 2;
+    (void)d;
+    return ns;
+}
+
+static ec_tokens ec_tk(const ec_dev *d)
+{
+    ec_tokens tk;
+    tk.tok = d->d_tok;
+    tk.pos = d->d_pos;
+    tk.slot = d->d_slot;
+    return tk;
+}
+
+static ec_kvgeo ec_geo(const ec_dev *d, int l)
+{
+    ec_kvgeo g;
+    g.kc = d->kc + d->layer_kv * l;
+    g.vc = d->vc + d->layer_kv * l;
+    g.B = d->B;
+    g.C = d->C;
+    g.kv = d->kv;
+    g.E = d->E;
+    g.hd = d->hd;
+    g.rope_cos = d->rope_cos;
+    g.rope_sin = d->rope_sin;
+    return g;
+}
+
+/* Profiling marks: event pairs around every launch while prof_on. */
+static int ec_prof_begin(ec_dev *d, int cls, double bytes)
+{
+    if (!d->prof_on || d->prof_n >= EC_PROF_MAX) return -1;
+    int i = d->prof_n++;
+    d->prof_cls[i] = cls;
+    d->prof_bytes[i] = bytes;
+    cudaEventRecord(d->prof_ev[2 * i], d->stream);
+    return i;
+}
+
+static void ec_prof_end(ec_dev *d, int i)
+{
+    if (i >= 0) cudaEventRecord(d->prof_ev[2 * i + 1], d->stream);
+}
+
+/* Algorithmic HBM bytes of one linear over M rows: weights (+scales, bias),
+ * activations in, outputs out. */
+static double ec_lin_bytes(const ec_lin *l, int M)
+{
+    double elt = l->wt == EC_W_I8 ? 1.0 : 2.0;
+    return (double)l->N * l->K * elt + (l->s ? 4.0 * l->N : 0.0) + (l->b ? 4.0 * l->N : 0.0) +
+           4.0 * M * l->K + 4.0 * M * l->N;
+}
+
+/* One linear: GEMV (M <= 8, fused epilogue) or the generic GEMM path. */
+static int ec_linear(ec_dev *d, const ec_lin *l, const float *X, int ldx, int M, float *out, int ldo,
+                     int epi, int l_idx)
+{
+    cudaStream_t st = d->stream;
+    if (M <= 8) {
+        ec_gemv_args a;
+        memset(&a, 0, sizeof a);
+        a.W = l->w; a.wscale = l->s; a.bias = l->b;
+        a.wt = l->wt; a.N = l->N; a.K = l->K; a.Kp = l->Kp;
+        a.blocks = l->blocks; a.nblocks = l->nblocks; a.block_rows = l->block_rows;
+        a.X = X; a.ldx = ldx; a.M = M;
+        a.out = out; a.ldo = ldo; a.epi = epi;
+        if (epi == EC_EPI_QKV) { a.tk = ec_tk(d); a.geo = ec_geo(d, l_idx); }
+        int pi = ec_prof_begin(d, l == &d->lm_lin ? EC_PC_LMHEAD : EC_PC_GEMV, ec_lin_bytes(l, M));
+        CK(ec_launch_gemv(&a, d->num_sms, st));
+        ec_prof_end(d, pi);
+        return 0;
+    }
+    /* generic path: plain GEMM into a temporary then the fused-epilogue work */
+    ec_gemm_args g;
+    memset(&g, 0, sizeof g);
+    g.W = l->w; g.wscale = l->s; g.bias = l->b;
+    g.wt = l->wt; g.N = l->N; g.K = l->K; g.Kp = l->Kp; g.M = M;
+    if (l->wt == EC_W_I8) {
+        CK(ec_launch_quant(d->aq, d->as, X, ldx, M, l->K, l->Kp, st));
+        g.Aq = d->aq;
+        g.a_scale = d->as;
+    } else {
+        g.X = X;
+        g.ldx = ldx;
+    }
+    if (epi == EC_EPI_STORE || epi == EC_EPI_RESID || epi == EC_EPI_GELU) {
+        g.out = out; g.ldo = ldo; g.epi = epi;
+        CK(ec_launch_gemm(&g, st));
+        return 0;
+    }
+    if (epi == EC_EPI_SWIGLU) {
+        /* gate|up side by side into `big` [M][2I], then silu(gate)*up */
+        g.out = d->big; g.ldo = l->N; g.epi = EC_EPI_STORE;
+        CK(ec_launch_gemm(&g, st));
+        CK(ec_launch_swiglu(out, ldo, d->big, l->N, d->I, M, st));
+        return 0;
+    }
+    /* EC_EPI_QKV: q|k|v rows into `out` (row stride ldo = E + 2kv), then
+     * RoPE + KV store in place; q stays in the first E columns */
+    g.out = out; g.ldo = ldo; g.epi = EC_EPI_STORE;
+    CK(ec_launch_gemm(&g, st));
+    CK(ec_launch_rope_kv(out, ldo, ec_tk(d), ec_geo(d, l_idx), d->H, d->KVH, M, st));
+    return 0;
+}
+
+/* Enqueue the layer stack and the final norm for M rows whose inputs are
+ * already in d_tok/d_pos/d_slot.  Leaves the normed final hidden state in h. */
+static int ec_enqueue_body(ec_dev *d, int M, int nsplit)
+{
+    cudaStream_t st = d->stream;
+    const int E = d->E;
+    int pi = ec_prof_begin(d, EC_PC_OTHER, 0.0);
+    CK(ec_launch_embed(d->x, d->wte, d->wpe, d->Ep, d->prec == 2, ec_tk(d), M, E, d->V, d->C, st));
+    ec_prof_end(d, pi);
+    if (d->taps_on && d->taps && M <= d->taps_rows)
+        CK(cudaMemcpyAsync(d->taps, d->x, (size_t)M * E * 4, cudaMemcpyDeviceToDevice, st));
+    const int ldqkv = E + 2 * d->kv;
+    ec_attn_args at;
+    memset(&at, 0, sizeof at);
+    at.q = d->qkv; at.ldq = ldqkv; at.out = d->att; at.ldo = E;
+    at.tk = ec_tk(d); at.H = d->H; at.KVH = d->KVH; at.M = M; at.window = d->window;
+    at.part = d->attn_part; at.nsplit = nsplit;
+    /* q lands in the first E columns of d->qkv (row stride E + 2kv) on both
+     * the GEMV (fused epilogue) and GEMM (rope_kv pass) paths. */
+    for (int l = 0; l < d->L; l++) {
+        ec_dlayer *W = &d->lw[l];
+        pi = ec_prof_begin(d, EC_PC_NORM, 8.0 * M * E);
+        CK(ec_launch_norm(d->h, d->x, W->n1g, W->n1b, M, E, d->eps, st));
+        ec_prof_end(d, pi);
+        if (ec_linear(d, &W->qkv, d->h, E, M, d->qkv, ldqkv, EC_EPI_QKV, l)) return -1;
+        at.geo = ec_geo(d, l);
+        pi = ec_prof_begin(d, EC_PC_ATTN, 0.0);
+        CK(ec_launch_attention(&at, st));
+        ec_prof_end(d, pi);
+        if (ec_linear(d, &W->o, d->att, E, M, d->x, E, EC_EPI_RESID, l)) return -1;
+        pi = ec_prof_begin(d, EC_PC_NORM, 8.0 * M * E);
+        CK(ec_launch_norm(d->h, d->x, W->n2g, W->n2b, M, E, d->eps, st));
+        ec_prof_end(d, pi);
+        const int wact = d->arch == ARCH_QWEN2 ? d->I : 4 * E;
+        if (ec_linear(d, &W->up, d->h, E, M, d->act, wact,
+                      d->arch == ARCH_QWEN2 ? EC_EPI_SWIGLU : EC_EPI_GELU, l)) return -1;
+        if (ec_linear(d, &W->down, d->act, wact, M, d->x, E, EC_EPI_RESID, l)) return -1;
+        if (d->taps_on && d->taps && M <= d->taps_rows)
+            CK(cudaMemcpyAsync(d->taps + (size_t)(l + 1) * M * E, d->x, (size_t)M * E * 4, cudaMemcpyDeviceToDevice, st));
+    }
+    pi = ec_prof_begin(d, EC_PC_NORM, 8.0 * M * E);
+    CK(ec_launch_norm(d->h, d->x, d->nfg, d->nfb, M, E, d->eps, st));
+    ec_prof_end(d, pi);
+    return 0;
+}
+
+/* lm_head rows [r0, r0+rows) of h -> d->logits [rows][v1-v0]. */
+static int ec_enqueue_lm(ec_dev *d, int r0, int rows)
+{
+    return ec_linear(d, &d->lm_lin, d->h + (size_t)r0 * d->E, d->E, rows, d->logits, d->v1 - d->v0, EC_EPI_STORE, 0);
+}
+
+/* Validate host inputs and stage tok/pos/slot into the pinned buffer. */
+static int ec_stage_inputs(ec_dev *d, const int *tokens, const int *positions, const int *seqs, int M)
+{
+    if (M < 1) { ec_seterr("M must be >= 1 (got %d)", M); return -1; }
+    if (!tokens || !positions) { ec_seterr("tokens/positions must not be NULL"); return -1; }
+    if (ec_ensure(d, M)) return -1;
+    CK(cudaStreamSynchronize(d->stream));   /* h_in may still feed a previous async copy */
+    int *ht = d->h_in, *hp = d->h_in + M, *hs = d->h_in + 2 * M;
+    for (int m = 0; m < M; m++) {
+        int t = tokens[m], p = positions[m];
+        int s = seqs ? seqs[m] : m;
+        if (s >= d->B) s = d->B - 1;   /* reference clamp, src/gpt2.c:512-513 */
+        if (t < 0 || t >= d->V) { ec_seterr("token id %d out of range [0,%d)", t, d->V); return -1; }
+        if (p < 0 || p >= d->C) { ec_seterr("position %d out of range [0,%d)", p, d->C); return -1; }
+        if (s < 0) { ec_seterr("slot %d is negative", s); return -1; }
+        ht[m] = t; hp[m] = p; hs[m] = s;
+    }
+    return 0;
+}
+
+static int ec_copy_inputs(ec_dev *d, int M)
+{
+    CK(cudaMemcpyAsync(d->d_tok, d->h_in, (size_t)M * 4, cudaMemcpyHostToDevice, d->stream));
+    CK(cudaMemcpyAsync(d->d_pos, d->h_in + M, (size_t)M * 4, cudaMemcpyHostToDevice, d->stream));
+    CK(cudaMemcpyAsync(d->d_slot, d->h_in + 2 * M, (size_t)M * 4, cudaMemcpyHostToDevice, d->stream));
+    return 0;
+}
+
+static int ec_max_len(const ec_dev *d, int M)
+{
+    int mx = 1;
+    for (int m = 0; m < M; m++) {
+        int p = d->h_in[M + m];
+        int lo = d->window > 0 ? p - d->window + 1 : 0;
+        if (lo < 0) lo = 0;
+        if (p + 1 - lo > mx) mx = p + 1 - lo;
+    }
+    return mx;
+}
+
+/* Find or capture the graph for (kind, M, nsplit). kind 0: body + lm_head
+ * (M <= 8), kind 1: body + lm_head + argmax, kind 2: decode step (kind 1 +
+ * step bookkeeping, recording ids in d_hist), kind 3: decode step without
+ * the id history. */
+static cudaGraphExec_t ec_graph_get(ec_dev *d, int kind, int M, int nsplit);
+
+static int ec_enqueue_step(ec_dev *d, int kind, int M, int nsplit)
+{
+    if (ec_enqueue_body(d, M, nsplit)) return -1;
+    if (ec_enqueue_lm(d, 0, M)) return -1;
+    int pi = ec_prof_begin(d, EC_PC_OTHER, 0.0);
+    if (kind >= 1) {
+        CK(ec_launch_argmax(d->d_ids, d->d_max, d->logits, d->v1 - d->v0, d->v1 - d->v0, M, d->v0,
+                            d->amax_part, d->amax_chunks, d->stream));
+    }
+    if (kind >= 2)
+        CK(ec_launch_step_advance(d->d_tok, d->d_pos, d->d_ids, M, kind == 2 ? d->d_hist : NULL, d->d_counter,
+                                  d->wrap_lo, d->wrap_hi, d->stream));
+    ec_prof_end(d, pi);
+    return 0;
+}
+
+static cudaGraphExec_t ec_graph_get(ec_dev *d, int kind, int M, int nsplit)
+{
+    for (int i = 0; i < d->ngraphs; i++)
+        if (d->graphs[i].kind == kind && d->graphs[i].M == M && d->graphs[i].nsplit == nsplit &&
+            (kind < 2 || (d->graphs[i].wrap_lo == d->wrap_lo && d->graphs[i].wrap_hi == d->wrap_hi)))
+            return d->graphs[i].exec;
+    if (d->ngraphs == EC_MAX_GRAPHS) {
+        cudaGraphExecDestroy(d->graphs[0].exec);
+        memmove(&d->graphs[0], &d->graphs[1], sizeof(ec_graph) * (EC_MAX_GRAPHS - 1));
+        d->ngraphs--;
+    }
+    cudaGraph_t gr = NULL;
+    cudaGraphExec_t ex = NULL;
+    if (cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        ec_seterr("begin capture failed");
+        return NULL;
+    }
+    int rc = ec_enqueue_step(d, kind, M, nsplit);
+    cudaError_t e = cudaStreamEndCapture(d->stream, &gr);
+    if (rc || e != cudaSuccess) {
+        if (!rc) ec_seterr("end capture: %s", cudaGetErrorString(e));
+        if (gr) cudaGraphDestroy(gr);
+        cudaGetLastError();
+        return NULL;
+    }
+    e = cudaGraphInstantiate(&ex, gr, 0);
+    cudaGraphDestroy(gr);
+    if (e != cudaSuccess) { ec_seterr("graph instantiate: %s", cudaGetErrorString(e)); return NULL; }
+    d->graphs[d->ngraphs].kind = kind;
+    d->graphs[d->ngraphs].M = M;
+    d->graphs[d->ngraphs].nsplit = nsplit;
+    d->graphs[d->ngraphs].wrap_lo = d->wrap_lo;
+    d->graphs[d->ngraphs].wrap_hi = d->wrap_hi;
+    d->graphs[d->ngraphs].exec = ex;
+    d->ngraphs++;
+    return ex;
+}
+
+static int ec_check_kernel_error(ec_dev *d)
+{
+    int code = 0;
+    CK(ec_kernel_error_take(d->stream, &code));
+    if (code) { ec_seterr("device kernel reported error code %d (bad index or wait timeout)", code); return -1; }
+    return 0;
+}
+
+static int ec_use_graphs(void)
+{
+    static int v = -1;
+    if (v < 0) {
+        const char *s = getenv("EDGECORE_B200_GRAPHS");
+        v = s ? atoi(s) != 0 : 1;
+    }
+    return v;
+}
+
+/* Forward to host logits (or host argmax when ids != NULL). */
+static int ec_forward_impl(GPT2 *g, const int *tokens, const int *positions, const int *seqs, int M,
+                           float *logits, int *ids, float *maxv)
+{
+    ec_dev *d = ec_lookup(g);
+    if (!d) { ec_seterr("model not loaded by this library"); return -1; }
+    int cur = 0;
+    cudaGetDevice(&cur);
+    if (cur != d->device) CK(cudaSetDevice(d->device));
+    if (ec_stage_inputs(d, tokens, positions, seqs, M)) return -1;
+    const int nsplit = ec_pick_nsplit(d, ec_max_len(d, M));
+    const int Vs = d->v1 - d->v0;
+    if (ec_ensure_attn(d, M, nsplit)) return -1;
+    if (ec_copy_inputs(d, M)) return -1;
+    if (M <= 8) {
+        if (ec_ensure_logits(d, 8) || ec_ensure_amax(d, 8)) return -1;
+        const int kind = ids ? 1 : 0;
+        if (ec_use_graphs() && !d->taps_on) {
+            cudaGraphExec_t ex = ec_graph_get(d, kind, M, nsplit);
+            if (!ex) return -1;
+            CK(cudaGraphLaunch(ex, d->stream));
+        } else if (ec_enqueue_step(d, kind, M, nsplit)) {
+            return -1;
+        }
+        if (ids) {
+            CK(cudaMemcpyAsync(d->h_ids, d->d_ids, (size_t)M * 4, cudaMemcpyDeviceToHost, d->stream));
+            CK(cudaMemcpyAsync(d->h_max, d->d_max, (size_t)M * 4, cudaMemcpyDeviceToHost, d->stream));
+            CK(cudaStreamSynchronize(d->stream));
+            memcpy(ids, d->h_ids, (size_t)M * 4);
+            if (maxv) memcpy(maxv, d->h_max, (size_t)M * 4);
+        } else {
+            size_t bytes = (size_t)M * Vs * 4;
+            if (bytes > d->h_logits_cap) {
+                cudaFreeHost(d->h_logits);
+                d->h_logits = NULL;
+                CK(cudaMallocHost((void **)&d->h_logits, bytes));
+                d->h_logits_cap = bytes;
+            }
+            CK(cudaMemcpyAsync(d->h_logits, d->logits, bytes, cudaMemcpyDeviceToHost, d->stream));
+            CK(cudaStreamSynchronize(d->stream));
+            memcpy(logits, d->h_logits, bytes);
+        }
+        return ec_check_kernel_error(d);
+    }
+    /* prefill-shaped: direct launches, lm_head in row chunks */
+    if (ec_enqueue_body(d, M, nsplit)) return -1;
+    int chunk = (int)((256u << 20) / ((size_t)Vs * 4));
+    if (chunk < 8) chunk = 8;
+    if (chunk > M) chunk = M;
+    if (ec_ensure_logits(d, chunk) || ec_ensure_amax(d, chunk)) return -1;
+    size_t hbytes = (size_t)chunk * Vs * 4;
+    if (!ids && hbytes > d->h_logits_cap) {
+        cudaFreeHost(d->h_logits);
+        d->h_logits = NULL;
+        CK(cudaMallocHost((void **)&d->h_logits, hbytes));
+        d->h_logits_cap = hbytes;
+    }
+    for (int r0 = 0; r0 < M; r0 += chunk) {
+        int rows = M - r0 < chunk ? M - r0 : chunk;
+        if (ec_enqueue_lm(d, r0, rows)) return -1;
+        if (ids) {
+            CK(ec_launch_argmax(d->d_ids + r0, d->d_max + r0, d->logits, Vs, Vs, rows, d->v0, d->amax_part,
+                                d->amax_chunks, d->stream));
+        } else {
+            CK(cudaMemcpyAsync(d->h_logits, d->logits, (size_t)rows * Vs * 4, cudaMemcpyDeviceToHost, d->stream));
+            CK(cudaStreamSynchronize(d->stream));
+            memcpy(logits + (size_t)r0 * Vs, d->h_logits, (size_t)rows * Vs * 4);
+        }
+    }
+    if (ids) {
+        CK(cudaMemcpyAsync(d->h_ids, d->d_ids, (size_t)M * 4, cudaMemcpyDeviceToHost, d->stream));
+        CK(cudaMemcpyAsync(d->h_max, d->d_max, (size_t)M * 4, cudaMemcpyDeviceToHost, d->stream));
+    }
+    CK(cudaStreamSynchronize(d->stream));
+    if (ids) {
+        memcpy(ids, d->h_ids, (size_t)M * 4);
+        if (maxv) memcpy(maxv, d->h_max, (size_t)M * 4);
+    }
+    return ec_check_kernel_error(d);
+}
+
+EC_EXPORT void gpt2_forward(GPT2 *g, const int *tokens, const int *positions, const int *seqs, int M, float *logits)
+{
+    if (ec_forward_impl(g, tokens, positions, seqs, M, logits, NULL, NULL)) ec_fatal("gpt2_forward");
+}
+
+EC_EXPORT void qwen2_forward(GPT2 *g, const int *tokens, const int *positions, const int *seqs, int M, float *logits)
+{
+    gpt2_forward(g, tokens, positions, seqs, M, logits);
+}
+
+/* ------------------------------------------------------------------ */
+/* extensions                                                           */
+/* ------------------------------------------------------------------ */
+
+EC_EXPORT GPT2 *ec_model_open(const char *path, int batch_cap, int max_ctx)
+{
+    GPT2 *g = calloc(1, sizeof *g);
+    if (!g) { ec_seterr("out of memory"); return NULL; }
+    if (gpt2_load(g, path, batch_cap, max_ctx)) { free(g); return NULL; }
+    return g;
+}
+
+EC_EXPORT void ec_model_close(GPT2 *g)
+{
+    if (!g) return;
+    gpt2_free(g);
+    free(g);
+}
+
+EC_EXPORT int ec_model_info(const GPT2 *g, int *o)
+{
+    ec_dev *d = ec_lookup(g);
+    if (!d) { ec_seterr("model not loaded"); return -1; }
+    int v[16] = {g->arch, g->precision, g->n_layer, g->n_head, g->n_kv_head, g->n_embd, g->head_dim,
+                 g->intermediate, g->vocab, g->n_ctx, gpt2_eff_ctx(g), g->batch_cap, g->n_kv_embd,
+                 g->tie_word_embeddings, d->device, 0};
+    memcpy(o, v, sizeof v);
+    return 0;
+}
+
+EC_EXPORT int ec_model_set_stream(GPT2 *g, void *stream)
+{
+    ec_dev *d = ec_lookup(g);
+    if (!d) { ec_seterr("model not loaded"); return -1; }
+    cudaStream_t s = stream ? (cudaStream_t)stream : d->own_stream;
+    if (s != d->stream) {
+        CK(cudaStreamSynchronize(d->stream));
+        d->stream = s;
+    }
+    return 0;
+}
+
+EC_EXPORT int ec_forward_device(GPT2 *g, const int *d_tokens, const int *d_positions, const int *d_seqs, int M,
+                                float *d_logits)
+{
+    ec_dev *d = ec_lookup(g);
+    if (!d) { ec_seterr("model not loaded"); return -1; }
+    if (M < 1 || M > 8) { ec_seterr("ec_forward_device: 1 <= M <= 8"); return -1; }
+    if (ec_ensure(d, M) || ec_ensure_logits(d, 8) || ec_ensure_amax(d, 8)) return -1;
+    int nsplit = ec_pick_nsplit(d, d->C);
+    if (ec_ensure_attn(d, M, nsplit)) return -1;
+    CK(cudaStreamSynchronize(d->stream));   /* h_in reuse */
+    CK(cudaMemcpyAsync(d->d_tok, d_tokens, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
+    CK(cudaMemcpyAsync(d->d_pos, d_positions, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
+    if (d_seqs) {
+        CK(cudaMemcpyAsync(d->d_slot, d_seqs, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
+    } else {
+        for (int m = 0; m < M; m++) d->h_in[2 * M + m] = m < d->B ? m : d->B - 1;
+        CK(cudaMemcpyAsync(d->d_slot, d->h_in + 2 * M, (size_t)M * 4, cudaMemcpyHostToDevice, d->stream));
+    }
+    cudaGraphExec_t ex = ec_graph_get(d, 0, M, nsplit);
+    if (!ex) return -1;
+    CK(cudaGraphLaunch(ex, d->stream));
+    CK(cudaMemcpyAsync(d_logits, d->logits, (size_t)M * (d->v1 - d->v0) * 4, cudaMemcpyDeviceToDevice, d->stream));
+    return 0;
+}
+
+EC_EXPORT int ec_forward_argmax(GPT2 *g, const int *tokens, const int *positions, const int *seqs, int M,
+                                int *out_ids, float *out_max)
+{
+    if (!out_ids) { ec_seterr("out_ids must not be NULL"); return -1; }
+    return ec_forward_impl(g, tokens, positions, seqs, M, NULL, out_ids, out_max);
+}
+
+EC_EXPORT int ec_forward_shard_argmax(GPT2 *g, const int *tokens, const int *positions, const int *seqs, int M,
+                                      int *out_ids, float *out_max)
+{
+    return ec_forward_argmax(g, tokens, positions, seqs, M, out_ids, out_max);
+}
+
+EC_EXPORT int ec_decode_greedy(GPT2 *g, int *d_tokens, int start_pos, int n_steps, int *d_out_ids)
+{
+    return ec_decode_greedy_cycle(g, d_tokens, start_pos, 0, n_steps, d_out_ids);
+}
+
+EC_EXPORT int ec_decode_greedy_cycle(GPT2 *g, int *d_tokens, int start_pos, int period, int n_steps,
+                                     int *d_out_ids)
+{
+    ec_dev *d = ec_lookup(g);
+    if (!d) { ec_seterr("model not loaded"); return -1; }
+    const int M = d->B;
+    if (M > 8) { ec_seterr("ec_decode_greedy: batch_cap must be <= 8 (got %d)", M); return -1; }
+    const int span = period > 0 && period < n_steps ? period : n_steps;
+    if (n_steps < 0 || period < 0 || start_pos < 0 || start_pos + span > d->C) {
+        ec_seterr("decode range [%d, %d) exceeds eff_ctx %d", start_pos, start_pos + span, d->C);
+        return -1;
+    }
+    if (n_steps == 0) return 0;
+    if (ec_ensure(d, M) || ec_ensure_logits(d, 8) || ec_ensure_amax(d, 8)) return -1;
+    d->wrap_lo = period > 0 ? start_pos : 0;
+    d->wrap_hi = period > 0 ? start_pos + period : 0;
+    int max_len = start_pos + span;
+    if (d->window > 0 && max_len > d->window) max_len = d->window;
+    int nsplit = ec_pick_nsplit(d, max_len);
+    if (ec_ensure_attn(d, M, nsplit)) return -1;
+    if (d_out_ids && d->hist_cap < n_steps * M) {
+        ec_free_graphs(d);
+        cudaFree(d->d_hist);
+        d->d_hist = NULL;
+        CK(cudaMalloc((void **)&d->d_hist, (size_t)n_steps * M * 4));
+        d->hist_cap = n_steps * M;
+    }
+    CK(cudaStreamSynchronize(d->stream));   /* h_in reuse */
+    for (int m = 0; m < M; m++) {
+        d->h_in[M + m] = start_pos;
+        d->h_in[2 * M + m] = m;
+    }
+    int rc = 0;
+    if (cudaMemcpyAsync(d->d_tok, d_tokens, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream) != cudaSuccess ||
+        cudaMemcpyAsync(d->d_pos, d->h_in + M, (size_t)M * 4, cudaMemcpyHostToDevice, d->stream) != cudaSuccess ||
+        cudaMemcpyAsync(d->d_slot, d->h_in + 2 * M, (size_t)M * 4, cudaMemcpyHostToDevice, d->stream) != cudaSuccess ||
+        cudaMemsetAsync(d->d_counter, 0, 4, d->stream) != cudaSuccess) {
+        ec_seterr("decode setup copy failed");
+        rc = -1;
+    }
+    cudaGraphExec_t ex = NULL;
+    if (!rc) {
+        ex = ec_graph_get(d, d_out_ids ? 2 : 3, M, nsplit);
+        if (!ex) rc = -1;
+    }
+    for (int i = 0; !rc && i < n_steps; i++)
+        if (cudaGraphLaunch(ex, d->stream) != cudaSuccess) { ec_seterr("graph launch failed"); rc = -1; }
+    if (!rc && d_out_ids)
+        if (cudaMemcpyAsync(d_out_ids, d->d_hist, (size_t)n_steps * M * 4, cudaMemcpyDeviceToDevice, d->stream) != cudaSuccess) rc = -1;
+    if (!rc && cudaMemcpyAsync(d_tokens, d->d_tok, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream) != cudaSuccess) rc = -1;
+    return rc;
+}
+
+EC_EXPORT int ec_model_set_taps(GPT2 *g, int enable)
+{
+    ec_dev *d = ec_lookup(g);
+    if (!d) { ec_seterr("model not loaded"); return -1; }
+    d->taps_on = enable > 0;
+    if (d->taps_on && (!d->taps || d->taps_rows < enable)) {
+        cudaFree(d->taps);
+        d->taps = NULL;
+        CK(cudaMalloc((void **)&d->taps, (size_t)(d->L + 1) * enable * d->E * 4));
+        d->taps_rows = enable;
+    }
+    return 0;
+}
+
+EC_EXPORT int ec_model_get_taps(GPT2 *g, float *out, int M)
+{
+    ec_dev *d = ec_lookup(g);
+    if (!d || !d->taps || M > d->taps_rows) { ec_seterr("taps not enabled for %d rows", M); return -1; }
+    CK(cudaStreamSynchronize(d->stream));
+    CK(cudaMemcpy(out, d->taps, (size_t)(d->L + 1) * M * d->E * 4, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+EC_EXPORT int ec_model_set_vocab_shard(GPT2 *g, int v_begin, int v_end)
+{
+    ec_dev *d = ec_lookup(g);
+    if (!d) { ec_seterr("model not loaded"); return -1; }
+    if (v_begin < 0 || v_end > d->V || v_begin >= v_end) { ec_seterr("bad vocab shard [%d,%d)", v_begin, v_end); return -1; }
+    CK(cudaStreamSynchronize(d->stream));
+    return ec_set_lm_shard(d, v_begin, v_end);
+}
+
+/* (max, idx) -> key: unsigned order = larger value first, then lower index. */
+EC_EXPORT uint64_t ec_argmax_key(float maxv, int idx)
+{
+    uint32_t b;
+    memcpy(&b, &maxv, 4);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);   /* order-preserving float bits */
+    return ((uint64_t)b << 32) | (uint32_t)(0x7fffffff - idx);
+}
+
+EC_EXPORT void ec_argmax_key_decode(uint64_t key, float *maxv, int *idx)
+{
+    uint32_t b = (uint32_t)(key >> 32);
+    b = (b & 0x80000000u) ? (b & 0x7fffffffu) : ~b;
+    if (maxv) memcpy(maxv, &b, 4);
+    if (idx) *idx = 0x7fffffff - (int)(uint32_t)(key & 0xffffffffu);
+}
+
+/* Instrumented decode: n_steps ungraphed greedy steps with a CUDA event pair
+ * around every launch.  out[c*3 + {0,1,2}] = {total ms, total algorithmic
+ * bytes, launches} for kernel class c (EC_PC_*); out[15] = steps. */
+EC_EXPORT int ec_decode_profile(GPT2 *g, int *d_tokens, int start_pos, int n_steps, double *out)
+{
+    ec_dev *d = ec_lookup(g);
+    if (!d) { ec_seterr("model not loaded"); return -1; }
+    const int M = d->B;
+    if (M > 8 || n_steps < 1 || start_pos < 0 || start_pos + n_steps > d->C) { ec_seterr("bad profile range"); return -1; }
+    if (ec_ensure(d, M) || ec_ensure_logits(d, 8) || ec_ensure_amax(d, 8)) return -1;
+    int max_len = start_pos + n_steps;
+    int nsplit = ec_pick_nsplit(d, max_len);
+    if (ec_ensure_attn(d, M, nsplit)) return -1;
+    if (!d->prof_ready) {
+        for (int i = 0; i < 2 * EC_PROF_MAX; i++) CK(cudaEventCreate(&d->prof_ev[i]));
+        d->prof_ready = 1;
+    }
+    CK(cudaStreamSynchronize(d->stream));
+    for (int m = 0; m < M; m++) { d->h_in[M + m] = start_pos; d->h_in[2 * M + m] = m; }
+    CK(cudaMemcpyAsync(d->d_tok, d_tokens, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
+    CK(cudaMemcpyAsync(d->d_pos, d->h_in + M, (size_t)M * 4, cudaMemcpyHostToDevice, d->stream));
+    CK(cudaMemcpyAsync(d->d_slot, d->h_in + 2 * M, (size_t)M * 4, cudaMemcpyHostToDevice, d->stream));
+    for (int i = 0; i < 16; i++) out[i] = 0.0;
+    d->wrap_lo = d->wrap_hi = 0;
+    for (int st = 0; st < n_steps; st++) {
+        d->prof_on = 1;
+        d->prof_n = 0;
+        int rc = ec_enqueue_step(d, 3, M, nsplit);
+        d->prof_on = 0;
+        if (rc) return -1;
+        CK(cudaStreamSynchronize(d->stream));
+        for (int i = 0; i < d->prof_n; i++) {
+            float ms = 0.0f;
+            CK(cudaEventElapsedTime(&ms, d->prof_ev[2 * i], d->prof_ev[2 * i + 1]));
+            int c = d->prof_cls[i];
+            out[c * 3 + 0] += ms;
+            out[c * 3 + 1] += d->prof_bytes[i];
+            out[c * 3 + 2] += 1.0;
+        }
+    }
+    out[15] = n_steps;
+    CK(cudaMemcpyAsync(d_tokens, d->d_tok, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
+    CK(cudaStreamSynchronize(d->stream));
+    return ec_check_kernel_error(d);
+}

@@ -1,0 +1,118 @@
+/*
+ * edgecore_b200.h -- entry points of libedgecore_b200.so beyond the reference
+ * EdgeCore ABI (which is declared, unchanged, in edgecore.h).
+ *
+ * All functions are plain C: pointers and sizes, no torch or CUDA types.
+ * A `stream` argument is a cudaStream_t passed as void* (NULL = the model's
+ * own stream / the legacy default stream for the standalone ops).
+ * Functions returning int return 0 on success and -1 on failure; the reason
+ * is available from ec_last_error().  Functions that mirror a `void` reference
+ * entry point abort the process on a CUDA error, like the reference aborts on
+ * a workspace overflow (reference src/gpt2.c:442-445).
+ */
+#ifndef EDGECORE_B200_H
+#define EDGECORE_B200_H
+
+#include "edgecore.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- library ---------------------------------------------------------- */
+
+/* Text of the last error recorded on this thread ("" if none). */
+const char *ec_last_error(void);
+
+/* Library version string, e.g. "edgecore_b200 0.1 sm_100a". */
+const char *ec_version(void);
+
+/* ---- model handle for FFI callers that cannot allocate a GPT2 ---------- */
+
+/* calloc a GPT2 and gpt2_load() it on the current CUDA device; NULL on error.
+ * Mirrors reference src/runtime_main.c:650-655 (stack GPT2 + gpt2_load). */
+GPT2 *ec_model_open(const char *path, int batch_cap, int max_ctx);
+
+/* gpt2_free() + free() of a handle from ec_model_open. */
+void ec_model_close(GPT2 *g);
+
+/* Copy scalar model metadata into out[0..15]:
+ * {arch, precision, n_layer, n_head, n_kv_head, n_embd, head_dim, intermediate,
+ *  vocab, n_ctx, eff_ctx, batch_cap, n_kv_embd, tie_word_embeddings, device, 0}. */
+int ec_model_info(const GPT2 *g, int *out16);
+
+/* Bind all subsequent work of the model to `stream` (NULL = its own stream). */
+int ec_model_set_stream(GPT2 *g, void *stream);
+
+/* ---- forward variants --------------------------------------------------- */
+
+/* gpt2_forward with DEVICE tokens/positions/seqs and DEVICE logits [M][vocab],
+ * enqueued on the model stream without a host synchronisation. */
+int ec_forward_device(GPT2 *g, const int *d_tokens, const int *d_positions,
+                      const int *d_seqs, int M, float *d_logits);
+
+/* Greedy forward: like gpt2_forward but returns only, per token row m, the
+ * argmax over the vocab (lowest index on ties, as reference
+ * src/runtime_main.c:213-219) and its logit.  Host pointers. */
+int ec_forward_argmax(GPT2 *g, const int *tokens, const int *positions,
+                      const int *seqs, int M, int *out_ids, float *out_max);
+
+/* Device-resident greedy decode of `n_steps` tokens for the batch_cap slots.
+ * d_tokens[batch_cap] holds the current token of every slot and is updated in
+ * place; step i runs at position start_pos + i for all slots; the sampled ids
+ * are written to d_out_ids[n_steps][batch_cap] (may be NULL).  The step is a
+ * captured CUDA graph replayed n_steps times (reference decode loop:
+ * src/runtime_main.c:336-352 with sample_token's greedy branch). */
+int ec_decode_greedy(GPT2 *g, int *d_tokens, int start_pos, int n_steps,
+                     int *d_out_ids);
+
+/* ec_decode_greedy with the positions cycling through [start_pos,
+ * start_pos + period): after the step at start_pos + period - 1 the next step
+ * runs at start_pos again, i.e. a new continuation of the same cached prefix.
+ * Lets a long measurement keep the context length of a short decode. */
+int ec_decode_greedy_cycle(GPT2 *g, int *d_tokens, int start_pos, int period, int n_steps,
+                           int *d_out_ids);
+
+/* Instrumented greedy decode for measurement: n_steps steps launched without
+ * a graph, with a CUDA event pair around every kernel launch on the model
+ * stream.  out[16]: for kernel class c in {0 layer GEMV, 1 lm_head GEMV,
+ * 2 attention, 3 norms, 4 other}: out[3c] = total ms, out[3c+1] = total
+ * algorithmic HBM bytes, out[3c+2] = launches; out[15] = steps. */
+int ec_decode_profile(GPT2 *g, int *d_tokens, int start_pos, int n_steps, double *out16);
+
+/* Per-layer taps of the last forward: copies the residual stream after the
+ * embedding and after every layer, [n_layer+1][M][n_embd] fp32, to host
+ * `out`.  Only valid after a forward with taps enabled by ec_model_set_taps. */
+int ec_model_set_taps(GPT2 *g, int enable);
+int ec_model_get_taps(GPT2 *g, float *out, int M);
+
+/* ---- vocab-sharded lm_head (column split across ranks) ----------------- */
+
+/* Restrict the model's lm_head to rows [v_begin, v_end) of the vocab.  After
+ * this, ec_forward_shard_argmax returns per-row (max logit, global argmax)
+ * of the shard; ranks combine them with ec_argmax_combine or a collective. */
+int ec_model_set_vocab_shard(GPT2 *g, int v_begin, int v_end);
+int ec_forward_shard_argmax(GPT2 *g, const int *tokens, const int *positions,
+                            const int *seqs, int M, int *out_ids, float *out_max);
+
+/* Encode (max, idx) as a 64-bit key whose unsigned order is "larger logit,
+ * then lower index": combining shards with an unsigned max gives the
+ * reference tie rule.  Decode inverts it. */
+uint64_t ec_argmax_key(float maxv, int idx);
+void ec_argmax_key_decode(uint64_t key, float *maxv, int *idx);
+
+/* ---- standalone ops (host or device pointers) --------------------------- */
+
+/* Per-row symmetric int8 activation quantisation, bit-exact with the int8
+ * branch of reference linear() (src/gpt2.c:446-461). */
+int ec_quantize_rows(int8_t *q, float *scale, const float *x, int M, int K);
+
+/* W8A8 linear: quantise X rows then gemm_int8 (reference src/gpt2.c:437-462). */
+int ec_linear_int8(float *C, const float *X, const int8_t *W,
+                   const float *w_scale, const float *bias, int M, int K, int N);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EDGECORE_B200_H */
