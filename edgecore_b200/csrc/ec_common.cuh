@@ -107,12 +107,20 @@ EC_DEV int ec_quant1(float x, float s) {
     return q > 127 ? 127 : (q < -128 ? -128 : q);
 }
 
+// Correctly rounded fp32 exp and tanh: the fp64 function (error < 1 ulp of
+// fp64) rounded once to fp32.  The reference calls the host libm's expf /
+// tanhf, which are not correctly rounded; every int8 quantisation downstream
+// is discontinuous, so this library pins the rounding of these functions to
+// the one well-defined choice and the oracle has a matching build.
+EC_DEV float ec_expf(float x) { return __double2float_rn(exp((double)x)); }
+EC_DEV float ec_tanhf(float x) { return __double2float_rn(tanh((double)x)); }
+
 // Reference gelu_new (src/gpt2.c:393-396) with its evaluation order kept.
 EC_DEV float ec_gelu(float x) {
     float c = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x);
-    float t = tanhf(__fmul_rn(0.7978845608028654f, __fadd_rn(x, c)));
+    float t = ec_tanhf(__fmul_rn(0.7978845608028654f, __fadd_rn(x, c)));
     return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, t));
 }
 
 // Reference SiLU (src/gpt2.c:587-590).
-EC_DEV float ec_silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
+EC_DEV float ec_silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, ec_expf(-x))); }

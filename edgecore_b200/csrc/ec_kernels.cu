@@ -202,7 +202,10 @@ k_gemv(const ec_gemv_args a, const int stages) {
         if (__syncthreads_or(!ok)) return;
         const unsigned char *st = stage0 + (size_t)s * L.stage_bytes;
 
-        const int wpr = rows >= 8 ? 1 : (rows >= 4 ? 2 : (rows >= 2 ? 4 : 8));
+        // warps per row: split a row's chunks across warps only when all rows
+        // of the block fit in one pass (rows * wpr <= 8), so part[] is
+        // written once per block
+        const int wpr = rows > 4 ? 1 : (rows > 2 ? 2 : (rows == 2 ? 4 : 8));
         const int conc = GEMV_WARPS / wpr;
         for (int r0 = 0; r0 < rows; r0 += conc) {
             const int r = r0 + warp / wpr, sub = warp % wpr;
@@ -358,6 +361,10 @@ extern "C" int ec_kernels_init(void) {
         e = cudaFuncSetAttribute(k_gemv<EC_W_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, g_ec_max_optin_smem);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(k_gemv<EC_W_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, g_ec_max_optin_smem);
+    if (e == cudaSuccess) {
+        ec_attention_exact_fits(1, 1, 8, 1);   // sets the exact-attention smem attribute outside any capture
+        e = cudaGetLastError();
+    }
     return (int)e;
 }
 
@@ -766,7 +773,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const ec_attn_args a)
     }
     double sum = 0.0;
     for (int p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
-        const float e = expf(sc[p - p0] - mx);
+        const float e = ec_expf(sc[p - p0] - mx);
         sc[p - p0] = e;
         sum += (double)e;
     }
@@ -810,9 +817,143 @@ __global__ void k_attn_combine(const ec_attn_args a) {
     }
 }
 
+// Exact-order attention: the reference's arithmetic step for step
+// (src/gpt2.c:743-777, :527-557) for all query heads of one KV head and one
+// token row.  Scores are the sequential fp32 dot over head_dim (products and
+// sums rounded separately), scaled in fp64; the max is global; weights are
+// (float)(exp(s - max) * (1 / sum)) with the sum in fp64; the output is the
+// sequential fp32 sum over positions of w * v, in position order.  Only the
+// fp64 sums are reassociated (they round to the same fp32 weights except in
+// ~2^-29 of cases).  One CTA per (KV head, token); scores live in shared
+// memory: maxlen * heads_per_group floats.
+#define ATTX_THREADS 256
+#define ATTX_MAX_GROUP 16
+
+__host__ __device__ inline size_t attx_smem_bytes(int G, int hd, int maxlen) {
+    return ((size_t)G * hd + (size_t)G * maxlen) * sizeof(float);
+}
+
+__global__ void __launch_bounds__(ATTX_THREADS) k_attn_exact(const ec_attn_args a) {
+    extern __shared__ __align__(16) float attx_smem[];
+    const int g = blockIdx.x, m = blockIdx.y;
+    const ec_kvgeo &geo = a.geo;
+    const int hd = geo.hd;
+    const int h0 = (g * a.H + a.KVH - 1) / a.KVH, h1 = ((g + 1) * a.H + a.KVH - 1) / a.KVH;
+    const int G = h1 - h0;
+    const int pos = a.tk.pos[m], slot = a.tk.slot[m];
+    if (pos < 0 || pos >= geo.C || slot < 0 || slot >= geo.B || G <= 0 || G > ATTX_MAX_GROUP) {
+        if (threadIdx.x == 0) atomicCAS(&g_ec_err, 0, EC_KERR_BAD_INDEX);
+        return;
+    }
+    int lo = 0;
+    if (a.window > 0) { lo = pos - a.window + 1; if (lo < 0) lo = 0; }
+    const int len = pos + 1 - lo;
+    if (len > a.maxlen) {
+        if (threadIdx.x == 0) atomicCAS(&g_ec_err, 0, EC_KERR_BAD_INDEX);
+        return;
+    }
+    float *qs = attx_smem;                 // [G][hd]
+    float *sc = attx_smem + G * hd;        // [G][maxlen]
+    const uint16_t *kb = geo.kc + (size_t)slot * geo.C * geo.kv + (size_t)g * hd;
+    const uint16_t *vb = geo.vc + (size_t)slot * geo.C * geo.kv + (size_t)g * hd;
+    for (int i = threadIdx.x; i < G * hd; i += blockDim.x)
+        qs[i] = a.q[(size_t)m * a.ldq + (size_t)(h0 + i / hd) * hd + (i % hd)];
+    __syncthreads();
+    const double inv_hd = 1.0 / sqrt((double)hd);
+
+    // scores, one position per thread, all heads of the group
+    for (int p = lo + (int)threadIdx.x; p <= pos; p += blockDim.x) {
+        const uint16_t *kp = kb + (size_t)p * geo.kv;
+        float acc[ATTX_MAX_GROUP];
+#pragma unroll
+        for (int hh = 0; hh < ATTX_MAX_GROUP; ++hh) acc[hh] = 0.0f;
+        for (int d = 0; d < hd; d += 8) {
+            float f[8];
+            ec_f16x8_to_f32(*reinterpret_cast<const uint4 *>(kp + d), f);
+#pragma unroll
+            for (int hh = 0; hh < ATTX_MAX_GROUP; ++hh) {
+                if (hh < G) {
+                    const float *q = qs + hh * hd + d;
+                    float t = acc[hh];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) t = __fadd_rn(t, __fmul_rn(q[e], f[e]));
+                    acc[hh] = t;
+                }
+            }
+        }
+#pragma unroll
+        for (int hh = 0; hh < ATTX_MAX_GROUP; ++hh)
+            if (hh < G) sc[hh * a.maxlen + (p - lo)] = (float)__dmul_rn((double)acc[hh], inv_hd);
+    }
+    __syncthreads();
+
+    // softmax weights, one warp per head
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int hh = warp; hh < G; hh += ATTX_THREADS / 32) {
+        float *s = sc + hh * a.maxlen;
+        float mx = -FLT_MAX;
+        for (int i = lane; i < len; i += 32) mx = ec_max_keep(mx, s[i]);
+        mx = ec_warp_max(mx);
+        double sum = 0.0;
+        for (int i = lane; i < len; i += 32) {
+            const float e = ec_expf(__fsub_rn(s[i], mx));
+            s[i] = e;
+            sum = __dadd_rn(sum, (double)e);
+        }
+        sum = ec_warp_sum_d(sum);
+        const double isum = __ddiv_rn(1.0, sum);
+        __syncwarp();
+        for (int i = lane; i < len; i += 32) s[i] = (float)__dmul_rn((double)s[i], isum);
+    }
+    __syncthreads();
+
+    // output: sequential fp32 accumulation over positions for every (head, d)
+    for (int idx = threadIdx.x; idx < G * hd; idx += blockDim.x) {
+        const int hh = idx / hd, d = idx % hd;
+        const float *w = sc + hh * a.maxlen;
+        const uint16_t *vp = vb + d;
+        float o = 0.0f;
+        int i = 0;
+        for (; i + 4 <= len; i += 4) {
+            const float v0 = __half2float(__ushort_as_half(vp[(size_t)(lo + i) * geo.kv]));
+            const float v1 = __half2float(__ushort_as_half(vp[(size_t)(lo + i + 1) * geo.kv]));
+            const float v2 = __half2float(__ushort_as_half(vp[(size_t)(lo + i + 2) * geo.kv]));
+            const float v3 = __half2float(__ushort_as_half(vp[(size_t)(lo + i + 3) * geo.kv]));
+            o = __fadd_rn(o, __fmul_rn(w[i], v0));
+            o = __fadd_rn(o, __fmul_rn(w[i + 1], v1));
+            o = __fadd_rn(o, __fmul_rn(w[i + 2], v2));
+            o = __fadd_rn(o, __fmul_rn(w[i + 3], v3));
+        }
+        for (; i < len; ++i)
+            o = __fadd_rn(o, __fmul_rn(w[i], __half2float(__ushort_as_half(vp[(size_t)(lo + i) * geo.kv]))));
+        a.out[(size_t)m * a.ldo + (size_t)(h0 + hh) * hd + d] = o;
+    }
+}
+
+static int g_attx_max_smem = 0;
+
+extern "C" int ec_attention_exact_fits(int H, int KVH, int hd, int maxlen) {
+    if (KVH <= 0 || H % KVH) return 0;
+    const int G = H / KVH;
+    if (G > ATTX_MAX_GROUP || maxlen < 1) return 0;
+    if (g_attx_max_smem == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_attx_max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        cudaFuncSetAttribute(k_attn_exact, cudaFuncAttributeMaxDynamicSharedMemorySize, g_attx_max_smem);
+    }
+    return attx_smem_bytes(G, hd, maxlen) <= (size_t)g_attx_max_smem;
+}
+
 extern "C" int ec_launch_attention(const ec_attn_args *a, cudaStream_t stream) {
     if (a->M <= 0) return 0;
     if (a->geo.hd > 256 || a->geo.hd % 8 || a->nsplit < 1) return (int)cudaErrorInvalidValue;
+    if (ec_attention_exact_fits(a->H, a->KVH, a->geo.hd, a->maxlen)) {
+        const int G = a->H / a->KVH;
+        dim3 g(a->KVH, a->M);
+        k_attn_exact<<<g, ATTX_THREADS, attx_smem_bytes(G, a->geo.hd, a->maxlen), stream>>>(*a);
+        return (int)cudaGetLastError();
+    }
     dim3 g1(a->nsplit, a->H, a->M);
     k_attn_part<<<g1, ATT_THREADS, 0, stream>>>(*a);
     dim3 g2(a->H, a->M);

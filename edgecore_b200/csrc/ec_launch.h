@@ -120,9 +120,15 @@ typedef struct {
     int H, KVH, M, window;        /* window > 0: sliding window */
     float *part;                  /* scratch: [M][H][nsplit][hd + 2] */
     int nsplit;
+    int maxlen;                   /* upper bound on attended positions per row */
 } ec_attn_args;
+/* Chooses the exact-order kernel (reference summation order; one CTA per
+ * (token, KV head) holding all scores in shared memory) when maxlen fits,
+ * else the split kernel (flash-decoding order, within 1e-6 of the reference). */
 int ec_launch_attention(const ec_attn_args *a, cudaStream_t stream);
 size_t ec_attention_scratch_floats(int M, int H, int hd, int nsplit);
+/* 1 if the exact-order kernel handles rows of up to maxlen positions. */
+int ec_attention_exact_fits(int H, int KVH, int hd, int maxlen);
 
 /* Row-wise argmax (lowest index on ties) of logits [M][ld] over [0, N),
  * reporting ids offset by id_base.  part is scratch of 2*M*nchunk words. */

@@ -217,7 +217,7 @@ typedef struct {
 enum { EC_PC_GEMV = 0, EC_PC_LMHEAD = 1, EC_PC_ATTN = 2, EC_PC_NORM = 3, EC_PC_OTHER = 4, EC_PC_N = 5 };
 
 typedef struct {
-    int M, nsplit, kind;       /* kind 0: logits forward, 1: argmax forward, 2/3: decode step */
+    int M, maxlen, kind;       /* kind 0: logits forward, 1: argmax forward, 2/3: decode step */
     int wrap_lo, wrap_hi;      /* decode position cycle (wrap_hi <= 0: none) */
     cudaGraphExec_t exec;
 } ec_graph;
@@ -580,9 +580,13 @@ static int ec_ensure(ec_dev *d, int M)
     return 0;
 }
 
-static int ec_ensure_attn(ec_dev *d, int M, int nsplit)
+static int ec_pick_nsplit(const ec_dev *d, int max_len);
+
+/* Split-attention scratch for rows of up to maxlen positions (the exact-order
+ * kernel needs none). */
+static int ec_ensure_attn(ec_dev *d, int M, int maxlen)
 {
-    size_t need = ec_attention_scratch_floats(M, d->H, d->hd, nsplit);
+    size_t need = ec_attention_scratch_floats(M, d->H, d->hd, ec_pick_nsplit(d, maxlen));
     if (need <= d->attn_part_floats) return 0;
     ec_free_graphs(d);
     cudaFree(d->attn_part);
@@ -968,6 +972,16 @@ static int ec_pick_nsplit(const ec_dev *d, int max_len)
     return ns;
 }
 
+/* Attended-length bucket for a call whose rows attend at most max_len
+ * positions: a power of two >= 64, capped at eff_ctx.  Graphs and the
+ * attention launch shape are keyed by it. */
+static int ec_len_bucket(const ec_dev *d, int max_len)
+{
+    int b = 64;
+    while (b < max_len) b *= 2;
+    return b < d->C ? b : d->C;
+}
+
 static ec_tokens ec_tk(const ec_dev *d)
 {
     ec_tokens tk;
@@ -1071,7 +1085,7 @@ static int ec_linear(ec_dev *d, const ec_lin *l, const float *X, int ldx, int M,
 
 /* Enqueue the layer stack and the final norm for M rows whose inputs are
  * already in d_tok/d_pos/d_slot.  Leaves the normed final hidden state in h. */
-static int ec_enqueue_body(ec_dev *d, int M, int nsplit)
+static int ec_enqueue_body(ec_dev *d, int M, int maxlen)
 {
     cudaStream_t st = d->stream;
     const int E = d->E;
@@ -1085,7 +1099,7 @@ static int ec_enqueue_body(ec_dev *d, int M, int nsplit)
     memset(&at, 0, sizeof at);
     at.q = d->qkv; at.ldq = ldqkv; at.out = d->att; at.ldo = E;
     at.tk = ec_tk(d); at.H = d->H; at.KVH = d->KVH; at.M = M; at.window = d->window;
-    at.part = d->attn_part; at.nsplit = nsplit;
+    at.part = d->attn_part; at.maxlen = maxlen; at.nsplit = ec_pick_nsplit(d, maxlen);
     /* q lands in the first E columns of d->qkv (row stride E + 2kv) on both
      * the GEMV (fused epilogue) and GEMM (rope_kv pass) paths. */
     for (int l = 0; l < d->L; l++) {
@@ -1161,15 +1175,15 @@ static int ec_max_len(const ec_dev *d, int M)
     return mx;
 }
 
-/* Find or capture the graph for (kind, M, nsplit). kind 0: body + lm_head
+/* Find or capture the graph for (kind, M, maxlen). kind 0: body + lm_head
  * (M <= 8), kind 1: body + lm_head + argmax, kind 2: decode step (kind 1 +
  * step bookkeeping, recording ids in d_hist), kind 3: decode step without
  * the id history. */
-static cudaGraphExec_t ec_graph_get(ec_dev *d, int kind, int M, int nsplit);
+static cudaGraphExec_t ec_graph_get(ec_dev *d, int kind, int M, int maxlen);
 
-static int ec_enqueue_step(ec_dev *d, int kind, int M, int nsplit)
+static int ec_enqueue_step(ec_dev *d, int kind, int M, int maxlen)
 {
-    if (ec_enqueue_body(d, M, nsplit)) return -1;
+    if (ec_enqueue_body(d, M, maxlen)) return -1;
     if (ec_enqueue_lm(d, 0, M)) return -1;
     int pi = ec_prof_begin(d, EC_PC_OTHER, 0.0);
     if (kind >= 1) {
@@ -1183,10 +1197,10 @@ static int ec_enqueue_step(ec_dev *d, int kind, int M, int nsplit)
     return 0;
 }
 
-static cudaGraphExec_t ec_graph_get(ec_dev *d, int kind, int M, int nsplit)
+static cudaGraphExec_t ec_graph_get(ec_dev *d, int kind, int M, int maxlen)
 {
     for (int i = 0; i < d->ngraphs; i++)
-        if (d->graphs[i].kind == kind && d->graphs[i].M == M && d->graphs[i].nsplit == nsplit &&
+        if (d->graphs[i].kind == kind && d->graphs[i].M == M && d->graphs[i].maxlen == maxlen &&
             (kind < 2 || (d->graphs[i].wrap_lo == d->wrap_lo && d->graphs[i].wrap_hi == d->wrap_hi)))
             return d->graphs[i].exec;
     if (d->ngraphs == EC_MAX_GRAPHS) {
@@ -1200,7 +1214,7 @@ static cudaGraphExec_t ec_graph_get(ec_dev *d, int kind, int M, int nsplit)
         ec_seterr("begin capture failed");
         return NULL;
     }
-    int rc = ec_enqueue_step(d, kind, M, nsplit);
+    int rc = ec_enqueue_step(d, kind, M, maxlen);
     cudaError_t e = cudaStreamEndCapture(d->stream, &gr);
     if (rc || e != cudaSuccess) {
         if (!rc) ec_seterr("end capture: %s", cudaGetErrorString(e));
@@ -1213,7 +1227,7 @@ static cudaGraphExec_t ec_graph_get(ec_dev *d, int kind, int M, int nsplit)
     if (e != cudaSuccess) { ec_seterr("graph instantiate: %s", cudaGetErrorString(e)); return NULL; }
     d->graphs[d->ngraphs].kind = kind;
     d->graphs[d->ngraphs].M = M;
-    d->graphs[d->ngraphs].nsplit = nsplit;
+    d->graphs[d->ngraphs].maxlen = maxlen;
     d->graphs[d->ngraphs].wrap_lo = d->wrap_lo;
     d->graphs[d->ngraphs].wrap_hi = d->wrap_hi;
     d->graphs[d->ngraphs].exec = ex;
@@ -1249,18 +1263,18 @@ static int ec_forward_impl(GPT2 *g, const int *tokens, const int *positions, con
     cudaGetDevice(&cur);
     if (cur != d->device) CK(cudaSetDevice(d->device));
     if (ec_stage_inputs(d, tokens, positions, seqs, M)) return -1;
-    const int nsplit = ec_pick_nsplit(d, ec_max_len(d, M));
+    const int maxlen = ec_len_bucket(d, ec_max_len(d, M));
     const int Vs = d->v1 - d->v0;
-    if (ec_ensure_attn(d, M, nsplit)) return -1;
+    if (ec_ensure_attn(d, M, maxlen)) return -1;
     if (ec_copy_inputs(d, M)) return -1;
     if (M <= 8) {
         if (ec_ensure_logits(d, 8) || ec_ensure_amax(d, 8)) return -1;
         const int kind = ids ? 1 : 0;
         if (ec_use_graphs() && !d->taps_on) {
-            cudaGraphExec_t ex = ec_graph_get(d, kind, M, nsplit);
+            cudaGraphExec_t ex = ec_graph_get(d, kind, M, maxlen);
             if (!ex) return -1;
             CK(cudaGraphLaunch(ex, d->stream));
-        } else if (ec_enqueue_step(d, kind, M, nsplit)) {
+        } else if (ec_enqueue_step(d, kind, M, maxlen)) {
             return -1;
         }
         if (ids) {
@@ -1284,7 +1298,7 @@ static int ec_forward_impl(GPT2 *g, const int *tokens, const int *positions, con
         return ec_check_kernel_error(d);
     }
     /* prefill-shaped: direct launches, lm_head in row chunks */
-    if (ec_enqueue_body(d, M, nsplit)) return -1;
+    if (ec_enqueue_body(d, M, maxlen)) return -1;
     int chunk = (int)((256u << 20) / ((size_t)Vs * 4));
     if (chunk < 8) chunk = 8;
     if (chunk > M) chunk = M;
@@ -1379,8 +1393,8 @@ EC_EXPORT int ec_forward_device(GPT2 *g, const int *d_tokens, const int *d_posit
     if (!d) { ec_seterr("model not loaded"); return -1; }
     if (M < 1 || M > 8) { ec_seterr("ec_forward_device: 1 <= M <= 8"); return -1; }
     if (ec_ensure(d, M) || ec_ensure_logits(d, 8) || ec_ensure_amax(d, 8)) return -1;
-    int nsplit = ec_pick_nsplit(d, d->C);
-    if (ec_ensure_attn(d, M, nsplit)) return -1;
+    int maxlen = ec_len_bucket(d, d->C);
+    if (ec_ensure_attn(d, M, maxlen)) return -1;
     CK(cudaStreamSynchronize(d->stream));   /* h_in reuse */
     CK(cudaMemcpyAsync(d->d_tok, d_tokens, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
     CK(cudaMemcpyAsync(d->d_pos, d_positions, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
@@ -1390,7 +1404,7 @@ EC_EXPORT int ec_forward_device(GPT2 *g, const int *d_tokens, const int *d_posit
         for (int m = 0; m < M; m++) d->h_in[2 * M + m] = m < d->B ? m : d->B - 1;
         CK(cudaMemcpyAsync(d->d_slot, d->h_in + 2 * M, (size_t)M * 4, cudaMemcpyHostToDevice, d->stream));
     }
-    cudaGraphExec_t ex = ec_graph_get(d, 0, M, nsplit);
+    cudaGraphExec_t ex = ec_graph_get(d, 0, M, maxlen);
     if (!ex) return -1;
     CK(cudaGraphLaunch(ex, d->stream));
     CK(cudaMemcpyAsync(d_logits, d->logits, (size_t)M * (d->v1 - d->v0) * 4, cudaMemcpyDeviceToDevice, d->stream));
@@ -1433,8 +1447,8 @@ EC_EXPORT int ec_decode_greedy_cycle(GPT2 *g, int *d_tokens, int start_pos, int 
     d->wrap_hi = period > 0 ? start_pos + period : 0;
     int max_len = start_pos + span;
     if (d->window > 0 && max_len > d->window) max_len = d->window;
-    int nsplit = ec_pick_nsplit(d, max_len);
-    if (ec_ensure_attn(d, M, nsplit)) return -1;
+    int maxlen = ec_len_bucket(d, max_len);
+    if (ec_ensure_attn(d, M, maxlen)) return -1;
     if (d_out_ids && d->hist_cap < n_steps * M) {
         ec_free_graphs(d);
         cudaFree(d->d_hist);
@@ -1457,7 +1471,7 @@ EC_EXPORT int ec_decode_greedy_cycle(GPT2 *g, int *d_tokens, int start_pos, int 
     }
     cudaGraphExec_t ex = NULL;
     if (!rc) {
-        ex = ec_graph_get(d, d_out_ids ? 2 : 3, M, nsplit);
+        ex = ec_graph_get(d, d_out_ids ? 2 : 3, M, maxlen);
         if (!ex) rc = -1;
     }
     for (int i = 0; !rc && i < n_steps; i++)
@@ -1528,8 +1542,8 @@ EC_EXPORT int ec_decode_profile(GPT2 *g, int *d_tokens, int start_pos, int n_ste
     if (M > 8 || n_steps < 1 || start_pos < 0 || start_pos + n_steps > d->C) { ec_seterr("bad profile range"); return -1; }
     if (ec_ensure(d, M) || ec_ensure_logits(d, 8) || ec_ensure_amax(d, 8)) return -1;
     int max_len = start_pos + n_steps;
-    int nsplit = ec_pick_nsplit(d, max_len);
-    if (ec_ensure_attn(d, M, nsplit)) return -1;
+    int maxlen = ec_len_bucket(d, max_len);
+    if (ec_ensure_attn(d, M, maxlen)) return -1;
     if (!d->prof_ready) {
         for (int i = 0; i < 2 * EC_PROF_MAX; i++) CK(cudaEventCreate(&d->prof_ev[i]));
         d->prof_ready = 1;
@@ -1544,7 +1558,7 @@ EC_EXPORT int ec_decode_profile(GPT2 *g, int *d_tokens, int start_pos, int n_ste
     for (int st = 0; st < n_steps; st++) {
         d->prof_on = 1;
         d->prof_n = 0;
-        int rc = ec_enqueue_step(d, 3, M, nsplit);
+        int rc = ec_enqueue_step(d, 3, M, maxlen);
         d->prof_on = 0;
         if (rc) return -1;
         CK(cudaStreamSynchronize(d->stream));

@@ -28,6 +28,20 @@
 
 #define ECO_API __attribute__((visibility("default")))
 
+/* Transcendentals.  The default build calls the host libm exactly as the
+ * reference does (its results are libm-specific: glibc's expf and tanhf are
+ * not correctly rounded).  Built with -DECO_CR_MATH (libecoracle_cr.so), the
+ * restatement uses correctly rounded fp32 results, obtained from the fp64
+ * functions, which is what the CUDA library computes; that build checks the
+ * GPU path bit-for-bit, the default build checks it against the reference. */
+#ifdef ECO_CR_MATH
+static float eco_expf(float x) { return (float)exp((double)x); }
+static float eco_tanhf(float x) { return (float)tanh((double)x); }
+#else
+#define eco_expf expf
+#define eco_tanhf tanhf
+#endif
+
 /* ------------------------------------------------------------------ */
 /* GEMM restatements                                                    */
 /* ------------------------------------------------------------------ */
@@ -160,12 +174,12 @@ static float eco_gelu(float x)
     float c = 0.044715f * x;
     c = c * x;
     c = c * x;
-    float t = tanhf(0.7978845608028654f * (x + c));
+    float t = eco_tanhf(0.7978845608028654f * (x + c));
     return (0.5f * x) * (1.0f + t);
 }
 
 /* reference src/gpt2.c:587-590 */
-static float eco_silu(float x) { return x / (1.0f + expf(-x)); }
+static float eco_silu(float x) { return x / (1.0f + eco_expf(-x)); }
 
 /* RoPE inverse frequencies incl. the YaRN ramp (reference src/gpt2.c:608-644). */
 ECO_API void eco_rope_inv_freq(double *inv, int half, double theta, int rope_type,
@@ -472,7 +486,7 @@ static void eco_attend(const float *q, const uint16_t *kb, const uint16_t *vb, i
         if (s > mx) mx = s;
     }
     double sum = 0.0;
-    for (int p = lo; p <= pos; p++) { sc[p] = expf(sc[p] - mx); sum += sc[p]; }
+    for (int p = lo; p <= pos; p++) { sc[p] = eco_expf(sc[p] - mx); sum += sc[p]; }
     double inv = 1.0 / sum;
     for (int p = lo; p <= pos; p++) sc[p] = (float)(sc[p] * inv);
     for (int d = 0; d < hd; d++) o[d] = 0.0f;

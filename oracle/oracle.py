@@ -48,10 +48,12 @@ class _Lib:
 
 
 class Restatement(_Lib):
-    """oracle/libecoracle.so."""
+    """oracle/libecoracle.so (host libm, as the reference), or with cr=True
+    oracle/libecoracle_cr.so (correctly rounded expf/tanhf, as the GPU)."""
 
-    def __init__(self):
-        super().__init__(HERE / "libecoracle.so")
+    def __init__(self, cr: bool = False):
+        super().__init__(HERE / ("libecoracle_cr.so" if cr else "libecoracle.so"))
+        self.cr = cr
         L = self.lib
         L.eco_open.restype = C.c_void_p
         L.eco_open.argtypes = [C.c_char_p, C.c_int, C.c_int]
