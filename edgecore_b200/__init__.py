@@ -45,6 +45,7 @@ def _declare(lib: C.CDLL) -> None:
         "ec_decode_greedy": (_i, [_vp, _vp, _i, _i, _vp]),
         "ec_decode_profile": (_i, [_vp, _vp, _i, _i, _vp]),
         "ec_decode_greedy_cycle": (_i, [_vp, _vp, _i, _i, _i, _vp]),
+        "ec_decode_trace": (_i, [_vp, _vp, _i, _i, _vp, _i]),
         "ec_model_set_taps": (_i, [_vp, _i]),
         "ec_model_get_taps": (_i, [_vp, _vp, _i]),
         "ec_model_set_vocab_shard": (_i, [_vp, _i, _i]),
@@ -269,6 +270,19 @@ class Model:
     def decode_greedy_cycle(self, d_tokens, start_pos: int, period: int, n_steps: int, d_out_ids=None) -> None:
         self._check(self.lib.ec_decode_greedy_cycle(self.h, _ptr(d_tokens), int(start_pos), int(period),
                                                     int(n_steps), _ptr(d_out_ids)))
+
+    TRACE_CODES = {1: "barrier", 2: "operand", 3: "tiles", 4: "attention", 5: "lm_head", 6: "argmax",
+                   7: "tile_in", 8: "tile_free", 9: "tile_done", 10: "issue"}
+
+    def decode_trace(self, d_tokens, start_pos: int, n_steps: int, cap: int = 1 << 16):
+        """Timeline of CTA 0 of the persistent decode kernel: list of (event, ns)
+        sorted by time (consumer and producer events interleaved)."""
+        buf = np.zeros(cap, np.uint64)
+        n = self.lib.ec_decode_trace(self.h, _ptr(d_tokens), int(start_pos), int(n_steps), _ptr(buf), cap)
+        if n < 0:
+            raise RuntimeError(last_error())
+        ev = [(self.TRACE_CODES.get(int(v) >> 56, "?"), int(v) & ((1 << 56) - 1)) for v in buf[:n]]
+        return sorted(ev, key=lambda e: e[1])
 
     def decode_profile(self, d_tokens, start_pos: int, n_steps: int) -> dict:
         """Per-kernel-class event timings of an instrumented decode."""

@@ -23,9 +23,9 @@ LIB = PKG / "libedgecore_b200.so"
 CUDA = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
-CU_SOURCES = ["ec_kernels.cu"]
-C_SOURCES = ["ec_model.c", "ec_abi.c"]
-HEADERS = [CSRC / "ec_launch.h", CSRC / "ec_common.cuh", ROOT / "include" / "edgecore.h",
+CU_SOURCES = ["ec_kernels.cu", "ec_decode.cu"]
+C_SOURCES = ["ec_host.c", "ec_abi.c"]
+HEADERS = [CSRC / "ec_launch.h", CSRC / "ec_common.cuh", CSRC / "ec_decode.h", ROOT / "include" / "edgecore.h",
            ROOT / "include" / "edgecore_b200.h"]
 
 

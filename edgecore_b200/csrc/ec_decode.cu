@@ -1,0 +1,1021 @@
+// ec_decode.cu -- persistent decode kernel: a whole forward step (embedding,
+// every layer, final norm, lm_head, greedy argmax) for M <= 8 token rows in
+// one cooperative launch, optionally looping over many decode steps.
+//
+// One CTA per SM, 9 warps:
+//   warp 0      producer: streams this CTA's share of every weight matrix, in
+//               execution order, through a ring of EC_MK_STAGES x 32 KB shared
+//               memory slots with bulk TMA copies (cp.async.bulk, this GPU's
+//               own memory only).  Weights do not depend on activations, so
+//               the producer runs ahead across phase and layer boundaries,
+//               bounded only by the ring.
+//   warps 1-8   consumers: the dependent chain of phases, separated by grid
+//               barriers (arrival counter in global memory):
+//     A  norm(x) -> int8 quantise -> q|k|v rows  -> RoPE, q, fp16 KV store
+//     B  exact-order attention, one (token, head) item per CTA
+//     C  quantise(attn) -> o rows -> residual add into x
+//     D  norm(x) -> quantise -> gate|up rows -> SwiGLU (GELU for GPT-2)
+//     E  quantise(act) -> down rows -> residual add into x
+//     F  final norm -> lm_head rows -> logits, per-CTA argmax
+//     G  every CTA merges the argmax partials -> next token
+//   Each CTA owns a contiguous slice of every matrix's rows; o and down share
+//   their partition, so a residual row of x is only ever written by its owner.
+//
+// Code size is kept small on purpose (the whole step runs from the
+// instruction cache): the token count is a template parameter (1, 2, 4 or 8
+// rows), and the tile loop, the norm and the operand builder exist once per
+// kernel as non-inlined functions shared by all phases.
+//
+// Numerics are those of the reference (src/gpt2.c, src/kernels.c): exact
+// int32 dots and the (bias + ((float)dot*as)*ws) epilogue, fp64 norm
+// statistics, fp64 RoPE, the exact-order attention of k_attn_exact, and
+// correctly rounded exp/tanh.  Every wait is bounded; a CTA that gives up
+// raises the shared abort flag so the others leave instead of spinning.
+#include "ec_common.cuh"
+#include "ec_launch.h"
+#include "ec_decode.h"
+
+#include <float.h>
+
+namespace {
+
+constexpr int MT = EC_MK_MT;
+constexpr int NCW = EC_MK_CONS_WARPS;
+constexpr int NCT = NCW * 32;
+constexpr int STAGES = EC_MK_STAGES;
+constexpr int TILE = EC_MK_TILE;
+constexpr int TROWS = EC_MK_MAX_TILE_ROWS;
+constexpr int ARCH_Q2 = 1;                        // ARCH_QWEN2
+constexpr long long SPIN_CYCLES = 4000000000LL;   // ~2 s: bound on any grid-barrier wait
+constexpr int ERR_TIMEOUT = 1, ERR_INDEX = 2;
+constexpr uint32_t T_ABORT = 0xffffffffu;         // tile counter value meaning "aborted"
+
+// Phase kinds of the shared tile loop.
+enum { PK_QKV = 0, PK_RESID = 1, PK_UP = 2, PK_LM = 3 };
+
+// Loop over the token rows m < p.M with compile-time indices (bounded by the
+// kernel's MM), so per-token arrays stay in registers.
+// Every user declares `const int nM = p.M;` (a register, not a reload).
+#define FOR_TOK(m) _Pragma("unroll") for (int m = 0; m < MM; ++m) if (m < nM)
+
+struct Lay {
+    uint32_t ring, xbuf, stage, nrm, part, redd, redf, redi, asc, ints, bars, lays, par, total;
+};
+
+__host__ __device__ inline uint32_t al16(uint32_t v) { return (v + 15u) & ~15u; }
+
+__host__ __device__ inline Lay mk_layout(int xbuf_bytes, int stage_bytes, int n_layer, int E) {
+    Lay L;
+    uint32_t o = 0;
+    L.ring = o;  o += STAGES * TILE;
+    L.xbuf = o;  o += al16((uint32_t)xbuf_bytes);
+    L.stage = o; o += al16((uint32_t)stage_bytes);
+    L.nrm = o;   o += 2u * al16((uint32_t)E * 4u);
+    L.part = o;  o += TROWS * NCW * MT * 4;
+    L.redd = o;  o += NCW * MT * 8;
+    L.redf = o;  o += NCW * MT * 4;
+    L.redi = o;  o += NCW * MT * 4;
+    L.asc = o;   o += MT * 4;
+    L.ints = o;  o += al16((3 * MT + 4) * 4);
+    L.bars = o;  o += 2 * STAGES * 8;
+    L.lays = o;  o += al16((uint32_t)n_layer * (uint32_t)sizeof(ec_mk_layer));
+    L.par = o;   o += al16((uint32_t)sizeof(ec_mk_params));
+    L.total = o;
+    return L;
+}
+
+extern __shared__ __align__(128) unsigned char g_smem[];
+
+struct Sm {
+    unsigned char *ring, *xbuf;
+    float *stage;
+    float *nrm;               // norm gain [E] and bias [E] of the running norm
+    float *part;
+    double *redd;
+    float *redf;
+    int *redi;
+    float *asc;
+    int *ltok, *lpos, *lslot;
+    volatile int *flag;       // [0]: abort
+    int *tcount;              // [2]: trace entries written (consumer, producer)
+    uint64_t *full, *empty;
+    const ec_mk_layer *lay;   // shared-memory copy of the layer descriptors
+    ec_mk_params *par;        // shared-memory copy of the kernel parameters
+};
+
+__device__ __forceinline__ Sm sm_of(const ec_mk_params &p) {
+    const Lay L = mk_layout(p.xbuf_bytes, p.stage_bytes, p.L, p.E);
+    Sm S;
+    S.ring = g_smem + L.ring;
+    S.xbuf = g_smem + L.xbuf;
+    S.stage = reinterpret_cast<float *>(g_smem + L.stage);
+    S.nrm = reinterpret_cast<float *>(g_smem + L.nrm);
+    S.part = reinterpret_cast<float *>(g_smem + L.part);
+    S.redd = reinterpret_cast<double *>(g_smem + L.redd);
+    S.redf = reinterpret_cast<float *>(g_smem + L.redf);
+    S.redi = reinterpret_cast<int *>(g_smem + L.redi);
+    S.asc = reinterpret_cast<float *>(g_smem + L.asc);
+    int *ints = reinterpret_cast<int *>(g_smem + L.ints);
+    S.ltok = ints;
+    S.lpos = ints + MT;
+    S.lslot = ints + 2 * MT;
+    S.flag = ints + 3 * MT;
+    S.tcount = ints + 3 * MT + 1;
+    S.full = reinterpret_cast<uint64_t *>(g_smem + L.bars);
+    S.empty = S.full + STAGES;
+    S.lay = reinterpret_cast<const ec_mk_layer *>(g_smem + L.lays);
+    S.par = reinterpret_cast<ec_mk_params *>(g_smem + L.par);
+    return S;
+}
+
+struct Rg { int r0, r1; };
+
+__device__ __forceinline__ Rg mk_range(const ec_mk_mat &m, int c, int G) {
+    const int U = m.N / m.unit;
+    const int u0 = (int)(((long long)c * U) / G), u1 = (int)(((long long)(c + 1) * U) / G);
+    return Rg{u0 * m.unit, u1 * m.unit};
+}
+
+__device__ __forceinline__ void cons_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// Consumer barrier that also ORs a predicate over the 256 consumer threads,
+// so that every warp takes the same abort decision.
+__device__ __forceinline__ bool cons_sync_or(bool v) {
+    int r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.s32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, 1, 256, p;\n\t"
+        "selp.s32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((int)v)
+        : "memory");
+    return r != 0;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(ec_smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ int elt_of(int wt) { return wt == EC_W_I8 ? 1 : 2; }
+
+// 16-byte asynchronous global -> shared copy through L2 (data written by
+// other SMs before the last grid barrier).
+__device__ __forceinline__ void cpa16(void *dst_smem, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(ec_smem_u32(dst_smem)), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cpa_wait_all() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// Issue the copy of n floats global -> shared with every 16-byte piece in
+// flight at once (scalar loads for a ragged tail or an unaligned source).
+// Completion: cpa_wait_all() by every issuing thread, then a consumer barrier.
+__device__ __forceinline__ void stage_issue(float *dst, const float *src, int n, int ct) {
+    int done = 0;
+    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+        const int n4 = n >> 2;
+        for (int i = ct; i < n4; i += NCT) cpa16(dst + 4 * i, src + 4 * i);
+        done = 4 * n4;
+    }
+    for (int i = done + ct; i < n; i += NCT) dst[i] = __ldcg(src + i);
+}
+
+// Timeline of CTA 0 when p.trace is set: consumer thread 0 writes the first
+// half of the buffer, the producer thread the second half, entries
+// (code << 56) | globaltimer ns.  Each half has its own count in shared memory.
+__device__ __forceinline__ void tmark(const ec_mk_params &p, const Sm &S, int who, int code) {
+    if (p.trace && blockIdx.x == 0) {
+        const int half = p.trace_cap / 2, cap = who ? p.trace_cap - half : half;
+        int &n = S.tcount[who];
+        if (n < cap) {
+            unsigned long long t;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+            p.trace[(size_t)who * half + n++] = ((unsigned long long)code << 56) | (t & 0x00ffffffffffffffull);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// producer
+// ---------------------------------------------------------------------------
+
+__device__ __noinline__ uint32_t mk_produce(const ec_mk_params &p, const ec_mk_mat &m, int wt, Rg rg, uint32_t t) {
+    const Sm S = sm_of(p);
+    const uint32_t row_bytes = (uint32_t)m.ldw * (uint32_t)elt_of(wt);
+    for (int r = rg.r0; r < rg.r1; r += m.tile_rows) {
+        const int nr = min(m.tile_rows, rg.r1 - r);
+        const int s = (int)(t % STAGES);
+        const uint32_t k = t / STAGES;
+        if (k > 0) {
+            bool ok = false;
+            for (uint32_t i = 0; i < EC_WAIT_LIMIT; ++i) {
+                if (ec_mbar_try_wait(&S.empty[s], (k - 1) & 1)) { ok = true; break; }
+                if (S.flag[0]) return T_ABORT;
+            }
+            if (!ok) { S.flag[0] = 1; atomicCAS(p.err, 0, ERR_TIMEOUT); return T_ABORT; }
+        }
+        const uint32_t bytes = (uint32_t)nr * row_bytes;
+        ec_mbar_expect_tx(&S.full[s], bytes);
+        ec_bulk_g2s(S.ring + (size_t)s * TILE, static_cast<const unsigned char *>(m.w) + (size_t)r * row_bytes,
+                    bytes, &S.full[s]);
+        tmark(p, S, 1, EC_TR_ISSUE);
+        ++t;
+    }
+    return t;
+}
+
+// ---------------------------------------------------------------------------
+// consumers: reductions over the 256 consumer threads (fixed order: lanes by
+// xor tree, warps in index order; every thread gets the totals)
+// ---------------------------------------------------------------------------
+
+template <int MM>
+__device__ __forceinline__ void red_sum_d(const ec_mk_params &p, const Sm &S, double v[MM], int ct) {
+    const int nM = p.M;
+    const int lane = ct & 31, w = ct >> 5;
+    FOR_TOK(m) v[m] = ec_warp_sum_d(v[m]);
+    cons_sync();
+    if (lane == 0) FOR_TOK(m) S.redd[w * MT + m] = v[m];
+    cons_sync();
+    FOR_TOK(m) {
+        double t = 0.0;
+        for (int i = 0; i < NCW; ++i) t = __dadd_rn(t, S.redd[i * MT + m]);
+        v[m] = t;
+    }
+}
+
+template <int MM>
+__device__ __forceinline__ void red_max_f(const ec_mk_params &p, const Sm &S, float v[MM], int ct) {
+    const int nM = p.M;
+    const int lane = ct & 31, w = ct >> 5;
+    FOR_TOK(m) v[m] = ec_warp_max(v[m]);
+    cons_sync();
+    if (lane == 0) FOR_TOK(m) S.redf[w * MT + m] = v[m];
+    cons_sync();
+    FOR_TOK(m) {
+        float t = S.redf[m];
+        for (int i = 1; i < NCW; ++i) t = ec_max_keep(t, S.redf[i * MT + m]);
+        v[m] = t;
+    }
+}
+
+__device__ __forceinline__ void am_merge(float &bv, int &bi, float v, int i) {
+    if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+}
+
+template <int MM>
+__device__ __forceinline__ void red_argmax(const ec_mk_params &p, const Sm &S, float bv[MM], int bi[MM], int ct) {
+    const int nM = p.M;
+    const int lane = ct & 31, w = ct >> 5;
+    FOR_TOK(m) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv[m], o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi[m], o);
+            am_merge(bv[m], bi[m], ov, oi);
+        }
+    }
+    cons_sync();
+    if (lane == 0) FOR_TOK(m) { S.redf[w * MT + m] = bv[m]; S.redi[w * MT + m] = bi[m]; }
+    cons_sync();
+    FOR_TOK(m) {
+        float v = S.redf[m];
+        int i = S.redi[m];
+        for (int k = 1; k < NCW; ++k) am_merge(v, i, S.redf[k * MT + m], S.redi[k * MT + m]);
+        bv[m] = v;
+        bi[m] = i;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// consumers: prologues
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float mk_embed(const ec_mk_params &p, int tok, int pos, int k) {
+    const bool bf = p.emb_bf16 != 0;
+    float e = ec_h2f(p.wte[(size_t)tok * p.ld_emb + k], bf);
+    if (p.wpe) e = __fadd_rn(e, ec_h2f(p.wpe[(size_t)pos * p.ld_emb + k], bf));
+    return e;
+}
+
+// Norm of the residual rows (or of the embedding, for layer 0) into S.stage
+// [M][E] fp32: LayerNorm when beta != NULL, else RMSNorm (reference
+// src/gpt2.c:398-414, :592-604), fp64 statistics.  The rows and the gains
+// come in with one round of asynchronous copies.
+template <int MM>
+__device__ __noinline__ void mk_norm(const ec_mk_params &p, bool from_embed, const float *g, const float *b, int ct) {
+    const Sm S = sm_of(p);
+    const int nM = p.M;
+    const int E = p.E;
+    float *st = S.stage;
+    float *gs = S.nrm, *bs = S.nrm + ((E + 3) & ~3);
+    stage_issue(gs, g, E, ct);
+    if (b) stage_issue(bs, b, E, ct);
+    if (!from_embed) stage_issue(st, p.x, nM * E, ct);
+    else FOR_TOK(m) for (int k = ct; k < E; k += NCT) st[m * E + k] = mk_embed(p, S.ltok[m], S.lpos[m], k);
+    cpa_wait_all();
+    cons_sync();
+    double s1[MM];
+    FOR_TOK(m) {
+        s1[m] = 0.0;
+        for (int k = ct; k < E; k += NCT) {
+            const double d = (double)st[m * E + k];
+            s1[m] = b ? __dadd_rn(s1[m], d) : __dadd_rn(s1[m], __dmul_rn(d, d));
+        }
+    }
+    red_sum_d<MM>(p, S, s1, ct);
+    double mean[MM], rstd[MM];
+    if (b) {
+        double s2[MM];
+        FOR_TOK(m) {
+            s2[m] = 0.0;
+            mean[m] = __ddiv_rn(s1[m], (double)E);
+            for (int k = ct; k < E; k += NCT) {
+                const double d = __dsub_rn((double)st[m * E + k], mean[m]);
+                s2[m] = __dadd_rn(s2[m], __dmul_rn(d, d));
+            }
+        }
+        red_sum_d<MM>(p, S, s2, ct);
+        FOR_TOK(m) rstd[m] = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(s2[m], (double)E), p.eps)));
+    } else {
+        FOR_TOK(m) {
+            mean[m] = 0.0;
+            rstd[m] = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(s1[m], (double)E), p.eps)));
+        }
+    }
+    FOR_TOK(m) {
+        for (int k = ct; k < E; k += NCT) {
+            const double d = b ? __dsub_rn((double)st[m * E + k], mean[m]) : (double)st[m * E + k];
+            const float t = (float)__dmul_rn(d, rstd[m]);
+            st[m * E + k] = b ? __fadd_rn(__fmul_rn(t, gs[k]), bs[k]) : __fmul_rn(t, gs[k]);
+        }
+    }
+    cons_sync();
+}
+
+// Build the GEMV operand for K-wide rows: int8 quantised rows (reference
+// src/gpt2.c:446-461) with scales in S.asc, or fp32 planes for 16-bit weights.
+// Source: S.stage (src == NULL) or global rows `src` with row stride K.
+template <int MM>
+__device__ __noinline__ void mk_operand(const ec_mk_params &p, const float *src, int K, int Kp, int wt, int ct) {
+    const Sm S = sm_of(p);
+    const int nM = p.M;
+    const bool fits = (size_t)p.M * K * 4 <= (size_t)p.stage_bytes;
+    float *st = S.stage;
+    if (src && fits) {   // one round of asynchronous copies into the staging area
+        stage_issue(st, src, nM * K, ct);
+        cpa_wait_all();
+        cons_sync();
+    }
+    const bool from_stage = !src || fits;
+    if (wt == EC_W_I8) {
+        float mx[MM];
+        FOR_TOK(m) {
+            mx[m] = 0.0f;
+            for (int k = ct; k < K; k += NCT)
+                mx[m] = ec_max_keep(mx[m], fabsf(from_stage ? st[m * K + k] : __ldcg(src + (size_t)m * K + k)));
+        }
+        red_max_f<MM>(p, S, mx, ct);
+        int8_t *xq = reinterpret_cast<int8_t *>(S.xbuf);
+        FOR_TOK(m) {
+            const float s = mx[m] > 0.0f ? __fdiv_rn(mx[m], 127.0f) : 1.0f;
+            if (ct == 0) S.asc[m] = s;
+            for (int k = ct; k < Kp; k += NCT) {
+                const float v = k < K ? (from_stage ? st[m * K + k] : __ldcg(src + (size_t)m * K + k)) : 0.0f;
+                xq[(size_t)m * Kp + k] = (int8_t)(k < K ? ec_quant1(v, s) : 0);
+            }
+        }
+    } else {
+        float *xs = reinterpret_cast<float *>(S.xbuf);
+        FOR_TOK(m) {
+            float *xm = xs + (size_t)m * Kp;
+            for (int k = ct; k < Kp; k += NCT) {
+                const float v = k < K ? (from_stage ? st[m * K + k] : __ldcg(src + (size_t)m * K + k)) : 0.0f;
+                const int c = k >> 3, e = k & 7;
+                xm[(e >> 2) * (Kp >> 1) + c * 4 + (e & 3)] = v;
+            }
+        }
+    }
+    cons_sync();
+}
+
+// ---------------------------------------------------------------------------
+// consumers: one phase's weight tiles -> dots -> epilogue (shared by all
+// phases; one copy per weight type and token bound)
+// ---------------------------------------------------------------------------
+
+template <int WT> struct AccT { typedef float T; };
+template <> struct AccT<EC_W_I8> { typedef int T; };
+
+constexpr int RB = 4;   // weight rows a consumer warp reduces together
+
+// acc[i][q] for a lane-dependent (i, q): an unrolled select, so the register
+// array is never indexed dynamically.
+template <int MM, typename Acc>
+__device__ __forceinline__ Acc pick(const Acc (&acc)[RB][MM], int i, int q) {
+    Acc v = 0;
+#pragma unroll
+    for (int a = 0; a < RB; ++a)
+#pragma unroll
+        for (int b = 0; b < MM; ++b)
+            if (a == i && b == q) v = acc[a][b];
+    return v;
+}
+
+// Final value of one output row r (its staged bytes at `row`, metadata tail
+// after Kp weights) for token q: reference gemm_int8 epilogue
+// bias + ((float)dot * a_scale) * w_scale (src/kernels.c), or dot + bias.
+template <int WT>
+__device__ __forceinline__ float mk_fin(int Kp, int meta, const Sm &S, const unsigned char *row,
+                                        typename AccT<WT>::T d, int q) {
+    const float *tail = reinterpret_cast<const float *>(row + (size_t)Kp * (WT == EC_W_I8 ? 1 : 2));
+    if (WT == EC_W_I8) {
+        const float t = __fmul_rn(__fmul_rn(__int2float_rn((int)d), S.asc[q]), (meta & 1) ? tail[0] : 1.0f);
+        return (meta & 2) ? __fadd_rn(tail[1], t) : t;
+    } else {
+        return (meta & 2) ? __fadd_rn((float)d, tail[1]) : (float)d;
+    }
+}
+
+// One phase's weight tiles.  Every consumer warp takes whole units (1 row,
+// or 2 for pair-packed rows) of each staged tile, RB rows at a time, with the
+// lanes splitting K; the unit -> warp assignment rotates from tile to tile.
+// A warp reduces its dots in registers and applies the epilogue itself (lane
+// e handles unit e / MM, token e % MM), then releases the ring slot: there is
+// no CTA-wide barrier per tile.  After an abort the remaining tiles are
+// skipped and the next grid barrier returns for every warp.
+template <int WT, int MM>
+__device__ __noinline__ uint32_t mk_phase(const ec_mk_params &p, int kind, int layer, uint32_t t, int ct) {
+    typedef typename AccT<WT>::T Acc;
+    constexpr int ELT = WT == EC_W_I8 ? 1 : 2;
+    const Sm S = sm_of(p);
+    const int nM = p.M;
+    const int G = gridDim.x, cta = blockIdx.x;
+    // layer: index of the layer (bit 16 set: the down projection of a
+    // PK_RESID phase, else its o projection); -1 for the lm_head
+    const ec_mk_layer &ly = S.lay[layer < 0 ? 0 : (layer & 0xffff)];
+    const ec_mk_mat &m = kind == PK_QKV ? ly.qkv : kind == PK_UP ? ly.up : kind == PK_LM ? p.lm
+                       : (layer & 0x10000) ? ly.down : ly.o;
+    const Rg rg = mk_range(m, cta, G);
+    const int lane = ct & 31, cw = ct >> 5;
+    const uint32_t row_bytes = (uint32_t)m.ldw * ELT;
+    const int Kp = m.Kp, meta = m.meta, tile_rows = m.tile_rows, mN = m.N;
+    const int nch = Kp * ELT / 16;
+    const int unit = m.unit, gmax = RB / unit;
+    const int half = p.hd >> 1;
+    const int eg = lane / MM, eq = lane % MM;    // this lane's epilogue (unit, token)
+    float bv = -INFINITY;                         // running argmax of token eq
+    int bi = 0x7fffffff;
+
+    for (int row0 = rg.r0; row0 < rg.r1; row0 += tile_rows) {
+        const int nr = min(tile_rows, rg.r1 - row0);
+        const int U = nr / unit;
+        const int s = (int)(t % STAGES);
+        const uint32_t k = t / STAGES;
+        ++t;
+        if (S.flag[0]) continue;
+        bool ok = false;
+        for (uint32_t i = 0; i < EC_WAIT_LIMIT; ++i) {
+            if (ec_mbar_try_wait(&S.full[s], k & 1)) { ok = true; break; }
+            if (S.flag[0]) break;
+        }
+        if (!ok) {
+            S.flag[0] = 1;
+            atomicCAS(p.err, 0, ERR_TIMEOUT);
+            continue;
+        }
+        if (ct == 0) tmark(p, S, 0, EC_TR_TILE_IN);
+        const unsigned char *stg = S.ring + (size_t)s * TILE;
+        const int rot = ((row0 - rg.r0) / unit) % NCW;
+        for (int u0 = (cw - rot + NCW) % NCW; u0 < U; u0 += NCW * gmax) {
+            int rr[RB];   // staged row of slot i, or -1 (warp-uniform)
+#pragma unroll
+            for (int i = 0; i < RB; ++i) {
+                const int ug = u0 + (unit == 2 ? (i >> 1) : i) * NCW;
+                rr[i] = ug < U ? ug * unit + (unit == 2 ? (i & 1) : 0) : -1;
+            }
+            Acc acc[RB][MM];
+#pragma unroll
+            for (int i = 0; i < RB; ++i)
+#pragma unroll
+                for (int q = 0; q < MM; ++q) acc[i][q] = 0;
+            for (int c = lane; c < nch; c += 32) {
+                if (WT == EC_W_I8) {
+                    uint4 w[RB];
+#pragma unroll
+                    for (int i = 0; i < RB; ++i)
+                        if (rr[i] >= 0) w[i] = *reinterpret_cast<const uint4 *>(stg + (size_t)rr[i] * row_bytes + (size_t)c * 16);
+                    const int8_t *xq = reinterpret_cast<const int8_t *>(S.xbuf);
+                    FOR_TOK(q) {
+                        const uint4 x = reinterpret_cast<const uint4 *>(xq + (size_t)q * Kp)[c];
+#pragma unroll
+                        for (int i = 0; i < RB; ++i) {
+                            if (rr[i] < 0) continue;
+                            int a = (int)acc[i][q];
+                            a = __dp4a((int)w[i].x, (int)x.x, a);
+                            a = __dp4a((int)w[i].y, (int)x.y, a);
+                            a = __dp4a((int)w[i].z, (int)x.z, a);
+                            a = __dp4a((int)w[i].w, (int)x.w, a);
+                            acc[i][q] = a;
+                        }
+                    }
+                } else {
+                    float f[RB][8];
+#pragma unroll
+                    for (int i = 0; i < RB; ++i) {
+                        if (rr[i] < 0) continue;
+                        const uint4 w = *reinterpret_cast<const uint4 *>(stg + (size_t)rr[i] * row_bytes + (size_t)c * 16);
+                        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            if (WT == EC_W_F16) {
+                                const float2 t2 = __half22float2(*reinterpret_cast<const __half2 *>(&u[j]));
+                                f[i][2 * j] = t2.x;
+                                f[i][2 * j + 1] = t2.y;
+                            } else {
+                                f[i][2 * j] = __uint_as_float(u[j] << 16);
+                                f[i][2 * j + 1] = __uint_as_float(u[j] & 0xffff0000u);
+                            }
+                        }
+                    }
+                    const float *xs = reinterpret_cast<const float *>(S.xbuf);
+                    FOR_TOK(q) {
+                        const float *xm = xs + (size_t)q * Kp;
+                        const float4 x0 = reinterpret_cast<const float4 *>(xm)[c];
+                        const float4 x1 = reinterpret_cast<const float4 *>(xm + (Kp >> 1))[c];
+#pragma unroll
+                        for (int i = 0; i < RB; ++i) {
+                            if (rr[i] < 0) continue;
+                            float a = (float)acc[i][q];
+                            a = fmaf(f[i][0], x0.x, a); a = fmaf(f[i][1], x0.y, a);
+                            a = fmaf(f[i][2], x0.z, a); a = fmaf(f[i][3], x0.w, a);
+                            a = fmaf(f[i][4], x1.x, a); a = fmaf(f[i][5], x1.y, a);
+                            a = fmaf(f[i][6], x1.z, a); a = fmaf(f[i][7], x1.w, a);
+                            acc[i][q] = a;
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < RB; ++i) {
+                if (rr[i] < 0) continue;
+                FOR_TOK(q) {
+                    if (WT == EC_W_I8) acc[i][q] = ec_warp_sum_i((int)acc[i][q]);
+                    else acc[i][q] = ec_warp_sum((float)acc[i][q]);
+                }
+            }
+
+            // ---- epilogue: lane (eg, eq) ----
+            if (eg >= gmax || eq >= nM) continue;
+            const int i0 = eg * unit;
+            const int r0 = i0 == 0 ? rr[0] : i0 == 1 ? rr[1] : i0 == 2 ? rr[2] : rr[3];
+            if (r0 < 0) continue;
+            const int q = eq;
+            const unsigned char *row = stg + (size_t)r0 * row_bytes;
+            const float v0 = mk_fin<WT>(Kp, meta, S, row, pick<MM>(acc, i0, q), q);
+            const float v1 = unit == 2 ? mk_fin<WT>(Kp, meta, S, row + row_bytes, pick<MM>(acc, i0 + 1, q), q) : 0.0f;
+            const int n = row0 + r0;   // matrix row of slot i0
+            if (kind == PK_QKV) {
+                const int pos = S.lpos[q], slot = S.lslot[q];
+                const size_t kvo = ((size_t)slot * p.C + pos) * p.kv;
+                if (p.arch == ARCH_Q2) {
+                    if (n < p.E + p.kv) {   // rotated pair (i, i + hd/2) of a q or k head
+                        const int head = n / p.hd, i2 = (n % p.hd) >> 1;
+                        const double c = p.rope_cos[(size_t)pos * half + i2], sn = p.rope_sin[(size_t)pos * half + i2];
+                        const float lo = (float)__dsub_rn(__dmul_rn((double)v0, c), __dmul_rn((double)v1, sn));
+                        const float hi = (float)__dadd_rn(__dmul_rn((double)v0, sn), __dmul_rn((double)v1, c));
+                        if (head < p.H) {
+                            float *qr = p.q + (size_t)q * p.E + (size_t)head * p.hd;
+                            qr[i2] = lo;
+                            qr[i2 + half] = hi;
+                        } else {
+                            uint16_t *kr = ly.kc + kvo + (size_t)(head - p.H) * p.hd;
+                            kr[i2] = ec_f2h(lo);
+                            kr[i2 + half] = ec_f2h(hi);
+                        }
+                    } else {
+                        const int col = n - p.E - p.kv;
+                        ly.vc[kvo + col] = ec_f2h(v0);
+                        ly.vc[kvo + col + 1] = ec_f2h(v1);
+                    }
+                } else {
+                    if (n < p.E) p.q[(size_t)q * p.E + n] = v0;
+                    else if (n < 2 * p.E) ly.kc[kvo + (n - p.E)] = ec_f2h(v0);
+                    else ly.vc[kvo + (n - 2 * p.E)] = ec_f2h(v0);
+                }
+            } else if (kind == PK_RESID) {
+                float *xp = p.x + (size_t)q * p.E + n;
+                *xp = __fadd_rn(__ldcg(xp), v0);
+            } else if (kind == PK_UP) {
+                if (p.arch == ARCH_Q2) p.act[(size_t)q * p.I + (n >> 1)] = __fmul_rn(ec_silu(v0), v1);
+                else p.act[(size_t)q * (4 * p.E) + n] = ec_gelu(v0);
+            } else {   // PK_LM
+                if (p.logits) p.logits[(size_t)q * mN + n] = v0;
+                am_merge(bv, bi, v0, p.v0 + n);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.empty[s]);   // this warp no longer reads the slot
+        if (ct == 0) tmark(p, S, 0, EC_TR_TILE_DONE);
+    }
+    if (kind == PK_LM) {
+        // lanes holding the same token: xor offsets >= MM; then warps in order
+#pragma unroll
+        for (int o = 16; o >= MM; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            am_merge(bv, bi, ov, oi);
+        }
+        cons_sync();
+        if (lane < MM) { S.redf[cw * MT + lane] = bv; S.redi[cw * MT + lane] = bi; }
+        cons_sync();
+        if (ct < p.M) {
+            float v = S.redf[ct];
+            int i = S.redi[ct];
+            for (int w = 1; w < NCW; ++w) am_merge(v, i, S.redf[w * MT + ct], S.redi[w * MT + ct]);
+            p.amax_v[(size_t)cta * MT + ct] = v;
+            p.amax_i[(size_t)cta * MT + ct] = i;
+        }
+    }
+    return t;
+}
+
+// ---------------------------------------------------------------------------
+// consumers: attention items (token m, head h), exact reference order
+// ---------------------------------------------------------------------------
+
+template <int MM>
+__device__ __noinline__ void mk_attention(const ec_mk_params &p, int layer, int ct) {
+    const Sm S = sm_of(p);
+    const int nM = p.M;
+    const ec_mk_layer &ly = S.lay[layer];
+    const int G = gridDim.x, cta = blockIdx.x;
+    const int hd = p.hd, kv = p.kv, H = p.H, E = p.E, CH = p.kvchunk;
+    const int ks = hd + 8;      // padded K row stride (halves): per-position reads avoid bank conflicts
+    const int per = hd >> 3;    // 16-byte pieces per cached row
+    float *qs = reinterpret_cast<float *>(S.xbuf);
+    float *sc = qs + ((hd + 3) & ~3);
+    uint16_t *kch = reinterpret_cast<uint16_t *>(sc + ((p.maxlen + 3) & ~3));
+    uint16_t *vch = kch + (size_t)CH * ks;
+    const uint16_t *kc = ly.kc, *vc = ly.vc;
+    const double inv_hd = 1.0 / sqrt((double)hd);
+    for (int it = cta; it < nM * H; it += G) {
+        const int m = it / H, h = it % H;
+        const int kvh = h * p.KVH / H;
+        const int pos = S.lpos[m], slot = S.lslot[m];
+        int lo = 0;
+        if (p.window > 0) { lo = pos - p.window + 1; if (lo < 0) lo = 0; }
+        const int len = pos + 1 - lo;
+        if (len > p.maxlen) {
+            if (ct == 0) atomicCAS(p.err, 0, ERR_INDEX);
+            continue;
+        }
+        const uint16_t *kb = kc + ((size_t)slot * p.C + lo) * kv + (size_t)kvh * hd;
+        const uint16_t *vb = vc + ((size_t)slot * p.C + lo) * kv + (size_t)kvh * hd;
+        // the q row and the first K and V chunks in flight together
+        for (int d = ct; d < (hd >> 2); d += NCT) cpa16(qs + 4 * d, p.q + (size_t)m * E + (size_t)h * hd + 4 * d);
+        {
+            const int n0 = min(CH, len);
+            for (int e = ct; e < n0 * per; e += NCT) {
+                const int i = e / per, j = e - (e / per) * per;
+                cpa16(kch + (size_t)i * ks + 8 * j, kb + (size_t)i * kv + 8 * j);
+                cpa16(vch + (size_t)i * hd + 8 * j, vb + (size_t)i * kv + 8 * j);
+            }
+        }
+        cpa_wait_all();
+        cons_sync();
+        // scores: sequential fp32 dot per position, scaled in double
+        float mx = -FLT_MAX;
+        for (int c0 = 0; c0 < len; c0 += CH) {
+            const int n = min(CH, len - c0);
+            if (c0 > 0) {
+                cons_sync();   // previous K chunk consumed
+                for (int e = ct; e < n * per; e += NCT) {
+                    const int i = e / per, j = e - (e / per) * per;
+                    cpa16(kch + (size_t)i * ks + 8 * j, kb + (size_t)(c0 + i) * kv + 8 * j);
+                }
+                cpa_wait_all();
+                cons_sync();
+            }
+            for (int i = ct; i < n; i += NCT) {
+                const uint16_t *kp = kch + (size_t)i * ks;
+                float a = 0.0f;
+                for (int d = 0; d < hd; d += 8) {
+                    const uint4 w = *reinterpret_cast<const uint4 *>(kp + d);
+                    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&u[j]));
+                        a = __fadd_rn(a, __fmul_rn(qs[d + 2 * j], f.x));
+                        a = __fadd_rn(a, __fmul_rn(qs[d + 2 * j + 1], f.y));
+                    }
+                }
+                const float sv = (float)__dmul_rn((double)a, inv_hd);
+                sc[c0 + i] = sv;
+                mx = ec_max_keep(mx, sv);
+            }
+        }
+        {
+            const int lane = ct & 31, w = ct >> 5;
+            mx = ec_warp_max(mx);
+            cons_sync();
+            if (lane == 0) S.redf[w * MT] = mx;
+            cons_sync();
+            float t = S.redf[0];
+            for (int i = 1; i < NCW; ++i) t = ec_max_keep(t, S.redf[i * MT]);
+            mx = t;
+        }
+        double sum = 0.0;
+        for (int i = ct; i < len; i += NCT) {
+            const float e = ec_expf(__fsub_rn(sc[i], mx));
+            sc[i] = e;
+            sum = __dadd_rn(sum, (double)e);
+        }
+        {
+            const int lane = ct & 31, w = ct >> 5;
+            sum = ec_warp_sum_d(sum);
+            cons_sync();
+            if (lane == 0) S.redd[w * MT] = sum;
+            cons_sync();
+            double t = 0.0;
+            for (int i = 0; i < NCW; ++i) t = __dadd_rn(t, S.redd[i * MT]);
+            sum = t;
+        }
+        const double isum = __ddiv_rn(1.0, sum);
+        for (int i = ct; i < len; i += NCT) sc[i] = (float)__dmul_rn((double)sc[i], isum);
+        cons_sync();
+        // P.V: sequential over positions for each output dimension
+        float o = 0.0f;
+        for (int c0 = 0; c0 < len; c0 += CH) {
+            const int n = min(CH, len - c0);
+            if (c0 > 0) {
+                cons_sync();   // previous V chunk consumed
+                for (int e = ct; e < n * per; e += NCT) {
+                    const int i = e / per, j = e - (e / per) * per;
+                    cpa16(vch + (size_t)i * hd + 8 * j, vb + (size_t)(c0 + i) * kv + 8 * j);
+                }
+                cpa_wait_all();
+                cons_sync();
+            }
+            if (ct < hd)
+                for (int i = 0; i < n; ++i)
+                    o = __fadd_rn(o, __fmul_rn(sc[c0 + i], __half2float(__ushort_as_half(vch[(size_t)i * hd + ct]))));
+        }
+        if (ct < hd) p.att[(size_t)m * E + (size_t)h * hd + ct] = o;
+        cons_sync();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// grid barrier among the consumers of all CTAs
+// ---------------------------------------------------------------------------
+
+__device__ __noinline__ bool mk_grid_sync(const ec_mk_params &p, unsigned target, int ct) {
+    const Sm S = sm_of(p);
+    if (cons_sync_or(S.flag[0] != 0)) {
+        if (ct == 0) atomicExch(p.abort_flag, 1);
+        return false;
+    }
+    if (ct == 0) {
+        __threadfence();
+        atomicAdd(p.bar, 1u);
+        const long long t0 = clock64();
+        for (;;) {
+            if (ld_acquire(p.bar) >= target) break;
+            if (*reinterpret_cast<volatile int *>(p.abort_flag)) { S.flag[0] = 1; break; }
+            if (clock64() - t0 > SPIN_CYCLES) {
+                S.flag[0] = 1;
+                atomicCAS(p.err, 0, ERR_TIMEOUT);
+                break;
+            }
+        }
+        __threadfence();
+    }
+    const bool stop = cons_sync_or(S.flag[0] != 0);
+    if (stop && ct == 0) atomicExch(p.abort_flag, 1);
+    return !stop;
+}
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+
+template <int LWT, int HWT, int MM>
+__global__ void __launch_bounds__(EC_MK_THREADS, 1) k_decode(const __grid_constant__ ec_mk_params pg, int n_steps) {
+    const Lay L = mk_layout(pg.xbuf_bytes, pg.stage_bytes, pg.L, pg.E);
+    const Sm S = sm_of(pg);
+    const int G = gridDim.x, cta = blockIdx.x;
+    const int M = pg.M;
+    {   // parameters -> shared memory: the helpers below read them through a
+        // reference, which for kernel-parameter space would be a slow generic load
+        uint32_t *dst = reinterpret_cast<uint32_t *>(S.par);
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(&pg);
+        for (int i = threadIdx.x; i < (int)(sizeof(ec_mk_params) / 4); i += blockDim.x) dst[i] = src[i];
+    }
+    const ec_mk_params &p = *S.par;
+    const int nM = M;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            ec_mbar_init(&S.full[s], 1);
+            ec_mbar_init(&S.empty[s], NCW);
+        }
+        ec_fence_mbar_init();
+        S.flag[0] = 0;
+        S.tcount[0] = S.tcount[1] = 0;
+    }
+    if (threadIdx.x < M) {
+        S.ltok[threadIdx.x] = pg.tok[threadIdx.x];
+        S.lpos[threadIdx.x] = pg.pos[threadIdx.x];
+        S.lslot[threadIdx.x] = pg.slot[threadIdx.x];
+    }
+    {   // layer descriptors -> shared memory (read on every phase and tile)
+        uint32_t *dst = reinterpret_cast<uint32_t *>(g_smem + L.lays);
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(pg.layers);
+        const int words = (int)((size_t)pg.L * sizeof(ec_mk_layer) / 4);
+        for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
+    }
+    __syncthreads();
+    // Inputs are checked identically by every CTA before any work, so a bad
+    // token / position / slot makes the whole grid return together.
+    for (int q = 0; q < M; ++q) {
+        const int tk = S.ltok[q], ps = S.lpos[q], sl = S.lslot[q];
+        if (tk < 0 || tk >= p.V || ps < 0 || ps >= p.C || sl < 0 || sl >= p.B) {
+            if (threadIdx.x == 0 && cta == 0) atomicCAS(p.err, 0, ERR_INDEX);
+            return;
+        }
+    }
+
+    if (threadIdx.x < 32) {
+        // ---------------- producer ----------------
+        if (threadIdx.x == 0) {
+            uint32_t t = 0;
+            for (int step = 0; t != T_ABORT && step < n_steps; ++step) {
+                for (int l = 0; t != T_ABORT && l < p.L; ++l) {
+                    const ec_mk_layer &ly = S.lay[l];
+                    t = mk_produce(p, ly.qkv, LWT, mk_range(ly.qkv, cta, G), t);
+                    if (t != T_ABORT) t = mk_produce(p, ly.o, LWT, mk_range(ly.o, cta, G), t);
+                    if (t != T_ABORT) t = mk_produce(p, ly.up, LWT, mk_range(ly.up, cta, G), t);
+                    if (t != T_ABORT) t = mk_produce(p, ly.down, LWT, mk_range(ly.down, cta, G), t);
+                }
+                if (t != T_ABORT) t = mk_produce(p, p.lm, HWT, mk_range(p.lm, cta, G), t);
+            }
+            if (t == T_ABORT) {
+                // give the copies already issued a bounded time to land
+                for (int s = 0; s < STAGES; ++s)
+                    for (uint32_t i = 0; i < (1u << 20); ++i)
+                        if (ec_mbar_try_wait(&S.full[s], 0) || ec_mbar_try_wait(&S.full[s], 1)) break;
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumers ----------------
+    const int ct = threadIdx.x - 32;
+    uint32_t t = 0;
+    unsigned target = 0;
+    const Rg xr = mk_range(S.lay[0].o, cta, G);   // residual rows owned by this CTA
+    const int xn = xr.r1 - xr.r0;
+#define SYNC_OR_RETURN()                                  \
+    do {                                                  \
+        target += (unsigned)G;                            \
+        if (!mk_grid_sync(p, target, ct)) return;         \
+        if (ct == 0) tmark(p, S, 0, EC_TR_SYNC);          \
+    } while (0)
+    for (int step = 0; step < n_steps; ++step) {
+        // residual rows := embedding (reference src/gpt2.c:488-499, :690-700)
+        for (int idx = ct; idx < xn * M; idx += NCT) {
+            const int q = idx / xn, n = xr.r0 + idx % xn;
+            const float e = mk_embed(p, S.ltok[q], S.lpos[q], n);
+            p.x[(size_t)q * p.E + n] = e;
+            if (p.taps) p.taps[(size_t)q * p.E + n] = e;
+        }
+        for (int l = 0; l < p.L; ++l) {
+            const ec_mk_layer &ly = S.lay[l];
+            // A: norm -> q|k|v
+            if (l > 0) SYNC_OR_RETURN();
+            mk_norm<MM>(p, l == 0, ly.n1g, ly.n1b, ct);
+            mk_operand<MM>(p, nullptr, p.E, ly.qkv.Kp, LWT, ct);
+            if (ct == 0) tmark(p, S, 0, EC_TR_PROLOGUE);
+            t = mk_phase<LWT, MM>(p, PK_QKV, l, t, ct);
+            if (ct == 0) tmark(p, S, 0, EC_TR_TILES);
+            // B: attention
+            SYNC_OR_RETURN();
+            mk_attention<MM>(p, l, ct);
+            if (ct == 0) tmark(p, S, 0, EC_TR_ATTN);
+            // C: o + residual
+            SYNC_OR_RETURN();
+            mk_operand<MM>(p, p.att, p.E, ly.o.Kp, LWT, ct);
+            if (ct == 0) tmark(p, S, 0, EC_TR_PROLOGUE);
+            t = mk_phase<LWT, MM>(p, PK_RESID, l, t, ct);
+            if (ct == 0) tmark(p, S, 0, EC_TR_TILES);
+            // D: norm -> gate|up / fc
+            SYNC_OR_RETURN();
+            mk_norm<MM>(p, false, ly.n2g, ly.n2b, ct);
+            mk_operand<MM>(p, nullptr, p.E, ly.up.Kp, LWT, ct);
+            if (ct == 0) tmark(p, S, 0, EC_TR_PROLOGUE);
+            t = mk_phase<LWT, MM>(p, PK_UP, l, t, ct);
+            if (ct == 0) tmark(p, S, 0, EC_TR_TILES);
+            // E: down / fc2 + residual
+            SYNC_OR_RETURN();
+            mk_operand<MM>(p, p.act, ly.down.K, ly.down.Kp, LWT, ct);
+            if (ct == 0) tmark(p, S, 0, EC_TR_PROLOGUE);
+            t = mk_phase<LWT, MM>(p, PK_RESID, l | 0x10000, t, ct);
+            if (ct == 0) tmark(p, S, 0, EC_TR_TILES);
+            if (p.taps)
+                for (int idx = ct; idx < xn * M; idx += NCT) {
+                    const int q = idx / xn, n = xr.r0 + idx % xn;
+                    p.taps[((size_t)(l + 1) * M + q) * p.E + n] = __ldcg(p.x + (size_t)q * p.E + n);
+                }
+        }
+        // F: final norm -> lm_head (per-CTA argmax partial written inside)
+        SYNC_OR_RETURN();
+        mk_norm<MM>(p, false, p.nfg, p.nfb, ct);
+        mk_operand<MM>(p, nullptr, p.E, p.lm.Kp, HWT, ct);
+        if (ct == 0) tmark(p, S, 0, EC_TR_PROLOGUE);
+        t = mk_phase<HWT, MM>(p, PK_LM, -1, t, ct);
+        if (ct == 0) tmark(p, S, 0, EC_TR_LM);
+        // G: merge the per-CTA partials (CTA order, lowest index on ties)
+        SYNC_OR_RETURN();
+        float bv[MM];
+        int bi[MM];
+#pragma unroll
+        for (int q = 0; q < MM; ++q) { bv[q] = -INFINITY; bi[q] = 0x7fffffff; }
+        for (int c = ct; c < G; c += NCT)
+            FOR_TOK(q) am_merge(bv[q], bi[q], __ldcg(p.amax_v + (size_t)c * MT + q), __ldcg(p.amax_i + (size_t)c * MT + q));
+        red_argmax<MM>(p, S, bv, bi, ct);
+        if (ct == 0) tmark(p, S, 0, EC_TR_ARGMAX);
+        FOR_TOK(q) if (ct == q) {
+            const int id = bi[q] == 0x7fffffff ? 0 : bi[q];
+            if (cta == 0) {
+                if (p.ids) p.ids[q] = id;
+                if (p.maxv) p.maxv[q] = bv[q];
+                if (p.hist) p.hist[(size_t)step * M + q] = id;
+            }
+            if (p.advance) {
+                S.ltok[q] = id;
+                const int np = S.lpos[q] + 1;
+                S.lpos[q] = (p.wrap_hi > 0 && np >= p.wrap_hi) ? p.wrap_lo : np;
+                if (cta == 0) { p.tok[q] = S.ltok[q]; p.pos[q] = S.lpos[q]; }
+            }
+        }
+        cons_sync();
+    }
+#undef SYNC_OR_RETURN
+}
+
+template <int LWT, int HWT, int MM>
+int mk_launch_t(const ec_mk_params *p, int n_steps, int grid, cudaStream_t stream) {
+    const Lay L = mk_layout(p->xbuf_bytes, p->stage_bytes, p->L, p->E);
+    cudaError_t e = cudaFuncSetAttribute(k_decode<LWT, HWT, MM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)L.total);
+    if (e != cudaSuccess) return (int)e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(EC_MK_THREADS);
+    cfg.dynamicSmemBytes = L.total;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return (int)cudaLaunchKernelEx(&cfg, k_decode<LWT, HWT, MM>, *p, n_steps);
+}
+
+template <int LWT, int HWT>
+int mk_launch_m(const ec_mk_params *p, int n_steps, int grid, cudaStream_t stream) {
+    if (p->M <= 1) return mk_launch_t<LWT, HWT, 1>(p, n_steps, grid, stream);
+    if (p->M <= 2) return mk_launch_t<LWT, HWT, 2>(p, n_steps, grid, stream);
+    if (p->M <= 4) return mk_launch_t<LWT, HWT, 4>(p, n_steps, grid, stream);
+    return mk_launch_t<LWT, HWT, 8>(p, n_steps, grid, stream);
+}
+
+}  // namespace
+
+extern "C" size_t ec_mk_smem_bytes(const ec_mk_params *p) {
+    return mk_layout(p->xbuf_bytes, p->stage_bytes, p->L, p->E).total;
+}
+
+extern "C" int ec_mk_smem_limit(void) {
+    int dev = 0, v = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    return v;
+}
+
+extern "C" int ec_mk_launch(const ec_mk_params *p, int n_steps, int grid, cudaStream_t stream) {
+    if (p->M < 1 || p->M > EC_MK_MT || n_steps < 1 || grid < 1) return (int)cudaErrorInvalidValue;
+    if (p->lwt == EC_W_I8 && p->hwt == EC_W_F16) return mk_launch_m<EC_W_I8, EC_W_F16>(p, n_steps, grid, stream);
+    if (p->lwt == EC_W_F16 && p->hwt == EC_W_F16) return mk_launch_m<EC_W_F16, EC_W_F16>(p, n_steps, grid, stream);
+    if (p->lwt == EC_W_BF16 && p->hwt == EC_W_BF16) return mk_launch_m<EC_W_BF16, EC_W_BF16>(p, n_steps, grid, stream);
+    return (int)cudaErrorInvalidValue;
+}

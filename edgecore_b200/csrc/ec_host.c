@@ -1,28 +1,30 @@
 /*
- * ec_model.c -- host side of the drop-in replacement for EdgeCore's
+ * ec_host.c -- host side of the drop-in replacement for EdgeCore's
  * src/gpt2.c: .ecm parsing, gpt2_load / gpt2_free / gpt2_forward /
  * qwen2_forward, and the edgecore_b200.h extensions built on them.
  *
  * A loaded model keeps the reference's host-visible state (the mmap'd file,
  * the bound host weight pointers, full-size host KV buffers, the tokenizer)
  * and adds device state, found through a registry keyed by the GPT2 address:
- *   - every linear weight uploaded once, rows padded to a multiple of 16
- *     elements; Qwen2 q|k|v and gate|up are fused into one matrix each (the
- *     reference quantises the same input once per projection, so fusing is
- *     exact), GPT-2 keeps its fused attn matrix;
+ *   - every linear uploaded once in the packed layout of ec_decode.h (rows
+ *     padded to a multiple of 16 elements; Qwen2 q|k|v fused with RoPE
+ *     partners adjacent, gate|up fused and interleaved; fusing is exact since
+ *     the reference quantises the same input once per projection);
  *   - a device KV arena [n_layer][batch_cap][eff_ctx][n_kv_embd] fp16, the
  *     reference cache layout (src/gpt2.c:312-317);
- *   - RoPE cos/sin tables in fp64, computed on the host with the reference
- *     formula so the rotation is bit-exact;
- *   - workspaces and, for decode-shaped calls, captured CUDA graphs.
+ *   - RoPE cos/sin tables in fp64 from the host libm with the reference
+ *     formula (src/gpt2.c:608-654), so the rotation is bit-exact;
+ *   - workspaces.
+ * Calls of M <= 8 token rows run the persistent decode kernel (one launch per
+ * step, ec_decode.cu); larger calls (prefill) run per-layer kernels.
  */
 #define _GNU_SOURCE
 #include "edgecore.h"
 #include "edgecore_b200.h"
 #include "ec_launch.h"
+#include "ec_decode.h"
 
 #include <cuda_runtime_api.h>
-#include <errno.h>
 #include <fcntl.h>
 #include <pthread.h>
 #include <stdarg.h>
@@ -52,15 +54,15 @@ static void ec_seterr(const char *fmt, ...)
 }
 
 EC_EXPORT const char *ec_last_error(void) { return g_err; }
-EC_EXPORT const char *ec_version(void) { return "edgecore_b200 0.1 sm_100a"; }
+EC_EXPORT const char *ec_version(void) { return "edgecore_b200 0.2 sm_100a"; }
 
-#define CK(call)                                                                   \
-    do {                                                                           \
-        cudaError_t e_ = (cudaError_t)(call);                                      \
-        if (e_ != cudaSuccess) {                                                   \
-            ec_seterr("%s:%d: %s: %s", __FILE__, __LINE__, #call, cudaGetErrorString(e_)); \
-            return -1;                                                             \
-        }                                                                          \
+#define CK(call)                                                                               \
+    do {                                                                                       \
+        cudaError_t e_ = (cudaError_t)(call);                                                  \
+        if (e_ != cudaSuccess) {                                                               \
+            ec_seterr("%s:%d: %s: %s", __FILE__, __LINE__, #call, cudaGetErrorString(e_));     \
+            return -1;                                                                         \
+        }                                                                                      \
     } while (0)
 
 /* For the void reference entry points: report and abort, as the reference
@@ -72,7 +74,7 @@ static void ec_fatal(const char *where)
 }
 
 /* ------------------------------------------------------------------ */
-/* .ecm parsing (format of reference src/gpt2.c:34-136)                 */
+/* .ecm parsing (the format read by reference src/gpt2.c:34-136)        */
 /* ------------------------------------------------------------------ */
 
 static const char *ec_readline(const char *p, const char *end, char *line, size_t cap)
@@ -90,13 +92,7 @@ static const char *ec_readline(const char *p, const char *end, char *line, size_
 
 static size_t ec_dtype_bytes(int dt)
 {
-    switch (dt) {
-    case 0: return 4;
-    case 1: return 2;
-    case 2: return 1;
-    case 4: return 2;
-    default: return 0;
-    }
+    return dt == 0 ? 4 : dt == 1 ? 2 : dt == 2 ? 1 : dt == 4 ? 2 : 0;
 }
 
 EC_EXPORT int ecm_parse(const void *data, size_t size, EcmTensor *out, int max, GPT2 *meta)
@@ -198,11 +194,9 @@ static const EcmTensor *ec_find(const EcmTensor *t, int n, const char *name)
 /* ------------------------------------------------------------------ */
 
 typedef struct {
-    void *w;            /* [N][Kp] */
-    float *s, *b;       /* [N] scales (int8), bias or NULL */
-    int N, K, Kp, wt;
-    ec_block *blocks;   /* device table */
-    int nblocks, block_rows;
+    void *w;            /* packed [N][ldw]: Kp weights + {scale, bias, 0, 0} fp32 tail */
+    float *s, *b;       /* [N] scales (int8), bias, or NULL (copies for the GEMM path) */
+    int N, K, Kp, ldw, wt, unit;
 } ec_lin;
 
 typedef struct {
@@ -210,37 +204,35 @@ typedef struct {
     ec_lin qkv, o, up, down;   /* up = gate|up (qwen2) or fc (gpt2); down = down / fc2 */
 } ec_dlayer;
 
-#define EC_MAX_GRAPHS 16
-#define EC_PROF_MAX 1024
-
 /* Kernel classes reported by ec_decode_profile. */
-enum { EC_PC_GEMV = 0, EC_PC_LMHEAD = 1, EC_PC_ATTN = 2, EC_PC_NORM = 3, EC_PC_OTHER = 4, EC_PC_N = 5 };
-
-typedef struct {
-    int M, maxlen, kind;       /* kind 0: logits forward, 1: argmax forward, 2/3: decode step */
-    int wrap_lo, wrap_hi;      /* decode position cycle (wrap_hi <= 0: none) */
-    cudaGraphExec_t exec;
-} ec_graph;
+enum { EC_PC_STEP = 0, EC_PC_GEMM = 1, EC_PC_ATTN = 2, EC_PC_NORM = 3, EC_PC_OTHER = 4, EC_PC_N = 5 };
+#define EC_PROF_MAX 1024
 
 typedef struct ec_dev {
     GPT2 *owner;
     int device, num_sms;
     cudaStream_t stream, own_stream;
-    int arch, prec, wt, L, E, Ep, H, KVH, hd, kv, I, V, C, B, window;
+    int arch, prec, wt, hwt, L, E, Ep, H, KVH, hd, kv, I, V, C, B, window;
     double eps;
     /* weights */
     uint16_t *wte, *wpe, *lm;
     float *nfg, *nfb;
     ec_dlayer *lw;
-    ec_lin lm_lin;             /* lm_head as a linear over the current vocab shard */
     int v0, v1;                /* vocab shard [v0, v1) */
     /* KV arena */
     uint16_t *kc, *vc;
     size_t layer_kv;           /* elements per layer: B*C*kv */
     double *rope_cos, *rope_sin;
+    /* persistent decode kernel */
+    ec_mk_layer *d_mk_layers;
+    int mk_grid;
+    unsigned *d_bar;
+    int *d_abort, *d_mk_err;
+    float *amax_v;
+    int *amax_i;
     /* workspaces */
     int cap;                   /* rows */
-    float *x, *h, *qkv, *att, *act, *big;
+    float *x, *h, *qkv, *q, *att, *act, *big;
     int8_t *aq;
     float *as;
     float *attn_part;
@@ -251,28 +243,22 @@ typedef struct ec_dev {
     int amax_chunks;
     int *d_tok, *d_pos, *d_slot, *d_ids;
     float *d_max;
-    int *d_counter, *d_hist;
+    int *d_hist;
     int hist_cap;
     int *h_in;                 /* pinned: tok | pos | slot */
     int *h_ids;
     float *h_max;
     float *h_logits;
     size_t h_logits_cap;
-    /* graphs */
-    ec_graph graphs[EC_MAX_GRAPHS];
-    int ngraphs;
     /* taps */
     int taps_on;
     float *taps;
     int taps_rows;
-    /* decode position cycle used by the step being enqueued */
-    int wrap_lo, wrap_hi;
-    /* per-launch event profiling (ec_decode_profile) */
-    int prof_on, prof_n;
+    /* per-launch event profiling */
+    int prof_on, prof_n, prof_ready;
     cudaEvent_t prof_ev[2 * EC_PROF_MAX];
     int prof_cls[EC_PROF_MAX];
     double prof_bytes[EC_PROF_MAX];
-    int prof_ready;
 } ec_dev;
 
 /* ---- registry: GPT2 address -> device state ---- */
@@ -320,154 +306,58 @@ static int ec_upload(void **dst, const void *src, size_t bytes)
     return 0;
 }
 
-/* Copy `rows` rows of `k` elements (elt bytes) into a device matrix with row
- * stride kp elements at row offset r0; padding was zeroed beforehand. */
-static int ec_upload_rows(void *dev, int r0, const void *src, int rows, int k, int kp, int elt)
+static int ec_upload_f32(float **dst, const float *src, int n)
 {
-    if (rows <= 0) return 0;
-    CK(cudaMemcpy2D((char *)dev + (size_t)r0 * kp * elt, (size_t)kp * elt, src, (size_t)k * elt,
-                    (size_t)k * elt, (size_t)rows, cudaMemcpyHostToDevice));
-    return 0;
+    if (!src) { *dst = NULL; return 0; }
+    return ec_upload((void **)dst, src, (size_t)n * sizeof(float));
 }
 
-/* Row-block tables.  Plain blocks of R rows; pair blocks (pair offset P) of R
- * rows from [j, j+R) and [j+P, j+P+R). */
-static int ec_pick_rows(int units, int row_bytes, int num_sms, int pair)
-{
-    /* enough blocks for ~2 CTAs per SM; staged bytes per block <= 48 KB */
-    int target = 2 * num_sms;
-    int r = units / target;
-    if (r < 1) r = 1;
-    int maxr = (48 * 1024) / (row_bytes * (pair ? 2 : 1));
-    if (maxr < 1) maxr = 1;
-    if (r > maxr) r = maxr;
-    int cap = pair ? 64 : 128;
-    if (r > cap) r = cap;
-    /* prefer a power of two */
-    int p2 = 1;
-    while (p2 * 2 <= r) p2 *= 2;
-    return p2;
-}
-
-static int ec_set_blocks(ec_lin *l, const ec_block *hb, int n, int block_rows)
-{
-    if (l->blocks) cudaFree(l->blocks);
-    l->blocks = NULL;
-    if (ec_upload((void **)&l->blocks, hb, (size_t)n * sizeof(ec_block))) return -1;
-    l->nblocks = n;
-    l->block_rows = block_rows;
-    return 0;
-}
-
-static int ec_plain_blocks(ec_lin *l, int row_begin, int row_end, int num_sms)
-{
-    int units = row_end - row_begin;
-    int R = ec_pick_rows(units, l->Kp * (l->wt == EC_W_I8 ? 1 : 2), num_sms, 0);
-    int n = (units + R - 1) / R;
-    ec_block *hb = calloc((size_t)n, sizeof *hb);
-    for (int i = 0; i < n; i++) {
-        hb[i].row0 = row_begin + i * R;
-        hb[i].nrows = (row_begin + (i + 1) * R <= row_end) ? R : row_end - hb[i].row0;
-    }
-    int rc = ec_set_blocks(l, hb, n, R);
-    free(hb);
-    return rc;
-}
-
-/* gate|up: pair blocks over the I gate rows with pair offset I. */
-static int ec_swiglu_blocks(ec_lin *l, int I, int num_sms)
-{
-    int R = ec_pick_rows(I, l->Kp * (l->wt == EC_W_I8 ? 1 : 2), num_sms, 1);
-    int n = (I + R - 1) / R;
-    ec_block *hb = calloc((size_t)n, sizeof *hb);
-    for (int i = 0; i < n; i++) {
-        hb[i].row0 = i * R;
-        hb[i].nrows = ((i + 1) * R <= I) ? R : I - i * R;
-        hb[i].pair = I;
-    }
-    int rc = ec_set_blocks(l, hb, n, 2 * R);
-    free(hb);
-    return rc;
-}
-
-/* qwen2 q|k|v: RoPE pair blocks inside every q and k head, plain blocks for v. */
-static int ec_qkv_rope_blocks(ec_lin *l, int E, int kv, int hd, int H, int KVH, int num_sms)
-{
-    int half = hd / 2;
-    int heads = H + KVH;
-    int R = ec_pick_rows(heads * half + kv / 2, l->Kp * (l->wt == EC_W_I8 ? 1 : 2), num_sms, 1);
-    while (half % R) R /= 2;
-    int per_head = half / R;
-    int nv = (kv + 2 * R - 1) / (2 * R);
-    int n = heads * per_head + nv;
-    ec_block *hb = calloc((size_t)n, sizeof *hb);
-    int i = 0;
-    for (int h = 0; h < heads; h++) {
-        int base = h < H ? h * hd : E + (h - H) * hd;
-        for (int j = 0; j < per_head; j++, i++) {
-            hb[i].row0 = base + j * R;
-            hb[i].nrows = R;
-            hb[i].pair = half;
-            hb[i].kind = EC_BK_ROPE;
-        }
-    }
-    for (int j = 0; j < nv; j++, i++) {
-        int r0 = E + kv + j * 2 * R;
-        hb[i].row0 = r0;
-        hb[i].nrows = (r0 + 2 * R <= E + 2 * kv) ? 2 * R : E + 2 * kv - r0;
-    }
-    int rc = ec_set_blocks(l, hb, n, 2 * R);
-    free(hb);
-    return rc;
-}
-
-/* Build a device linear from up to three stacked host matrices (same K). */
-static int ec_make_lin(ec_lin *l, int wt, int K, int nparts, const void *const *w, const float *const *s,
-                       const float *const *b, const int *rows)
+/* Build a packed linear: row r of the device matrix is host row rows_w[r]
+ * (K elements), its scale *rows_s[r] and bias *rows_b[r] (either table or
+ * entry may be NULL: scale 1 / no bias).  Host tensors may be unaligned. */
+static int ec_make_lin(ec_lin *l, int wt, int K, int N, int unit, const void *const *rows_w,
+                       const float *const *rows_s, const float *const *rows_b)
 {
     memset(l, 0, sizeof *l);
-    int N = 0;
-    for (int i = 0; i < nparts; i++) N += rows[i];
-    int elt = wt == EC_W_I8 ? 1 : 2;
+    const int elt = wt == EC_W_I8 ? 1 : 2;
     l->N = N;
     l->K = K;
     l->Kp = round16(K);
+    l->ldw = l->Kp + 16 / elt;
     l->wt = wt;
-    CK(cudaMalloc(&l->w, (size_t)N * l->Kp * elt));
-    CK(cudaMemset(l->w, 0, (size_t)N * l->Kp * elt));
-    int r = 0;
-    for (int i = 0; i < nparts; i++) {
-        if (ec_upload_rows(l->w, r, w[i], rows[i], K, l->Kp, elt)) return -1;
-        r += rows[i];
+    l->unit = unit;
+    const size_t rb = (size_t)l->ldw * elt;
+    unsigned char *hw = calloc((size_t)N, rb);
+    if (!hw) { ec_seterr("out of host memory"); return -1; }
+    for (int r = 0; r < N; r++) {
+        unsigned char *row = hw + (size_t)r * rb;
+        memcpy(row, rows_w[r], (size_t)K * elt);
+        float tail[4] = {1.0f, 0.0f, 0.0f, 0.0f};
+        if (rows_s && rows_s[r]) memcpy(&tail[0], rows_s[r], 4);
+        if (rows_b && rows_b[r]) memcpy(&tail[1], rows_b[r], 4);
+        memcpy(row + (size_t)l->Kp * elt, tail, sizeof tail);
     }
+    int rc = ec_upload(&l->w, hw, (size_t)N * rb);
+    free(hw);
+    if (rc) return -1;
     int have_s = 0, have_b = 0;
-    for (int i = 0; i < nparts; i++) {
-        have_s |= s && s[i] != NULL;
-        have_b |= b && b[i] != NULL;
+    for (int r = 0; r < N; r++) {
+        have_s |= rows_s && rows_s[r] != NULL;
+        have_b |= rows_b && rows_b[r] != NULL;
     }
-    if (have_s || have_b) {
-        float *tmp = malloc((size_t)N * sizeof(float));
-        for (int pass = 0; pass < 2; pass++) {
-            if (pass == 0 && !have_s) continue;
-            if (pass == 1 && !have_b) continue;
-            const float *const *src = pass == 0 ? s : b;
-            r = 0;
-            for (int i = 0; i < nparts; i++) {
-                for (int j = 0; j < rows[i]; j++) {
-                    float v = pass == 0 ? 1.0f : 0.0f;
-                    if (src[i]) memcpy(&v, (const char *)src[i] + (size_t)j * 4, 4);  /* may be unaligned */
-                    tmp[r + j] = v;
-                }
-                r += rows[i];
-            }
-            if (ec_upload((void **)(pass == 0 ? &l->s : &l->b), tmp, (size_t)N * sizeof(float))) {
-                free(tmp);
-                return -1;
-            }
+    float *tmp = malloc((size_t)N * sizeof(float));
+    for (int pass = 0; pass < 2 && !rc; pass++) {
+        if (!(pass == 0 ? have_s : have_b)) continue;
+        const float *const *src = pass == 0 ? rows_s : rows_b;
+        for (int r = 0; r < N; r++) {
+            float v = pass == 0 ? 1.0f : 0.0f;
+            if (src[r]) memcpy(&v, src[r], 4);
+            tmp[r] = v;
         }
-        free(tmp);
+        rc = ec_upload((void **)(pass == 0 ? &l->s : &l->b), tmp, (size_t)N * sizeof(float));
     }
-    return 0;
+    free(tmp);
+    return rc;
 }
 
 static void ec_free_lin(ec_lin *l)
@@ -475,70 +365,181 @@ static void ec_free_lin(ec_lin *l)
     cudaFree(l->w);
     cudaFree(l->s);
     cudaFree(l->b);
-    cudaFree(l->blocks);
     memset(l, 0, sizeof *l);
 }
 
-static int ec_upload_f32(float **dst, const float *src, int n)
+#define ROWP(base, r, K, elt) ((const void *)((const char *)(base) + (size_t)(r) * (K) * (elt)))
+#define SCP(base, r) ((base) ? (const float *)((const char *)(base) + (size_t)(r) * 4) : NULL)
+
+/* A plain linear (file order). */
+static int ec_plain_lin(ec_lin *l, int wt, const void *w, const float *s, const float *b, int N, int K)
 {
-    if (!src) { *dst = NULL; return 0; }
-    return ec_upload((void **)dst, src, (size_t)n * sizeof(float));
+    const int elt = wt == EC_W_I8 ? 1 : 2;
+    const void **rw = malloc((size_t)N * sizeof *rw);
+    const float **rs = malloc((size_t)N * sizeof *rs), **rbias = malloc((size_t)N * sizeof *rbias);
+    for (int r = 0; r < N; r++) {
+        rw[r] = ROWP(w, r, K, elt);
+        rs[r] = SCP(s, r);
+        rbias[r] = SCP(b, r);
+    }
+    int rc = ec_make_lin(l, wt, K, N, 1, rw, rs, rbias);
+    free(rw); free(rs); free(rbias);
+    return rc;
+}
+
+/* Qwen2 q|k|v packed: in every q and k head the RoPE partners i and
+ * i + head_dim/2 become rows 2i and 2i+1; then the v rows in file order.
+ * The reference passes no bias to these projections (src/gpt2.c:709-711). */
+static int ec_qkv_lin(ec_lin *l, int wt, const struct LayerW *S, int E, int kv, int hd, int H, int KVH)
+{
+    const int elt = wt == EC_W_I8 ? 1 : 2, half = hd / 2, N = E + 2 * kv;
+    const void **rw = malloc((size_t)N * sizeof *rw);
+    const float **rs = malloc((size_t)N * sizeof *rs);
+    int r = 0;
+    for (int h = 0; h < H + KVH; h++) {
+        const void *w = h < H ? S->q_w : S->k_w;
+        const float *s = h < H ? S->q_s : S->k_s;
+        const int base = (h < H ? h : h - H) * hd;
+        for (int i = 0; i < half; i++)
+            for (int t = 0; t < 2; t++, r++) {
+                rw[r] = ROWP(w, base + i + t * half, E, elt);
+                rs[r] = SCP(s, base + i + t * half);
+            }
+    }
+    for (int d = 0; d < kv; d++, r++) {
+        rw[r] = ROWP(S->v_w, d, E, elt);
+        rs[r] = SCP(S->v_s, d);
+    }
+    int rc = ec_make_lin(l, wt, E, N, 2, rw, rs, NULL);
+    free(rw); free(rs);
+    return rc;
+}
+
+/* Qwen2 gate|up interleaved: row 2j = gate j, row 2j+1 = up j. */
+static int ec_gateup_lin(ec_lin *l, int wt, const struct LayerW *S, int E, int I)
+{
+    const int elt = wt == EC_W_I8 ? 1 : 2;
+    const void **rw = malloc((size_t)2 * I * sizeof *rw);
+    const float **rs = malloc((size_t)2 * I * sizeof *rs);
+    for (int j = 0; j < I; j++) {
+        rw[2 * j] = ROWP(S->gate_w, j, E, elt);
+        rs[2 * j] = SCP(S->gate_s, j);
+        rw[2 * j + 1] = ROWP(S->up_w, j, E, elt);
+        rs[2 * j + 1] = SCP(S->up_s, j);
+    }
+    int rc = ec_make_lin(l, wt, E, 2 * I, 2, rw, rs, NULL);
+    free(rw); free(rs);
+    return rc;
 }
 
 /* RoPE tables: inverse frequencies with the YaRN ramp and cos/sin per position
  * scaled by the attention factor, in fp64 (reference src/gpt2.c:608-654). */
 static int ec_rope_tables(ec_dev *d, const GPT2 *g)
 {
-    int half = d->hd / 2;
+    const int half = d->hd / 2, dim = 2 * half;
     double *inv = malloc((size_t)half * sizeof(double));
-    int dim = 2 * half;
     for (int i = 0; i < half; i++) inv[i] = pow(1.0 / g->rope_theta, (double)(2 * i) / (double)dim);
     if (g->rope_type == ROPE_YARN) {
         const double two_pi = 6.28318530717958647692;
-        double lb = log(g->rope_theta);
+        const double lb = log(g->rope_theta);
         double lo = floor((double)dim * log(g->yarn_orig_max / (32.0 * two_pi)) / (2.0 * lb));
         double hi = ceil((double)dim * log(g->yarn_orig_max / (1.0 * two_pi)) / (2.0 * lb));
         if (lo < 0.0) lo = 0.0;
         if (hi > (double)(dim - 1)) hi = (double)(dim - 1);
-        double span = hi - lo < 1.0 ? 1.0 : hi - lo;
+        const double span = hi - lo < 1.0 ? 1.0 : hi - lo;
         for (int i = 0; i < half; i++) {
             double ramp = ((double)i - lo) / span;
             ramp = ramp < 0.0 ? 0.0 : (ramp > 1.0 ? 1.0 : ramp);
-            double e = inv[i];
+            const double e = inv[i];
             inv[i] = (e / g->yarn_factor) * ramp + e * (1.0 - ramp);
         }
     }
-    size_t n = (size_t)d->C * half;
+    const size_t n = (size_t)d->C * half;
     double *c = malloc(n * sizeof(double)), *s = malloc(n * sizeof(double));
-    double scale = g->yarn_attention_factor;
+    const double scale = g->yarn_attention_factor;
     for (int p = 0; p < d->C; p++)
         for (int i = 0; i < half; i++) {
-            double f = (double)p * inv[i];
+            const double f = (double)p * inv[i];
             c[(size_t)p * half + i] = cos(f) * scale;
             s[(size_t)p * half + i] = sin(f) * scale;
         }
     int rc = ec_upload((void **)&d->rope_cos, c, n * sizeof(double));
     if (!rc) rc = ec_upload((void **)&d->rope_sin, s, n * sizeof(double));
-    free(inv);
-    free(c);
-    free(s);
+    free(inv); free(c); free(s);
     return rc;
 }
 
-static void ec_free_graphs(ec_dev *d)
+/* 16-bit [rows][E] table -> device with row stride Ep. */
+static int ec_upload_table(uint16_t **dst, const uint16_t *src, int rows, int E, int Ep)
 {
-    for (int i = 0; i < d->ngraphs; i++) cudaGraphExecDestroy(d->graphs[i].exec);
-    d->ngraphs = 0;
+    CK(cudaMalloc((void **)dst, (size_t)rows * Ep * 2));
+    if (Ep != E) CK(cudaMemset(*dst, 0, (size_t)rows * Ep * 2));
+    CK(cudaMemcpy2D(*dst, (size_t)Ep * 2, src, (size_t)E * 2, (size_t)E * 2, (size_t)rows, cudaMemcpyHostToDevice));
+    return 0;
 }
+
+/* ---- persistent-kernel descriptors ---- */
+
+static ec_mk_mat ec_mk_of(const ec_lin *l)
+{
+    ec_mk_mat m;
+    memset(&m, 0, sizeof m);
+    m.w = l->w;
+    m.N = l->N;
+    m.K = l->K;
+    m.Kp = l->Kp;
+    m.ldw = l->ldw;
+    m.meta = l->ldw > l->Kp ? ((l->s ? 1 : 0) | (l->b ? 2 : 0)) : 0;
+    m.unit = l->unit;
+    const int rb = l->ldw * (l->wt == EC_W_I8 ? 1 : 2);
+    int tr = EC_MK_TILE / rb;
+    if (tr > EC_MK_MAX_TILE_ROWS) tr = EC_MK_MAX_TILE_ROWS;
+    /* whole units for each of the consumer warps when the slot allows */
+    if (tr >= EC_MK_CONS_WARPS * l->unit) tr -= tr % (EC_MK_CONS_WARPS * l->unit);
+    else tr -= tr % l->unit;
+    m.tile_rows = tr;   /* 0 if a unit of rows does not fit a ring slot */
+    return m;
+}
+
+static int ec_mk_build(ec_dev *d)
+{
+    ec_mk_layer *h = calloc((size_t)d->L, sizeof *h);
+    int ok = 1;
+    for (int l = 0; l < d->L; l++) {
+        const ec_dlayer *W = &d->lw[l];
+        h[l].qkv = ec_mk_of(&W->qkv);
+        h[l].o = ec_mk_of(&W->o);
+        h[l].up = ec_mk_of(&W->up);
+        h[l].down = ec_mk_of(&W->down);
+        ok &= h[l].qkv.tile_rows > 0 && h[l].o.tile_rows > 0 && h[l].up.tile_rows > 0 && h[l].down.tile_rows > 0;
+        h[l].n1g = W->n1g; h[l].n1b = W->n1b; h[l].n2g = W->n2g; h[l].n2b = W->n2b;
+        h[l].kc = d->kc + d->layer_kv * l;
+        h[l].vc = d->vc + d->layer_kv * l;
+    }
+    int rc = ec_upload((void **)&d->d_mk_layers, h, (size_t)d->L * sizeof *h);
+    free(h);
+    if (rc) return -1;
+    d->mk_grid = ok ? d->num_sms : 0;   /* 0: the persistent kernel is not usable */
+    CK(cudaMalloc((void **)&d->d_bar, 16));
+    CK(cudaMalloc((void **)&d->d_abort, 16));
+    CK(cudaMalloc((void **)&d->d_mk_err, 16));
+    CK(cudaMemset(d->d_mk_err, 0, 16));
+    CK(cudaMalloc((void **)&d->amax_v, (size_t)d->num_sms * EC_MK_MT * 4));
+    CK(cudaMalloc((void **)&d->amax_i, (size_t)d->num_sms * EC_MK_MT * 4));
+    return 0;
+}
+
+/* ---- workspaces ---- */
 
 static void ec_free_work(ec_dev *d)
 {
-    cudaFree(d->x); cudaFree(d->h); cudaFree(d->qkv); cudaFree(d->att); cudaFree(d->act); cudaFree(d->big);
-    cudaFree(d->aq); cudaFree(d->as); cudaFree(d->d_tok); cudaFree(d->d_pos); cudaFree(d->d_slot);
+    cudaFree(d->x); cudaFree(d->h); cudaFree(d->qkv); cudaFree(d->q); cudaFree(d->att); cudaFree(d->act);
+    cudaFree(d->big); cudaFree(d->aq); cudaFree(d->as); cudaFree(d->d_tok); cudaFree(d->d_pos); cudaFree(d->d_slot);
     cudaFree(d->d_ids); cudaFree(d->d_max);
     cudaFreeHost(d->h_in); cudaFreeHost(d->h_ids); cudaFreeHost(d->h_max);
-    d->x = d->h = d->qkv = d->att = d->act = d->big = NULL;
-    d->aq = NULL; d->as = NULL;
+    d->x = d->h = d->qkv = d->q = d->att = d->act = d->big = NULL;
+    d->aq = NULL;
+    d->as = NULL;
     d->d_tok = d->d_pos = d->d_slot = d->d_ids = NULL;
     d->d_max = NULL;
     d->h_in = d->h_ids = NULL;
@@ -546,23 +547,23 @@ static void ec_free_work(ec_dev *d)
     d->cap = 0;
 }
 
-/* Grow the row-indexed workspaces to at least M rows.  Graphs captured with
- * the old buffers are dropped. */
+/* Grow the row-indexed workspaces to at least M rows. */
 static int ec_ensure(ec_dev *d, int M)
 {
     if (M <= d->cap) return 0;
     int cap = d->cap ? d->cap : 8;
     while (cap < M) cap *= 2;
-    ec_free_graphs(d);
+    CK(cudaStreamSynchronize(d->stream));
     ec_free_work(d);
-    int act = d->arch == ARCH_QWEN2 ? d->I : 4 * d->E;
-    int big = d->arch == ARCH_QWEN2 ? 2 * d->I : 1;
-    int kmax = d->E > d->I ? d->E : d->I;
-    if (d->arch == ARCH_GPT2) kmax = 4 * d->E;
+    const int act = d->arch == ARCH_QWEN2 ? d->I : 4 * d->E;
+    const int big = d->arch == ARCH_QWEN2 ? 2 * d->I : 1;
+    const int qkvw = d->E + 2 * d->kv;
+    int kmax = d->arch == ARCH_QWEN2 ? (d->E > d->I ? d->E : d->I) : 4 * d->E;
     kmax = round16(kmax);
     CK(cudaMalloc((void **)&d->x, (size_t)cap * d->E * 4));
     CK(cudaMalloc((void **)&d->h, (size_t)cap * d->E * 4));
-    CK(cudaMalloc((void **)&d->qkv, (size_t)cap * (d->E + 2 * d->kv) * 4));
+    CK(cudaMalloc((void **)&d->qkv, (size_t)cap * qkvw * 4));
+    CK(cudaMalloc((void **)&d->q, (size_t)cap * d->E * 4));
     CK(cudaMalloc((void **)&d->att, (size_t)cap * d->E * 4));
     CK(cudaMalloc((void **)&d->act, (size_t)cap * act * 4));
     CK(cudaMalloc((void **)&d->big, (size_t)cap * big * 4));
@@ -580,15 +581,30 @@ static int ec_ensure(ec_dev *d, int M)
     return 0;
 }
 
-static int ec_pick_nsplit(const ec_dev *d, int max_len);
+static int ec_pick_nsplit(int max_len)
+{
+    /* ~64 positions per split, power of two, each split <= 1024 positions */
+    const int need = (max_len + 63) / 64;
+    int ns = 1;
+    while (ns < need && ns < 64) ns *= 2;
+    while ((max_len + ns - 1) / ns > 1024) ns *= 2;
+    return ns;
+}
 
-/* Split-attention scratch for rows of up to maxlen positions (the exact-order
- * kernel needs none). */
+/* Attended-length bound for a call whose rows attend at most max_len
+ * positions: a power of two >= 64, capped at eff_ctx. */
+static int ec_len_bucket(const ec_dev *d, int max_len)
+{
+    int b = 64;
+    while (b < max_len) b *= 2;
+    return b < d->C ? b : d->C;
+}
+
 static int ec_ensure_attn(ec_dev *d, int M, int maxlen)
 {
-    size_t need = ec_attention_scratch_floats(M, d->H, d->hd, ec_pick_nsplit(d, maxlen));
+    const size_t need = ec_attention_scratch_floats(M, d->H, d->hd, ec_pick_nsplit(maxlen));
     if (need <= d->attn_part_floats) return 0;
-    ec_free_graphs(d);
+    CK(cudaStreamSynchronize(d->stream));
     cudaFree(d->attn_part);
     d->attn_part = NULL;
     CK(cudaMalloc((void **)&d->attn_part, need * 4));
@@ -596,11 +612,10 @@ static int ec_ensure_attn(ec_dev *d, int M, int maxlen)
     return 0;
 }
 
-/* Device logits buffer of `rows` rows of the shard width. */
 static int ec_ensure_logits(ec_dev *d, int rows)
 {
     if (rows <= d->logit_rows) return 0;
-    ec_free_graphs(d);
+    CK(cudaStreamSynchronize(d->stream));
     cudaFree(d->logits);
     d->logits = NULL;
     CK(cudaMalloc((void **)&d->logits, (size_t)rows * (d->v1 - d->v0) * 4));
@@ -610,12 +625,12 @@ static int ec_ensure_logits(ec_dev *d, int rows)
 
 static int ec_ensure_amax(ec_dev *d, int M)
 {
-    int chunks = 2 * d->num_sms;
+    const int chunks = 2 * d->num_sms;
+    const int rows = d->cap > M ? d->cap : M;
     if (d->amax_part && d->amax_chunks >= chunks && d->cap >= M) return 0;
-    ec_free_graphs(d);
+    CK(cudaStreamSynchronize(d->stream));
     cudaFree(d->amax_part);
     d->amax_part = NULL;
-    int rows = d->cap > M ? d->cap : M;
     CK(cudaMalloc(&d->amax_part, (size_t)rows * chunks * 8));
     d->amax_chunks = chunks;
     return 0;
@@ -627,8 +642,7 @@ static void ec_dev_free(ec_dev *d)
     int cur = 0;
     cudaGetDevice(&cur);
     cudaSetDevice(d->device);
-    cudaStreamSynchronize(d->stream);
-    ec_free_graphs(d);
+    if (d->stream) cudaStreamSynchronize(d->stream);
     ec_free_work(d);
     if (d->lw) {
         for (int l = 0; l < d->L; l++) {
@@ -638,12 +652,13 @@ static void ec_dev_free(ec_dev *d)
         }
         free(d->lw);
     }
-    cudaFree(d->lm_lin.blocks);
     if (d->lm != d->wte) cudaFree(d->lm);
     cudaFree(d->wte); cudaFree(d->wpe); cudaFree(d->nfg); cudaFree(d->nfb);
     cudaFree(d->kc); cudaFree(d->vc); cudaFree(d->rope_cos); cudaFree(d->rope_sin);
+    cudaFree(d->d_mk_layers); cudaFree(d->d_bar); cudaFree(d->d_abort); cudaFree(d->d_mk_err);
+    cudaFree(d->amax_v); cudaFree(d->amax_i);
     cudaFree(d->attn_part); cudaFree(d->logits); cudaFree(d->amax_part);
-    cudaFree(d->d_counter); cudaFree(d->d_hist); cudaFree(d->taps);
+    cudaFree(d->d_hist); cudaFree(d->taps);
     cudaFreeHost(d->h_logits);
     if (d->prof_ready)
         for (int i = 0; i < 2 * EC_PROF_MAX; i++) cudaEventDestroy(d->prof_ev[i]);
@@ -652,30 +667,28 @@ static void ec_dev_free(ec_dev *d)
     cudaSetDevice(cur);
 }
 
-/* 16-bit [rows][E] table -> device with row stride Ep. */
-static int ec_upload_table(uint16_t **dst, const uint16_t *src, int rows, int E, int Ep)
-{
-    CK(cudaMalloc((void **)dst, (size_t)rows * Ep * 2));
-    if (Ep != E) CK(cudaMemset(*dst, 0, (size_t)rows * Ep * 2));
-    return ec_upload_rows(*dst, 0, src, rows, E, Ep, 2);
-}
-
 static int ec_set_lm_shard(ec_dev *d, int v0, int v1)
 {
     d->v0 = v0;
     d->v1 = v1;
-    ec_lin *l = &d->lm_lin;
-    l->w = (char *)d->lm + (size_t)v0 * d->Ep * 2;
-    l->s = l->b = NULL;
-    l->N = v1 - v0;
-    l->K = d->E;
-    l->Kp = d->Ep;
-    l->wt = d->prec == 2 ? EC_W_BF16 : EC_W_F16;
     d->logit_rows = 0;
     cudaFree(d->logits);
     d->logits = NULL;
-    ec_free_graphs(d);
-    return ec_plain_blocks(l, 0, l->N, d->num_sms);
+    return 0;
+}
+
+static ec_lin ec_lm_lin(const ec_dev *d)
+{
+    ec_lin l;
+    memset(&l, 0, sizeof l);
+    l.w = (char *)d->lm + (size_t)d->v0 * d->Ep * 2;
+    l.N = d->v1 - d->v0;
+    l.K = d->E;
+    l.Kp = d->Ep;
+    l.ldw = d->Ep;   /* the embedding table: no metadata tail */
+    l.wt = d->hwt;
+    l.unit = 1;
+    return l;
 }
 
 static int ec_dev_build(GPT2 *g, ec_dev *d)
@@ -689,6 +702,7 @@ static int ec_dev_build(GPT2 *g, ec_dev *d)
     d->arch = g->arch;
     d->prec = g->precision;
     d->wt = g->precision == 0 ? EC_W_I8 : (g->precision == 1 ? EC_W_F16 : EC_W_BF16);
+    d->hwt = g->precision == 2 ? EC_W_BF16 : EC_W_F16;
     d->L = g->n_layer;
     d->E = g->n_embd;
     d->Ep = round16(g->n_embd);
@@ -703,6 +717,7 @@ static int ec_dev_build(GPT2 *g, ec_dev *d)
     d->eps = g->eps;
     d->window = g->arch == ARCH_QWEN2 ? g->sliding_window : 0;
     if (d->hd % 8 || d->hd > 256 || d->hd < 8) { ec_seterr("unsupported head_dim %d", d->hd); return -1; }
+    if (d->E != d->H * d->hd) { ec_seterr("n_embd must equal n_head * head_dim"); return -1; }
 
     if (ec_upload_table(&d->wte, g->wte, d->V, d->E, d->Ep)) return -1;
     if (g->wpe && ec_upload_table(&d->wpe, g->wpe, g->n_ctx, d->E, d->Ep)) return -1;
@@ -714,37 +729,26 @@ static int ec_dev_build(GPT2 *g, ec_dev *d)
     if (ec_upload_f32(&d->nfg, g->lnf_g, d->E) || ec_upload_f32(&d->nfb, g->lnf_b, d->E)) return -1;
 
     d->lw = calloc((size_t)d->L, sizeof *d->lw);
+    const int E = d->E, kv = d->kv, I = d->I;
     for (int l = 0; l < d->L; l++) {
         const struct LayerW *S = &g->lw[l];
         ec_dlayer *W = &d->lw[l];
-        if (ec_upload_f32(&W->n1g, S->ln1_g, d->E) || ec_upload_f32(&W->n2g, S->ln2_g, d->E)) return -1;
+        if (ec_upload_f32(&W->n1g, S->ln1_g, E) || ec_upload_f32(&W->n2g, S->ln2_g, E)) return -1;
         if (d->arch == ARCH_GPT2) {
-            if (ec_upload_f32(&W->n1b, S->ln1_b, d->E) || ec_upload_f32(&W->n2b, S->ln2_b, d->E)) return -1;
-            int E = d->E;
-            { const void *w[1] = {S->attn_w}; const float *s[1] = {S->attn_s}; const float *b[1] = {S->attn_b}; int r[1] = {3 * E};
-              if (ec_make_lin(&W->qkv, d->wt, E, 1, w, s, b, r) || ec_plain_blocks(&W->qkv, 0, 3 * E, d->num_sms)) return -1; }
-            { const void *w[1] = {S->proj_w}; const float *s[1] = {S->proj_s}; const float *b[1] = {S->proj_b}; int r[1] = {E};
-              if (ec_make_lin(&W->o, d->wt, E, 1, w, s, b, r) || ec_plain_blocks(&W->o, 0, E, d->num_sms)) return -1; }
-            { const void *w[1] = {S->fc_w}; const float *s[1] = {S->fc_s}; const float *b[1] = {S->fc_b}; int r[1] = {4 * E};
-              if (ec_make_lin(&W->up, d->wt, E, 1, w, s, b, r) || ec_plain_blocks(&W->up, 0, 4 * E, d->num_sms)) return -1; }
-            { const void *w[1] = {S->fc2_w}; const float *s[1] = {S->fc2_s}; const float *b[1] = {S->fc2_b}; int r[1] = {E};
-              if (ec_make_lin(&W->down, d->wt, 4 * E, 1, w, s, b, r) || ec_plain_blocks(&W->down, 0, E, d->num_sms)) return -1; }
+            if (ec_upload_f32(&W->n1b, S->ln1_b, E) || ec_upload_f32(&W->n2b, S->ln2_b, E)) return -1;
+            if (ec_plain_lin(&W->qkv, d->wt, S->attn_w, S->attn_s, S->attn_b, 3 * E, E) ||
+                ec_plain_lin(&W->o, d->wt, S->proj_w, S->proj_s, S->proj_b, E, E) ||
+                ec_plain_lin(&W->up, d->wt, S->fc_w, S->fc_s, S->fc_b, 4 * E, E) ||
+                ec_plain_lin(&W->down, d->wt, S->fc2_w, S->fc2_s, S->fc2_b, E, 4 * E)) return -1;
         } else {
-            int E = d->E, kv = d->kv, I = d->I;
-            /* The reference passes NULL bias to every Qwen2 projection
-             * (src/gpt2.c:709-711, :781, :788-792): stored biases are unused. */
-            { const void *w[3] = {S->q_w, S->k_w, S->v_w}; const float *s[3] = {S->q_s, S->k_s, S->v_s}; int r[3] = {E, kv, kv};
-              if (ec_make_lin(&W->qkv, d->wt, E, 3, w, s, NULL, r) ||
-                  ec_qkv_rope_blocks(&W->qkv, E, kv, d->hd, d->H, d->KVH, d->num_sms)) return -1; }
-            { const void *w[1] = {S->o_w}; const float *s[1] = {S->o_s}; int r[1] = {E};
-              if (ec_make_lin(&W->o, d->wt, E, 1, w, s, NULL, r) || ec_plain_blocks(&W->o, 0, E, d->num_sms)) return -1; }
-            { const void *w[2] = {S->gate_w, S->up_w}; const float *s[2] = {S->gate_s, S->up_s}; int r[2] = {I, I};
-              if (ec_make_lin(&W->up, d->wt, E, 2, w, s, NULL, r) || ec_swiglu_blocks(&W->up, I, d->num_sms)) return -1; }
-            { const void *w[1] = {S->down_w}; const float *s[1] = {S->down_s}; int r[1] = {E};
-              if (ec_make_lin(&W->down, d->wt, I, 1, w, s, NULL, r) || ec_plain_blocks(&W->down, 0, E, d->num_sms)) return -1; }
+            /* no biases: the reference passes NULL to every Qwen2 projection */
+            if (ec_qkv_lin(&W->qkv, d->wt, S, E, kv, d->hd, d->H, d->KVH) ||
+                ec_plain_lin(&W->o, d->wt, S->o_w, S->o_s, NULL, E, E) ||
+                ec_gateup_lin(&W->up, d->wt, S, E, I) ||
+                ec_plain_lin(&W->down, d->wt, S->down_w, S->down_s, NULL, E, I)) return -1;
         }
     }
-    if (ec_set_lm_shard(d, 0, d->V)) return -1;
+    ec_set_lm_shard(d, 0, d->V);
 
     d->layer_kv = (size_t)d->B * d->C * d->kv;
     CK(cudaMalloc((void **)&d->kc, d->layer_kv * d->L * 2));
@@ -752,7 +756,7 @@ static int ec_dev_build(GPT2 *g, ec_dev *d)
     CK(cudaMemset(d->kc, 0, d->layer_kv * d->L * 2));
     CK(cudaMemset(d->vc, 0, d->layer_kv * d->L * 2));
     if (d->arch == ARCH_QWEN2 && ec_rope_tables(d, g)) return -1;
-    CK(cudaMalloc((void **)&d->d_counter, 4));
+    if (ec_mk_build(d)) return -1;
     if (ec_ensure(d, d->B > 8 ? d->B : 8)) return -1;
     CK(cudaDeviceSynchronize());
     return 0;
@@ -778,7 +782,7 @@ static void ec_host_free(GPT2 *g)
 {
     if (g->tok.id_to_token && tokenizer_free) tokenizer_free(&g->tok);
     free(g->lw);
-    size_t kvb = ec_shadow_bytes(g);
+    const size_t kvb = ec_shadow_bytes(g);
     if (g->k_cache) munmap(g->k_cache, kvb ? kvb : 4096);
     if (g->v_cache) munmap(g->v_cache, kvb ? kvb : 4096);
     if (g->file_data) {
@@ -799,6 +803,14 @@ static void ec_defaults_qwen2(GPT2 *g)
     if (g->yarn_attention_factor <= 0) g->yarn_attention_factor = 1.0;
 }
 
+static int ec_load_fail(EcmTensor *t, const char *msg, const char *arg)
+{
+    ec_seterr(msg, arg);
+    fprintf(stderr, "%s\n", g_err);
+    free(t);
+    return -1;
+}
+
 static int ec_load_host(GPT2 *g, const char *path, int batch_cap, int max_ctx)
 {
     memset(g, 0, sizeof *g);
@@ -817,61 +829,54 @@ static int ec_load_host(GPT2 *g, const char *path, int batch_cap, int max_ctx)
     g->file_mapped = 1;
 
     EcmTensor *t = calloc(512, sizeof *t);
-    int n = ecm_parse(g->file_data, g->file_size, t, 512, g);
-    if (n < 0) { free(t); ec_seterr("ecm: parse failed"); return -1; }
+    const int n = ecm_parse(g->file_data, g->file_size, t, 512, g);
+    if (n < 0) return ec_load_fail(t, "ecm: parse failed%s", "");
     const char *base = g->file_data;
     for (int i = 0; i < n; i++)
-        if (t[i].offset + t[i].bytes > g->file_size) {
-            ec_seterr("ecm: tensor %s past end of file", t[i].name);
-            free(t);
-            return -1;
-        }
+        if (t[i].offset + t[i].bytes > g->file_size) return ec_load_fail(t, "ecm: tensor %s past end of file", t[i].name);
     const EcmTensor *wte = ec_find(t, n, "wte"), *lnf = ec_find(t, n, "ln_f.g");
-    if (!wte || !lnf) { free(t); fprintf(stderr, "ecm: missing core tensors (wte, ln_f.g)\n"); ec_seterr("ecm: missing wte/ln_f.g"); return -1; }
+    if (!wte || !lnf) return ec_load_fail(t, "ecm: missing core tensors (wte, ln_f.g)%s", "");
     g->wte = (const uint16_t *)(base + wte->offset);
     g->lnf_g = (const float *)(base + lnf->offset);
     const char *lin0 = g->arch == ARCH_QWEN2 ? "blocks.0.q.w" : "blocks.0.attn.w";
     const EcmTensor *t0 = ec_find(t, n, lin0);
-    if (!t0) { free(t); fprintf(stderr, "ecm: missing %s\n", lin0); ec_seterr("ecm: missing %s", lin0); return -1; }
+    if (!t0) return ec_load_fail(t, "ecm: missing %s", lin0);
     if (t0->dtype == 1) g->precision = 1;
     else if (t0->dtype == 2) g->precision = 0;
     else if (t0->dtype == 4) g->precision = 2;
-    else { free(t); fprintf(stderr, "ecm: unexpected linear weight dtype\n"); ec_seterr("ecm: linear dtype"); return -1; }
+    else return ec_load_fail(t, "ecm: unexpected linear weight dtype%s", "");
     if (g->arch == ARCH_QWEN2) ec_defaults_qwen2(g);
     if (g->arch == ARCH_GPT2) {
         const EcmTensor *wpe = ec_find(t, n, "wpe"), *lnb = ec_find(t, n, "ln_f.b");
-        if (!wpe || !lnb) { free(t); fprintf(stderr, "ecm: missing wpe / ln_f.b\n"); ec_seterr("ecm: missing wpe/ln_f.b"); return -1; }
+        if (!wpe || !lnb) return ec_load_fail(t, "ecm: missing wpe / ln_f.b%s", "");
         g->wpe = (const uint16_t *)(base + wpe->offset);
         g->lnf_b = (const float *)(base + lnb->offset);
         g->n_kv_embd = g->n_embd;
         g->n_kv_head = g->n_head;
         g->intermediate = 4 * g->n_embd;
-        g->head_dim = g->n_embd / g->n_head;
+        g->head_dim = g->n_embd / (g->n_head > 0 ? g->n_head : 1);
     } else {
         const EcmTensor *lmh = ec_find(t, n, "lm_head.w");
         if (lmh && !g->tie_word_embeddings) g->lm_head = (const uint16_t *)(base + lmh->offset);
         if (g->tie_word_embeddings || !lmh) g->tie_word_embeddings = 1;
     }
+    if (g->vocab <= 0 || g->n_layer <= 0 || g->n_embd <= 0 || g->n_head <= 0 || g->n_ctx <= 0)
+        return ec_load_fail(t, "ecm: bad dimensions%s", "");
+    if (wte->bytes < (size_t)g->vocab * g->n_embd * 2) return ec_load_fail(t, "ecm: wte smaller than vocab x n_embd%s", "");
     g->lw = calloc((size_t)g->n_layer, sizeof *g->lw);
     char nm[256];
     for (int l = 0; l < g->n_layer; l++) {
         struct LayerW *W = &g->lw[l];
-#define EC_BIND(field, fmt)                                                   \
-        do {                                                                  \
-            snprintf(nm, sizeof nm, fmt, l);                                  \
-            const EcmTensor *x_ = ec_find(t, n, nm);                          \
-            if (x_) W->field = (const float *)(base + x_->offset);            \
-        } while (0)
-        EC_BIND(ln1_g, "blocks.%d.ln_1.g");
-        EC_BIND(ln1_b, "blocks.%d.ln_1.b");
-        EC_BIND(ln2_g, "blocks.%d.ln_2.g");
-        EC_BIND(ln2_b, "blocks.%d.ln_2.b");
-#undef EC_BIND
+        const float **nv[4] = {&W->ln1_g, &W->ln1_b, &W->ln2_g, &W->ln2_b};
+        const char *nn[4] = {"ln_1.g", "ln_1.b", "ln_2.g", "ln_2.b"};
+        for (int i = 0; i < 4; i++) {
+            snprintf(nm, sizeof nm, "blocks.%d.%s", l, nn[i]);
+            const EcmTensor *x = ec_find(t, n, nm);
+            if (x) *nv[i] = (const float *)(base + x->offset);
+        }
         if (!W->ln1_g || !W->ln2_g || (g->arch == ARCH_GPT2 && (!W->ln1_b || !W->ln2_b))) {
-            free(t);
-            ec_seterr("ecm: missing norm tensors of layer %d", l);
-            fprintf(stderr, "%s\n", g_err);
-            return -1;
+            snprintf(nm, sizeof nm, "blocks.%d.ln_*", l);
+            return ec_load_fail(t, "ecm: missing norm tensors %s", nm);
         }
         const char *qn[7] = {"q", "k", "v", "o", "gate", "up", "down"};
         const void **qw[7] = {&W->q_w, &W->k_w, &W->v_w, &W->o_w, &W->gate_w, &W->up_w, &W->down_w};
@@ -881,7 +886,7 @@ static int ec_load_host(GPT2 *g, const char *path, int batch_cap, int max_ctx)
         const void **gw[4] = {&W->attn_w, &W->proj_w, &W->fc_w, &W->fc2_w};
         const float **gs[4] = {&W->attn_s, &W->proj_s, &W->fc_s, &W->fc2_s};
         const float **gb[4] = {&W->attn_b, &W->proj_b, &W->fc_b, &W->fc2_b};
-        int cnt = g->arch == ARCH_QWEN2 ? 7 : 4;
+        const int cnt = g->arch == ARCH_QWEN2 ? 7 : 4;
         for (int s = 0; s < cnt; s++) {
             const char *sf = g->arch == ARCH_QWEN2 ? qn[s] : gn[s];
             snprintf(nm, sizeof nm, "blocks.%d.%s.w", l, sf);
@@ -891,10 +896,8 @@ static int ec_load_host(GPT2 *g, const char *path, int batch_cap, int max_ctx)
             snprintf(nm, sizeof nm, "blocks.%d.%s.b", l, sf);
             const EcmTensor *tb = ec_find(t, n, nm);
             if (!tw || (g->arch == ARCH_GPT2 && !tb) || (g->arch == ARCH_GPT2 && g->precision == 0 && !ts)) {
-                free(t);
-                fprintf(stderr, "ecm: missing %s tensors\n", nm);
-                ec_seterr("ecm: missing %s", nm);
-                return -1;
+                snprintf(nm, sizeof nm, "blocks.%d.%s", l, sf);
+                return ec_load_fail(t, "ecm: missing %s tensors", nm);
             }
             const void *wp = base + tw->offset;
             const float *sp = (g->precision == 0 && ts) ? (const float *)(base + ts->offset) : NULL;
@@ -903,22 +906,16 @@ static int ec_load_host(GPT2 *g, const char *path, int batch_cap, int max_ctx)
             else { *gw[s] = wp; *gs[s] = sp; *gb[s] = bp; }
         }
     }
-    int V = g->vocab;
-    if (V <= 0 || g->n_layer <= 0 || g->n_embd <= 0 || g->n_head <= 0 || g->n_ctx <= 0) {
-        free(t); ec_seterr("ecm: bad dimensions"); return -1;
-    }
-    if (wte->bytes < (size_t)V * g->n_embd * 2) { free(t); ec_seterr("ecm: wte smaller than vocab x n_embd"); return -1; }
-    size_t kvb = ec_shadow_bytes(g);
+    const size_t kvb = ec_shadow_bytes(g);
     g->k_cache = ec_shadow_alloc(kvb);
     g->v_cache = ec_shadow_alloc(kvb);
-    if (!g->k_cache || !g->v_cache) { free(t); ec_seterr("host KV shadow allocation failed"); return -1; }
+    if (!g->k_cache || !g->v_cache) return ec_load_fail(t, "host KV shadow allocation failed%s", "");
     if (tokenizer_load) {
         const EcmTensor *tv = ec_find(t, n, "tokenizer.vocab"), *tm = ec_find(t, n, "tokenizer.merges");
-        if (!tv || !tm) { free(t); fprintf(stderr, "ecm: tokenizer blobs missing\n"); ec_seterr("ecm: tokenizer blobs missing"); return -1; }
+        if (!tv || !tm) return ec_load_fail(t, "ecm: tokenizer blobs missing%s", "");
         if (tokenizer_load(&g->tok, base + tv->offset, tv->bytes, base + tm->offset, tm->bytes, g->vocab,
-                           g->arch == ARCH_QWEN2 ? 1 : 0) != 0) {
-            free(t); ec_seterr("tokenizer_load failed"); return -1;
-        }
+                           g->arch == ARCH_QWEN2 ? 1 : 0) != 0)
+            return ec_load_fail(t, "tokenizer_load failed%s", "");
     }
     free(t);
     return 0;
@@ -961,27 +958,6 @@ EC_EXPORT void gpt2_free(GPT2 *g)
 /* forward                                                              */
 /* ------------------------------------------------------------------ */
 
-static int ec_pick_nsplit(const ec_dev *d, int max_len)
-{
-    /* ~64 positions per split, power of two, each split <= 1024 positions */
-    int need = (max_len + 63) / 64;
-    int ns = 1;
-    while (ns < need && ns < 64) ns *= 2;
-    while ((max_len + ns - 1) / ns > 1024) ns *= 2;
-    (void)d;
-    return ns;
-}
-
-/* Attended-length bucket for a call whose rows attend at most max_len
- * positions: a power of two >= 64, capped at eff_ctx.  Graphs and the
- * attention launch shape are keyed by it. */
-static int ec_len_bucket(const ec_dev *d, int max_len)
-{
-    int b = 64;
-    while (b < max_len) b *= 2;
-    return b < d->C ? b : d->C;
-}
-
 static ec_tokens ec_tk(const ec_dev *d)
 {
     ec_tokens tk;
@@ -1010,7 +986,7 @@ static ec_kvgeo ec_geo(const ec_dev *d, int l)
 static int ec_prof_begin(ec_dev *d, int cls, double bytes)
 {
     if (!d->prof_on || d->prof_n >= EC_PROF_MAX) return -1;
-    int i = d->prof_n++;
+    const int i = d->prof_n++;
     d->prof_cls[i] = cls;
     d->prof_bytes[i] = bytes;
     cudaEventRecord(d->prof_ev[2 * i], d->stream);
@@ -1026,35 +1002,38 @@ static void ec_prof_end(ec_dev *d, int i)
  * activations in, outputs out. */
 static double ec_lin_bytes(const ec_lin *l, int M)
 {
-    double elt = l->wt == EC_W_I8 ? 1.0 : 2.0;
-    return (double)l->N * l->K * elt + (l->s ? 4.0 * l->N : 0.0) + (l->b ? 4.0 * l->N : 0.0) +
-           4.0 * M * l->K + 4.0 * M * l->N;
+    const double elt = l->wt == EC_W_I8 ? 1.0 : 2.0;
+    return (double)l->N * l->K * elt + (l->s ? 4.0 * l->N : 0.0) + (l->b ? 4.0 * l->N : 0.0) + 4.0 * M * l->K +
+           4.0 * M * l->N;
 }
 
-/* One linear: GEMV (M <= 8, fused epilogue) or the generic GEMM path. */
-static int ec_linear(ec_dev *d, const ec_lin *l, const float *X, int ldx, int M, float *out, int ldo,
-                     int epi, int l_idx)
+/* Algorithmic HBM bytes of one decode step of M rows whose attention reads
+ * `kv_positions` cached positions per row on average. */
+static double ec_step_bytes(const ec_dev *d, int M, double kv_positions)
+{
+    double b = 0.0;
+    for (int l = 0; l < d->L; l++) {
+        const ec_dlayer *W = &d->lw[l];
+        b += ec_lin_bytes(&W->qkv, M) + ec_lin_bytes(&W->o, M) + ec_lin_bytes(&W->up, M) + ec_lin_bytes(&W->down, M);
+        b += 4.0 * 4 * d->E;                                         /* norm gains/biases */
+    }
+    const ec_lin lm = ec_lm_lin(d);
+    b += ec_lin_bytes(&lm, M);
+    b += (double)M * d->L * 2.0 * d->kv * 2.0 * kv_positions;       /* K and V reads */
+    b += (double)M * d->L * 2.0 * d->kv * 2.0;                      /* K and V writes */
+    b += (double)M * d->E * 2.0;                                     /* embedding row */
+    return b;
+}
+
+/* One linear on the generic GEMM path (any M): out = X . W^T with epilogue. */
+static int ec_linear(ec_dev *d, const ec_lin *l, const float *X, int ldx, int M, float *out, int ldo, int epi)
 {
     cudaStream_t st = d->stream;
-    if (M <= 8) {
-        ec_gemv_args a;
-        memset(&a, 0, sizeof a);
-        a.W = l->w; a.wscale = l->s; a.bias = l->b;
-        a.wt = l->wt; a.N = l->N; a.K = l->K; a.Kp = l->Kp;
-        a.blocks = l->blocks; a.nblocks = l->nblocks; a.block_rows = l->block_rows;
-        a.X = X; a.ldx = ldx; a.M = M;
-        a.out = out; a.ldo = ldo; a.epi = epi;
-        if (epi == EC_EPI_QKV) { a.tk = ec_tk(d); a.geo = ec_geo(d, l_idx); }
-        int pi = ec_prof_begin(d, l == &d->lm_lin ? EC_PC_LMHEAD : EC_PC_GEMV, ec_lin_bytes(l, M));
-        CK(ec_launch_gemv(&a, d->num_sms, st));
-        ec_prof_end(d, pi);
-        return 0;
-    }
-    /* generic path: plain GEMM into a temporary then the fused-epilogue work */
     ec_gemm_args g;
     memset(&g, 0, sizeof g);
     g.W = l->w; g.wscale = l->s; g.bias = l->b;
-    g.wt = l->wt; g.N = l->N; g.K = l->K; g.Kp = l->Kp; g.M = M;
+    g.wt = l->wt; g.N = l->N; g.K = l->K; g.Kp = l->Kp; g.ldw = l->ldw; g.M = M;
+    int pi = ec_prof_begin(d, EC_PC_GEMM, ec_lin_bytes(l, M));
     if (l->wt == EC_W_I8) {
         CK(ec_launch_quant(d->aq, d->as, X, ldx, M, l->K, l->Kp, st));
         g.Aq = d->aq;
@@ -1063,63 +1042,53 @@ static int ec_linear(ec_dev *d, const ec_lin *l, const float *X, int ldx, int M,
         g.X = X;
         g.ldx = ldx;
     }
-    if (epi == EC_EPI_STORE || epi == EC_EPI_RESID || epi == EC_EPI_GELU) {
-        g.out = out; g.ldo = ldo; g.epi = epi;
-        CK(ec_launch_gemm(&g, st));
-        return 0;
-    }
-    if (epi == EC_EPI_SWIGLU) {
-        /* gate|up side by side into `big` [M][2I], then silu(gate)*up */
-        g.out = d->big; g.ldo = l->N; g.epi = EC_EPI_STORE;
-        CK(ec_launch_gemm(&g, st));
-        CK(ec_launch_swiglu(out, ldo, d->big, l->N, d->I, M, st));
-        return 0;
-    }
-    /* EC_EPI_QKV: q|k|v rows into `out` (row stride ldo = E + 2kv), then
-     * RoPE + KV store in place; q stays in the first E columns */
-    g.out = out; g.ldo = ldo; g.epi = EC_EPI_STORE;
+    g.out = out; g.ldo = ldo; g.epi = epi;
     CK(ec_launch_gemm(&g, st));
-    CK(ec_launch_rope_kv(out, ldo, ec_tk(d), ec_geo(d, l_idx), d->H, d->KVH, M, st));
+    ec_prof_end(d, pi);
     return 0;
 }
 
-/* Enqueue the layer stack and the final norm for M rows whose inputs are
- * already in d_tok/d_pos/d_slot.  Leaves the normed final hidden state in h. */
+/* Per-layer kernels for rows already staged in d_tok/d_pos/d_slot: the
+ * prefill path.  Leaves the normed final hidden state in d->h. */
 static int ec_enqueue_body(ec_dev *d, int M, int maxlen)
 {
     cudaStream_t st = d->stream;
-    const int E = d->E;
+    const int E = d->E, ldqkv = E + 2 * d->kv;
     int pi = ec_prof_begin(d, EC_PC_OTHER, 0.0);
     CK(ec_launch_embed(d->x, d->wte, d->wpe, d->Ep, d->prec == 2, ec_tk(d), M, E, d->V, d->C, st));
     ec_prof_end(d, pi);
     if (d->taps_on && d->taps && M <= d->taps_rows)
         CK(cudaMemcpyAsync(d->taps, d->x, (size_t)M * E * 4, cudaMemcpyDeviceToDevice, st));
-    const int ldqkv = E + 2 * d->kv;
     ec_attn_args at;
     memset(&at, 0, sizeof at);
-    at.q = d->qkv; at.ldq = ldqkv; at.out = d->att; at.ldo = E;
+    at.q = d->q; at.ldq = E; at.out = d->att; at.ldo = E;
     at.tk = ec_tk(d); at.H = d->H; at.KVH = d->KVH; at.M = M; at.window = d->window;
-    at.part = d->attn_part; at.maxlen = maxlen; at.nsplit = ec_pick_nsplit(d, maxlen);
-    /* q lands in the first E columns of d->qkv (row stride E + 2kv) on both
-     * the GEMV (fused epilogue) and GEMM (rope_kv pass) paths. */
+    at.part = d->attn_part; at.maxlen = maxlen; at.nsplit = ec_pick_nsplit(maxlen);
+    const int wact = d->arch == ARCH_QWEN2 ? d->I : 4 * E;
     for (int l = 0; l < d->L; l++) {
         ec_dlayer *W = &d->lw[l];
         pi = ec_prof_begin(d, EC_PC_NORM, 8.0 * M * E);
         CK(ec_launch_norm(d->h, d->x, W->n1g, W->n1b, M, E, d->eps, st));
         ec_prof_end(d, pi);
-        if (ec_linear(d, &W->qkv, d->h, E, M, d->qkv, ldqkv, EC_EPI_QKV, l)) return -1;
+        if (ec_linear(d, &W->qkv, d->h, E, M, d->qkv, ldqkv, EC_EPI_STORE)) return -1;
+        pi = ec_prof_begin(d, EC_PC_OTHER, 0.0);
+        CK(ec_launch_qkv_split(d->q, d->qkv, ldqkv, ec_tk(d), ec_geo(d, l), d->H, d->KVH, d->arch == ARCH_QWEN2, M, st));
+        ec_prof_end(d, pi);
         at.geo = ec_geo(d, l);
         pi = ec_prof_begin(d, EC_PC_ATTN, 0.0);
         CK(ec_launch_attention(&at, st));
         ec_prof_end(d, pi);
-        if (ec_linear(d, &W->o, d->att, E, M, d->x, E, EC_EPI_RESID, l)) return -1;
+        if (ec_linear(d, &W->o, d->att, E, M, d->x, E, EC_EPI_RESID)) return -1;
         pi = ec_prof_begin(d, EC_PC_NORM, 8.0 * M * E);
         CK(ec_launch_norm(d->h, d->x, W->n2g, W->n2b, M, E, d->eps, st));
         ec_prof_end(d, pi);
-        const int wact = d->arch == ARCH_QWEN2 ? d->I : 4 * E;
-        if (ec_linear(d, &W->up, d->h, E, M, d->act, wact,
-                      d->arch == ARCH_QWEN2 ? EC_EPI_SWIGLU : EC_EPI_GELU, l)) return -1;
-        if (ec_linear(d, &W->down, d->act, wact, M, d->x, E, EC_EPI_RESID, l)) return -1;
+        if (d->arch == ARCH_QWEN2) {
+            if (ec_linear(d, &W->up, d->h, E, M, d->big, 2 * d->I, EC_EPI_STORE)) return -1;
+            CK(ec_launch_swiglu(d->act, d->I, d->big, 2 * d->I, d->I, M, st));
+        } else {
+            if (ec_linear(d, &W->up, d->h, E, M, d->act, wact, EC_EPI_GELU)) return -1;
+        }
+        if (ec_linear(d, &W->down, d->act, wact, M, d->x, E, EC_EPI_RESID)) return -1;
         if (d->taps_on && d->taps && M <= d->taps_rows)
             CK(cudaMemcpyAsync(d->taps + (size_t)(l + 1) * M * E, d->x, (size_t)M * E * 4, cudaMemcpyDeviceToDevice, st));
     }
@@ -1132,7 +1101,8 @@ static int ec_enqueue_body(ec_dev *d, int M, int maxlen)
 /* lm_head rows [r0, r0+rows) of h -> d->logits [rows][v1-v0]. */
 static int ec_enqueue_lm(ec_dev *d, int r0, int rows)
 {
-    return ec_linear(d, &d->lm_lin, d->h + (size_t)r0 * d->E, d->E, rows, d->logits, d->v1 - d->v0, EC_EPI_STORE, 0);
+    const ec_lin lm = ec_lm_lin(d);
+    return ec_linear(d, &lm, d->h + (size_t)r0 * d->E, d->E, rows, d->logits, d->v1 - d->v0, EC_EPI_STORE);
 }
 
 /* Validate host inputs and stage tok/pos/slot into the pinned buffer. */
@@ -1144,7 +1114,7 @@ static int ec_stage_inputs(ec_dev *d, const int *tokens, const int *positions, c
     CK(cudaStreamSynchronize(d->stream));   /* h_in may still feed a previous async copy */
     int *ht = d->h_in, *hp = d->h_in + M, *hs = d->h_in + 2 * M;
     for (int m = 0; m < M; m++) {
-        int t = tokens[m], p = positions[m];
+        const int t = tokens[m], p = positions[m];
         int s = seqs ? seqs[m] : m;
         if (s >= d->B) s = d->B - 1;   /* reference clamp, src/gpt2.c:512-513 */
         if (t < 0 || t >= d->V) { ec_seterr("token id %d out of range [0,%d)", t, d->V); return -1; }
@@ -1167,7 +1137,7 @@ static int ec_max_len(const ec_dev *d, int M)
 {
     int mx = 1;
     for (int m = 0; m < M; m++) {
-        int p = d->h_in[M + m];
+        const int p = d->h_in[M + m];
         int lo = d->window > 0 ? p - d->window + 1 : 0;
         if (lo < 0) lo = 0;
         if (p + 1 - lo > mx) mx = p + 1 - lo;
@@ -1175,85 +1145,90 @@ static int ec_max_len(const ec_dev *d, int M)
     return mx;
 }
 
-/* Find or capture the graph for (kind, M, maxlen). kind 0: body + lm_head
- * (M <= 8), kind 1: body + lm_head + argmax, kind 2: decode step (kind 1 +
- * step bookkeeping, recording ids in d_hist), kind 3: decode step without
- * the id history. */
-static cudaGraphExec_t ec_graph_get(ec_dev *d, int kind, int M, int maxlen);
-
-static int ec_enqueue_step(ec_dev *d, int kind, int M, int maxlen)
-{
-    if (ec_enqueue_body(d, M, maxlen)) return -1;
-    if (ec_enqueue_lm(d, 0, M)) return -1;
-    int pi = ec_prof_begin(d, EC_PC_OTHER, 0.0);
-    if (kind >= 1) {
-        CK(ec_launch_argmax(d->d_ids, d->d_max, d->logits, d->v1 - d->v0, d->v1 - d->v0, M, d->v0,
-                            d->amax_part, d->amax_chunks, d->stream));
-    }
-    if (kind >= 2)
-        CK(ec_launch_step_advance(d->d_tok, d->d_pos, d->d_ids, M, kind == 2 ? d->d_hist : NULL, d->d_counter,
-                                  d->wrap_lo, d->wrap_hi, d->stream));
-    ec_prof_end(d, pi);
-    return 0;
-}
-
-static cudaGraphExec_t ec_graph_get(ec_dev *d, int kind, int M, int maxlen)
-{
-    for (int i = 0; i < d->ngraphs; i++)
-        if (d->graphs[i].kind == kind && d->graphs[i].M == M && d->graphs[i].maxlen == maxlen &&
-            (kind < 2 || (d->graphs[i].wrap_lo == d->wrap_lo && d->graphs[i].wrap_hi == d->wrap_hi)))
-            return d->graphs[i].exec;
-    if (d->ngraphs == EC_MAX_GRAPHS) {
-        cudaGraphExecDestroy(d->graphs[0].exec);
-        memmove(&d->graphs[0], &d->graphs[1], sizeof(ec_graph) * (EC_MAX_GRAPHS - 1));
-        d->ngraphs--;
-    }
-    cudaGraph_t gr = NULL;
-    cudaGraphExec_t ex = NULL;
-    if (cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
-        ec_seterr("begin capture failed");
-        return NULL;
-    }
-    int rc = ec_enqueue_step(d, kind, M, maxlen);
-    cudaError_t e = cudaStreamEndCapture(d->stream, &gr);
-    if (rc || e != cudaSuccess) {
-        if (!rc) ec_seterr("end capture: %s", cudaGetErrorString(e));
-        if (gr) cudaGraphDestroy(gr);
-        cudaGetLastError();
-        return NULL;
-    }
-    e = cudaGraphInstantiate(&ex, gr, 0);
-    cudaGraphDestroy(gr);
-    if (e != cudaSuccess) { ec_seterr("graph instantiate: %s", cudaGetErrorString(e)); return NULL; }
-    d->graphs[d->ngraphs].kind = kind;
-    d->graphs[d->ngraphs].M = M;
-    d->graphs[d->ngraphs].maxlen = maxlen;
-    d->graphs[d->ngraphs].wrap_lo = d->wrap_lo;
-    d->graphs[d->ngraphs].wrap_hi = d->wrap_hi;
-    d->graphs[d->ngraphs].exec = ex;
-    d->ngraphs++;
-    return ex;
-}
-
 static int ec_check_kernel_error(ec_dev *d)
 {
-    int code = 0;
+    int code = 0, mk = 0;
     CK(ec_kernel_error_take(d->stream, &code));
-    if (code) { ec_seterr("device kernel reported error code %d (bad index or wait timeout)", code); return -1; }
+    CK(cudaMemcpy(&mk, d->d_mk_err, 4, cudaMemcpyDeviceToHost));
+    if (mk) CK(cudaMemset(d->d_mk_err, 0, 4));
+    if (code || mk) {
+        ec_seterr("device kernel reported error code %d/%d (bad index or bounded wait gave up)", code, mk);
+        return -1;
+    }
     return 0;
 }
 
-static int ec_use_graphs(void)
+/* ---- the persistent decode kernel ---- */
+
+/* Fill the kernel parameters for M rows attending at most maxlen positions;
+ * returns -1 if the kernel cannot take this call (shared memory). */
+static int ec_mk_plan(ec_dev *d, int M, int maxlen, ec_mk_params *p)
 {
-    static int v = -1;
-    if (v < 0) {
-        const char *s = getenv("EDGECORE_B200_GRAPHS");
-        v = s ? atoi(s) != 0 : 1;
+    if (!d->mk_grid || M < 1 || M > EC_MK_MT) return -1;
+    /* 16-byte asynchronous copies of q rows and cached K/V rows */
+    if (d->hd % 8 || d->kv % 8 || d->E % 4) return -1;
+    memset(p, 0, sizeof *p);
+    p->L = d->L;   /* the layer table and the norm vectors are part of the shared-memory layout */
+    p->E = d->E;
+    const int Kdown = d->lw[0].down.Kp, Kmax = d->Ep > Kdown ? d->Ep : Kdown;
+    const int opb = d->wt == EC_W_I8 ? 1 : 4;
+    int xbuf = M * Kmax * opb;
+    if (M * d->Ep * 4 > xbuf) xbuf = M * d->Ep * 4;           /* lm_head fp32 planes */
+    xbuf = (xbuf + 15) & ~15;
+    int stage = M * d->E * 4;                                  /* norm rows */
+    stage = (stage + 15) & ~15;
+    const int limit = ec_mk_smem_limit();
+    /* attention scratch (q row, scores, one K and one V chunk) overlays xbuf+stage */
+    int ch = 256;
+    while (ch > 8 && ch / 2 >= maxlen) ch /= 2;
+    for (;;) {
+        const int attn = 4 * ((d->hd + 3) & ~3) + 4 * ((maxlen + 3) & ~3) + ch * (d->hd + 8) * 2 + ch * d->hd * 2 + 64;
+        p->xbuf_bytes = xbuf;
+        p->stage_bytes = attn - xbuf > stage ? ((attn - xbuf + 15) & ~15) : stage;
+        if ((int)ec_mk_smem_bytes(p) <= limit) break;
+        if (ch <= 8) return -1;
+        ch /= 2;
     }
-    return v;
+    p->kvchunk = ch;
+    const int want = (M * Kdown * 4 + 15) & ~15;               /* down-proj input staged */
+    if (want > p->stage_bytes) {
+        const int keep = p->stage_bytes;
+        p->stage_bytes = want;
+        if ((int)ec_mk_smem_bytes(p) > limit) p->stage_bytes = keep;
+    }
+    p->arch = d->arch;
+    p->lwt = d->wt;
+    p->hwt = d->hwt;
+    p->L = d->L; p->E = d->E; p->H = d->H; p->KVH = d->KVH; p->hd = d->hd; p->kv = d->kv; p->I = d->I;
+    p->V = d->V; p->C = d->C; p->B = d->B; p->window = d->window; p->M = M;
+    p->eps = d->eps;
+    p->wte = d->wte; p->wpe = d->wpe; p->ld_emb = d->Ep; p->emb_bf16 = d->prec == 2;
+    p->nfg = d->nfg; p->nfb = d->nfb;
+    const ec_lin lm = ec_lm_lin(d);
+    p->lm = ec_mk_of(&lm);
+    if (p->lm.tile_rows <= 0) return -1;
+    p->v0 = d->v0;
+    p->rope_cos = d->rope_cos; p->rope_sin = d->rope_sin;
+    p->layers = d->d_mk_layers;
+    p->x = d->x; p->q = d->q; p->att = d->att; p->act = d->act;
+    p->amax_v = d->amax_v; p->amax_i = d->amax_i;
+    p->tok = d->d_tok; p->pos = d->d_pos; p->slot = d->d_slot;
+    p->bar = d->d_bar; p->abort_flag = d->d_abort; p->err = d->d_mk_err;
+    p->maxlen = maxlen;
+    p->taps = (d->taps_on && d->taps && M <= d->taps_rows) ? d->taps : NULL;
+    return 0;
 }
 
-/* Forward to host logits (or host argmax when ids != NULL). */
+static int ec_mk_run(ec_dev *d, const ec_mk_params *p, int n_steps)
+{
+    CK(cudaMemsetAsync(d->d_bar, 0, 4, d->stream));
+    CK(cudaMemsetAsync(d->d_abort, 0, 4, d->stream));
+    CK(ec_mk_launch(p, n_steps, d->mk_grid, d->stream));
+    return 0;
+}
+
+/* ---- host-array forward ---- */
+
 static int ec_forward_impl(GPT2 *g, const int *tokens, const int *positions, const int *seqs, int M,
                            float *logits, int *ids, float *maxv)
 {
@@ -1265,18 +1240,15 @@ static int ec_forward_impl(GPT2 *g, const int *tokens, const int *positions, con
     if (ec_stage_inputs(d, tokens, positions, seqs, M)) return -1;
     const int maxlen = ec_len_bucket(d, ec_max_len(d, M));
     const int Vs = d->v1 - d->v0;
-    if (ec_ensure_attn(d, M, maxlen)) return -1;
     if (ec_copy_inputs(d, M)) return -1;
-    if (M <= 8) {
-        if (ec_ensure_logits(d, 8) || ec_ensure_amax(d, 8)) return -1;
-        const int kind = ids ? 1 : 0;
-        if (ec_use_graphs() && !d->taps_on) {
-            cudaGraphExec_t ex = ec_graph_get(d, kind, M, maxlen);
-            if (!ex) return -1;
-            CK(cudaGraphLaunch(ex, d->stream));
-        } else if (ec_enqueue_step(d, kind, M, maxlen)) {
-            return -1;
-        }
+    ec_mk_params mp;
+    if (ec_mk_plan(d, M, maxlen, &mp) == 0) {
+        if (!ids && ec_ensure_logits(d, M)) return -1;
+        mp.logits = ids ? NULL : d->logits;
+        mp.ids = d->d_ids;
+        mp.maxv = d->d_max;
+        mp.advance = 0;
+        if (ec_mk_run(d, &mp, 1)) return -1;
         if (ids) {
             CK(cudaMemcpyAsync(d->h_ids, d->d_ids, (size_t)M * 4, cudaMemcpyDeviceToHost, d->stream));
             CK(cudaMemcpyAsync(d->h_max, d->d_max, (size_t)M * 4, cudaMemcpyDeviceToHost, d->stream));
@@ -1284,7 +1256,7 @@ static int ec_forward_impl(GPT2 *g, const int *tokens, const int *positions, con
             memcpy(ids, d->h_ids, (size_t)M * 4);
             if (maxv) memcpy(maxv, d->h_max, (size_t)M * 4);
         } else {
-            size_t bytes = (size_t)M * Vs * 4;
+            const size_t bytes = (size_t)M * Vs * 4;
             if (bytes > d->h_logits_cap) {
                 cudaFreeHost(d->h_logits);
                 d->h_logits = NULL;
@@ -1297,13 +1269,14 @@ static int ec_forward_impl(GPT2 *g, const int *tokens, const int *positions, con
         }
         return ec_check_kernel_error(d);
     }
-    /* prefill-shaped: direct launches, lm_head in row chunks */
+    /* prefill path: per-layer kernels, lm_head in row chunks */
+    if (ec_ensure_attn(d, M, maxlen)) return -1;
     if (ec_enqueue_body(d, M, maxlen)) return -1;
     int chunk = (int)((256u << 20) / ((size_t)Vs * 4));
     if (chunk < 8) chunk = 8;
     if (chunk > M) chunk = M;
     if (ec_ensure_logits(d, chunk) || ec_ensure_amax(d, chunk)) return -1;
-    size_t hbytes = (size_t)chunk * Vs * 4;
+    const size_t hbytes = (size_t)chunk * Vs * 4;
     if (!ids && hbytes > d->h_logits_cap) {
         cudaFreeHost(d->h_logits);
         d->h_logits = NULL;
@@ -1311,7 +1284,7 @@ static int ec_forward_impl(GPT2 *g, const int *tokens, const int *positions, con
         d->h_logits_cap = hbytes;
     }
     for (int r0 = 0; r0 < M; r0 += chunk) {
-        int rows = M - r0 < chunk ? M - r0 : chunk;
+        const int rows = M - r0 < chunk ? M - r0 : chunk;
         if (ec_enqueue_lm(d, r0, rows)) return -1;
         if (ids) {
             CK(ec_launch_argmax(d->d_ids + r0, d->d_max + r0, d->logits, Vs, Vs, rows, d->v0, d->amax_part,
@@ -1367,9 +1340,9 @@ EC_EXPORT int ec_model_info(const GPT2 *g, int *o)
 {
     ec_dev *d = ec_lookup(g);
     if (!d) { ec_seterr("model not loaded"); return -1; }
-    int v[16] = {g->arch, g->precision, g->n_layer, g->n_head, g->n_kv_head, g->n_embd, g->head_dim,
-                 g->intermediate, g->vocab, g->n_ctx, gpt2_eff_ctx(g), g->batch_cap, g->n_kv_embd,
-                 g->tie_word_embeddings, d->device, 0};
+    const int v[16] = {g->arch, g->precision, g->n_layer, g->n_head, g->n_kv_head, g->n_embd, g->head_dim,
+                       g->intermediate, g->vocab, g->n_ctx, gpt2_eff_ctx(g), g->batch_cap, g->n_kv_embd,
+                       g->tie_word_embeddings, d->device, 0};
     memcpy(o, v, sizeof v);
     return 0;
 }
@@ -1391,10 +1364,10 @@ EC_EXPORT int ec_forward_device(GPT2 *g, const int *d_tokens, const int *d_posit
 {
     ec_dev *d = ec_lookup(g);
     if (!d) { ec_seterr("model not loaded"); return -1; }
-    if (M < 1 || M > 8) { ec_seterr("ec_forward_device: 1 <= M <= 8"); return -1; }
-    if (ec_ensure(d, M) || ec_ensure_logits(d, 8) || ec_ensure_amax(d, 8)) return -1;
-    int maxlen = ec_len_bucket(d, d->C);
-    if (ec_ensure_attn(d, M, maxlen)) return -1;
+    if (M < 1 || M > EC_MK_MT) { ec_seterr("ec_forward_device: 1 <= M <= %d", EC_MK_MT); return -1; }
+    if (ec_ensure(d, M)) return -1;
+    ec_mk_params mp;
+    if (ec_mk_plan(d, M, d->C, &mp)) { ec_seterr("ec_forward_device: eff_ctx too long for the decode kernel"); return -1; }
     CK(cudaStreamSynchronize(d->stream));   /* h_in reuse */
     CK(cudaMemcpyAsync(d->d_tok, d_tokens, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
     CK(cudaMemcpyAsync(d->d_pos, d_positions, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
@@ -1404,11 +1377,9 @@ EC_EXPORT int ec_forward_device(GPT2 *g, const int *d_tokens, const int *d_posit
         for (int m = 0; m < M; m++) d->h_in[2 * M + m] = m < d->B ? m : d->B - 1;
         CK(cudaMemcpyAsync(d->d_slot, d->h_in + 2 * M, (size_t)M * 4, cudaMemcpyHostToDevice, d->stream));
     }
-    cudaGraphExec_t ex = ec_graph_get(d, 0, M, maxlen);
-    if (!ex) return -1;
-    CK(cudaGraphLaunch(ex, d->stream));
-    CK(cudaMemcpyAsync(d_logits, d->logits, (size_t)M * (d->v1 - d->v0) * 4, cudaMemcpyDeviceToDevice, d->stream));
-    return 0;
+    mp.logits = d_logits;
+    mp.advance = 0;
+    return ec_mk_run(d, &mp, 1);
 }
 
 EC_EXPORT int ec_forward_argmax(GPT2 *g, const int *tokens, const int *positions, const int *seqs, int M,
@@ -1424,9 +1395,19 @@ EC_EXPORT int ec_forward_shard_argmax(GPT2 *g, const int *tokens, const int *pos
     return ec_forward_argmax(g, tokens, positions, seqs, M, out_ids, out_max);
 }
 
-EC_EXPORT int ec_decode_greedy(GPT2 *g, int *d_tokens, int start_pos, int n_steps, int *d_out_ids)
+/* Stage a decode run: tokens from device, positions start_pos, slots 0..M-1. */
+static int ec_decode_setup(ec_dev *d, int *d_tokens, int start_pos, int M)
 {
-    return ec_decode_greedy_cycle(g, d_tokens, start_pos, 0, n_steps, d_out_ids);
+    if (ec_ensure(d, M)) return -1;
+    CK(cudaStreamSynchronize(d->stream));   /* h_in reuse */
+    for (int m = 0; m < M; m++) {
+        d->h_in[M + m] = start_pos;
+        d->h_in[2 * M + m] = m;
+    }
+    CK(cudaMemcpyAsync(d->d_tok, d_tokens, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
+    CK(cudaMemcpyAsync(d->d_pos, d->h_in + M, (size_t)M * 4, cudaMemcpyHostToDevice, d->stream));
+    CK(cudaMemcpyAsync(d->d_slot, d->h_in + 2 * M, (size_t)M * 4, cudaMemcpyHostToDevice, d->stream));
+    return 0;
 }
 
 EC_EXPORT int ec_decode_greedy_cycle(GPT2 *g, int *d_tokens, int start_pos, int period, int n_steps,
@@ -1435,51 +1416,142 @@ EC_EXPORT int ec_decode_greedy_cycle(GPT2 *g, int *d_tokens, int start_pos, int 
     ec_dev *d = ec_lookup(g);
     if (!d) { ec_seterr("model not loaded"); return -1; }
     const int M = d->B;
-    if (M > 8) { ec_seterr("ec_decode_greedy: batch_cap must be <= 8 (got %d)", M); return -1; }
+    if (M > EC_MK_MT) { ec_seterr("ec_decode_greedy: batch_cap must be <= %d (got %d)", EC_MK_MT, M); return -1; }
     const int span = period > 0 && period < n_steps ? period : n_steps;
     if (n_steps < 0 || period < 0 || start_pos < 0 || start_pos + span > d->C) {
         ec_seterr("decode range [%d, %d) exceeds eff_ctx %d", start_pos, start_pos + span, d->C);
         return -1;
     }
     if (n_steps == 0) return 0;
-    if (ec_ensure(d, M) || ec_ensure_logits(d, 8) || ec_ensure_amax(d, 8)) return -1;
-    d->wrap_lo = period > 0 ? start_pos : 0;
-    d->wrap_hi = period > 0 ? start_pos + period : 0;
     int max_len = start_pos + span;
     if (d->window > 0 && max_len > d->window) max_len = d->window;
-    int maxlen = ec_len_bucket(d, max_len);
-    if (ec_ensure_attn(d, M, maxlen)) return -1;
+    ec_mk_params mp;
+    if (ec_mk_plan(d, M, ec_len_bucket(d, max_len), &mp)) {
+        ec_seterr("decode range too long for the decode kernel's shared memory");
+        return -1;
+    }
     if (d_out_ids && d->hist_cap < n_steps * M) {
-        ec_free_graphs(d);
+        CK(cudaStreamSynchronize(d->stream));
         cudaFree(d->d_hist);
         d->d_hist = NULL;
         CK(cudaMalloc((void **)&d->d_hist, (size_t)n_steps * M * 4));
         d->hist_cap = n_steps * M;
     }
-    CK(cudaStreamSynchronize(d->stream));   /* h_in reuse */
-    for (int m = 0; m < M; m++) {
-        d->h_in[M + m] = start_pos;
-        d->h_in[2 * M + m] = m;
+    if (ec_decode_setup(d, d_tokens, start_pos, M)) return -1;
+    mp.hist = d_out_ids ? d->d_hist : NULL;
+    mp.advance = 1;
+    mp.wrap_lo = period > 0 ? start_pos : 0;
+    mp.wrap_hi = period > 0 ? start_pos + period : 0;
+    if (ec_mk_run(d, &mp, n_steps)) return -1;
+    if (d_out_ids)
+        CK(cudaMemcpyAsync(d_out_ids, d->d_hist, (size_t)n_steps * M * 4, cudaMemcpyDeviceToDevice, d->stream));
+    CK(cudaMemcpyAsync(d_tokens, d->d_tok, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
+    return 0;
+}
+
+EC_EXPORT int ec_decode_greedy(GPT2 *g, int *d_tokens, int start_pos, int n_steps, int *d_out_ids)
+{
+    return ec_decode_greedy_cycle(g, d_tokens, start_pos, 0, n_steps, d_out_ids);
+}
+
+/* Instrumented decode: each step is one launch of the persistent kernel with
+ * an event pair around it (class 0), so out[0..2] = {ms, algorithmic bytes,
+ * launches} of that kernel.  Models the kernel cannot take fall back to the
+ * per-layer kernels with an event pair around every launch. */
+EC_EXPORT int ec_decode_profile(GPT2 *g, int *d_tokens, int start_pos, int n_steps, double *out)
+{
+    ec_dev *d = ec_lookup(g);
+    if (!d) { ec_seterr("model not loaded"); return -1; }
+    const int M = d->B;
+    if (M > EC_MK_MT || n_steps < 1 || start_pos < 0 || start_pos + n_steps > d->C) { ec_seterr("bad profile range"); return -1; }
+    if (!d->prof_ready) {
+        for (int i = 0; i < 2 * EC_PROF_MAX; i++) CK(cudaEventCreate(&d->prof_ev[i]));
+        d->prof_ready = 1;
     }
-    int rc = 0;
-    if (cudaMemcpyAsync(d->d_tok, d_tokens, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream) != cudaSuccess ||
-        cudaMemcpyAsync(d->d_pos, d->h_in + M, (size_t)M * 4, cudaMemcpyHostToDevice, d->stream) != cudaSuccess ||
-        cudaMemcpyAsync(d->d_slot, d->h_in + 2 * M, (size_t)M * 4, cudaMemcpyHostToDevice, d->stream) != cudaSuccess ||
-        cudaMemsetAsync(d->d_counter, 0, 4, d->stream) != cudaSuccess) {
-        ec_seterr("decode setup copy failed");
-        rc = -1;
+    for (int i = 0; i < 16; i++) out[i] = 0.0;
+    const int maxlen = ec_len_bucket(d, start_pos + n_steps);
+    ec_mk_params mp;
+    if (ec_mk_plan(d, M, maxlen, &mp) == 0) {
+        if (ec_decode_setup(d, d_tokens, start_pos, M)) return -1;
+        mp.advance = 1;
+        for (int st = 0; st < n_steps; st++) {
+            CK(cudaMemsetAsync(d->d_bar, 0, 4, d->stream));
+            CK(cudaMemsetAsync(d->d_abort, 0, 4, d->stream));
+            CK(cudaEventRecord(d->prof_ev[0], d->stream));
+            CK(ec_mk_launch(&mp, 1, d->mk_grid, d->stream));
+            CK(cudaEventRecord(d->prof_ev[1], d->stream));
+            CK(cudaStreamSynchronize(d->stream));
+            float ms = 0.0f;
+            CK(cudaEventElapsedTime(&ms, d->prof_ev[0], d->prof_ev[1]));
+            out[EC_PC_STEP * 3 + 0] += ms;
+            out[EC_PC_STEP * 3 + 1] += ec_step_bytes(d, M, start_pos + st + 1);
+            out[EC_PC_STEP * 3 + 2] += 1.0;
+        }
+    } else {
+        if (ec_decode_setup(d, d_tokens, start_pos, M) || ec_ensure_logits(d, 8) || ec_ensure_amax(d, 8) ||
+            ec_ensure_attn(d, M, maxlen)) return -1;
+        for (int st = 0; st < n_steps; st++) {
+            d->prof_on = 1;
+            d->prof_n = 0;
+            int rc = ec_enqueue_body(d, M, maxlen) || ec_enqueue_lm(d, 0, M);
+            int pi = ec_prof_begin(d, EC_PC_OTHER, 0.0);
+            if (!rc && (ec_launch_argmax(d->d_ids, d->d_max, d->logits, d->v1 - d->v0, d->v1 - d->v0, M, d->v0,
+                                         d->amax_part, d->amax_chunks, d->stream) ||
+                        ec_launch_step_advance(d->d_tok, d->d_pos, d->d_ids, M, NULL, NULL, 0, 0, d->stream)))
+                rc = -1;
+            ec_prof_end(d, pi);
+            d->prof_on = 0;
+            if (rc) return -1;
+            CK(cudaStreamSynchronize(d->stream));
+            for (int i = 0; i < d->prof_n; i++) {
+                float ms = 0.0f;
+                CK(cudaEventElapsedTime(&ms, d->prof_ev[2 * i], d->prof_ev[2 * i + 1]));
+                out[d->prof_cls[i] * 3 + 0] += ms;
+                out[d->prof_cls[i] * 3 + 1] += d->prof_bytes[i];
+                out[d->prof_cls[i] * 3 + 2] += 1.0;
+            }
+        }
     }
-    cudaGraphExec_t ex = NULL;
-    if (!rc) {
-        ex = ec_graph_get(d, d_out_ids ? 2 : 3, M, maxlen);
-        if (!ex) rc = -1;
+    out[15] = n_steps;
+    CK(cudaMemcpyAsync(d_tokens, d->d_tok, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
+    CK(cudaStreamSynchronize(d->stream));
+    return ec_check_kernel_error(d);
+}
+
+/* One decode launch of n_steps with the timeline of CTA 0 recorded: host
+ * `out[cap]` receives (code << 56) | globaltimer-ns entries, those of the
+ * consumer thread first, then those of the producer thread; returns the
+ * number of entries or -1. */
+EC_EXPORT int ec_decode_trace(GPT2 *g, int *d_tokens, int start_pos, int n_steps, unsigned long long *out, int cap)
+{
+    ec_dev *d = ec_lookup(g);
+    if (!d) { ec_seterr("model not loaded"); return -1; }
+    const int M = d->B;
+    if (M > EC_MK_MT || n_steps < 1 || cap < 1 || start_pos < 0 || start_pos + n_steps > d->C) {
+        ec_seterr("bad trace range");
+        return -1;
     }
-    for (int i = 0; !rc && i < n_steps; i++)
-        if (cudaGraphLaunch(ex, d->stream) != cudaSuccess) { ec_seterr("graph launch failed"); rc = -1; }
-    if (!rc && d_out_ids)
-        if (cudaMemcpyAsync(d_out_ids, d->d_hist, (size_t)n_steps * M * 4, cudaMemcpyDeviceToDevice, d->stream) != cudaSuccess) rc = -1;
-    if (!rc && cudaMemcpyAsync(d_tokens, d->d_tok, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream) != cudaSuccess) rc = -1;
-    return rc;
+    ec_mk_params mp;
+    if (ec_mk_plan(d, M, ec_len_bucket(d, start_pos + n_steps), &mp)) { ec_seterr("decode kernel not applicable"); return -1; }
+    unsigned long long *dt = NULL;
+    CK(cudaMalloc((void **)&dt, (size_t)cap * 8));
+    CK(cudaMemsetAsync(dt, 0, (size_t)cap * 8, d->stream));
+    if (ec_decode_setup(d, d_tokens, start_pos, M)) { cudaFree(dt); return -1; }
+    mp.advance = 1;
+    mp.trace = dt;
+    mp.trace_cap = cap;
+    int rc = ec_mk_run(d, &mp, n_steps);
+    if (!rc && cudaMemcpyAsync(out, dt, (size_t)cap * 8, cudaMemcpyDeviceToHost, d->stream) != cudaSuccess) rc = -1;
+    if (!rc && cudaStreamSynchronize(d->stream) != cudaSuccess) rc = -1;
+    cudaFree(dt);
+    if (rc) { ec_seterr("traced decode failed"); return -1; }
+    /* compact the two halves (consumer thread, producer thread) */
+    const int half = cap / 2;
+    int n = 0;
+    for (int i = 0; i < half && out[i]; ++i) n++;
+    for (int i = half; i < cap && out[i]; ++i) out[n++] = out[i];
+    for (int i = n; i < cap; ++i) out[i] = 0;
+    return ec_check_kernel_error(d) ? -1 : n;
 }
 
 EC_EXPORT int ec_model_set_taps(GPT2 *g, int enable)
@@ -1488,6 +1560,7 @@ EC_EXPORT int ec_model_set_taps(GPT2 *g, int enable)
     if (!d) { ec_seterr("model not loaded"); return -1; }
     d->taps_on = enable > 0;
     if (d->taps_on && (!d->taps || d->taps_rows < enable)) {
+        CK(cudaStreamSynchronize(d->stream));
         cudaFree(d->taps);
         d->taps = NULL;
         CK(cudaMalloc((void **)&d->taps, (size_t)(d->L + 1) * enable * d->E * 4));
@@ -1529,50 +1602,4 @@ EC_EXPORT void ec_argmax_key_decode(uint64_t key, float *maxv, int *idx)
     b = (b & 0x80000000u) ? (b & 0x7fffffffu) : ~b;
     if (maxv) memcpy(maxv, &b, 4);
     if (idx) *idx = 0x7fffffff - (int)(uint32_t)(key & 0xffffffffu);
-}
-
-/* Instrumented decode: n_steps ungraphed greedy steps with a CUDA event pair
- * around every launch.  out[c*3 + {0,1,2}] = {total ms, total algorithmic
- * bytes, launches} for kernel class c (EC_PC_*); out[15] = steps. */
-EC_EXPORT int ec_decode_profile(GPT2 *g, int *d_tokens, int start_pos, int n_steps, double *out)
-{
-    ec_dev *d = ec_lookup(g);
-    if (!d) { ec_seterr("model not loaded"); return -1; }
-    const int M = d->B;
-    if (M > 8 || n_steps < 1 || start_pos < 0 || start_pos + n_steps > d->C) { ec_seterr("bad profile range"); return -1; }
-    if (ec_ensure(d, M) || ec_ensure_logits(d, 8) || ec_ensure_amax(d, 8)) return -1;
-    int max_len = start_pos + n_steps;
-    int maxlen = ec_len_bucket(d, max_len);
-    if (ec_ensure_attn(d, M, maxlen)) return -1;
-    if (!d->prof_ready) {
-        for (int i = 0; i < 2 * EC_PROF_MAX; i++) CK(cudaEventCreate(&d->prof_ev[i]));
-        d->prof_ready = 1;
-    }
-    CK(cudaStreamSynchronize(d->stream));
-    for (int m = 0; m < M; m++) { d->h_in[M + m] = start_pos; d->h_in[2 * M + m] = m; }
-    CK(cudaMemcpyAsync(d->d_tok, d_tokens, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
-    CK(cudaMemcpyAsync(d->d_pos, d->h_in + M, (size_t)M * 4, cudaMemcpyHostToDevice, d->stream));
-    CK(cudaMemcpyAsync(d->d_slot, d->h_in + 2 * M, (size_t)M * 4, cudaMemcpyHostToDevice, d->stream));
-    for (int i = 0; i < 16; i++) out[i] = 0.0;
-    d->wrap_lo = d->wrap_hi = 0;
-    for (int st = 0; st < n_steps; st++) {
-        d->prof_on = 1;
-        d->prof_n = 0;
-        int rc = ec_enqueue_step(d, 3, M, maxlen);
-        d->prof_on = 0;
-        if (rc) return -1;
-        CK(cudaStreamSynchronize(d->stream));
-        for (int i = 0; i < d->prof_n; i++) {
-            float ms = 0.0f;
-            CK(cudaEventElapsedTime(&ms, d->prof_ev[2 * i], d->prof_ev[2 * i + 1]));
-            int c = d->prof_cls[i];
-            out[c * 3 + 0] += ms;
-            out[c * 3 + 1] += d->prof_bytes[i];
-            out[c * 3 + 2] += 1.0;
-        }
-    }
-    out[15] = n_steps;
-    CK(cudaMemcpyAsync(d_tokens, d->d_tok, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
-    CK(cudaStreamSynchronize(d->stream));
-    return ec_check_kernel_error(d);
 }

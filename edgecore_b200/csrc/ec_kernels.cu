@@ -9,7 +9,7 @@
 //   k_gemm_simt   generic tiled GEMM for any M (prefill until the tcgen05 path
 //                 takes over), same numerics.
 //   k_quant       per-row activation quantisation (reference gpt2.c:446-461).
-//   k_embed, k_norm, k_rope_kv, k_swiglu, k_gelu, k_attn_part/k_attn_combine,
+//   k_embed, k_norm, k_qkv_split, k_swiglu, k_gelu, k_attn_exact, k_attn_part/combine,
 //   k_argmax*, k_step_advance.
 //
 // Every index that comes from the caller (token ids, positions, slots) is
@@ -40,10 +40,10 @@ struct GemvSmem {
 
 __host__ __device__ inline uint32_t ec_align16(uint32_t v) { return (v + 15u) & ~15u; }
 
-__host__ __device__ inline GemvSmem gemv_layout(int wt, int M, int Kp, int block_rows, int stages) {
+__host__ __device__ inline GemvSmem gemv_layout(int wt, int M, int Kp, int ldw, int block_rows, int stages) {
     GemvSmem s;
     const uint32_t elt = wt == EC_W_I8 ? 1u : 2u;
-    s.stage_bytes = ec_align16((uint32_t)block_rows * (uint32_t)Kp * elt);
+    s.stage_bytes = ec_align16((uint32_t)block_rows * (uint32_t)ldw * elt);
     uint32_t off = s.stage_bytes * (uint32_t)stages;
     s.x_off = off;
     off += ec_align16((uint32_t)M * (uint32_t)Kp * (wt == EC_W_I8 ? 1u : 4u));
@@ -97,7 +97,8 @@ k_gemv(const ec_gemv_args a, const int stages) {
     typedef typename GemvAcc<WT>::T Acc;
     extern __shared__ __align__(128) unsigned char smem[];
     const int M = a.M;
-    const GemvSmem L = gemv_layout(WT, M, a.Kp, a.block_rows, stages);
+    const int ldw = a.ldw ? a.ldw : a.Kp;
+    const GemvSmem L = gemv_layout(WT, M, a.Kp, ldw, a.block_rows, stages);
     unsigned char *stage0 = smem;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bar_off);
     Acc *val = reinterpret_cast<Acc *>(smem + L.val_off);
@@ -106,8 +107,8 @@ k_gemv(const ec_gemv_args a, const int stages) {
     float *red = reinterpret_cast<float *>(smem + L.red_off);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t elt = WT == EC_W_I8 ? 1u : 2u;
-    const uint32_t row_bytes = (uint32_t)a.Kp * elt;
-    const int nch = (int)(row_bytes / 16u);            // 16-byte chunks per row
+    const uint32_t row_bytes = (uint32_t)ldw * elt;   // staged row stride
+    const int nch = (int)((uint32_t)a.Kp * elt / 16u);  // 16-byte weight chunks per row
     const int nmine = (a.nblocks - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
     if (nmine <= 0) return;
 
@@ -381,10 +382,12 @@ extern "C" int ec_launch_gemv(const ec_gemv_args *a, int num_sms, cudaStream_t s
     const int cap = num_sms * per_sm_target;
     int stages = 1;
     if (grid > cap) { grid = cap; stages = 3; }
-    GemvSmem L = gemv_layout(a->wt, a->M, a->Kp, a->block_rows, stages);
+    const int ldw = a->ldw ? a->ldw : a->Kp;
+    if (ldw < a->Kp || (ldw * (a->wt == EC_W_I8 ? 1 : 2)) % 16 != 0) return (int)cudaErrorInvalidValue;
+    GemvSmem L = gemv_layout(a->wt, a->M, a->Kp, ldw, a->block_rows, stages);
     while (stages > 1 && (int)L.total > g_ec_max_optin_smem / per_sm_target) {
         --stages;
-        L = gemv_layout(a->wt, a->M, a->Kp, a->block_rows, stages);
+        L = gemv_layout(a->wt, a->M, a->Kp, ldw, a->block_rows, stages);
     }
     if ((int)L.total > g_ec_max_optin_smem) return (int)cudaErrorInvalidValue;
     switch (a->wt) {
@@ -439,7 +442,7 @@ __global__ void __launch_bounds__(256) k_gemm_i8(const ec_gemm_args a) {
             if (m0 + r < a.M && k0 + c < a.Kp)
                 va = *reinterpret_cast<const uint4 *>(a.Aq + (size_t)(m0 + r) * a.Kp + k0 + c);
             if (n0 + r < a.N && k0 + c < a.Kp)
-                vw = *reinterpret_cast<const uint4 *>(static_cast<const int8_t *>(a.W) + (size_t)(n0 + r) * a.Kp + k0 + c);
+                vw = *reinterpret_cast<const uint4 *>(static_cast<const int8_t *>(a.W) + (size_t)(n0 + r) * a.ldw + k0 + c);
             *reinterpret_cast<uint4 *>(&As[r][c]) = va;
             *reinterpret_cast<uint4 *>(&Ws[r][c]) = vw;
         }
@@ -482,7 +485,7 @@ __global__ void __launch_bounds__(256) k_gemm_f(const ec_gemm_args a) {
             const int r = e / BK, c = e % BK;
             const int k = k0 + c;
             As[c][r] = (m0 + r < a.M && k < a.K) ? a.X[(size_t)(m0 + r) * a.ldx + k] : 0.0f;
-            Ws[c][r] = (n0 + r < a.N && k < a.Kp) ? ec_h2f(W[(size_t)(n0 + r) * a.Kp + k], WT == EC_W_BF16) : 0.0f;
+            Ws[c][r] = (n0 + r < a.N && k < a.Kp) ? ec_h2f(W[(size_t)(n0 + r) * a.ldw + k], WT == EC_W_BF16) : 0.0f;
         }
         __syncthreads();
 #pragma unroll 8
@@ -508,14 +511,16 @@ __global__ void __launch_bounds__(256) k_gemm_f(const ec_gemm_args a) {
         }
 }
 
-extern "C" int ec_launch_gemm(const ec_gemm_args *a, cudaStream_t stream) {
-    if (a->M <= 0 || a->N <= 0) return 0;
-    if (a->Kp % 16) return (int)cudaErrorInvalidValue;
-    dim3 grid((a->N + GT_BN - 1) / GT_BN, (a->M + GT_BM - 1) / GT_BM);
+extern "C" int ec_launch_gemm(const ec_gemm_args *args, cudaStream_t stream) {
+    ec_gemm_args a = *args;
+    if (a.M <= 0 || a.N <= 0) return 0;
+    if (a.ldw == 0) a.ldw = a.Kp;
+    if (a.Kp % 16 || a.ldw < a.Kp || (a.ldw * (a.wt == EC_W_I8 ? 1 : 2)) % 16) return (int)cudaErrorInvalidValue;
+    dim3 grid((a.N + GT_BN - 1) / GT_BN, (a.M + GT_BM - 1) / GT_BM);
     if (grid.y > 65535) return (int)cudaErrorInvalidValue;
-    if (a->wt == EC_W_I8) k_gemm_i8<<<grid, 256, 0, stream>>>(*a);
-    else if (a->wt == EC_W_F16) k_gemm_f<EC_W_F16><<<grid, 256, 0, stream>>>(*a);
-    else k_gemm_f<EC_W_BF16><<<grid, 256, 0, stream>>>(*a);
+    if (a.wt == EC_W_I8) k_gemm_i8<<<grid, 256, 0, stream>>>(a);
+    else if (a.wt == EC_W_F16) k_gemm_f<EC_W_F16><<<grid, 256, 0, stream>>>(a);
+    else k_gemm_f<EC_W_BF16><<<grid, 256, 0, stream>>>(a);
     return (int)cudaGetLastError();
 }
 
@@ -634,48 +639,63 @@ extern "C" int ec_launch_norm(float *out, const float *x, const float *gamma, co
     return (int)cudaGetLastError();
 }
 
-// RoPE + KV store from a [M][ldq] buffer whose columns are q | k | v.
-__global__ void __launch_bounds__(256) k_rope_kv(float *qkv, int ldq, ec_tokens tk, ec_kvgeo g, int H, int KVH) {
+// Split the q|k|v rows of a GEMM output [M][ldq] (packed layout: RoPE
+// partners adjacent for Qwen2 when packed != 0, file order for GPT-2): RoPE
+// q and k (fp64, reference src/gpt2.c:656-665), q -> q_out [M][E] in head
+// order, k and v -> fp16 KV cache at (slot, pos).
+__global__ void __launch_bounds__(256) k_qkv_split(float *q_out, const float *qkv, int ldq, ec_tokens tk,
+                                                   ec_kvgeo g, int H, int KVH, int packed) {
     const int m = blockIdx.x;
     const int pos = tk.pos[m], slot = tk.slot[m];
     if (pos < 0 || pos >= g.C || slot < 0 || slot >= g.B) {
         if (threadIdx.x == 0) atomicCAS(&g_ec_err, 0, EC_KERR_BAD_INDEX);
         return;
     }
-    float *row = qkv + (size_t)m * ldq;
-    const int half = g.hd >> 1;
-    if (g.rope_cos) {
+    const float *row = qkv + (size_t)m * ldq;
+    float *qo = q_out + (size_t)m * g.E;
+    uint16_t *kr = g.kc + ((size_t)slot * g.C + pos) * g.kv;
+    uint16_t *vr = g.vc + ((size_t)slot * g.C + pos) * g.kv;
+    if (packed) {
+        const int half = g.hd >> 1;
         const int npairs = (H + KVH) * half;
         for (int idx = threadIdx.x; idx < npairs; idx += blockDim.x) {
             const int h = idx / half, i = idx % half;
-            float *v = row + (h < H ? h * g.hd : g.E + (h - H) * g.hd);
+            const float *v = row + (size_t)h * g.hd + 2 * i;
             const double c = g.rope_cos[(size_t)pos * half + i], s = g.rope_sin[(size_t)pos * half + i];
-            const double av = (double)v[i], bv = (double)v[i + half];
-            v[i] = (float)__dsub_rn(__dmul_rn(av, c), __dmul_rn(bv, s));
-            v[i + half] = (float)__dadd_rn(__dmul_rn(av, s), __dmul_rn(bv, c));
+            const double av = (double)v[0], bv = (double)v[1];
+            const float lo = (float)__dsub_rn(__dmul_rn(av, c), __dmul_rn(bv, s));
+            const float hi = (float)__dadd_rn(__dmul_rn(av, s), __dmul_rn(bv, c));
+            if (h < H) {
+                qo[h * g.hd + i] = lo;
+                qo[h * g.hd + i + half] = hi;
+            } else {
+                kr[(h - H) * g.hd + i] = ec_f2h(lo);
+                kr[(h - H) * g.hd + i + half] = ec_f2h(hi);
+            }
         }
-        __syncthreads();
-    }
-    uint16_t *kr = g.kc + ((size_t)slot * g.C + pos) * g.kv;
-    uint16_t *vr = g.vc + ((size_t)slot * g.C + pos) * g.kv;
-    for (int d = threadIdx.x; d < g.kv; d += blockDim.x) {
-        kr[d] = ec_f2h(row[g.E + d]);
-        vr[d] = ec_f2h(row[g.E + g.kv + d]);
+        for (int d = threadIdx.x; d < g.kv; d += blockDim.x) vr[d] = ec_f2h(row[g.E + g.kv + d]);
+    } else {
+        for (int n = threadIdx.x; n < g.E; n += blockDim.x) qo[n] = row[n];
+        for (int d = threadIdx.x; d < g.kv; d += blockDim.x) {
+            kr[d] = ec_f2h(row[g.E + d]);
+            vr[d] = ec_f2h(row[g.E + g.kv + d]);
+        }
     }
 }
 
-extern "C" int ec_launch_rope_kv(float *qkv, int ldq, ec_tokens tk, ec_kvgeo geo, int H, int KVH, int M,
-                                 cudaStream_t stream) {
+extern "C" int ec_launch_qkv_split(float *q_out, const float *qkv, int ldq, ec_tokens tk, ec_kvgeo geo, int H,
+                                   int KVH, int packed, int M, cudaStream_t stream) {
     if (M <= 0) return 0;
-    k_rope_kv<<<M, 256, 0, stream>>>(qkv, ldq, tk, geo, H, KVH);
+    k_qkv_split<<<M, 256, 0, stream>>>(q_out, qkv, ldq, tk, geo, H, KVH, packed);
     return (int)cudaGetLastError();
 }
 
+// out[m][j] = silu(gate) * up with gate|up interleaved: gu[m][2j], gu[m][2j+1].
 __global__ void k_swiglu(float *out, int ldo, const float *gu, int ldg, int I, int M) {
     const size_t n = (size_t)M * I;
     for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < n; idx += (size_t)gridDim.x * blockDim.x) {
         const size_t m = idx / I, j = idx % I;
-        const float g = gu[m * ldg + j], u = gu[m * ldg + I + j];
+        const float g = gu[m * ldg + 2 * j], u = gu[m * ldg + 2 * j + 1];
         out[m * ldo + j] = __fmul_rn(ec_silu(g), u);
     }
 }

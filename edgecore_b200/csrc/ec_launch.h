@@ -53,10 +53,11 @@ typedef struct {
 } ec_kvgeo;
 
 typedef struct {
-    const void *W;            /* [N][Kp] weights (type wt), row-major          */
+    const void *W;            /* [N][ldw] weights (type wt), row-major         */
     const float *wscale;      /* [N] per-row scale (int8 only)                 */
     const float *bias;        /* [N] or NULL                                   */
     int wt, N, K, Kp;
+    int ldw;                  /* row stride in elements (>= Kp; 0 means Kp)    */
     const ec_block *blocks;   /* device table                                   */
     int nblocks;
     int block_rows;           /* max staged rows per block (nrows * (pair?2:1)) */
@@ -80,6 +81,7 @@ int ec_launch_gemv(const ec_gemv_args *a, int num_sms, cudaStream_t stream);
 typedef struct {
     const void *W; const float *wscale; const float *bias;
     int wt, N, K, Kp;
+    int ldw;                                  /* W row stride (0: Kp)  */
     const int8_t *Aq; const float *a_scale;   /* int8 weights */
     const float *X; int ldx;                  /* 16-bit weights */
     int M;
@@ -99,12 +101,12 @@ int ec_launch_embed(float *x, const uint16_t *wte, const uint16_t *wpe, int ld, 
 int ec_launch_norm(float *out, const float *x, const float *gamma, const float *beta,
                    int M, int E, double eps, cudaStream_t stream);
 
-/* Split q/k/v rows of a [M][E+2kv] buffer: RoPE q (in place) and k, store
- * k/v as fp16 into the cache.  q ends up in qkv's first E columns. */
-int ec_launch_rope_kv(float *qkv, int ldq, ec_tokens tk, ec_kvgeo geo, int H, int KVH, int M,
-                      cudaStream_t stream);
+/* Split the q|k|v rows of a GEMM output [M][ldq] (Qwen2 packed layout when
+ * packed != 0): RoPE, q -> q_out [M][E] in head order, k/v -> fp16 cache. */
+int ec_launch_qkv_split(float *q_out, const float *qkv, int ldq, ec_tokens tk, ec_kvgeo geo, int H,
+                        int KVH, int packed, int M, cudaStream_t stream);
 
-/* out[m][j] = silu(gu[m][j]) * gu[m][I + j] (gate/up side by side). */
+/* out[m][j] = silu(gu[m][2j]) * gu[m][2j+1] (gate|up interleaved). */
 int ec_launch_swiglu(float *out, int ldo, const float *gu, int ldg, int I, int M,
                      cudaStream_t stream);
 

@@ -80,6 +80,16 @@ int ec_decode_greedy_cycle(GPT2 *g, int *d_tokens, int start_pos, int period, in
  * algorithmic HBM bytes, out[3c+2] = launches; out[15] = steps. */
 int ec_decode_profile(GPT2 *g, int *d_tokens, int start_pos, int n_steps, double *out16);
 
+/* Decode n_steps (as ec_decode_greedy) recording the timeline of CTA 0 of the
+ * persistent decode kernel: out[cap] receives entries (code << 56) |
+ * globaltimer-ns, first those of one consumer thread (codes 1 barrier passed,
+ * 2 operand built, 3 weight tiles done, 4 attention done, 5 lm_head done,
+ * 6 argmax merged, 7 tile data arrived, 8 ring slot released, 9 tile epilogue
+ * done), then those of the producer thread (10 tile copy issued), each part
+ * holding at most cap/2 entries.  Returns the number of entries, or -1. */
+int ec_decode_trace(GPT2 *g, int *d_tokens, int start_pos, int n_steps,
+                    unsigned long long *out, int cap);
+
 /* Per-layer taps of the last forward: copies the residual stream after the
  * embedding and after every layer, [n_layer+1][M][n_embd] fp32, to host
  * `out`.  Only valid after a forward with taps enabled by ec_model_set_taps. */
