@@ -288,7 +288,7 @@ class Model:
         """Per-kernel-class event timings of an instrumented decode."""
         out = np.zeros(16, np.float64)
         self._check(self.lib.ec_decode_profile(self.h, _ptr(d_tokens), int(start_pos), int(n_steps), _ptr(out)))
-        names = ("layer_gemv", "lm_head_gemv", "attention", "norm", "other")
+        names = ("decode_step", "gemm", "attention", "norm", "other")
         return {n: {"ms": out[3 * i], "bytes": out[3 * i + 1], "launches": int(out[3 * i + 2])}
                 for i, n in enumerate(names)} | {"steps": int(out[15])}
 

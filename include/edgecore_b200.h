@@ -57,11 +57,12 @@ int ec_forward_device(GPT2 *g, const int *d_tokens, const int *d_positions,
 int ec_forward_argmax(GPT2 *g, const int *tokens, const int *positions,
                       const int *seqs, int M, int *out_ids, float *out_max);
 
-/* Device-resident greedy decode of `n_steps` tokens for the batch_cap slots.
- * d_tokens[batch_cap] holds the current token of every slot and is updated in
- * place; step i runs at position start_pos + i for all slots; the sampled ids
- * are written to d_out_ids[n_steps][batch_cap] (may be NULL).  The step is a
- * captured CUDA graph replayed n_steps times (reference decode loop:
+/* Device-resident greedy decode of `n_steps` tokens for the batch_cap slots
+ * (batch_cap <= 8).  d_tokens[batch_cap] holds the current token of every
+ * slot and is updated in place; step i runs at position start_pos + i for all
+ * slots; the sampled ids are written to d_out_ids[n_steps][batch_cap] (may be
+ * NULL).  All n_steps steps run inside one launch of the persistent decode
+ * kernel, the argmax of each step feeding the next (reference decode loop:
  * src/runtime_main.c:336-352 with sample_token's greedy branch). */
 int ec_decode_greedy(GPT2 *g, int *d_tokens, int start_pos, int n_steps,
                      int *d_out_ids);
@@ -73,11 +74,12 @@ int ec_decode_greedy(GPT2 *g, int *d_tokens, int start_pos, int n_steps,
 int ec_decode_greedy_cycle(GPT2 *g, int *d_tokens, int start_pos, int period, int n_steps,
                            int *d_out_ids);
 
-/* Instrumented greedy decode for measurement: n_steps steps launched without
- * a graph, with a CUDA event pair around every kernel launch on the model
- * stream.  out[16]: for kernel class c in {0 layer GEMV, 1 lm_head GEMV,
- * 2 attention, 3 norms, 4 other}: out[3c] = total ms, out[3c+1] = total
- * algorithmic HBM bytes, out[3c+2] = launches; out[15] = steps. */
+/* Instrumented greedy decode for measurement: n_steps steps, one kernel
+ * launch per step, with a CUDA event pair around every kernel launch on the
+ * model stream.  out[16]: for kernel class c in {0 persistent decode step,
+ * 1 GEMM, 2 attention, 3 norms, 4 other} (classes 1-4 only when the
+ * persistent kernel cannot take the model): out[3c] = total ms, out[3c+1] =
+ * total algorithmic HBM bytes, out[3c+2] = launches; out[15] = steps. */
 int ec_decode_profile(GPT2 *g, int *d_tokens, int start_pos, int n_steps, double *out16);
 
 /* Decode n_steps (as ec_decode_greedy) recording the timeline of CTA 0 of the
