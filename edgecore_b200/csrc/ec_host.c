@@ -54,6 +54,9 @@ static void ec_seterr(const char *fmt, ...)
 }
 
 EC_EXPORT const char *ec_last_error(void) { return g_err; }
+
+/* For the other translation units of the library (not exported). */
+void ec_set_error_text(const char *msg) { ec_seterr("%s", msg); }
 EC_EXPORT const char *ec_version(void) { return "edgecore_b200 0.2 sm_100a"; }
 
 #define CK(call)                                                                               \

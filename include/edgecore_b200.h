@@ -123,6 +123,23 @@ int ec_quantize_rows(int8_t *q, float *scale, const float *x, int M, int K);
 int ec_linear_int8(float *C, const float *X, const int8_t *W,
                    const float *w_scale, const float *bias, int M, int K, int N);
 
+/* ec_linear_int8 that allocates no device memory: no counterpart in the
+ * reference (whose CPU op needs none).  For callers that cannot allocate on
+ * the request path -- HBM handed to a caching allocator, or a decode loop
+ * that must not be stalled by cudaMalloc's device synchronisation.  The
+ * int8 activations and their scales live in a fixed 4 MiB per-device static
+ * buffer: requires M*K + 4*M (rounded up to 256) <= 4 MiB, K % 16 == 0 and
+ * device pointers only; larger sizes are rejected with an error.  The first
+ * call on a device does the set-up (scratch address lookup, kernel
+ * attributes and loading) and should come before any stream capture.  Work
+ * is enqueued on `stream` (cudaStream_t, NULL = legacy default) without a
+ * host wait.  Calls that can overlap on the device share the one buffer and
+ * race: order them on one stream or with events.  Returns 0 or -1 (reason
+ * in ec_last_error()). */
+int ec_linear_int8_noalloc(float *C, const float *X, const int8_t *W,
+                           const float *w_scale, const float *bias, int M, int K, int N,
+                           void *stream);
+
 #ifdef __cplusplus
 }
 #endif
