@@ -107,6 +107,18 @@ EC_DEV int ec_quant1(float x, float s) {
     return q > 127 ? 127 : (q < -128 ? -128 : q);
 }
 
+// ec_quant1 without a division per element: r = 1/s correctly rounded, so
+// t = x*r is within 2^-16 of the exact x/s for |x/s| <= 127.5, and so is the
+// rounded quotient x/s.  Unless t lies within 2^-12 of a half-integer, both
+// round to the same integer; near a tie (or for out-of-range t) the exact
+// division decides.
+EC_DEV int ec_quant_fast(float x, float s, float r) {
+    const float t = __fmul_rn(x, r);
+    const float n = rintf(t);
+    if (fabsf(fabsf(t - n) - 0.5f) < 0x1p-12f || !(fabsf(t) <= 127.5f)) return ec_quant1(x, s);
+    return (int)n;
+}
+
 // Correctly rounded fp32 exp and tanh: the fp64 function (error < 1 ulp of
 // fp64) rounded once to fp32.  The reference calls the host libm's expf /
 // tanhf, which are not correctly rounded; every int8 quantisation downstream

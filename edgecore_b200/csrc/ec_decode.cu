@@ -50,16 +50,25 @@ constexpr long long SPIN_CYCLES = 4000000000LL;   // ~2 s: bound on any grid-bar
 constexpr int ERR_TIMEOUT = 1, ERR_INDEX = 2;
 constexpr uint32_t T_ABORT = 0xffffffffu;         // tile counter value meaning "aborted"
 
-// Phase kinds of the shared tile loop.
+// Phase kinds of the shared tile loop, and the five matrix shapes whose
+// per-CTA row ranges are computed once per launch.
 enum { PK_QKV = 0, PK_RESID = 1, PK_UP = 2, PK_LM = 3 };
+enum { MI_QKV = 0, MI_O = 1, MI_UP = 2, MI_DOWN = 3, MI_LM = 4, MI_N = 5 };
 
 // Loop over the token rows m < p.M with compile-time indices (bounded by the
 // kernel's MM), so per-token arrays stay in registers.
 // Every user declares `const int nM = p.M;` (a register, not a reload).
 #define FOR_TOK(m) _Pragma("unroll") for (int m = 0; m < MM; ++m) if (m < nM)
 
+// Loop over k = ct, ct + NCT, ... < n, four iterations unrolled per round so
+// that independent loads and arithmetic overlap; k still ascends per thread.
+#define FOR_K4(k, n)                                                  \
+    for (int k0_ = ct; k0_ < (n); k0_ += 4 * NCT)                    \
+        _Pragma("unroll") for (int j_ = 0; j_ < 4; ++j_)             \
+            if (const int k = k0_ + j_ * NCT; k < (n))
+
 struct Lay {
-    uint32_t ring, xbuf, stage, nrm, part, redd, redf, redi, asc, ints, bars, lays, par, total;
+    uint32_t ring, xbuf, stage, nrm, redd, redf, redi, asc, ints, bars, lays, par, total;
 };
 
 __host__ __device__ inline uint32_t al16(uint32_t v) { return (v + 15u) & ~15u; }
@@ -71,12 +80,11 @@ __host__ __device__ inline Lay mk_layout(int xbuf_bytes, int stage_bytes, int n_
     L.xbuf = o;  o += al16((uint32_t)xbuf_bytes);
     L.stage = o; o += al16((uint32_t)stage_bytes);
     L.nrm = o;   o += 2u * al16((uint32_t)E * 4u);
-    L.part = o;  o += TROWS * NCW * MT * 4;
-    L.redd = o;  o += NCW * MT * 8;
-    L.redf = o;  o += NCW * MT * 4;
+    L.redd = o;  o += 2 * NCW * MT * 8;
+    L.redf = o;  o += 2 * NCW * MT * 4;
     L.redi = o;  o += NCW * MT * 4;
     L.asc = o;   o += MT * 4;
-    L.ints = o;  o += al16((3 * MT + 4) * 4);
+    L.ints = o;  o += al16((3 * MT + 4 + 2 * MI_N) * 4);
     L.bars = o;  o += 2 * STAGES * 8;
     L.lays = o;  o += al16((uint32_t)n_layer * (uint32_t)sizeof(ec_mk_layer));
     L.par = o;   o += al16((uint32_t)sizeof(ec_mk_params));
@@ -86,18 +94,20 @@ __host__ __device__ inline Lay mk_layout(int xbuf_bytes, int stage_bytes, int n_
 
 extern __shared__ __align__(128) unsigned char g_smem[];
 
+struct Rg { int r0, r1; };
+
 struct Sm {
     unsigned char *ring, *xbuf;
     float *stage;
     float *nrm;               // norm gain [E] and bias [E] of the running norm
-    float *part;
-    double *redd;
-    float *redf;
+    double *redd;             // [2][NCW][MT]: two slots, see red_sum_d
+    float *redf;              // [2][NCW][MT]
     int *redi;
     float *asc;
     int *ltok, *lpos, *lslot;
     volatile int *flag;       // [0]: abort
     int *tcount;              // [2]: trace entries written (consumer, producer)
+    Rg *rg;                   // [MI_N]: this CTA's row range of each matrix shape
     uint64_t *full, *empty;
     const ec_mk_layer *lay;   // shared-memory copy of the layer descriptors
     ec_mk_params *par;        // shared-memory copy of the kernel parameters
@@ -110,7 +120,6 @@ __device__ __forceinline__ Sm sm_of(const ec_mk_params &p) {
     S.xbuf = g_smem + L.xbuf;
     S.stage = reinterpret_cast<float *>(g_smem + L.stage);
     S.nrm = reinterpret_cast<float *>(g_smem + L.nrm);
-    S.part = reinterpret_cast<float *>(g_smem + L.part);
     S.redd = reinterpret_cast<double *>(g_smem + L.redd);
     S.redf = reinterpret_cast<float *>(g_smem + L.redf);
     S.redi = reinterpret_cast<int *>(g_smem + L.redi);
@@ -121,6 +130,7 @@ __device__ __forceinline__ Sm sm_of(const ec_mk_params &p) {
     S.lslot = ints + 2 * MT;
     S.flag = ints + 3 * MT;
     S.tcount = ints + 3 * MT + 1;
+    S.rg = reinterpret_cast<Rg *>(ints + 3 * MT + 4);
     S.full = reinterpret_cast<uint64_t *>(g_smem + L.bars);
     S.empty = S.full + STAGES;
     S.lay = reinterpret_cast<const ec_mk_layer *>(g_smem + L.lays);
@@ -128,27 +138,25 @@ __device__ __forceinline__ Sm sm_of(const ec_mk_params &p) {
     return S;
 }
 
-struct Rg { int r0, r1; };
-
 __device__ __forceinline__ Rg mk_range(const ec_mk_mat &m, int c, int G) {
     const int U = m.N / m.unit;
     const int u0 = (int)(((long long)c * U) / G), u1 = (int)(((long long)(c + 1) * U) / G);
     return Rg{u0 * m.unit, u1 * m.unit};
 }
 
-__device__ __forceinline__ void cons_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+__device__ __forceinline__ void cons_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "memory"); }
 
-// Consumer barrier that also ORs a predicate over the 256 consumer threads,
+// Consumer barrier that also ORs a predicate over the NCT consumer threads,
 // so that every warp takes the same abort decision.
 __device__ __forceinline__ bool cons_sync_or(bool v) {
     int r;
     asm volatile(
         "{\n\t.reg .pred p, q;\n\t"
         "setp.ne.s32 p, %1, 0;\n\t"
-        "bar.red.or.pred q, 1, 256, p;\n\t"
+        "bar.red.or.pred q, 1, %2, p;\n\t"
         "selp.s32 %0, 1, 0, q;\n\t}"
         : "=r"(r)
-        : "r"((int)v)
+        : "r"((int)v), "n"(NCT)
         : "memory");
     return r != 0;
 }
@@ -233,36 +241,43 @@ __device__ __noinline__ uint32_t mk_produce(const ec_mk_params &p, const ec_mk_m
 }
 
 // ---------------------------------------------------------------------------
-// consumers: reductions over the 256 consumer threads (fixed order: lanes by
+// consumers: reductions over the NCT consumer threads (fixed order: lanes by
 // xor tree, warps in index order; every thread gets the totals)
 // ---------------------------------------------------------------------------
 
+// CTA-wide reductions over the NCT consumer threads: lanes by xor tree (or
+// redux), warps in index order, every thread gets the totals.  Each call
+// site uses its own slot of the reduction buffers, and every buffer slot is
+// read before a consumer barrier that precedes its next write, so one
+// barrier per reduction suffices.
 template <int MM>
-__device__ __forceinline__ void red_sum_d(const ec_mk_params &p, const Sm &S, double v[MM], int ct) {
+__device__ __forceinline__ void red_sum_d(const ec_mk_params &p, const Sm &S, double v[MM], int ct, int slot) {
     const int nM = p.M;
     const int lane = ct & 31, w = ct >> 5;
+    double *buf = S.redd + slot * NCW * MT;
     FOR_TOK(m) v[m] = ec_warp_sum_d(v[m]);
-    cons_sync();
-    if (lane == 0) FOR_TOK(m) S.redd[w * MT + m] = v[m];
+    if (lane == 0) FOR_TOK(m) buf[w * MT + m] = v[m];
     cons_sync();
     FOR_TOK(m) {
         double t = 0.0;
-        for (int i = 0; i < NCW; ++i) t = __dadd_rn(t, S.redd[i * MT + m]);
+        for (int i = 0; i < NCW; ++i) t = __dadd_rn(t, buf[i * MT + m]);
         v[m] = t;
     }
 }
 
+// Max of non-negative, non-NaN values: their bit patterns order like the
+// values, so one redux instruction reduces a warp.
 template <int MM>
-__device__ __forceinline__ void red_max_f(const ec_mk_params &p, const Sm &S, float v[MM], int ct) {
+__device__ __forceinline__ void red_max_f(const ec_mk_params &p, const Sm &S, float v[MM], int ct, int slot) {
     const int nM = p.M;
     const int lane = ct & 31, w = ct >> 5;
-    FOR_TOK(m) v[m] = ec_warp_max(v[m]);
-    cons_sync();
-    if (lane == 0) FOR_TOK(m) S.redf[w * MT + m] = v[m];
+    float *buf = S.redf + slot * NCW * MT;
+    FOR_TOK(m) v[m] = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(v[m])));
+    if (lane == 0) FOR_TOK(m) buf[w * MT + m] = v[m];
     cons_sync();
     FOR_TOK(m) {
-        float t = S.redf[m];
-        for (int i = 1; i < NCW; ++i) t = ec_max_keep(t, S.redf[i * MT + m]);
+        float t = buf[m];
+        for (int i = 1; i < NCW; ++i) t = ec_max_keep(t, buf[i * MT + m]);
         v[m] = t;
     }
 }
@@ -283,7 +298,6 @@ __device__ __forceinline__ void red_argmax(const ec_mk_params &p, const Sm &S, f
             am_merge(bv[m], bi[m], ov, oi);
         }
     }
-    cons_sync();
     if (lane == 0) FOR_TOK(m) { S.redf[w * MT + m] = bv[m]; S.redi[w * MT + m] = bi[m]; }
     cons_sync();
     FOR_TOK(m) {
@@ -326,24 +340,24 @@ __device__ __noinline__ void mk_norm(const ec_mk_params &p, bool from_embed, con
     double s1[MM];
     FOR_TOK(m) {
         s1[m] = 0.0;
-        for (int k = ct; k < E; k += NCT) {
+        FOR_K4(k, E) {
             const double d = (double)st[m * E + k];
             s1[m] = b ? __dadd_rn(s1[m], d) : __dadd_rn(s1[m], __dmul_rn(d, d));
         }
     }
-    red_sum_d<MM>(p, S, s1, ct);
+    red_sum_d<MM>(p, S, s1, ct, 0);
     double mean[MM], rstd[MM];
     if (b) {
         double s2[MM];
         FOR_TOK(m) {
             s2[m] = 0.0;
             mean[m] = __ddiv_rn(s1[m], (double)E);
-            for (int k = ct; k < E; k += NCT) {
+            FOR_K4(k, E) {
                 const double d = __dsub_rn((double)st[m * E + k], mean[m]);
                 s2[m] = __dadd_rn(s2[m], __dmul_rn(d, d));
             }
         }
-        red_sum_d<MM>(p, S, s2, ct);
+        red_sum_d<MM>(p, S, s2, ct, 1);
         FOR_TOK(m) rstd[m] = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(s2[m], (double)E), p.eps)));
     } else {
         FOR_TOK(m) {
@@ -352,7 +366,7 @@ __device__ __noinline__ void mk_norm(const ec_mk_params &p, bool from_embed, con
         }
     }
     FOR_TOK(m) {
-        for (int k = ct; k < E; k += NCT) {
+        FOR_K4(k, E) {
             const double d = b ? __dsub_rn((double)st[m * E + k], mean[m]) : (double)st[m * E + k];
             const float t = (float)__dmul_rn(d, rstd[m]);
             st[m * E + k] = b ? __fadd_rn(__fmul_rn(t, gs[k]), bs[k]) : __fmul_rn(t, gs[k]);
@@ -376,28 +390,52 @@ __device__ __noinline__ void mk_operand(const ec_mk_params &p, const float *src,
         cons_sync();
     }
     const bool from_stage = !src || fits;
+    const bool vec = from_stage && (K & 3) == 0;   // rows as float4 (Kp is a multiple of 16)
     if (wt == EC_W_I8) {
         float mx[MM];
         FOR_TOK(m) {
             mx[m] = 0.0f;
-            for (int k = ct; k < K; k += NCT)
-                mx[m] = ec_max_keep(mx[m], fabsf(from_stage ? st[m * K + k] : __ldcg(src + (size_t)m * K + k)));
+            if (vec) {
+                const float4 *r4 = reinterpret_cast<const float4 *>(st + (size_t)m * K);
+                FOR_K4(c, K >> 2) {
+                    const float4 v = r4[c];
+                    mx[m] = ec_max_keep(ec_max_keep(ec_max_keep(ec_max_keep(mx[m], fabsf(v.x)), fabsf(v.y)), fabsf(v.z)), fabsf(v.w));
+                }
+            } else {
+                for (int k = ct; k < K; k += NCT)
+                    mx[m] = ec_max_keep(mx[m], fabsf(from_stage ? st[m * K + k] : __ldcg(src + (size_t)m * K + k)));
+            }
         }
-        red_max_f<MM>(p, S, mx, ct);
+        red_max_f<MM>(p, S, mx, ct, 0);
         int8_t *xq = reinterpret_cast<int8_t *>(S.xbuf);
         FOR_TOK(m) {
             const float s = mx[m] > 0.0f ? __fdiv_rn(mx[m], 127.0f) : 1.0f;
+            const float r = __fdiv_rn(1.0f, s);
             if (ct == 0) S.asc[m] = s;
-            for (int k = ct; k < Kp; k += NCT) {
-                const float v = k < K ? (from_stage ? st[m * K + k] : __ldcg(src + (size_t)m * K + k)) : 0.0f;
-                xq[(size_t)m * Kp + k] = (int8_t)(k < K ? ec_quant1(v, s) : 0);
+            if (vec) {
+                const float4 *r4 = reinterpret_cast<const float4 *>(st + (size_t)m * K);
+                char4 *q4 = reinterpret_cast<char4 *>(xq + (size_t)m * Kp);
+                FOR_K4(c, Kp >> 2) {
+                    char4 o = make_char4(0, 0, 0, 0);
+                    if (4 * c < K) {
+                        const float4 v = r4[c];
+                        o = make_char4((signed char)ec_quant_fast(v.x, s, r), (signed char)ec_quant_fast(v.y, s, r),
+                                       (signed char)ec_quant_fast(v.z, s, r), (signed char)ec_quant_fast(v.w, s, r));
+                    }
+                    q4[c] = o;
+                }
+            } else {
+                for (int k = ct; k < Kp; k += NCT) {
+                    const float v = k < K ? (from_stage ? st[m * K + k] : __ldcg(src + (size_t)m * K + k)) : 0.0f;
+                    xq[(size_t)m * Kp + k] = (int8_t)(k < K ? ec_quant_fast(v, s, r) : 0);
+                }
             }
         }
     } else {
         float *xs = reinterpret_cast<float *>(S.xbuf);
         FOR_TOK(m) {
             float *xm = xs + (size_t)m * Kp;
-            for (int k = ct; k < Kp; k += NCT) {
+            FOR_K4(k, Kp) {
                 const float v = k < K ? (from_stage ? st[m * K + k] : __ldcg(src + (size_t)m * K + k)) : 0.0f;
                 const int c = k >> 3, e = k & 7;
                 xm[(e >> 2) * (Kp >> 1) + c * 4 + (e & 3)] = v;
@@ -417,21 +455,52 @@ template <> struct AccT<EC_W_I8> { typedef int T; };
 
 constexpr int RB = 4;   // weight rows a consumer warp reduces together
 
-// acc[i][q] for a lane-dependent (i, q): an unrolled select, so the register
-// array is never indexed dynamically.
-template <int MM, typename Acc>
-__device__ __forceinline__ Acc pick(const Acc (&acc)[RB][MM], int i, int q) {
-    Acc v = 0;
+// Sum of each of the V = RB*MM per-lane values over the warp, transposed:
+// the values are halved between lane pairs at offsets 16, 8, ... (each lane
+// keeps one half and adds its partner's copy of that half), so V values take
+// V-1 shuffles instead of 5*V; the remaining offsets add duplicates.  Lane L
+// ends with the total of value vidx<V>(L); lanes differing only in their low
+// log2(32/V) bits hold the same total.  Integer sums are exact; float sums
+// are deterministic (every step is a commutative pair sum).
+template <int V, typename T>
+__device__ __forceinline__ T tr_reduce(T (&a)[V], int lane) {
+    static_assert(V >= 1 && V <= 32 && (V & (V - 1)) == 0, "V must be a power of two <= 32");
+    int n = V;
 #pragma unroll
-    for (int a = 0; a < RB; ++a)
+    for (int o = 16; o >= 1; o >>= 1) {
+        if (n > 1) {
+            const bool up = (lane & o) != 0;
 #pragma unroll
-        for (int b = 0; b < MM; ++b)
-            if (a == i && b == q) v = acc[a][b];
-    return v;
+            for (int v = 0; v < V / 2; ++v) {
+                if (v < n / 2) {
+                    const T send = up ? a[v] : a[v + n / 2];
+                    const T keep = up ? a[v + n / 2] : a[v];
+                    a[v] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                }
+            }
+            n >>= 1;
+        } else {
+            a[0] = a[0] + __shfl_xor_sync(0xffffffffu, a[0], o);
+        }
+    }
+    return a[0];
 }
 
-// Final value of one output row r (its staged bytes at `row`, metadata tail
-// after Kp weights) for token q: reference gemm_int8 epilogue
+template <int V>
+__device__ __forceinline__ int vidx(int lane) {
+    int idx = 0, w = V >> 1;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        if (w >= 1) {
+            if (lane & o) idx += w;
+            w >>= 1;
+        }
+    }
+    return idx;
+}
+
+// Final value of one output row (staged bytes at `row`, metadata tail after
+// Kp weights) for token q: reference gemm_int8 epilogue
 // bias + ((float)dot * a_scale) * w_scale (src/kernels.c), or dot + bias.
 template <int WT>
 __device__ __forceinline__ float mk_fin(int Kp, int meta, const Sm &S, const unsigned char *row,
@@ -447,32 +516,38 @@ __device__ __forceinline__ float mk_fin(int Kp, int meta, const Sm &S, const uns
 
 // One phase's weight tiles.  Every consumer warp takes whole units (1 row,
 // or 2 for pair-packed rows) of each staged tile, RB rows at a time, with the
-// lanes splitting K; the unit -> warp assignment rotates from tile to tile.
-// A warp reduces its dots in registers and applies the epilogue itself (lane
-// e handles unit e / MM, token e % MM), then releases the ring slot: there is
-// no CTA-wide barrier per tile.  After an abort the remaining tiles are
-// skipped and the next grid barrier returns for every warp.
+// lanes splitting K (4 chunks of 16 bytes per lane per round, unrolled); the
+// unit -> warp assignment rotates from tile to tile.  A warp reduces its dots
+// with tr_reduce and applies the epilogue itself, one lane per (row, token),
+// then releases the ring slot: there is no CTA-wide barrier per tile.  After
+// an abort the remaining tiles are skipped and the next grid barrier returns
+// for every warp.
 template <int WT, int MM>
 __device__ __noinline__ uint32_t mk_phase(const ec_mk_params &p, int kind, int layer, uint32_t t, int ct) {
     typedef typename AccT<WT>::T Acc;
     constexpr int ELT = WT == EC_W_I8 ? 1 : 2;
+    constexpr int V = RB * MM;           // values reduced per group
+    constexpr int D = 32 / V;            // lanes holding the same total
     const Sm S = sm_of(p);
     const int nM = p.M;
-    const int G = gridDim.x, cta = blockIdx.x;
+    const int cta = blockIdx.x;
     // layer: index of the layer (bit 16 set: the down projection of a
     // PK_RESID phase, else its o projection); -1 for the lm_head
     const ec_mk_layer &ly = S.lay[layer < 0 ? 0 : (layer & 0xffff)];
-    const ec_mk_mat &m = kind == PK_QKV ? ly.qkv : kind == PK_UP ? ly.up : kind == PK_LM ? p.lm
-                       : (layer & 0x10000) ? ly.down : ly.o;
-    const Rg rg = mk_range(m, cta, G);
+    const int mi = kind == PK_QKV ? MI_QKV : kind == PK_UP ? MI_UP : kind == PK_LM ? MI_LM
+                 : (layer & 0x10000) ? MI_DOWN : MI_O;
+    const ec_mk_mat &m = mi == MI_QKV ? ly.qkv : mi == MI_UP ? ly.up : mi == MI_LM ? p.lm : mi == MI_DOWN ? ly.down : ly.o;
+    const Rg rg = S.rg[mi];
     const int lane = ct & 31, cw = ct >> 5;
     const uint32_t row_bytes = (uint32_t)m.ldw * ELT;
     const int Kp = m.Kp, meta = m.meta, tile_rows = m.tile_rows, mN = m.N;
     const int nch = Kp * ELT / 16;
     const int unit = m.unit, gmax = RB / unit;
     const int half = p.hd >> 1;
-    const int eg = lane / MM, eq = lane % MM;    // this lane's epilogue (unit, token)
-    float bv = -INFINITY;                         // running argmax of token eq
+    const int my = vidx<V>(lane);               // this lane's (row slot, token) after the reduction
+    const int my_i = my / MM, my_q = my % MM;
+    const bool my_lane = (lane & (D - 1)) == 0 && my_q < nM && (unit == 1 || (my_i & 1) == 0);
+    float bv = -INFINITY;                         // running argmax of token my_q
     int bi = 0x7fffffff;
 
     for (int row0 = rg.r0; row0 < rg.r1; row0 += tile_rows) {
@@ -494,7 +569,7 @@ __device__ __noinline__ uint32_t mk_phase(const ec_mk_params &p, int kind, int l
         }
         if (ct == 0) tmark(p, S, 0, EC_TR_TILE_IN);
         const unsigned char *stg = S.ring + (size_t)s * TILE;
-        const int rot = ((row0 - rg.r0) / unit) % NCW;
+        const int rot = (unit == 2 ? (row0 - rg.r0) >> 1 : row0 - rg.r0) % NCW;
         for (int u0 = (cw - rot + NCW) % NCW; u0 < U; u0 += NCW * gmax) {
             int rr[RB];   // staged row of slot i, or -1 (warp-uniform)
 #pragma unroll
@@ -502,87 +577,82 @@ __device__ __noinline__ uint32_t mk_phase(const ec_mk_params &p, int kind, int l
                 const int ug = u0 + (unit == 2 ? (i >> 1) : i) * NCW;
                 rr[i] = ug < U ? ug * unit + (unit == 2 ? (i & 1) : 0) : -1;
             }
-            Acc acc[RB][MM];
+            Acc acc[V];
 #pragma unroll
-            for (int i = 0; i < RB; ++i)
+            for (int v = 0; v < V; ++v) acc[v] = 0;
+            for (int cb = lane; cb < nch; cb += 128) {
 #pragma unroll
-                for (int q = 0; q < MM; ++q) acc[i][q] = 0;
-            for (int c = lane; c < nch; c += 32) {
-                if (WT == EC_W_I8) {
-                    uint4 w[RB];
+                for (int j = 0; j < 4; ++j) {
+                    const int c = cb + 32 * j;
+                    if (c >= nch) break;
+                    if (WT == EC_W_I8) {
+                        uint4 w[RB];
 #pragma unroll
-                    for (int i = 0; i < RB; ++i)
-                        if (rr[i] >= 0) w[i] = *reinterpret_cast<const uint4 *>(stg + (size_t)rr[i] * row_bytes + (size_t)c * 16);
-                    const int8_t *xq = reinterpret_cast<const int8_t *>(S.xbuf);
-                    FOR_TOK(q) {
-                        const uint4 x = reinterpret_cast<const uint4 *>(xq + (size_t)q * Kp)[c];
+                        for (int i = 0; i < RB; ++i)
+                            if (rr[i] >= 0) w[i] = *reinterpret_cast<const uint4 *>(stg + (size_t)rr[i] * row_bytes + (size_t)c * 16);
+                        const int8_t *xq = reinterpret_cast<const int8_t *>(S.xbuf);
+                        FOR_TOK(q) {
+                            const uint4 x = reinterpret_cast<const uint4 *>(xq + (size_t)q * Kp)[c];
+#pragma unroll
+                            for (int i = 0; i < RB; ++i) {
+                                if (rr[i] < 0) continue;
+                                int a = (int)acc[i * MM + q];
+                                a = __dp4a((int)w[i].x, (int)x.x, a);
+                                a = __dp4a((int)w[i].y, (int)x.y, a);
+                                a = __dp4a((int)w[i].z, (int)x.z, a);
+                                a = __dp4a((int)w[i].w, (int)x.w, a);
+                                acc[i * MM + q] = a;
+                            }
+                        }
+                    } else {
+                        float f[RB][8];
 #pragma unroll
                         for (int i = 0; i < RB; ++i) {
                             if (rr[i] < 0) continue;
-                            int a = (int)acc[i][q];
-                            a = __dp4a((int)w[i].x, (int)x.x, a);
-                            a = __dp4a((int)w[i].y, (int)x.y, a);
-                            a = __dp4a((int)w[i].z, (int)x.z, a);
-                            a = __dp4a((int)w[i].w, (int)x.w, a);
-                            acc[i][q] = a;
+                            const uint4 w = *reinterpret_cast<const uint4 *>(stg + (size_t)rr[i] * row_bytes + (size_t)c * 16);
+                            const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                if (WT == EC_W_F16) {
+                                    const float2 t2 = __half22float2(*reinterpret_cast<const __half2 *>(&u[e]));
+                                    f[i][2 * e] = t2.x;
+                                    f[i][2 * e + 1] = t2.y;
+                                } else {
+                                    f[i][2 * e] = __uint_as_float(u[e] << 16);
+                                    f[i][2 * e + 1] = __uint_as_float(u[e] & 0xffff0000u);
+                                }
+                            }
                         }
-                    }
-                } else {
-                    float f[RB][8];
+                        const float *xs = reinterpret_cast<const float *>(S.xbuf);
+                        FOR_TOK(q) {
+                            const float *xm = xs + (size_t)q * Kp;
+                            const float4 x0 = reinterpret_cast<const float4 *>(xm)[c];
+                            const float4 x1 = reinterpret_cast<const float4 *>(xm + (Kp >> 1))[c];
 #pragma unroll
-                    for (int i = 0; i < RB; ++i) {
-                        if (rr[i] < 0) continue;
-                        const uint4 w = *reinterpret_cast<const uint4 *>(stg + (size_t)rr[i] * row_bytes + (size_t)c * 16);
-                        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            if (WT == EC_W_F16) {
-                                const float2 t2 = __half22float2(*reinterpret_cast<const __half2 *>(&u[j]));
-                                f[i][2 * j] = t2.x;
-                                f[i][2 * j + 1] = t2.y;
-                            } else {
-                                f[i][2 * j] = __uint_as_float(u[j] << 16);
-                                f[i][2 * j + 1] = __uint_as_float(u[j] & 0xffff0000u);
+                            for (int i = 0; i < RB; ++i) {
+                                if (rr[i] < 0) continue;
+                                float a = (float)acc[i * MM + q];
+                                a = fmaf(f[i][0], x0.x, a); a = fmaf(f[i][1], x0.y, a);
+                                a = fmaf(f[i][2], x0.z, a); a = fmaf(f[i][3], x0.w, a);
+                                a = fmaf(f[i][4], x1.x, a); a = fmaf(f[i][5], x1.y, a);
+                                a = fmaf(f[i][6], x1.z, a); a = fmaf(f[i][7], x1.w, a);
+                                acc[i * MM + q] = a;
                             }
                         }
                     }
-                    const float *xs = reinterpret_cast<const float *>(S.xbuf);
-                    FOR_TOK(q) {
-                        const float *xm = xs + (size_t)q * Kp;
-                        const float4 x0 = reinterpret_cast<const float4 *>(xm)[c];
-                        const float4 x1 = reinterpret_cast<const float4 *>(xm + (Kp >> 1))[c];
-#pragma unroll
-                        for (int i = 0; i < RB; ++i) {
-                            if (rr[i] < 0) continue;
-                            float a = (float)acc[i][q];
-                            a = fmaf(f[i][0], x0.x, a); a = fmaf(f[i][1], x0.y, a);
-                            a = fmaf(f[i][2], x0.z, a); a = fmaf(f[i][3], x0.w, a);
-                            a = fmaf(f[i][4], x1.x, a); a = fmaf(f[i][5], x1.y, a);
-                            a = fmaf(f[i][6], x1.z, a); a = fmaf(f[i][7], x1.w, a);
-                            acc[i][q] = a;
-                        }
-                    }
                 }
             }
-#pragma unroll
-            for (int i = 0; i < RB; ++i) {
-                if (rr[i] < 0) continue;
-                FOR_TOK(q) {
-                    if (WT == EC_W_I8) acc[i][q] = ec_warp_sum_i((int)acc[i][q]);
-                    else acc[i][q] = ec_warp_sum((float)acc[i][q]);
-                }
-            }
+            const Acc tot = tr_reduce<V>(acc, lane);
+            const Acc oth = __shfl_xor_sync(0xffffffffu, tot, 8);   // row slot my_i ^ 1, same token
 
-            // ---- epilogue: lane (eg, eq) ----
-            if (eg >= gmax || eq >= nM) continue;
-            const int i0 = eg * unit;
-            const int r0 = i0 == 0 ? rr[0] : i0 == 1 ? rr[1] : i0 == 2 ? rr[2] : rr[3];
-            if (r0 < 0) continue;
-            const int q = eq;
+            // ---- epilogue: one lane per (row slot, token) ----
+            const int r0 = my_i == 0 ? rr[0] : my_i == 1 ? rr[1] : my_i == 2 ? rr[2] : rr[3];
+            if (!my_lane || my_i >= gmax * unit || r0 < 0) continue;
+            const int q = my_q;
             const unsigned char *row = stg + (size_t)r0 * row_bytes;
-            const float v0 = mk_fin<WT>(Kp, meta, S, row, pick<MM>(acc, i0, q), q);
-            const float v1 = unit == 2 ? mk_fin<WT>(Kp, meta, S, row + row_bytes, pick<MM>(acc, i0 + 1, q), q) : 0.0f;
-            const int n = row0 + r0;   // matrix row of slot i0
+            const float v0 = mk_fin<WT>(Kp, meta, S, row, tot, q);
+            const float v1 = unit == 2 ? mk_fin<WT>(Kp, meta, S, row + row_bytes, oth, q) : 0.0f;
+            const int n = row0 + r0;   // matrix row of this lane's slot
             if (kind == PK_QKV) {
                 const int pos = S.lpos[q], slot = S.lslot[q];
                 const size_t kvo = ((size_t)slot * p.C + pos) * p.kv;
@@ -627,17 +697,18 @@ __device__ __noinline__ uint32_t mk_phase(const ec_mk_params &p, int kind, int l
         if (ct == 0) tmark(p, S, 0, EC_TR_TILE_DONE);
     }
     if (kind == PK_LM) {
-        // lanes holding the same token: xor offsets >= MM; then warps in order
+        // lanes holding the same token: every offset except the token bits
 #pragma unroll
-        for (int o = 16; o >= MM; o >>= 1) {
+        for (int o = 16; o >= 1; o >>= 1) {
+            if (o <= 4 && o * MM > 4) continue;
             const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
             const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
             am_merge(bv, bi, ov, oi);
         }
         cons_sync();
-        if (lane < MM) { S.redf[cw * MT + lane] = bv; S.redi[cw * MT + lane] = bi; }
+        if (my < MM && (lane & (D - 1)) == 0) { S.redf[cw * MT + my_q] = bv; S.redi[cw * MT + my_q] = bi; }
         cons_sync();
-        if (ct < p.M) {
+        if (ct < nM) {
             float v = S.redf[ct];
             int i = S.redi[ct];
             for (int w = 1; w < NCW; ++w) am_merge(v, i, S.redf[w * MT + ct], S.redi[w * MT + ct]);
@@ -708,6 +779,7 @@ __device__ __noinline__ void mk_attention(const ec_mk_params &p, int layer, int 
             for (int i = ct; i < n; i += NCT) {
                 const uint16_t *kp = kch + (size_t)i * ks;
                 float a = 0.0f;
+#pragma unroll 4
                 for (int d = 0; d < hd; d += 8) {
                     const uint4 w = *reinterpret_cast<const uint4 *>(kp + d);
                     const uint32_t u[4] = {w.x, w.y, w.z, w.w};
@@ -726,7 +798,6 @@ __device__ __noinline__ void mk_attention(const ec_mk_params &p, int layer, int 
         {
             const int lane = ct & 31, w = ct >> 5;
             mx = ec_warp_max(mx);
-            cons_sync();
             if (lane == 0) S.redf[w * MT] = mx;
             cons_sync();
             float t = S.redf[0];
@@ -742,7 +813,6 @@ __device__ __noinline__ void mk_attention(const ec_mk_params &p, int layer, int 
         {
             const int lane = ct & 31, w = ct >> 5;
             sum = ec_warp_sum_d(sum);
-            cons_sync();
             if (lane == 0) S.redd[w * MT] = sum;
             cons_sync();
             double t = 0.0;
@@ -765,9 +835,20 @@ __device__ __noinline__ void mk_attention(const ec_mk_params &p, int layer, int 
                 cpa_wait_all();
                 cons_sync();
             }
-            if (ct < hd)
-                for (int i = 0; i < n; ++i)
+            if (ct < hd) {
+                // products are independent; only the sum runs in position order
+                int i = 0;
+                for (; i + 8 <= n; i += 8) {
+                    float pr[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        pr[j] = __fmul_rn(sc[c0 + i + j], __half2float(__ushort_as_half(vch[(size_t)(i + j) * hd + ct])));
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) o = __fadd_rn(o, pr[j]);
+                }
+                for (; i < n; ++i)
                     o = __fadd_rn(o, __fmul_rn(sc[c0 + i], __half2float(__ushort_as_half(vch[(size_t)i * hd + ct]))));
+            }
         }
         if (ct < hd) p.att[(size_t)m * E + (size_t)h * hd + ct] = o;
         cons_sync();
@@ -844,6 +925,14 @@ __global__ void __launch_bounds__(EC_MK_THREADS, 1) k_decode(const __grid_consta
         for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
     }
     __syncthreads();
+    if (threadIdx.x == 0) {   // row ranges: every layer has the same shapes
+        S.rg[MI_QKV] = mk_range(S.lay[0].qkv, cta, G);
+        S.rg[MI_O] = mk_range(S.lay[0].o, cta, G);
+        S.rg[MI_UP] = mk_range(S.lay[0].up, cta, G);
+        S.rg[MI_DOWN] = mk_range(S.lay[0].down, cta, G);
+        S.rg[MI_LM] = mk_range(p.lm, cta, G);
+    }
+    __syncthreads();
     // Inputs are checked identically by every CTA before any work, so a bad
     // token / position / slot makes the whole grid return together.
     for (int q = 0; q < M; ++q) {
@@ -861,12 +950,12 @@ __global__ void __launch_bounds__(EC_MK_THREADS, 1) k_decode(const __grid_consta
             for (int step = 0; t != T_ABORT && step < n_steps; ++step) {
                 for (int l = 0; t != T_ABORT && l < p.L; ++l) {
                     const ec_mk_layer &ly = S.lay[l];
-                    t = mk_produce(p, ly.qkv, LWT, mk_range(ly.qkv, cta, G), t);
-                    if (t != T_ABORT) t = mk_produce(p, ly.o, LWT, mk_range(ly.o, cta, G), t);
-                    if (t != T_ABORT) t = mk_produce(p, ly.up, LWT, mk_range(ly.up, cta, G), t);
-                    if (t != T_ABORT) t = mk_produce(p, ly.down, LWT, mk_range(ly.down, cta, G), t);
+                    t = mk_produce(p, ly.qkv, LWT, S.rg[MI_QKV], t);
+                    if (t != T_ABORT) t = mk_produce(p, ly.o, LWT, S.rg[MI_O], t);
+                    if (t != T_ABORT) t = mk_produce(p, ly.up, LWT, S.rg[MI_UP], t);
+                    if (t != T_ABORT) t = mk_produce(p, ly.down, LWT, S.rg[MI_DOWN], t);
                 }
-                if (t != T_ABORT) t = mk_produce(p, p.lm, HWT, mk_range(p.lm, cta, G), t);
+                if (t != T_ABORT) t = mk_produce(p, p.lm, HWT, S.rg[MI_LM], t);
             }
             if (t == T_ABORT) {
                 // give the copies already issued a bounded time to land
@@ -882,7 +971,7 @@ __global__ void __launch_bounds__(EC_MK_THREADS, 1) k_decode(const __grid_consta
     const int ct = threadIdx.x - 32;
     uint32_t t = 0;
     unsigned target = 0;
-    const Rg xr = mk_range(S.lay[0].o, cta, G);   // residual rows owned by this CTA
+    const Rg xr = S.rg[MI_O];   // residual rows owned by this CTA
     const int xn = xr.r1 - xr.r0;
 #define SYNC_OR_RETURN()                                  \
     do {                                                  \

@@ -497,9 +497,7 @@ static ec_mk_mat ec_mk_of(const ec_lin *l)
     const int rb = l->ldw * (l->wt == EC_W_I8 ? 1 : 2);
     int tr = EC_MK_TILE / rb;
     if (tr > EC_MK_MAX_TILE_ROWS) tr = EC_MK_MAX_TILE_ROWS;
-    /* whole units for each of the consumer warps when the slot allows */
-    if (tr >= EC_MK_CONS_WARPS * l->unit) tr -= tr % (EC_MK_CONS_WARPS * l->unit);
-    else tr -= tr % l->unit;
+    tr -= tr % l->unit;   /* as many whole units as a ring slot holds: fewest tiles per CTA */
     m.tile_rows = tr;   /* 0 if a unit of rows does not fit a ring slot */
     return m;
 }
