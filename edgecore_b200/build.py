@@ -23,7 +23,7 @@ LIB = PKG / "libedgecore_b200.so"
 CUDA = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
-CU_SOURCES = ["ec_kernels.cu", "ec_decode.cu", "ec_noalloc.cu"]
+CU_SOURCES = ["ec_kernels.cu", "ec_decode.cu", "ec_tc.cu", "ec_noalloc.cu"]
 C_SOURCES = ["ec_host.c", "ec_abi.c"]
 HEADERS = [CSRC / "ec_launch.h", CSRC / "ec_common.cuh", CSRC / "ec_decode.h", ROOT / "include" / "edgecore.h",
            ROOT / "include" / "edgecore_b200.h"]

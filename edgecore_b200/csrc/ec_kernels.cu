@@ -516,6 +516,11 @@ extern "C" int ec_launch_gemm(const ec_gemm_args *args, cudaStream_t stream) {
     if (a.M <= 0 || a.N <= 0) return 0;
     if (a.ldw == 0) a.ldw = a.Kp;
     if (a.Kp % 16 || a.ldw < a.Kp || (a.ldw * (a.wt == EC_W_I8 ? 1 : 2)) % 16) return (int)cudaErrorInvalidValue;
+    if (a.wt == EC_W_I8 && a.M >= EC_TC_MIN_M) {   // tensor cores unless the operands miss their alignment rules
+        const int rc = ec_launch_gemm_tc(&a, stream);
+        if (rc != (int)cudaErrorNotSupported) return rc;
+        cudaGetLastError();
+    }
     dim3 grid((a.N + GT_BN - 1) / GT_BN, (a.M + GT_BM - 1) / GT_BM);
     if (grid.y > 65535) return (int)cudaErrorInvalidValue;
     if (a.wt == EC_W_I8) k_gemm_i8<<<grid, 256, 0, stream>>>(a);
@@ -1064,5 +1069,6 @@ extern "C" int ec_kernel_error_take(cudaStream_t stream, int *code) {
     if (e != cudaSuccess) return (int)e;
     if (*code) e = cudaMemcpyToSymbolAsync(g_ec_err, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e == cudaSuccess && !*code) e = (cudaError_t)ec_tc_error_take(code);
     return (int)e;
 }

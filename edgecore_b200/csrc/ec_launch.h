@@ -89,6 +89,13 @@ typedef struct {
 } ec_gemm_args;
 int ec_launch_gemm(const ec_gemm_args *a, cudaStream_t stream);
 
+/* The int8-weight GEMM on tcgen05 tensor cores (ec_tc.cu), used by
+ * ec_launch_gemm for M >= EC_TC_MIN_M; cudaErrorNotSupported when the operands
+ * miss its alignment rules.  ec_tc_error_take reads and clears its error word. */
+#define EC_TC_MIN_M 32
+int ec_launch_gemm_tc(const ec_gemm_args *a, cudaStream_t stream);
+int ec_tc_error_take(int *code);
+
 /* Per-row symmetric int8 quantisation of X [M][ldx] (K used, Kp written). */
 int ec_launch_quant(int8_t *q, float *scale, const float *X, int ldx, int M, int K, int Kp,
                     cudaStream_t stream);
