@@ -57,6 +57,12 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=512)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--op-sweep", action="store_true",
+                    help="instead of the decode benchmark: BASELINE config 1's int8 operator sweep "
+                         "(M in 1/8/64/512 and the 16384 prefill rows of config 3, Qwen2.5-0.5B (N,K) shapes), "
+                         "one JSON line per shape")
+    ap.add_argument("--sweep-m", type=int, default=0, help="--op-sweep: only this M")
+    ap.add_argument("--sweep-n", type=int, default=0, help="--op-sweep: only this N")
     return ap.parse_args()
 
 
@@ -310,8 +316,48 @@ def ours_arm(args, rank: int, world: int, local: int) -> None:
         dist.destroy_process_group()
 
 
+def op_sweep(args) -> None:
+    """gemm_int8 through the C ABI with device operands: X int8 [M][K] (the
+    A2 quantisation output), W int8 [N][K], per-row scales.  Times include the
+    entry point's host work and its synchronisation per call; kernel-only
+    times come from ncu on the same command."""
+    import torch
+
+    import edgecore_b200 as ec
+    torch.manual_seed(0)
+    for M in (1, 8, 64, 512, 16384):
+        for N, K in ((1152, 896), (896, 896), (4864, 896), (896, 4864), (151936, 896)):
+            if M == 16384 and N == 151936:
+                continue   # fp16 in the model; 9.9 GB of fp32 output
+            if (args.sweep_m and M != args.sweep_m) or (args.sweep_n and N != args.sweep_n):
+                continue
+            A = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda")
+            W = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda")
+            a_s = torch.rand(M, device="cuda") * 1e-2 + 1e-3
+            w_s = torch.rand(N, device="cuda") * 1.9e-2 + 1e-3
+            out = torch.empty((M, N), device="cuda")
+            for _ in range(max(args.warmup, 3)):
+                ec.gemm_int8(A, a_s, W, w_s, out=out)
+            torch.cuda.synchronize()
+            reps = 20
+            t0 = time.perf_counter()
+            for _ in range(reps):
+                ec.gemm_int8(A, a_s, W, w_s, out=out)
+            torch.cuda.synchronize()
+            us = (time.perf_counter() - t0) / reps * 1e6
+            algo = N * K + 4 * N + M * K + 4 * M + 4 * M * N
+            print(json.dumps({"op_sweep": "gemm_int8", "M": M, "N": N, "K": K, "us_per_call": us,
+                              "int8_tops": 2.0 * M * N * K / us / 1e6, "algorithmic_gbs": algo / us / 1e3,
+                              "path": "tcgen05" if M >= 32 else "weight-streaming GEMV" if M <= 8 else "SIMT"}),
+                  flush=True)
+            del A, W, out
+
+
 def main():
     args = parse()
+    if args.op_sweep:
+        op_sweep(args)
+        return
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
