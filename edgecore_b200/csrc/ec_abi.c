@@ -20,7 +20,7 @@
 #define EC_EXPORT __attribute__((visibility("default")))
 #define EC_MAX_DEV 16
 
-enum { S_A, S_AS, S_B, S_BS, S_BIAS, S_C, S_Q, S_QS, S_N };
+enum { S_A, S_AS, S_B, S_BS, S_BIAS, S_C, S_Q, S_QS, S_SPLIT, S_N };
 
 static pthread_mutex_t g_abi_mu = PTHREAD_MUTEX_INITIALIZER;
 static struct { void *p[S_N]; size_t cap[S_N]; int sms; } g_scr[EC_MAX_DEV];
@@ -158,6 +158,11 @@ static int run_linear(abi_ctx *c, int wt, float *C, const float *X, const int8_t
             const void *dX;
             if (dev_view(c, S_A, X, M, K, K, 4, &dX)) return -1;
             g.X = dX; g.ldx = K;
+            if (M >= EC_TC_MIN_M) {   /* tensor cores: activation parts workspace */
+                g.split_bytes = ec_gemm_tc_split_bytes(wt, M, Kp);
+                g.split = scratch(c->dev, S_SPLIT, g.split_bytes);
+                if (!g.split) g.split_bytes = 0;
+            }
         }
         ACK(ec_launch_gemm(&g, 0));
         m0 = M;

@@ -238,6 +238,8 @@ typedef struct ec_dev {
     float *x, *h, *qkv, *q, *att, *act, *big;
     int8_t *aq;
     float *as;
+    void *split;          /* 16-bit activation parts for the tensor-core GEMMs */
+    size_t split_bytes;
     float *attn_part;
     size_t attn_part_floats;
     float *logits;
@@ -540,6 +542,9 @@ static void ec_free_work(ec_dev *d)
     cudaFreeHost(d->h_in); cudaFreeHost(d->h_ids); cudaFreeHost(d->h_max);
     d->x = d->h = d->qkv = d->q = d->att = d->act = d->big = NULL;
     d->aq = NULL;
+    cudaFree(d->split);
+    d->split = NULL;
+    d->split_bytes = 0;
     d->as = NULL;
     d->d_tok = d->d_pos = d->d_slot = d->d_ids = NULL;
     d->d_max = NULL;
@@ -570,6 +575,10 @@ static int ec_ensure(ec_dev *d, int M)
     CK(cudaMalloc((void **)&d->big, (size_t)cap * big * 4));
     CK(cudaMalloc((void **)&d->aq, (size_t)cap * kmax));
     CK(cudaMalloc((void **)&d->as, (size_t)cap * 4));
+    if (cap >= EC_TC_MIN_M) {   /* the lm_head is always 16-bit; bf16 needs three parts */
+        d->split_bytes = ec_gemm_tc_split_bytes(d->prec == 2 ? EC_W_BF16 : EC_W_F16, cap, kmax);
+        CK(cudaMalloc(&d->split, d->split_bytes));
+    }
     CK(cudaMalloc((void **)&d->d_tok, (size_t)cap * 4));
     CK(cudaMalloc((void **)&d->d_pos, (size_t)cap * 4));
     CK(cudaMalloc((void **)&d->d_slot, (size_t)cap * 4));
@@ -1044,6 +1053,7 @@ static int ec_linear(ec_dev *d, const ec_lin *l, const float *X, int ldx, int M,
         g.ldx = ldx;
     }
     g.out = out; g.ldo = ldo; g.epi = epi;
+    g.split = d->split; g.split_bytes = d->split_bytes;
     CK(ec_launch_gemm(&g, st));
     ec_prof_end(d, pi);
     return 0;

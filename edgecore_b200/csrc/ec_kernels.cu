@@ -516,7 +516,7 @@ extern "C" int ec_launch_gemm(const ec_gemm_args *args, cudaStream_t stream) {
     if (a.M <= 0 || a.N <= 0) return 0;
     if (a.ldw == 0) a.ldw = a.Kp;
     if (a.Kp % 16 || a.ldw < a.Kp || (a.ldw * (a.wt == EC_W_I8 ? 1 : 2)) % 16) return (int)cudaErrorInvalidValue;
-    if (a.wt == EC_W_I8 && a.M >= EC_TC_MIN_M) {   // tensor cores unless the operands miss their alignment rules
+    if (a.M >= EC_TC_MIN_M) {   // tensor cores unless the operands miss their alignment rules
         const int rc = ec_launch_gemm_tc(&a, stream);
         if (rc != (int)cudaErrorNotSupported) return rc;
         cudaGetLastError();

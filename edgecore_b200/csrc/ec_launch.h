@@ -86,14 +86,20 @@ typedef struct {
     const float *X; int ldx;                  /* 16-bit weights */
     int M;
     float *out; int ldo; int epi;
+    void *split; size_t split_bytes;          /* 16-bit weights on tensor cores: workspace
+                                                 of ec_gemm_tc_split_bytes() bytes,
+                                                 256-byte aligned (NULL: SIMT kernel) */
 } ec_gemm_args;
 int ec_launch_gemm(const ec_gemm_args *a, cudaStream_t stream);
 
-/* The int8-weight GEMM on tcgen05 tensor cores (ec_tc.cu), used by
- * ec_launch_gemm for M >= EC_TC_MIN_M; cudaErrorNotSupported when the operands
- * miss its alignment rules.  ec_tc_error_take reads and clears its error word. */
+/* The GEMMs on tcgen05 tensor cores (ec_tc.cu), used by ec_launch_gemm for
+ * M >= EC_TC_MIN_M: int8 weights directly, fp16/bf16 weights with the
+ * activations split into 16-bit parts in the `split` workspace;
+ * cudaErrorNotSupported when the operands miss its alignment rules.
+ * ec_tc_error_take reads and clears its error word. */
 #define EC_TC_MIN_M 32
 int ec_launch_gemm_tc(const ec_gemm_args *a, cudaStream_t stream);
+size_t ec_gemm_tc_split_bytes(int wt, int M, int Kp);
 int ec_tc_error_take(int *code);
 
 /* Per-row symmetric int8 quantisation of X [M][ldx] (K used, Kp written). */

@@ -1,23 +1,35 @@
-// ec_tc.cu -- W8A8 GEMM on the 5th-generation tensor cores (tcgen05):
-//   out[m][n] = epi( bias[n] + ((float)(sum_k Aq[m][k] * W[n][k]) * a_scale[m]) * w_scale[n] )
-// with Aq int8 [M][Kp] (row stride Kp), W int8 [N][ldw] (K-major rows, the
-// packed layout of the host code), int32 accumulation in tensor memory.  The
-// int8 x int8 products and their int32 sums are exact, so the result is
-// bit-identical to the reference gemm_int8 (src/kernels.c:153-168) and to the
-// SIMT kernels, whatever the order of the tensor core's additions.
+// ec_tc.cu -- GEMMs on the 5th-generation tensor cores (tcgen05) for M >= 32
+// rows (prefill, batched decode):
 //
-// Persistent CTAs (one per SM) walk 128 x 256 output tiles
-// (tcgen05.mma.cta_group::1.kind::i8, M = 128, N = 256, K = 32 per
-// instruction) over K in 128-byte stages:
-//   warp 0     TMA producer: A [128][128 B] and W [256][128 B] boxes with the
-//              128-byte swizzle into a 4-stage ring that runs across tiles
-//   warp 1     allocates all 512 TMEM columns = two 256-column accumulators;
-//              one thread issues the MMAs of a tile into the free accumulator
-//              and commits stages back to the producer, the accumulator to
-//              the epilogue
+//   int8 weights (kind::i8):
+//     out[m][n] = epi( bias[n] + ((float)(sum_k Aq[m][k] * W[n][k]) * a_scale[m]) * w_scale[n] )
+//   Aq int8 [M][Kp] = the quantised activations; int32 accumulation in tensor
+//   memory.  Products and sums are exact integers, so the result is
+//   bit-identical to the reference gemm_int8 (src/kernels.c:153-168).
+//
+//   fp16 / bf16 weights (kind::f16):
+//     out[m][n] = epi( (sum_k X[m][k] * W[n][k]) (+ bias[n]) )
+//   with X fp32.  An MMA needs A and B of the same 16-bit type, so a pre-pass
+//   (k_split16) writes each activation row as S 16-bit parts whose sum is the
+//   fp32 value: fp16 weights -> hi + lo fp16 of the row scaled by an exact
+//   power of two (max |x| in [2^13, 2^14)), ~2^-22 relative; bf16 weights ->
+//   three bf16 parts, ~2^-27.  Every part is one more MMA against the same W
+//   tile; fp32 accumulation; the epilogue multiplies the power of two back
+//   exactly.  The result differs from the reference's fp32 dot (8-lane AVX2
+//   order, src/kernels.c:29-64) only by summation order, like the SIMT path.
+//
+// Persistent CTAs (one per SM) walk 128 x BN output tiles over K in 128-byte
+// stages:
+//   warp 0     TMA producer: the A part boxes [128][128 B] and the W box
+//              [BN][128 B] with the 128-byte swizzle into a ring that runs
+//              across tiles
+//   warp 1     allocates 2 x BN TMEM columns = two accumulators; one thread
+//              issues the MMAs of a tile into the free accumulator and
+//              commits stages back to the producer, the accumulator to the
+//              epilogue
 //   warps 2-9  epilogue of the other accumulator meanwhile: tcgen05.ld (warp
 //              w reads TMEM lanes 32*(w%4)..+31 = tile rows; warps w and w+4
-//              split the 256 columns), scale and bias per element, transpose
+//              split the columns), scale and bias per element, transpose
 //              through shared memory, coalesced 16-byte stores (store,
 //              residual add or GELU)
 // Loads never use cluster multicast; every wait is bounded and TMEM is freed
@@ -28,23 +40,43 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <pthread.h>
+#include <string.h>
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BKB = 128;          // tile rows, tile cols, K bytes per stage
-constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BKB, B_BYTES = BN * BKB;  // 16 KB + 32 KB per stage
+constexpr int BM = 128, BKB = 128;                     // tile rows, K bytes per stage
 constexpr int THREADS = 320;                           // producer, MMA, 8 epilogue warps
-constexpr int TMEM_COLS = 512;                         // two 256-column accumulators
 constexpr int EPI_WARPS = 8, EPI_COLS = 16;           // two warps per TMEM lane group, 16-column chunks
 constexpr int EPI_LD = 20;                             // staging row stride (floats): 16-byte rows, no bank conflicts
 constexpr int EPI_BYTES = EPI_WARPS * 32 * EPI_LD * 4;
-constexpr int CST_BYTES = EPI_WARPS * 2 * (BN / 2) * 4;      // per epilogue warp: w_scale and bias of its 128 columns
-constexpr int SMEM_BYTES = 1024 /* alignment slack */ + STAGES * (A_BYTES + B_BYTES) + EPI_BYTES + CST_BYTES + 256;
+constexpr int A_BYTES = BM * BKB;                      // one A part per stage: 16 KB
 
-// Instruction descriptor, kind::i8: D = s32, A = B = signed 8-bit, both
-// K-major, N = 256, M = 128.
-constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+// Per weight type: A parts, tile columns, ring depth, instruction descriptor.
+// Instruction descriptor fields: [4,6) D format (1 f32, 2 s32), [7,10) A and
+// [10,13) B format (i8: 1 = signed; f16 kind: 0 = f16, 1 = bf16), bits 15/16
+// K-major (0), [17,23) N >> 3, [24,29) M >> 4.
+template <int WT> struct TcCfg;
+template <> struct TcCfg<EC_W_I8> {
+    static constexpr int S = 1, BN = 256, STAGES = 4, ELT = 1;
+    static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+};
+template <> struct TcCfg<EC_W_F16> {
+    static constexpr int S = 2, BN = 256, STAGES = 3, ELT = 2;
+    static constexpr uint32_t IDESC = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+};
+template <> struct TcCfg<EC_W_BF16> {
+    static constexpr int S = 3, BN = 128, STAGES = 3, ELT = 2;
+    static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+};
+
+template <int WT> __host__ __device__ constexpr int b_bytes() { return TcCfg<WT>::BN * BKB; }
+template <int WT> __host__ __device__ constexpr int stage_bytes() { return TcCfg<WT>::S * A_BYTES + b_bytes<WT>(); }
+template <int WT> __host__ __device__ constexpr int cst_bytes() { return EPI_WARPS * 2 * (TcCfg<WT>::BN / 2) * 4; }
+template <int WT> __host__ __device__ constexpr int smem_bytes() {
+    return 1024 /* alignment slack */ + TcCfg<WT>::STAGES * stage_bytes<WT>() + EPI_BYTES + cst_bytes<WT>() + 256;
+}
+static_assert(smem_bytes<EC_W_I8>() <= 232448 && smem_bytes<EC_W_F16>() <= 232448 && smem_bytes<EC_W_BF16>() <= 232448,
+              "shared memory per CTA");
 
 __device__ int g_tc_err;
 
@@ -63,12 +95,20 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
         ::"r"(dst), "l"(map), "r"(bar), "r"(x), "r"(y) : "memory");
 }
 
-__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-        ::"r"(tmem_d), "l"(da), "l"(db), "r"(IDESC), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+template <int WT>
+__device__ __forceinline__ void mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+    if (WT == EC_W_I8)
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+            ::"r"(tmem_d), "l"(da), "l"(db), "r"(TcCfg<WT>::IDESC), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+    else
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+            ::"r"(tmem_d), "l"(da), "l"(db), "r"(TcCfg<WT>::IDESC), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
 }
 
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
@@ -77,18 +117,6 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// Bounded wait on an mbarrier phase; false (and the error word set) if it
-// never completes or another role has already given up.
-__device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile int *stop) {
-    for (uint32_t i = 0; i < EC_WAIT_LIMIT; ++i) {
-        if (ec_mbar_try_wait(bar, parity)) return true;
-        if (*stop) return false;
-    }
-    *stop = 1;
-    atomicCAS(&g_tc_err, 0, EC_KERR_WAIT_TIMEOUT);
-    return false;
-}
 
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
@@ -103,17 +131,40 @@ __device__ __forceinline__ float epi_apply(int epi, float o, float v) {
     return epi == EC_EPI_RESID ? __fadd_rn(o, v) : epi == EC_EPI_GELU ? ec_gelu(v) : v;
 }
 
+// Bounded wait on an mbarrier phase; false (and the error word set) if it
+// never completes or another role has already given up.
+__device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile int *stop) {
+    for (uint32_t i = 0; i < EC_WAIT_LIMIT; ++i) {
+        if (ec_mbar_try_wait(bar, parity)) return true;
+        if (*stop) return false;
+    }
+    *stop = 1;
+    atomicCAS(&g_tc_err, 0, EC_KERR_WAIT_TIMEOUT);
+    return false;
+}
+
+struct TcMaps {
+    CUtensorMap a[3];   // A parts (one for int8)
+    CUtensorMap b;      // weights
+};
+
+// row_scale: a_scale (int8) or the power-of-two row scale of the split (16-bit)
+template <int WT>
 __global__ void __launch_bounds__(THREADS, 1)
-k_gemm_tc_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const ec_gemm_args a,
-             int flags) {   // bit 0: 16-byte aligned output rows
+k_gemm_tc(const __grid_constant__ TcMaps maps, const ec_gemm_args a, const float *row_scale,
+          int flags) {   // bit 0: 16-byte aligned output rows
+    constexpr int S = TcCfg<WT>::S, BN = TcCfg<WT>::BN, STAGES = TcCfg<WT>::STAGES;
+    constexpr int SB = stage_bytes<WT>();
+    constexpr int KSTEP = 32;                                      // bytes of K per MMA instruction (both kinds)
+    constexpr int TMEM_COLS = 2 * BN;                              // two accumulators
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t raw = ec_smem_u32(smem_raw);
-    const uint32_t base = (raw + 1023u) & ~1023u;                       // 1024-byte aligned (128-byte swizzle atoms)
+    const uint32_t base = (raw + 1023u) & ~1023u;                  // 1024-byte aligned (128-byte swizzle atoms)
     unsigned char *gbase = smem_raw + (base - raw);
-    const uint32_t sA = base, sB = base + STAGES * A_BYTES;
-    float *stage_out = reinterpret_cast<float *>(gbase + STAGES * (A_BYTES + B_BYTES));
-    float *cst = reinterpret_cast<float *>(gbase + STAGES * (A_BYTES + B_BYTES) + EPI_BYTES);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(gbase + STAGES * (A_BYTES + B_BYTES) + EPI_BYTES + CST_BYTES);
+    // stage s: A parts at base + s*SB + p*A_BYTES, W at base + s*SB + S*A_BYTES
+    float *stage_out = reinterpret_cast<float *>(gbase + STAGES * SB);
+    float *cst = reinterpret_cast<float *>(gbase + STAGES * SB + EPI_BYTES);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(gbase + STAGES * SB + EPI_BYTES + cst_bytes<WT>());
     uint64_t *full = bars, *empty = bars + STAGES;
     uint64_t *accf = bars + 2 * STAGES, *acce = accf + 2, *drain = acce + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
@@ -122,7 +173,9 @@ k_gemm_tc_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
     int *consumed = issued + 1;                  // ... and whose loads the MMA thread waited for
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nk = (a.Kp + BKB - 1) / BKB;
+    const int kbytes = a.Kp * TcCfg<WT>::ELT;
+    const int nk = (kbytes + BKB - 1) / BKB;
+    const int kel = BKB / TcCfg<WT>::ELT;                          // K elements per stage
     const int mt = (a.M + BM - 1) / BM, nt = (a.N + BN - 1) / BN;
     const int tiles = mt * nt;
 
@@ -158,9 +211,11 @@ k_gemm_tc_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
                 for (int kb = 0; kb < nk; ++kb, ++g) {
                     const int s = g % STAGES;
                     if (g >= STAGES && !tc_wait(&empty[s], (uint32_t)((g / STAGES - 1) & 1), stop)) break;
-                    ec_mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
-                    tma_load_2d(sA + s * A_BYTES, &tmA, ec_smem_u32(&full[s]), kb * BKB, m0);
-                    tma_load_2d(sB + s * B_BYTES, &tmB, ec_smem_u32(&full[s]), kb * BKB, n0);
+                    const uint32_t st = base + (uint32_t)(s * SB);
+                    ec_mbar_expect_tx(&full[s], (uint32_t)SB);
+#pragma unroll
+                    for (int p = 0; p < S; ++p) tma_load_2d(st + p * A_BYTES, &maps.a[p], ec_smem_u32(&full[s]), kb * kel, m0);
+                    tma_load_2d(st + S * A_BYTES, &maps.b, ec_smem_u32(&full[s]), kb * kel, n0);
                     *issued = g + 1;
                 }
             }
@@ -178,10 +233,13 @@ k_gemm_tc_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
                     const int s = g % STAGES;
                     if (!tc_wait(&full[s], (uint32_t)((g / STAGES) & 1), stop)) { ok = false; break; }
                     tc_fence_after();
-                    const uint64_t da = sw128_desc(sA + s * A_BYTES), db = sw128_desc(sB + s * B_BYTES);
+                    const uint32_t st = base + (uint32_t)(s * SB);
+                    const uint64_t db = sw128_desc(st + S * A_BYTES);
 #pragma unroll
-                    for (int k = 0; k < BKB / 32; ++k)   // 32 bytes of K per instruction: +2 in 16-byte units
-                        mma_i8(d, da + 2 * k, db + 2 * k, (kb | k) != 0);
+                    for (int k = 0; k < BKB / KSTEP; ++k)     // +2 in 16-byte units per 32 bytes of K
+#pragma unroll
+                        for (int p = 0; p < S; ++p)
+                            mma<WT>(d, sw128_desc(st + p * A_BYTES) + 2 * k, db + 2 * k, (kb | k | p) != 0);
                     mma_commit(ec_smem_u32(&empty[s]));   // stage reusable once these MMAs have read it
                     *consumed = g + 1;
                 }
@@ -195,8 +253,9 @@ k_gemm_tc_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
     } else {   // epilogue: warps 2..9
         const int lg = warp & 3;                 // TMEM lane group this warp may access
         const int ch = (warp - 2) >> 2;          // column half of the tile
+        constexpr int HALF = BN / 2;
         float *st = stage_out + (size_t)(warp - 2) * 32 * EPI_LD;
-        float *cws = cst + (size_t)(warp - 2) * BN, *cb = cws + BN / 2;   // this warp's 128 columns
+        float *cws = cst + (size_t)(warp - 2) * BN, *cb = cws + HALF;   // this warp's columns
         const bool vec_out = flags & 1;
         int tc = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++tc) {
@@ -206,12 +265,12 @@ k_gemm_tc_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
             // their latency hides behind the MMAs: the row scale of this lane
             // and w_scale / bias of the warp's columns (lane j: j, j+32, ...).
             const int mrow = m0 + lg * 32 + lane;          // this lane's row in the TMEM read
-            const float as = mrow < a.M ? __ldg(a.a_scale + mrow) : 0.0f;
-            float cw[4], cbv[4];
+            const float rs = mrow < a.M ? __ldg(row_scale + mrow) : 0.0f;
+            float cw[HALF / 32], cbv[HALF / 32];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int n = n0 + ch * (BN / 2) + lane + 32 * q;
-                cw[q] = a.wscale && n < a.N ? __ldg(a.wscale + n) : 1.0f;
+            for (int q = 0; q < HALF / 32; ++q) {
+                const int n = n0 + ch * HALF + lane + 32 * q;
+                cw[q] = WT == EC_W_I8 && a.wscale && n < a.N ? __ldg(a.wscale + n) : 1.0f;
                 cbv[q] = a.bias && n < a.N ? __ldg(a.bias + n) : 0.0f;
             }
             int ready = 0;   // one lane waits; the warp takes its answer (tcgen05.ld is warp-collective)
@@ -220,28 +279,33 @@ k_gemm_tc_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
             if (!ready) break;
             tc_fence_after();
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
+            for (int q = 0; q < HALF / 32; ++q) {
                 cws[lane + 32 * q] = cw[q];
                 cb[lane + 32 * q] = cbv[q];
             }
             __syncwarp();
-            for (int c0 = ch * (BN / 2); c0 < (ch + 1) * (BN / 2) && n0 + c0 < a.N; c0 += EPI_COLS) {
+            for (int c0 = ch * HALF; c0 < (ch + 1) * HALF && n0 + c0 < a.N; c0 += EPI_COLS) {
                 uint32_t r[16];
                 tmem_ld16(tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)(b * BN + c0), r);
                 // scale + bias in the row-per-lane layout; the column constants
-                // are the same for every lane (broadcast loads, 4 at a time)
+                // are the same for every lane (broadcast reads, 4 at a time)
 #pragma unroll
                 for (int j = 0; j < EPI_COLS; j += 4) {
-                    const int cc = c0 - ch * (BN / 2) + j;           // column within this warp's half
-                    const float4 ws4 = *reinterpret_cast<const float4 *>(cws + cc);   // broadcast reads
+                    const int cc = c0 - ch * HALF + j;              // column within this warp's half
+                    const float4 ws4 = *reinterpret_cast<const float4 *>(cws + cc);
                     const float4 bs4 = *reinterpret_cast<const float4 *>(cb + cc);
                     const float ws[4] = {ws4.x, ws4.y, ws4.z, ws4.w}, bs[4] = {bs4.x, bs4.y, bs4.z, bs4.w};
-                    float4 v;
-                    v.x = __fadd_rn(bs[0], __fmul_rn(__fmul_rn(__int2float_rn((int)r[j + 0]), as), ws[0]));
-                    v.y = __fadd_rn(bs[1], __fmul_rn(__fmul_rn(__int2float_rn((int)r[j + 1]), as), ws[1]));
-                    v.z = __fadd_rn(bs[2], __fmul_rn(__fmul_rn(__int2float_rn((int)r[j + 2]), as), ws[2]));
-                    v.w = __fadd_rn(bs[3], __fmul_rn(__fmul_rn(__int2float_rn((int)r[j + 3]), as), ws[3]));
-                    *reinterpret_cast<float4 *>(st + lane * EPI_LD + j) = v;
+                    float vv[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        if (WT == EC_W_I8) {
+                            vv[e] = __fadd_rn(bs[e], __fmul_rn(__fmul_rn(__int2float_rn((int)r[j + e]), rs), ws[e]));
+                        } else {
+                            const float dot = __fmul_rn(__uint_as_float(r[j + e]), rs);   // exact: power of two
+                            vv[e] = a.bias ? __fadd_rn(dot, bs[e]) : dot;
+                        }
+                    }
+                    *reinterpret_cast<float4 *>(st + lane * EPI_LD + j) = make_float4(vv[0], vv[1], vv[2], vv[3]);
                 }
                 __syncwarp();
                 // coalesced: 4 lanes per row (16 bytes each), 8 rows per pass
@@ -262,8 +326,8 @@ k_gemm_tc_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
                         }
                         *reinterpret_cast<float4 *>(o) = w;
                     } else {
-                        const float *vv = reinterpret_cast<const float *>(&v);
-                        for (int e = 0; e < 4 && n + e < a.N; ++e) o[e] = epi_apply(a.epi, o[e], vv[e]);
+                        const float *vp = reinterpret_cast<const float *>(&v);
+                        for (int e = 0; e < 4 && n + e < a.N; ++e) o[e] = epi_apply(a.epi, o[e], vp[e]);
                     }
                 }
                 __syncwarp();
@@ -290,9 +354,57 @@ k_gemm_tc_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
     }
 }
 
+// Activation rows fp32 [M][ldx] -> S 16-bit parts [S][M][Kp] (zero padded
+// past K) whose sum is the row times 2^-e, and rscale[m] = 2^e (see the file
+// comment).  One CTA per row.
+template <int WT>
+__global__ void __launch_bounds__(256) k_split16(uint16_t *parts, float *rscale, const float *X, int ldx, int M, int K,
+                                                 int Kp) {
+    const int m = blockIdx.x;
+    const float *x = X + (size_t)m * ldx;
+    __shared__ float red[8];
+    float sm = 1.0f, rs = 1.0f;
+    if (WT == EC_W_F16) {
+        float mx = 0.0f;
+        for (int k = threadIdx.x; k < K; k += blockDim.x) mx = ec_max_keep(mx, fabsf(x[k]));
+        mx = ec_warp_max(mx);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+        __syncthreads();
+        mx = red[0];
+        for (int i = 1; i < 8; ++i) mx = ec_max_keep(mx, red[i]);
+        if (mx > 0.0f && mx < INFINITY) {   // max |x| * 2^-e in [2^13, 2^14)
+            int ex;
+            frexpf(mx, &ex);
+            sm = ldexpf(1.0f, 14 - ex);
+            rs = ldexpf(1.0f, ex - 14);
+        }
+    }
+    if (threadIdx.x == 0) rscale[m] = rs;
+    const size_t plane = (size_t)M * Kp;
+    uint16_t *p0 = parts + (size_t)m * Kp;
+    for (int k = threadIdx.x; k < Kp; k += blockDim.x) {
+        const float v = k < K ? __fmul_rn(x[k], sm) : 0.0f;
+        if (WT == EC_W_F16) {
+            const __half h = __float2half_rn(v);
+            const float r = __fsub_rn(v, __half2float(h));
+            p0[k] = __half_as_ushort(h);
+            p0[plane + k] = __half_as_ushort(__float2half_rn(r));
+        } else {
+            const __nv_bfloat16 b0 = __float2bfloat16_rn(v);
+            const float r1 = __fsub_rn(v, __bfloat162float(b0));
+            const __nv_bfloat16 b1 = __float2bfloat16_rn(r1);
+            const float r2 = __fsub_rn(r1, __bfloat162float(b1));
+            p0[k] = __bfloat16_as_ushort(b0);
+            p0[plane + k] = __bfloat16_as_ushort(b1);
+            p0[2 * plane + k] = __bfloat16_as_ushort(__float2bfloat16_rn(r2));
+        }
+    }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 pthread_once_t g_once = PTHREAD_ONCE_INIT;
-int g_attr_set[64];
+int g_attr_set[3][64];
+int g_sms[64];
 
 void resolve_encode() {
     void *fn = nullptr;
@@ -302,54 +414,100 @@ void resolve_encode() {
         g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
 }
 
-// 2-D map of an int8 [rows][inner] matrix with row stride `stride` bytes, box
-// [box_rows][128 bytes], 128-byte swizzle; out-of-range elements read as 0.
-int make_map(CUtensorMap *map, const void *ptr, int inner, int rows, int stride, int box_rows) {
+// 2-D map of a [rows][inner] matrix of 1- or 2-byte elements with row stride
+// `stride` bytes, box [box_rows][128 bytes], 128-byte swizzle; out-of-range
+// elements read as 0.
+int make_map(CUtensorMap *map, const void *ptr, int elt, int inner, int rows, int stride, int box_rows) {
     const cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)stride};
-    const cuuint32_t box[2] = {(cuuint32_t)BKB, (cuuint32_t)box_rows};
+    const cuuint32_t box[2] = {(cuuint32_t)(BKB / elt), (cuuint32_t)box_rows};
     const cuuint32_t es[2] = {1, 1};
-    const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(ptr), dims, strides, box, es,
-                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const CUresult r = g_encode(map, elt == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 2,
+                                const_cast<void *>(ptr), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
+}
+
+template <int WT>
+int launch(const ec_gemm_args &a, const void *const *aparts, const float *row_scale, int dev, cudaStream_t stream) {
+    constexpr int S = TcCfg<WT>::S, BN = TcCfg<WT>::BN, ELT = TcCfg<WT>::ELT;
+    if (!g_attr_set[WT][dev]) {
+        const cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes<WT>());
+        if (e != cudaSuccess) return (int)e;
+        g_attr_set[WT][dev] = 1;
+    }
+    TcMaps maps;
+    memset(&maps, 0, sizeof maps);
+    int rc = 0;
+    for (int p = 0; p < S && !rc; ++p) rc = make_map(&maps.a[p], aparts[p], ELT, a.Kp, a.M, a.Kp * ELT, BM);
+    if (!rc) rc = make_map(&maps.b, a.W, ELT, a.Kp, a.N, a.ldw * ELT, BN);
+    if (rc) return rc;
+    const long long tiles = (long long)((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
+    if (tiles > 0x7fffffffLL) return (int)cudaErrorInvalidValue;
+    const int grid = (int)(tiles < (long long)g_sms[dev] ? tiles : g_sms[dev]);
+    const int flags = (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 && (a.ldo & 3) == 0 ? 1 : 0;
+    k_gemm_tc<WT><<<grid, THREADS, smem_bytes<WT>(), stream>>>(maps, a, row_scale, flags);
+    return (int)cudaGetLastError();
 }
 
 }  // namespace
 
-// Tensor-core path for int8 weights; returns cudaErrorNotSupported when the
-// operands do not meet its alignment rules (the caller then uses the SIMT
-// kernel).
+extern "C" size_t ec_gemm_tc_split_bytes(int wt, int M, int Kp) {
+    if (wt == EC_W_I8) return 0;
+    const size_t S = wt == EC_W_F16 ? 2 : 3;
+    return (S * (size_t)M * Kp * 2 + 255) / 256 * 256 + (size_t)M * 4;
+}
+
+// Tensor-core path (M >= EC_TC_MIN_M); cudaErrorNotSupported when the
+// operands miss its alignment rules or a 16-bit GEMM has no split workspace
+// (the caller then uses the SIMT kernel).
 extern "C" int ec_launch_gemm_tc(const ec_gemm_args *args, cudaStream_t stream) {
     ec_gemm_args a = *args;
     if (a.M <= 0 || a.N <= 0) return 0;
     if (a.ldw == 0) a.ldw = a.Kp;
-    if (a.wt != EC_W_I8 || !a.Aq || !a.a_scale || a.Kp % 16 || a.ldw % 16 || a.ldw < a.Kp ||
-        (reinterpret_cast<uintptr_t>(a.Aq) & 15) || (reinterpret_cast<uintptr_t>(a.W) & 15) ||
+    const int elt = a.wt == EC_W_I8 ? 1 : 2;
+    if (a.Kp % 16 || (a.ldw * elt) % 16 || a.ldw < a.Kp || (reinterpret_cast<uintptr_t>(a.W) & 15) ||
         (a.epi != EC_EPI_STORE && a.epi != EC_EPI_RESID && a.epi != EC_EPI_GELU))
         return (int)cudaErrorNotSupported;
+    if (a.wt == EC_W_I8) {
+        if (!a.Aq || !a.a_scale || (reinterpret_cast<uintptr_t>(a.Aq) & 15)) return (int)cudaErrorNotSupported;
+    } else {
+        if (!a.X || !a.split || a.split_bytes < ec_gemm_tc_split_bytes(a.wt, a.M, a.Kp) ||
+            (reinterpret_cast<uintptr_t>(a.split) & 255))
+            return (int)cudaErrorNotSupported;
+    }
     pthread_once(&g_once, resolve_encode);
     if (!g_encode) return (int)cudaErrorNotSupported;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return (int)e;
-    if (dev >= 0 && dev < 64 && !g_attr_set[dev]) {
-        e = cudaFuncSetAttribute(k_gemm_tc_i8, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (dev < 0 || dev >= 64) return (int)cudaErrorNotSupported;
+    if (!g_sms[dev]) {
+        e = cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return (int)e;
-        g_attr_set[dev] = 1;
     }
-    CUtensorMap ta, tb;
-    int rc = make_map(&ta, a.Aq, a.Kp, a.M, a.Kp, BM);
-    if (!rc) rc = make_map(&tb, a.W, a.Kp, a.N, a.ldw, BN);
-    if (rc) return rc;
-    static int sms[64];
-    if (dev >= 0 && dev < 64 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-    const long long tiles = (long long)((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
-    if (tiles > 0x7fffffffLL) return (int)cudaErrorInvalidValue;
-    const int grid = (int)(tiles < (long long)sms[dev] ? tiles : sms[dev]);
-    const int flags = (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 && (a.ldo & 3) == 0 ? 1 : 0;
-    k_gemm_tc_i8<<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, a, flags);
-    return (int)cudaGetLastError();
+    if (a.wt == EC_W_I8) {
+        const void *parts[1] = {a.Aq};
+        return launch<EC_W_I8>(a, parts, a.a_scale, dev, stream);
+    }
+    // 16-bit weights: split the activations first (Kp % 16 == 0 keeps every
+    // part 16-byte aligned)
+    const size_t plane = (size_t)a.M * a.Kp;
+    uint16_t *parts16 = static_cast<uint16_t *>(a.split);
+    float *rscale = reinterpret_cast<float *>(static_cast<unsigned char *>(a.split) +
+                                              ((a.wt == EC_W_F16 ? 2 : 3) * plane * 2 + 255) / 256 * 256);
+    const void *parts[3] = {parts16, parts16 + plane, parts16 + 2 * plane};
+    if (a.wt == EC_W_F16) {
+        k_split16<EC_W_F16><<<a.M, 256, 0, stream>>>(parts16, rscale, a.X, a.ldx, a.M, a.K, a.Kp);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return (int)e;
+        return launch<EC_W_F16>(a, parts, rscale, dev, stream);
+    }
+    k_split16<EC_W_BF16><<<a.M, 256, 0, stream>>>(parts16, rscale, a.X, a.ldx, a.M, a.K, a.Kp);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return (int)e;
+    return launch<EC_W_BF16>(a, parts, rscale, dev, stream);
 }
 
 extern "C" int ec_tc_error_take(int *code) {
