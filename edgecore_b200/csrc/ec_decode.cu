@@ -68,18 +68,20 @@ enum { MI_QKV = 0, MI_O = 1, MI_UP = 2, MI_DOWN = 3, MI_LM = 4, MI_N = 5 };
             if (const int k = k0_ + j_ * NCT; k < (n))
 
 struct Lay {
-    uint32_t ring, xbuf, stage, nrm, redd, redf, redi, asc, ints, bars, lays, par, total;
+    uint32_t ring, xbuf, stage, nrm, rope, xown, redd, redf, redi, asc, ints, bars, lays, par, total;
 };
 
 __host__ __device__ inline uint32_t al16(uint32_t v) { return (v + 15u) & ~15u; }
 
-__host__ __device__ inline Lay mk_layout(int xbuf_bytes, int stage_bytes, int n_layer, int E) {
+__host__ __device__ inline Lay mk_layout(int xbuf_bytes, int stage_bytes, int n_layer, int E, int hd, int own_rows) {
     Lay L;
     uint32_t o = 0;
     L.ring = o;  o += STAGES * TILE;
     L.xbuf = o;  o += al16((uint32_t)xbuf_bytes);
     L.stage = o; o += al16((uint32_t)stage_bytes);
     L.nrm = o;   o += 2u * al16((uint32_t)E * 4u);
+    L.rope = o;  o += al16((uint32_t)MT * (uint32_t)hd * 8u);          // cos, sin rows of each token's position
+    L.xown = o;  o += al16((uint32_t)MT * (uint32_t)own_rows * 4u);    // residual rows owned by this CTA
     L.redd = o;  o += 2 * NCW * MT * 8;
     L.redf = o;  o += 2 * NCW * MT * 4;
     L.redi = o;  o += NCW * MT * 4;
@@ -100,6 +102,8 @@ struct Sm {
     unsigned char *ring, *xbuf;
     float *stage;
     float *nrm;               // norm gain [E] and bias [E] of the running norm
+    double *rope;             // [MT][hd/2] cos then [MT][hd/2] sin at each token's position
+    float *xown;              // [MT][own_rows] residual rows owned by this CTA (also in p.x)
     double *redd;             // [2][NCW][MT]: two slots, see red_sum_d
     float *redf;              // [2][NCW][MT]
     int *redi;
@@ -114,12 +118,14 @@ struct Sm {
 };
 
 __device__ __forceinline__ Sm sm_of(const ec_mk_params &p) {
-    const Lay L = mk_layout(p.xbuf_bytes, p.stage_bytes, p.L, p.E);
+    const Lay L = mk_layout(p.xbuf_bytes, p.stage_bytes, p.L, p.E, p.hd, p.own_rows);
     Sm S;
     S.ring = g_smem + L.ring;
     S.xbuf = g_smem + L.xbuf;
     S.stage = reinterpret_cast<float *>(g_smem + L.stage);
     S.nrm = reinterpret_cast<float *>(g_smem + L.nrm);
+    S.rope = reinterpret_cast<double *>(g_smem + L.rope);
+    S.xown = reinterpret_cast<float *>(g_smem + L.xown);
     S.redd = reinterpret_cast<double *>(g_smem + L.redd);
     S.redf = reinterpret_cast<float *>(g_smem + L.redf);
     S.redi = reinterpret_cast<int *>(g_smem + L.redi);
@@ -659,7 +665,7 @@ __device__ __noinline__ uint32_t mk_phase(const ec_mk_params &p, int kind, int l
                 if (p.arch == ARCH_Q2) {
                     if (n < p.E + p.kv) {   // rotated pair (i, i + hd/2) of a q or k head
                         const int head = n / p.hd, i2 = (n % p.hd) >> 1;
-                        const double c = p.rope_cos[(size_t)pos * half + i2], sn = p.rope_sin[(size_t)pos * half + i2];
+                        const double c = S.rope[(size_t)q * half + i2], sn = S.rope[(size_t)(MT + q) * half + i2];
                         const float lo = (float)__dsub_rn(__dmul_rn((double)v0, c), __dmul_rn((double)v1, sn));
                         const float hi = (float)__dadd_rn(__dmul_rn((double)v0, sn), __dmul_rn((double)v1, c));
                         if (head < p.H) {
@@ -681,9 +687,11 @@ __device__ __noinline__ uint32_t mk_phase(const ec_mk_params &p, int kind, int l
                     else if (n < 2 * p.E) ly.kc[kvo + (n - p.E)] = ec_f2h(v0);
                     else ly.vc[kvo + (n - 2 * p.E)] = ec_f2h(v0);
                 }
-            } else if (kind == PK_RESID) {
-                float *xp = p.x + (size_t)q * p.E + n;
-                *xp = __fadd_rn(__ldcg(xp), v0);
+            } else if (kind == PK_RESID) {   // rows of this CTA's own residual slice
+                float *xo = S.xown + (size_t)q * p.own_rows + (n - rg.r0);
+                const float v = __fadd_rn(*xo, v0);
+                *xo = v;
+                p.x[(size_t)q * p.E + n] = v;
             } else if (kind == PK_UP) {
                 if (p.arch == ARCH_Q2) p.act[(size_t)q * p.I + (n >> 1)] = __fmul_rn(ec_silu(v0), v1);
                 else p.act[(size_t)q * (4 * p.E) + n] = ec_gelu(v0);
@@ -891,7 +899,7 @@ __device__ __noinline__ bool mk_grid_sync(const ec_mk_params &p, unsigned target
 
 template <int LWT, int HWT, int MM>
 __global__ void __launch_bounds__(EC_MK_THREADS, 1) k_decode(const __grid_constant__ ec_mk_params pg, int n_steps) {
-    const Lay L = mk_layout(pg.xbuf_bytes, pg.stage_bytes, pg.L, pg.E);
+    const Lay L = mk_layout(pg.xbuf_bytes, pg.stage_bytes, pg.L, pg.E, pg.hd, pg.own_rows);
     const Sm S = sm_of(pg);
     const int G = gridDim.x, cta = blockIdx.x;
     const int M = pg.M;
@@ -980,10 +988,21 @@ __global__ void __launch_bounds__(EC_MK_THREADS, 1) k_decode(const __grid_consta
         if (ct == 0) tmark(p, S, 0, EC_TR_SYNC);          \
     } while (0)
     for (int step = 0; step < n_steps; ++step) {
+        // this step's RoPE rows, in flight while the embedding and the first
+        // norm run (the norm's cp.async wait completes them)
+        if (p.rope_cos) {
+            const int half = p.hd >> 1, pairs = half >> 1;   // 16-byte pieces of one row
+            for (int idx = ct; idx < 2 * M * pairs; idx += NCT) {
+                const int tab = idx / (M * pairs), rem = idx % (M * pairs), q = rem / pairs, j = rem % pairs;
+                const double *src = (tab ? p.rope_sin : p.rope_cos) + (size_t)S.lpos[q] * half + 2 * j;
+                cpa16(S.rope + (size_t)(tab * MT + q) * half + 2 * j, src);
+            }
+        }
         // residual rows := embedding (reference src/gpt2.c:488-499, :690-700)
         for (int idx = ct; idx < xn * M; idx += NCT) {
             const int q = idx / xn, n = xr.r0 + idx % xn;
             const float e = mk_embed(p, S.ltok[q], S.lpos[q], n);
+            S.xown[(size_t)q * p.own_rows + (n - xr.r0)] = e;
             p.x[(size_t)q * p.E + n] = e;
             if (p.taps) p.taps[(size_t)q * p.E + n] = e;
         }
@@ -1022,7 +1041,7 @@ __global__ void __launch_bounds__(EC_MK_THREADS, 1) k_decode(const __grid_consta
             if (p.taps)
                 for (int idx = ct; idx < xn * M; idx += NCT) {
                     const int q = idx / xn, n = xr.r0 + idx % xn;
-                    p.taps[((size_t)(l + 1) * M + q) * p.E + n] = __ldcg(p.x + (size_t)q * p.E + n);
+                    p.taps[((size_t)(l + 1) * M + q) * p.E + n] = S.xown[(size_t)q * p.own_rows + (n - xr.r0)];
                 }
         }
         // F: final norm -> lm_head (per-CTA argmax partial written inside)
@@ -1063,7 +1082,7 @@ __global__ void __launch_bounds__(EC_MK_THREADS, 1) k_decode(const __grid_consta
 
 template <int LWT, int HWT, int MM>
 int mk_launch_t(const ec_mk_params *p, int n_steps, int grid, cudaStream_t stream) {
-    const Lay L = mk_layout(p->xbuf_bytes, p->stage_bytes, p->L, p->E);
+    const Lay L = mk_layout(p->xbuf_bytes, p->stage_bytes, p->L, p->E, p->hd, p->own_rows);
     cudaError_t e = cudaFuncSetAttribute(k_decode<LWT, HWT, MM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)L.total);
     if (e != cudaSuccess) return (int)e;
@@ -1091,7 +1110,7 @@ int mk_launch_m(const ec_mk_params *p, int n_steps, int grid, cudaStream_t strea
 }  // namespace
 
 extern "C" size_t ec_mk_smem_bytes(const ec_mk_params *p) {
-    return mk_layout(p->xbuf_bytes, p->stage_bytes, p->L, p->E).total;
+    return mk_layout(p->xbuf_bytes, p->stage_bytes, p->L, p->E, p->hd, p->own_rows).total;
 }
 
 extern "C" int ec_mk_smem_limit(void) {

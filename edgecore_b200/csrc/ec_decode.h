@@ -72,6 +72,7 @@ typedef struct {
     int *abort_flag;            /* set by any CTA that gives up            */
     int *err;
     int maxlen;                 /* max attended positions per row          */
+    int own_rows;               /* >= residual rows owned by one CTA       */
     int kvchunk;                /* cached positions staged per attention
                                    chunk (K and V buffers in shared memory) */
     int xbuf_bytes;             /* activation smem: operand buffer ...      */

@@ -1179,8 +1179,10 @@ static int ec_mk_plan(ec_dev *d, int M, int maxlen, ec_mk_params *p)
     /* 16-byte asynchronous copies of q rows and cached K/V rows */
     if (d->hd % 8 || d->kv % 8 || d->E % 4) return -1;
     memset(p, 0, sizeof *p);
-    p->L = d->L;   /* the layer table and the norm vectors are part of the shared-memory layout */
-    p->E = d->E;
+    p->L = d->L;   /* the layer table, norm vectors, RoPE rows and owned residual rows */
+    p->E = d->E;   /* are part of the shared-memory layout */
+    p->hd = d->hd;
+    p->own_rows = (d->E + d->mk_grid - 1) / d->mk_grid + 1;
     const int Kdown = d->lw[0].down.Kp, Kmax = d->Ep > Kdown ? d->Ep : Kdown;
     const int opb = d->wt == EC_W_I8 ? 1 : 4;
     int xbuf = M * Kmax * opb;
