@@ -62,10 +62,7 @@ enum { MI_QKV = 0, MI_O = 1, MI_UP = 2, MI_DOWN = 3, MI_LM = 4, MI_N = 5 };
 
 // Loop over k = ct, ct + NCT, ... < n, four iterations unrolled per round so
 // that independent loads and arithmetic overlap; k still ascends per thread.
-#define FOR_K4(k, n)                                                  \
-    for (int k0_ = ct; k0_ < (n); k0_ += 4 * NCT)                    \
-        _Pragma("unroll") for (int j_ = 0; j_ < 4; ++j_)             \
-            if (const int k = k0_ + j_ * NCT; k < (n))
+#define FOR_K4(k, n) _Pragma("unroll 1") for (int k = ct; k < (n); k += NCT)
 
 struct Lay {
     uint32_t ring, xbuf, stage, nrm, rope, xown, redd, redf, redi, asc, ints, bars, lays, par, total;
@@ -196,25 +193,30 @@ __device__ __forceinline__ void stage_issue(float *dst, const float *src, int n,
     int done = 0;
     if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
         const int n4 = n >> 2;
+#pragma unroll 1
         for (int i = ct; i < n4; i += NCT) cpa16(dst + 4 * i, src + 4 * i);
         done = 4 * n4;
     }
+#pragma unroll 1
     for (int i = done + ct; i < n; i += NCT) dst[i] = __ldcg(src + i);
 }
 
 // Timeline of CTA 0 when p.trace is set: consumer thread 0 writes the first
 // half of the buffer, the producer thread the second half, entries
 // (code << 56) | globaltimer ns.  Each half has its own count in shared memory.
-__device__ __forceinline__ void tmark(const ec_mk_params &p, const Sm &S, int who, int code) {
-    if (p.trace && blockIdx.x == 0) {
-        const int half = p.trace_cap / 2, cap = who ? p.trace_cap - half : half;
-        int &n = S.tcount[who];
-        if (n < cap) {
-            unsigned long long t;
-            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-            p.trace[(size_t)who * half + n++] = ((unsigned long long)code << 56) | (t & 0x00ffffffffffffffull);
-        }
+__device__ __noinline__ void tmark_rec(const ec_mk_params &p, int *tcount, int who, int code) {
+    const int half = p.trace_cap / 2, cap = who ? p.trace_cap - half : half;
+    int &n = tcount[who];
+    if (n < cap) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        p.trace[(size_t)who * half + n++] = ((unsigned long long)code << 56) | (t & 0x00ffffffffffffffull);
     }
+}
+
+// The check stays inline, the recording out of line (kept off the hot path).
+__device__ __forceinline__ void tmark(const ec_mk_params &p, const Sm &S, int who, int code) {
+    if (p.trace && blockIdx.x == 0) tmark_rec(p, S.tcount, who, code);
 }
 
 // ---------------------------------------------------------------------------
@@ -897,6 +899,18 @@ __device__ __noinline__ bool mk_grid_sync(const ec_mk_params &p, unsigned target
 // the kernel
 // ---------------------------------------------------------------------------
 
+// Residual rows owned by this CTA after layer `slot - 1` -> taps[slot] (debug
+// capture; out of line, off the hot path).
+__device__ __noinline__ void mk_taps(const ec_mk_params &p, int slot, int ct) {
+    const Sm S = sm_of(p);
+    const Rg xr = S.rg[MI_O];
+    const int xn = xr.r1 - xr.r0, M = p.M;
+    for (int idx = ct; idx < xn * M; idx += NCT) {
+        const int q = idx / xn, n = xr.r0 + idx % xn;
+        p.taps[((size_t)slot * M + q) * p.E + n] = S.xown[(size_t)q * p.own_rows + (n - xr.r0)];
+    }
+}
+
 template <int LWT, int HWT, int MM>
 __global__ void __launch_bounds__(EC_MK_THREADS, 1) k_decode(const __grid_constant__ ec_mk_params pg, int n_steps) {
     const Lay L = mk_layout(pg.xbuf_bytes, pg.stage_bytes, pg.L, pg.E, pg.hd, pg.own_rows);
@@ -1038,11 +1052,7 @@ __global__ void __launch_bounds__(EC_MK_THREADS, 1) k_decode(const __grid_consta
             if (ct == 0) tmark(p, S, 0, EC_TR_PROLOGUE);
             t = mk_phase<LWT, MM>(p, PK_RESID, l | 0x10000, t, ct);
             if (ct == 0) tmark(p, S, 0, EC_TR_TILES);
-            if (p.taps)
-                for (int idx = ct; idx < xn * M; idx += NCT) {
-                    const int q = idx / xn, n = xr.r0 + idx % xn;
-                    p.taps[((size_t)(l + 1) * M + q) * p.E + n] = S.xown[(size_t)q * p.own_rows + (n - xr.r0)];
-                }
+            if (p.taps) mk_taps(p, l + 1, ct);
         }
         // F: final norm -> lm_head (per-CTA argmax partial written inside)
         SYNC_OR_RETURN();
