@@ -44,7 +44,6 @@ constexpr int NCW = EC_MK_CONS_WARPS;
 constexpr int NCT = NCW * 32;
 constexpr int STAGES = EC_MK_STAGES;
 constexpr int TILE = EC_MK_TILE;
-constexpr int TROWS = EC_MK_MAX_TILE_ROWS;
 constexpr int ARCH_Q2 = 1;                        // ARCH_QWEN2
 constexpr long long SPIN_CYCLES = 4000000000LL;   // ~2 s: bound on any grid-barrier wait
 constexpr int ERR_TIMEOUT = 1, ERR_INDEX = 2;
@@ -60,9 +59,10 @@ enum { MI_QKV = 0, MI_O = 1, MI_UP = 2, MI_DOWN = 3, MI_LM = 4, MI_N = 5 };
 // Every user declares `const int nM = p.M;` (a register, not a reload).
 #define FOR_TOK(m) _Pragma("unroll") for (int m = 0; m < MM; ++m) if (m < nM)
 
-// Loop over k = ct, ct + NCT, ... < n, four iterations unrolled per round so
-// that independent loads and arithmetic overlap; k still ascends per thread.
-#define FOR_K4(k, n) _Pragma("unroll 1") for (int k = ct; k < (n); k += NCT)
+// Loop over k = ct, ct + NCT, ... < n, deliberately not unrolled: the step
+// runs most of its code once per phase, so it is bound by instruction fetch
+// and code size costs more than an unrolled copy's extra parallelism gains.
+#define FOR_K(k, n) _Pragma("unroll 1") for (int k = ct; k < (n); k += NCT)
 
 struct Lay {
     uint32_t ring, xbuf, stage, nrm, rope, xown, redd, redf, redi, asc, ints, bars, lays, par, total;
@@ -72,19 +72,22 @@ __host__ __device__ inline uint32_t al16(uint32_t v) { return (v + 15u) & ~15u; 
 
 __host__ __device__ inline Lay mk_layout(int xbuf_bytes, int stage_bytes, int n_layer, int E, int hd, int own_rows) {
     Lay L;
+    // fixed-size regions first, at compile-time offsets (no address arithmetic
+    // in the helpers), then the regions sized by the model
     uint32_t o = 0;
+    L.ints = o;  o += al16((3 * MT + 4 + 2 * MI_N) * 4);
+    L.bars = o;  o += 2 * STAGES * 8;
+    L.redd = o;  o += 2 * NCW * MT * 8;
+    L.redf = o;  o += 2 * NCW * MT * 4;
+    L.redi = o;  o += NCW * MT * 4;
+    L.asc = o;   o += MT * 4;
+    o = (o + 127u) & ~127u;
     L.ring = o;  o += STAGES * TILE;
     L.xbuf = o;  o += al16((uint32_t)xbuf_bytes);
     L.stage = o; o += al16((uint32_t)stage_bytes);
     L.nrm = o;   o += 2u * al16((uint32_t)E * 4u);
     L.rope = o;  o += al16((uint32_t)MT * (uint32_t)hd * 8u);          // cos, sin rows of each token's position
     L.xown = o;  o += al16((uint32_t)MT * (uint32_t)own_rows * 4u);    // residual rows owned by this CTA
-    L.redd = o;  o += 2 * NCW * MT * 8;
-    L.redf = o;  o += 2 * NCW * MT * 4;
-    L.redi = o;  o += NCW * MT * 4;
-    L.asc = o;   o += MT * 4;
-    L.ints = o;  o += al16((3 * MT + 4 + 2 * MI_N) * 4);
-    L.bars = o;  o += 2 * STAGES * 8;
     L.lays = o;  o += al16((uint32_t)n_layer * (uint32_t)sizeof(ec_mk_layer));
     L.par = o;   o += al16((uint32_t)sizeof(ec_mk_params));
     L.total = o;
@@ -348,7 +351,7 @@ __device__ __noinline__ void mk_norm(const ec_mk_params &p, bool from_embed, con
     double s1[MM];
     FOR_TOK(m) {
         s1[m] = 0.0;
-        FOR_K4(k, E) {
+        FOR_K(k, E) {
             const double d = (double)st[m * E + k];
             s1[m] = b ? __dadd_rn(s1[m], d) : __dadd_rn(s1[m], __dmul_rn(d, d));
         }
@@ -360,7 +363,7 @@ __device__ __noinline__ void mk_norm(const ec_mk_params &p, bool from_embed, con
         FOR_TOK(m) {
             s2[m] = 0.0;
             mean[m] = __ddiv_rn(s1[m], (double)E);
-            FOR_K4(k, E) {
+            FOR_K(k, E) {
                 const double d = __dsub_rn((double)st[m * E + k], mean[m]);
                 s2[m] = __dadd_rn(s2[m], __dmul_rn(d, d));
             }
@@ -374,7 +377,7 @@ __device__ __noinline__ void mk_norm(const ec_mk_params &p, bool from_embed, con
         }
     }
     FOR_TOK(m) {
-        FOR_K4(k, E) {
+        FOR_K(k, E) {
             const double d = b ? __dsub_rn((double)st[m * E + k], mean[m]) : (double)st[m * E + k];
             const float t = (float)__dmul_rn(d, rstd[m]);
             st[m * E + k] = b ? __fadd_rn(__fmul_rn(t, gs[k]), bs[k]) : __fmul_rn(t, gs[k]);
@@ -405,7 +408,7 @@ __device__ __noinline__ void mk_operand(const ec_mk_params &p, const float *src,
             mx[m] = 0.0f;
             if (vec) {
                 const float4 *r4 = reinterpret_cast<const float4 *>(st + (size_t)m * K);
-                FOR_K4(c, K >> 2) {
+                FOR_K(c, K >> 2) {
                     const float4 v = r4[c];
                     mx[m] = ec_max_keep(ec_max_keep(ec_max_keep(ec_max_keep(mx[m], fabsf(v.x)), fabsf(v.y)), fabsf(v.z)), fabsf(v.w));
                 }
@@ -423,7 +426,7 @@ __device__ __noinline__ void mk_operand(const ec_mk_params &p, const float *src,
             if (vec) {
                 const float4 *r4 = reinterpret_cast<const float4 *>(st + (size_t)m * K);
                 char4 *q4 = reinterpret_cast<char4 *>(xq + (size_t)m * Kp);
-                FOR_K4(c, Kp >> 2) {
+                FOR_K(c, Kp >> 2) {
                     char4 o = make_char4(0, 0, 0, 0);
                     if (4 * c < K) {
                         const float4 v = r4[c];
@@ -443,11 +446,109 @@ __device__ __noinline__ void mk_operand(const ec_mk_params &p, const float *src,
         float *xs = reinterpret_cast<float *>(S.xbuf);
         FOR_TOK(m) {
             float *xm = xs + (size_t)m * Kp;
-            FOR_K4(k, Kp) {
+            FOR_K(k, Kp) {
                 const float v = k < K ? (from_stage ? st[m * K + k] : __ldcg(src + (size_t)m * K + k)) : 0.0f;
                 const int c = k >> 3, e = k & 7;
                 xm[(e >> 2) * (Kp >> 1) + c * 4 + (e & 3)] = v;
             }
+        }
+    }
+    cons_sync();
+}
+
+// Int8 operand of one phase in a single pass, shared by the four per-layer
+// call sites so that one copy of the code serves them all: the K-wide rows
+// come from `src` (o / down inputs) or are the norm of the residual rows
+// (q|k|v and gate|up inputs; the embedding for layer 0), then quantise into
+// S.xbuf with scales in S.asc.  Same arithmetic, in the same order, as
+// mk_norm followed by mk_operand; the max of |x| is taken while the
+// normalised values are written, which saves a pass and a barrier.
+template <int MM>
+__device__ __noinline__ void mk_prep(const ec_mk_params &p, const float *src, int K, int Kp, bool from_embed,
+                                     const float *g, const float *b, int ct) {
+    const Sm S = sm_of(p);
+    const int nM = p.M;
+    float *st = S.stage;
+    float *gs = S.nrm, *bs = S.nrm + ((K + 3) & ~3);
+    if (g) {
+        stage_issue(gs, g, K, ct);
+        if (b) stage_issue(bs, b, K, ct);
+    }
+    if (!from_embed) stage_issue(st, src, nM * K, ct);
+    else FOR_TOK(m) FOR_K(k, K) st[m * K + k] = mk_embed(p, S.ltok[m], S.lpos[m], k);
+    cpa_wait_all();
+    cons_sync();
+    float mx[MM];
+    FOR_TOK(m) mx[m] = 0.0f;
+    if (g) {
+        double s1[MM], mean[MM], rstd[MM];
+        FOR_TOK(m) {
+            s1[m] = 0.0;
+            FOR_K(k, K) {
+                const double d = (double)st[m * K + k];
+                s1[m] = b ? __dadd_rn(s1[m], d) : __dadd_rn(s1[m], __dmul_rn(d, d));
+            }
+        }
+        red_sum_d<MM>(p, S, s1, ct, 0);
+        if (b) {
+            double s2[MM];
+            FOR_TOK(m) {
+                s2[m] = 0.0;
+                mean[m] = __ddiv_rn(s1[m], (double)K);
+                FOR_K(k, K) {
+                    const double d = __dsub_rn((double)st[m * K + k], mean[m]);
+                    s2[m] = __dadd_rn(s2[m], __dmul_rn(d, d));
+                }
+            }
+            red_sum_d<MM>(p, S, s2, ct, 1);
+            FOR_TOK(m) rstd[m] = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(s2[m], (double)K), p.eps)));
+        } else {
+            FOR_TOK(m) {
+                mean[m] = 0.0;
+                rstd[m] = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(s1[m], (double)K), p.eps)));
+            }
+        }
+        FOR_TOK(m) {
+            float4 *r4 = reinterpret_cast<float4 *>(st + (size_t)m * K);
+            FOR_K(c, K >> 2) {
+                float e[4];
+                *reinterpret_cast<float4 *>(e) = r4[c];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int k = 4 * c + j;
+                    const double d = b ? __dsub_rn((double)e[j], mean[m]) : (double)e[j];
+                    const float t = (float)__dmul_rn(d, rstd[m]);
+                    e[j] = b ? __fadd_rn(__fmul_rn(t, gs[k]), bs[k]) : __fmul_rn(t, gs[k]);
+                    mx[m] = ec_max_keep(mx[m], fabsf(e[j]));
+                }
+                r4[c] = *reinterpret_cast<const float4 *>(e);
+            }
+        }
+    } else {
+        FOR_TOK(m) {
+            const float4 *r4 = reinterpret_cast<const float4 *>(st + (size_t)m * K);
+            FOR_K(c, K >> 2) {
+                const float4 v = r4[c];
+                mx[m] = ec_max_keep(ec_max_keep(ec_max_keep(ec_max_keep(mx[m], fabsf(v.x)), fabsf(v.y)), fabsf(v.z)), fabsf(v.w));
+            }
+        }
+    }
+    red_max_f<MM>(p, S, mx, ct, 0);   // its barrier also orders the writes above before the reads below
+    int8_t *xq = reinterpret_cast<int8_t *>(S.xbuf);
+    FOR_TOK(m) {
+        const float s = mx[m] > 0.0f ? __fdiv_rn(mx[m], 127.0f) : 1.0f;
+        const float r = __fdiv_rn(1.0f, s);
+        if (ct == 0) S.asc[m] = s;
+        const float4 *r4 = reinterpret_cast<const float4 *>(st + (size_t)m * K);
+        char4 *q4 = reinterpret_cast<char4 *>(xq + (size_t)m * Kp);
+        FOR_K(c, Kp >> 2) {
+            char4 o = make_char4(0, 0, 0, 0);
+            if (4 * c < K) {
+                const float4 v = r4[c];
+                o = make_char4((signed char)ec_quant_fast(v.x, s, r), (signed char)ec_quant_fast(v.y, s, r),
+                               (signed char)ec_quant_fast(v.z, s, r), (signed char)ec_quant_fast(v.w, s, r));
+            }
+            q4[c] = o;
         }
     }
     cons_sync();
@@ -993,6 +1094,9 @@ __global__ void __launch_bounds__(EC_MK_THREADS, 1) k_decode(const __grid_consta
     const int ct = threadIdx.x - 32;
     uint32_t t = 0;
     unsigned target = 0;
+    // int8 layers: the single-pass operand builder (its inputs must fit the staging area)
+    const bool I8P = LWT == EC_W_I8 && (size_t)M * (size_t)S.lay[0].down.K * 4 <= (size_t)p.stage_bytes &&
+                     (size_t)M * (size_t)p.E * 4 <= (size_t)p.stage_bytes && (p.E & 3) == 0 && (S.lay[0].down.K & 3) == 0;
     const Rg xr = S.rg[MI_O];   // residual rows owned by this CTA
     const int xn = xr.r1 - xr.r0;
 #define SYNC_OR_RETURN()                                  \
@@ -1024,8 +1128,8 @@ __global__ void __launch_bounds__(EC_MK_THREADS, 1) k_decode(const __grid_consta
             const ec_mk_layer &ly = S.lay[l];
             // A: norm -> q|k|v
             if (l > 0) SYNC_OR_RETURN();
-            mk_norm<MM>(p, l == 0, ly.n1g, ly.n1b, ct);
-            mk_operand<MM>(p, nullptr, p.E, ly.qkv.Kp, LWT, ct);
+            if (I8P) mk_prep<MM>(p, p.x, p.E, ly.qkv.Kp, l == 0, ly.n1g, ly.n1b, ct);
+            else { mk_norm<MM>(p, l == 0, ly.n1g, ly.n1b, ct); mk_operand<MM>(p, nullptr, p.E, ly.qkv.Kp, LWT, ct); }
             if (ct == 0) tmark(p, S, 0, EC_TR_PROLOGUE);
             t = mk_phase<LWT, MM>(p, PK_QKV, l, t, ct);
             if (ct == 0) tmark(p, S, 0, EC_TR_TILES);
@@ -1035,20 +1139,22 @@ __global__ void __launch_bounds__(EC_MK_THREADS, 1) k_decode(const __grid_consta
             if (ct == 0) tmark(p, S, 0, EC_TR_ATTN);
             // C: o + residual
             SYNC_OR_RETURN();
-            mk_operand<MM>(p, p.att, p.E, ly.o.Kp, LWT, ct);
+            if (I8P) mk_prep<MM>(p, p.att, p.E, ly.o.Kp, false, nullptr, nullptr, ct);
+            else mk_operand<MM>(p, p.att, p.E, ly.o.Kp, LWT, ct);
             if (ct == 0) tmark(p, S, 0, EC_TR_PROLOGUE);
             t = mk_phase<LWT, MM>(p, PK_RESID, l, t, ct);
             if (ct == 0) tmark(p, S, 0, EC_TR_TILES);
             // D: norm -> gate|up / fc
             SYNC_OR_RETURN();
-            mk_norm<MM>(p, false, ly.n2g, ly.n2b, ct);
-            mk_operand<MM>(p, nullptr, p.E, ly.up.Kp, LWT, ct);
+            if (I8P) mk_prep<MM>(p, p.x, p.E, ly.up.Kp, false, ly.n2g, ly.n2b, ct);
+            else { mk_norm<MM>(p, false, ly.n2g, ly.n2b, ct); mk_operand<MM>(p, nullptr, p.E, ly.up.Kp, LWT, ct); }
             if (ct == 0) tmark(p, S, 0, EC_TR_PROLOGUE);
             t = mk_phase<LWT, MM>(p, PK_UP, l, t, ct);
             if (ct == 0) tmark(p, S, 0, EC_TR_TILES);
             // E: down / fc2 + residual
             SYNC_OR_RETURN();
-            mk_operand<MM>(p, p.act, ly.down.K, ly.down.Kp, LWT, ct);
+            if (I8P) mk_prep<MM>(p, p.act, ly.down.K, ly.down.Kp, false, nullptr, nullptr, ct);
+            else mk_operand<MM>(p, p.act, ly.down.K, ly.down.Kp, LWT, ct);
             if (ct == 0) tmark(p, S, 0, EC_TR_PROLOGUE);
             t = mk_phase<LWT, MM>(p, PK_RESID, l | 0x10000, t, ct);
             if (ct == 0) tmark(p, S, 0, EC_TR_TILES);
