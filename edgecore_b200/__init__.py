@@ -228,14 +228,19 @@ class Model:
         except Exception:
             pass
 
-    def forward(self, tokens, positions, seqs=None) -> np.ndarray:
-        """gpt2_forward with host arrays: logits [M][vocab] fp32."""
+    def forward(self, tokens, positions, seqs=None, out=None) -> np.ndarray:
+        """gpt2_forward with host arrays: logits [M][vocab] fp32, written into
+        `out` when given (a C-contiguous float32 [M][vocab] array, reused the
+        way the reference runtime reuses its one logits buffer)."""
         t, p = _np(tokens, np.int32), _np(positions, np.int32)
         s = None if seqs is None else _np(seqs, np.int32)
         M = len(t)
-        logits = np.empty((M, self.vocab), np.float32)
-        self.lib.gpt2_forward(self.h, _ptr(t), _ptr(p), _ptr(s), M, _ptr(logits))
-        return logits
+        if out is None:
+            out = np.empty((M, self.vocab), np.float32)
+        elif out.dtype != np.float32 or not out.flags.c_contiguous or out.shape != (M, self.vocab):
+            raise ValueError(f"out must be a C-contiguous float32 array of shape ({M}, {self.vocab})")
+        self.lib.gpt2_forward(self.h, _ptr(t), _ptr(p), _ptr(s), M, _ptr(out))
+        return out
 
     def forward_argmax(self, tokens, positions, seqs=None, shard: bool = False):
         t, p = _np(tokens, np.int32), _np(positions, np.int32)

@@ -37,6 +37,8 @@
 
 #include <float.h>
 
+#include <atomic>
+
 namespace {
 
 constexpr int MT = EC_MK_MT;
@@ -1205,9 +1207,16 @@ __global__ void __launch_bounds__(EC_MK_THREADS, 1) k_decode(const __grid_consta
 template <int LWT, int HWT, int MM>
 int mk_launch_t(const ec_mk_params *p, int n_steps, int grid, cudaStream_t stream) {
     const Lay L = mk_layout(p->xbuf_bytes, p->stage_bytes, p->L, p->E, p->hd, p->own_rows);
-    cudaError_t e = cudaFuncSetAttribute(k_decode<LWT, HWT, MM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)L.total);
-    if (e != cudaSuccess) return (int)e;
+    // the shared-memory opt-in is per device: raise it only when it grows
+    static std::atomic<int> opted[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || opted[dev].load(std::memory_order_relaxed) < (int)L.total) {
+        cudaError_t e = cudaFuncSetAttribute(k_decode<LWT, HWT, MM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)L.total);
+        if (e != cudaSuccess) return (int)e;
+        if (dev >= 0 && dev < 64) opted[dev].store((int)L.total, std::memory_order_relaxed);
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(EC_MK_THREADS);

@@ -523,8 +523,9 @@ static int ec_mk_build(ec_dev *d)
     free(h);
     if (rc) return -1;
     d->mk_grid = ok ? d->num_sms : 0;   /* 0: the persistent kernel is not usable */
-    CK(cudaMalloc((void **)&d->d_bar, 16));
-    CK(cudaMalloc((void **)&d->d_abort, 16));
+    /* barrier counter and abort flag side by side: one reset per launch */
+    CK(cudaMalloc((void **)&d->d_bar, 32));
+    d->d_abort = (int *)(d->d_bar + 4);
     CK(cudaMalloc((void **)&d->d_mk_err, 16));
     CK(cudaMemset(d->d_mk_err, 0, 16));
     CK(cudaMalloc((void **)&d->amax_v, (size_t)d->num_sms * EC_MK_MT * 4));
@@ -665,7 +666,7 @@ static void ec_dev_free(ec_dev *d)
     if (d->lm != d->wte) cudaFree(d->lm);
     cudaFree(d->wte); cudaFree(d->wpe); cudaFree(d->nfg); cudaFree(d->nfb);
     cudaFree(d->kc); cudaFree(d->vc); cudaFree(d->rope_cos); cudaFree(d->rope_sin);
-    cudaFree(d->d_mk_layers); cudaFree(d->d_bar); cudaFree(d->d_abort); cudaFree(d->d_mk_err);
+    cudaFree(d->d_mk_layers); cudaFree(d->d_bar); cudaFree(d->d_mk_err);
     cudaFree(d->amax_v); cudaFree(d->amax_i);
     cudaFree(d->attn_part); cudaFree(d->logits); cudaFree(d->amax_part);
     cudaFree(d->d_hist); cudaFree(d->taps);
@@ -1234,8 +1235,7 @@ static int ec_mk_plan(ec_dev *d, int M, int maxlen, ec_mk_params *p)
 
 static int ec_mk_run(ec_dev *d, const ec_mk_params *p, int n_steps)
 {
-    CK(cudaMemsetAsync(d->d_bar, 0, 4, d->stream));
-    CK(cudaMemsetAsync(d->d_abort, 0, 4, d->stream));
+    CK(cudaMemsetAsync(d->d_bar, 0, 32, d->stream));   /* counter and abort flag */
     CK(ec_mk_launch(p, n_steps, d->mk_grid, d->stream));
     return 0;
 }
@@ -1488,8 +1488,7 @@ EC_EXPORT int ec_decode_profile(GPT2 *g, int *d_tokens, int start_pos, int n_ste
         if (ec_decode_setup(d, d_tokens, start_pos, M)) return -1;
         mp.advance = 1;
         for (int st = 0; st < n_steps; st++) {
-            CK(cudaMemsetAsync(d->d_bar, 0, 4, d->stream));
-            CK(cudaMemsetAsync(d->d_abort, 0, 4, d->stream));
+            CK(cudaMemsetAsync(d->d_bar, 0, 32, d->stream));   /* counter and abort flag */
             CK(cudaEventRecord(d->prof_ev[0], d->stream));
             CK(ec_mk_launch(&mp, 1, d->mk_grid, d->stream));
             CK(cudaEventRecord(d->prof_ev[1], d->stream));
