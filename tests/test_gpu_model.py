@@ -109,12 +109,16 @@ def test_argmax_and_device_decode_agree_with_logits(tiny_models, cuda):
         toks = synth.prompt_ids(spec.vocab, 9, seed=4)
         m.forward(toks, np.arange(9), np.zeros(9, np.int32))
         cur, host_ids = int(toks[-1]), []
+        buf = np.full((1, spec.vocab), np.nan, np.float32)   # one reused logits buffer
         for i in range(12):
             lg = m.forward([cur], [9 + i])[0]
             ids, mx = m.forward_argmax([cur], [9 + i])
             assert ids[0] == int(np.argmax(lg)) and mx[0] == lg.max()
+            assert m.forward([cur], [9 + i], out=buf) is buf and np.array_equal(buf[0], lg)
             cur = int(ids[0])
             host_ids.append(cur)
+        with pytest.raises(ValueError):
+            m.forward([cur], [21], out=np.empty((1, spec.vocab), np.float64))
         m.forward(toks, np.arange(9), np.zeros(9, np.int32))
         d_tok = torch.tensor([int(toks[-1])], dtype=torch.int32, device="cuda")
         d_out = torch.zeros(12, dtype=torch.int32, device="cuda")
