@@ -1,8 +1,8 @@
 """Generate the golden vectors under tests/golden/ from the REFERENCE itself.
 
-Run here, where the reference tree exists (it does not exist on the GPU box):
+Run where a checkout of the reference exists (the GPU machines have none):
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py [--reference <reference checkout>]
 
 Sources of truth, all the reference's own code:
   * quant_export.npz  -- edgecore/ecm.py quantize_int8_symmetric (A1), imported
