@@ -997,7 +997,8 @@ __device__ __noinline__ bool mk_grid_sync(const ec_mk_params &p, unsigned target
                 break;
             }
         }
-        __threadfence();
+        // no fence here: the acquire load that saw the count orders this
+        // thread's later reads, and the CTA barrier below passes that order on
     }
     const bool stop = cons_sync_or(S.flag[0] != 0);
     if (stop && ct == 0) atomicExch(p.abort_flag, 1);
