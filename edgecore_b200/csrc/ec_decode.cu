@@ -985,8 +985,9 @@ __device__ __noinline__ bool mk_grid_sync(const ec_mk_params &p, unsigned target
         return false;
     }
     if (ct == 0) {
-        __threadfence();
-        atomicAdd(p.bar, 1u);
+        // arrive with release semantics: the CTA barrier above put every
+        // warp's writes of this phase before this add (release is cumulative)
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
         const long long t0 = clock64();
         for (;;) {
             if (ld_acquire(p.bar) >= target) break;
