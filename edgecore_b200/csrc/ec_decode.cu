@@ -181,6 +181,12 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
     return v;
 }
 
+__device__ __forceinline__ int ld_relaxed_i(const int *p) {
+    int v;
+    asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ int elt_of(int wt) { return wt == EC_W_I8 ? 1 : 2; }
 
 // 16-byte asynchronous global -> shared copy through L2 (data written by
@@ -989,9 +995,10 @@ __device__ __noinline__ bool mk_grid_sync(const ec_mk_params &p, unsigned target
         // warp's writes of this phase before this add (release is cumulative)
         asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
         const long long t0 = clock64();
-        for (;;) {
+        for (unsigned it = 1;; ++it) {
             if (ld_acquire(p.bar) >= target) break;
-            if (*reinterpret_cast<volatile int *>(p.abort_flag)) { S.flag[0] = 1; break; }
+            if ((it & 15u) != 0) continue;   // the abort flag and the clock: every 16th poll
+            if (ld_relaxed_i(p.abort_flag)) { S.flag[0] = 1; break; }
             if (clock64() - t0 > SPIN_CYCLES) {
                 S.flag[0] = 1;
                 atomicCAS(p.err, 0, ERR_TIMEOUT);
