@@ -57,7 +57,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=32)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=512)
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0,
+                    help="minimum timed seconds of the reference CPU decode (both the reference arm and the "
+                         "cpu_baseline leg, which runs the reference arm in a child process)")
     ap.add_argument("--op-sweep", action="store_true",
                     help="instead of the decode benchmark: BASELINE config 1's int8 operator sweep "
                          "(M in 1/8/64/512 and the 16384 prefill rows of config 3, Qwen2.5-0.5B (N,K) shapes), "
@@ -85,20 +87,85 @@ def config_dict(world: int) -> dict:
 # ---- clocks -------------------------------------------------------------------
 
 class ClockSampler:
+    """SM clocks and throttle reasons sampled during the timed region: NVML
+    polled every 10 ms from a thread (one sample is always taken at start and
+    at stop, so even a timed region of a few ms has a record); nvidia-smi at
+    its 20 ms floor where NVML is missing."""
+
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD_S = 0.010
+    # NVML clock-event reason bits
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
     def __init__(self, gpu_index: int):
+        import threading
+        self.rows: list[tuple[float, float, float, int]] = []
+        self.p = None
+        self.nv = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(self._nvml_index(gpu_index))
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            self.nv = None
+        if self.nv is not None:
+            self.stop_ev = threading.Event()
+            self._sample()
+            self.th = threading.Thread(target=self._loop, daemon=True)
+            self.th.start()
+            return
         self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                       "-i", str(gpu_index), "-lms", "100"], stdout=self.tmp,
+                                       "-i", str(gpu_index), "-lms", "20"], stdout=self.tmp,
                                       stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
 
+    @staticmethod
+    def _nvml_index(local: int) -> int:
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if vis:
+            try:
+                return int(vis.split(",")[local])
+            except (ValueError, IndexError):
+                pass
+        return local
+
+    def _sample(self) -> None:
+        nv = self.nv
+        try:
+            sm = float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+            pw = nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
+            rs = int(nv.nvmlDeviceGetCurrentClocksEventReasons(self.h))
+            self.rows.append((time.perf_counter(), sm, pw, rs))
+        except Exception:
+            pass
+
+    def _loop(self) -> None:
+        while not self.stop_ev.wait(self.PERIOD_S):
+            self._sample()
+
     def stop(self) -> dict:
+        if self.nv is not None:
+            self.stop_ev.set()
+            self.th.join(timeout=5)
+            self._sample()
+            try:
+                self.nv.nvmlShutdown()
+            except Exception:
+                pass
+            if not self.rows:
+                return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "source": "nvml"}
+            sm = [r[1] for r in self.rows]
+            reasons = sorted({n for r in self.rows for n, b in self.BITS.items() if r[3] & b})
+            return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                    "samples": len(self.rows), "power_w_max": max(r[2] for r in self.rows),
+                    "source": f"nvml every {1e3 * self.PERIOD_S:.0f} ms"}
         if self.p is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
         self.p.terminate()
@@ -115,14 +182,17 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if "Active" in v and "Not" not in v})
         return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
-                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows)}
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows),
+                "source": "nvidia-smi -lms 20"}
 
 
 # ---- CPU reference ------------------------------------------------------------
 
-def run_reference_decode(path: Path, steps: int, warmup: int, budget_s: float, threads: int):
+def run_reference_decode(path: Path, steps: int, warmup: int, min_s: float, threads: int, cap_s: float = 120.0):
     """Reference CPU decode (oracle/_ref, built from the reference sources;
-    the restatement if that is absent).  Returns (tok/s, steps timed, kind)."""
+    the restatement if that is absent): `warmup` untimed steps, then timed
+    steps until at least `steps` steps and `min_s` seconds are done (at most
+    `cap_s` seconds).  Returns (tok/s, steps timed, kind)."""
     from oracle import oracle
     try:
         R = oracle.Reference(threads=threads)
@@ -138,7 +208,8 @@ def run_reference_decode(path: Path, steps: int, warmup: int, budget_s: float, t
     cur = int(np.argmax(lg[-1]))
     pos = PROMPT
     total, done = 0.0, 0
-    for i in range(warmup + steps):
+    i = 0
+    while True:
         t0 = time.perf_counter()
         lg = m.forward(np.array([cur], np.int32), np.array([pos], np.int32))
         dt = time.perf_counter() - t0
@@ -147,8 +218,9 @@ def run_reference_decode(path: Path, steps: int, warmup: int, budget_s: float, t
         if i >= warmup:
             total += dt
             done += 1
-            if total >= budget_s:
+            if (done >= steps and total >= min_s) or total >= cap_s:
                 break
+        i += 1
     m.close()
     return done / total, done, kind
 
@@ -158,11 +230,13 @@ def reference_arm(args, rank: int, world: int) -> None:
         return
     path = synth.ensure_model(synth.CONFIGS[CONFIG_KEY])
     threads = host_cores()
-    tps, done, kind = run_reference_decode(path, args.steps, min(args.warmup, 3), 120.0, threads)
-    sample = (f"{done} timed decode steps (of --steps {args.steps}, capped at 120 s) after a {PROMPT}-token "
-              f"prefill, {threads} threads, gpt2_forward per step as the reference runtime times it")
+    warm = max(args.warmup, 3)
+    tps, done, kind = run_reference_decode(path, args.steps, warm, args.cpu_seconds, threads)
+    sample = (f"{done} timed decode steps (at least --steps {args.steps} and {args.cpu_seconds:.0f} s, at most "
+              f"120 s) after a {PROMPT}-token prefill and {warm} warm-up steps, {threads} threads, "
+              f"gpt2_forward per step as the reference runtime times it")
     line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": world,
-            "steps": done, "warmup": min(args.warmup, 3), "ms_per_step": 1000.0 / tps, "higher_is_better": True,
+            "steps": done, "warmup": warm, "ms_per_step": 1000.0 / tps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded random-init weights)",
             "config": config_dict(1),
             "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": kind, "sample": sample},
@@ -301,10 +375,7 @@ def ours_arm(args, rank: int, world: int, local: int) -> None:
     launches = 1   # the timed region is one launch of the persistent decode kernel
     cpu = None
     if rank == 0 and world == 1:
-        tps, done, kind = run_reference_decode(path, 10_000, 2, args.cpu_seconds, host_cores())
-        cpu = {"value": tps, "unit": "tok/s", "cores": host_cores(), "kind": kind,
-               "sample": f"{done} decode steps (~{args.cpu_seconds:.0f} s) of the same workload after a "
-                         f"{PROMPT}-token prefill, reference C compiled from its sources"}
+        cpu = cpu_baseline_leg(args)
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
                 "warmup": max(args.warmup, 3), "ms_per_step": ms_max / args.steps, "higher_is_better": True,
@@ -320,6 +391,24 @@ def ours_arm(args, rank: int, world: int, local: int) -> None:
     m.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def cpu_baseline_leg(args) -> dict:
+    """The reference arm run in a child process (same code, same conditions as
+    `--impl reference`: no CUDA context or torch threads in the process that
+    times the CPU)."""
+    cmd = [sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1",
+           "--warmup", str(max(args.warmup, 3)), "--cpu-seconds", str(args.cpu_seconds)]
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK")}
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=600)
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    if r.returncode != 0 or not lines:
+        return {"value": None, "unit": "tok/s", "cores": host_cores(), "kind": "reference",
+                "sample": f"reference arm failed: rc {r.returncode}: {r.stderr[-300:]}"}
+    ref = json.loads(lines[-1])
+    out = dict(ref["cpu_baseline"])
+    out["sample"] = "child process `bench.py --impl reference`: " + out["sample"]
+    return out
 
 
 def op_sweep(args) -> None:

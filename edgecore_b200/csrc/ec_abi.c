@@ -131,9 +131,11 @@ static int run_linear(abi_ctx *c, int wt, float *C, const float *X, const int8_t
                 if (dev_view(c, S_A, X, M, K, K, 4, &dX)) return -1;
                 g.X = dX; g.ldx = K;
             }
-            ACK(ec_launch_gemv(&g, g_scr[c->dev].sms, 0));
-            m0 += rows;
-            continue;
+            if (ec_gemv_fits(&g)) {   /* else rows too long for its shared memory: the GEMM below */
+                ACK(ec_launch_gemv(&g, g_scr[c->dev].sms, 0));
+                m0 += rows;
+                continue;
+            }
         }
         ec_gemm_args g;
         memset(&g, 0, sizeof g);
@@ -172,6 +174,20 @@ static int run_linear(abi_ctx *c, int wt, float *C, const float *X, const int8_t
     int code = 0;
     ACK(ec_kernel_error_take(0, &code));
     if (code) { snprintf(c->err, sizeof c->err, "kernel error code %d", code); return -1; }
+    return 0;
+}
+
+EC_EXPORT int ec_device_error_take(void *stream, int *code)
+{
+    if (!code) { ec_set_error_text("ec_device_error_take: code must not be NULL"); return -1; }
+    *code = 0;
+    const int e = ec_kernel_error_take((cudaStream_t)stream, code);
+    if (e) {
+        char msg[160];
+        snprintf(msg, sizeof msg, "ec_device_error_take: CUDA error %d (%s)", e, cudaGetErrorString((cudaError_t)e));
+        ec_set_error_text(msg);
+        return -1;
+    }
     return 0;
 }
 

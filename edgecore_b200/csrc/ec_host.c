@@ -1603,8 +1603,10 @@ EC_EXPORT int ec_model_set_vocab_shard(GPT2 *g, int v_begin, int v_end)
 EC_EXPORT uint64_t ec_argmax_key(float maxv, int idx)
 {
     uint32_t b;
+    if (maxv == 0.0f) maxv = 0.0f;   /* -0 and +0 compare equal in the reference's '>' scan */
     memcpy(&b, &maxv, 4);
-    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);   /* order-preserving float bits */
+    if (maxv != maxv) b = 0u;        /* NaN never wins a '>' comparison: below every number */
+    else b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);   /* order-preserving float bits */
     return ((uint64_t)b << 32) | (uint32_t)(0x7fffffff - idx);
 }
 

@@ -369,6 +369,22 @@ extern "C" int ec_kernels_init(void) {
     return (int)e;
 }
 
+// Shared memory of one GEMV launch with the fewest stages (1), or 0 when the
+// arguments are outside what the kernel takes.
+static size_t gemv_min_smem(const ec_gemv_args *a) {
+    if (a->M <= 0 || a->M > GEMV_MT || a->block_rows <= 0 || a->block_rows > GEMV_MAX_ROWS || (a->Kp % 16) != 0)
+        return 0;
+    const int ldw = a->ldw ? a->ldw : a->Kp;
+    if (ldw < a->Kp || (ldw * (a->wt == EC_W_I8 ? 1 : 2)) % 16 != 0) return 0;
+    return gemv_layout(a->wt, a->M, a->Kp, ldw, a->block_rows, 1).total;
+}
+
+extern "C" int ec_gemv_fits(const ec_gemv_args *a) {
+    if (g_ec_max_optin_smem == 0 && ec_kernels_init() != 0) return 0;
+    const size_t need = gemv_min_smem(a);
+    return need > 0 && need <= (size_t)g_ec_max_optin_smem;
+}
+
 extern "C" int ec_launch_gemv(const ec_gemv_args *a, int num_sms, cudaStream_t stream) {
     if (a->M <= 0 || a->nblocks <= 0) return 0;
     if (a->M > GEMV_MT || a->block_rows > GEMV_MAX_ROWS || (a->Kp % 16) != 0) return (int)cudaErrorInvalidValue;

@@ -76,6 +76,10 @@ typedef struct {
  * quantisation (int8) and epilogue. */
 int ec_launch_gemv(const ec_gemv_args *a, int num_sms, cudaStream_t stream);
 
+/* 1 when ec_launch_gemv can take these arguments (M, block rows, K alignment
+ * and the shared memory of one staged block plus the activation rows), else 0. */
+int ec_gemv_fits(const ec_gemv_args *a);
+
 /* Generic GEMM for any M: A int8 [M][Kp] + a_scale[M] (int8 weights) or
  * A fp32 [M][ldx] (16-bit weights); plain/resid/gelu epilogues only. */
 typedef struct {
@@ -99,6 +103,12 @@ int ec_launch_gemm(const ec_gemm_args *a, cudaStream_t stream);
  * ec_tc_error_take reads and clears its error word. */
 #define EC_TC_MIN_M 32
 int ec_launch_gemm_tc(const ec_gemm_args *a, cudaStream_t stream);
+
+/* One-time set-up of the tensor-core GEMMs on the current device (driver
+ * entry point of the tensor-map encoder, kernel shared-memory attributes,
+ * SM count), so that no later launch does it; cudaErrorNotSupported when the
+ * driver has no tensor-map encoder (ec_launch_gemm then uses the SIMT kernels). */
+int ec_tc_init(void);
 size_t ec_gemm_tc_split_bytes(int wt, int M, int Kp);
 int ec_tc_error_take(int *code);
 
@@ -163,6 +173,9 @@ int ec_kernel_error_take(cudaStream_t stream, int *code);
 
 /* One-time per-device kernel attribute setup (dynamic shared memory limits). */
 int ec_kernels_init(void);
+
+/* Text for ec_last_error() of the calling thread (ec_host.c). */
+void ec_set_error_text(const char *msg);
 
 #ifdef __cplusplus
 }

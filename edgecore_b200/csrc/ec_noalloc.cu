@@ -20,9 +20,18 @@
 //    at zero: the quantisation kernel writes every scale and every byte of
 //    every row before the GEMV / GEMM reads them.
 //  * The first call on each device does the set-up: it looks up the scratch
-//    address with cudaGetSymbolAddress and sets the kernels' attributes, and
-//    the CUDA runtime loads the kernels it launches.  Make that first call
-//    before starting any stream capture on that device.
+//    address with cudaGetSymbolAddress, sets the shared-memory attributes of
+//    the GEMV and of the tensor-core GEMMs and resolves the driver's
+//    tensor-map encoder, and the CUDA runtime loads the kernels it launches.
+//    Make that first call before starting any stream capture on that device.
+//  * M <= 8 runs the weight-streaming GEMV when one staged W row plus the M
+//    int8 activation rows fit the GEMV's shared memory (K up to about
+//    113,000 at M = 1, 25,000 at M = 8); otherwise, and for M > 8, the GEMM
+//    kernels run.
+//  * Device-side failures (a bounded wait that gave up inside a kernel) are
+//    not visible in the return code, which only covers the checks and the
+//    launches: after synchronising the stream, ec_device_error_take() reads
+//    and clears the library's device error words.
 //  * The work is enqueued on `stream` and the call returns without waiting.
 //    There is ONE scratch buffer per device: calls whose work can overlap on
 //    the device (different streams without ordering between them, or several
@@ -38,8 +47,6 @@
 
 #define EC_NOALLOC_SCRATCH_BYTES (4u << 20)
 #define EC_NOALLOC_MAX_DEV 16
-
-extern "C" void ec_set_error_text(const char *msg);   // ec_host.c: text for ec_last_error()
 
 // The scratch: file scope, fixed size, part of the module image on every
 // device the library runs on.
@@ -63,6 +70,13 @@ bool is_device_ptr(const void *p, int dev) {
 int fail(const char *msg) {
     ec_set_error_text(msg);
     return -1;
+}
+
+// Text for a code returned by the launch helpers (cudaError_t values).
+void code_text(char *buf, size_t n, int code) {
+    const char *name = cudaGetErrorName((cudaError_t)code);
+    snprintf(buf, n, "CUDA error %d (%s: %s)", code, name ? name : "?",
+             cudaGetErrorString((cudaError_t)code));
 }
 
 }  // namespace
@@ -98,12 +112,18 @@ extern "C" __attribute__((visibility("default"))) int ec_linear_int8_noalloc(
     pthread_mutex_lock(&g_setup_mu);
     if (!g_scratch_ptr[dev]) {
         void *p = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev);
-        if (e == cudaSuccess && ec_kernels_init() != 0) e = cudaGetLastError();
-        if (e != cudaSuccess) {
+        int e = (int)cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e == 0) e = (int)cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e == 0) e = ec_kernels_init();
+        if (e == 0) {
+            e = ec_tc_init();
+            if (e == (int)cudaErrorNotSupported) e = 0;   // no encoder: the GEMM falls back to SIMT kernels
+        }
+        if (e != 0) {
             pthread_mutex_unlock(&g_setup_mu);
-            snprintf(msg, sizeof msg, "ec_linear_int8_noalloc: set-up failed: %s", cudaGetErrorString(e));
+            char ct[160];
+            code_text(ct, sizeof ct, e);
+            snprintf(msg, sizeof msg, "ec_linear_int8_noalloc: set-up failed: %s", ct);
             return fail(msg);
         }
         g_scratch_ptr[dev] = static_cast<unsigned char *>(p);
@@ -117,9 +137,10 @@ extern "C" __attribute__((visibility("default"))) int ec_linear_int8_noalloc(
     int8_t *aq = reinterpret_cast<int8_t *>(scr + scale_bytes);
     int e = ec_launch_quant(aq, a_scale, X, K, M, K, K, st);
     if (e == 0) {
+        ec_gemv_args g;
+        memset(&g, 0, sizeof g);
+        bool gemv = false;
         if (M <= 8) {
-            ec_gemv_args g;
-            memset(&g, 0, sizeof g);
             g.W = W; g.wscale = w_scale; g.bias = bias;
             g.wt = EC_W_I8; g.N = N; g.K = K; g.Kp = K; g.ldw = K;
             int R = (N + 2 * sms - 1) / (2 * sms);   // about two row blocks per SM
@@ -132,6 +153,9 @@ extern "C" __attribute__((visibility("default"))) int ec_linear_int8_noalloc(
             g.nblocks = (N + R - 1) / R;
             g.Xq = aq; g.xscale = a_scale; g.ldx = K;
             g.M = M; g.out = C; g.ldo = N; g.epi = EC_EPI_STORE;
+            gemv = ec_gemv_fits(&g) != 0;   // long rows: the GEMM below instead
+        }
+        if (gemv) {
             e = ec_launch_gemv(&g, sms, st);
         } else {
             ec_gemm_args g;
@@ -144,7 +168,9 @@ extern "C" __attribute__((visibility("default"))) int ec_linear_int8_noalloc(
         }
     }
     if (e != 0) {
-        snprintf(msg, sizeof msg, "ec_linear_int8_noalloc: launch failed: %s", cudaGetErrorString((cudaError_t)e));
+        char ct[160];
+        code_text(ct, sizeof ct, e);
+        snprintf(msg, sizeof msg, "ec_linear_int8_noalloc: launch failed: %s", ct);
         return fail(msg);
     }
     return 0;

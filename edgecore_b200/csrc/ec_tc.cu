@@ -430,12 +430,21 @@ int make_map(CUtensorMap *map, const void *ptr, int elt, int inner, int rows, in
 }
 
 template <int WT>
-int launch(const ec_gemm_args &a, const void *const *aparts, const float *row_scale, int dev, cudaStream_t stream) {
-    constexpr int S = TcCfg<WT>::S, BN = TcCfg<WT>::BN, ELT = TcCfg<WT>::ELT;
+int set_attr(int dev) {
     if (!g_attr_set[WT][dev]) {
         const cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes<WT>());
         if (e != cudaSuccess) return (int)e;
         g_attr_set[WT][dev] = 1;
+    }
+    return 0;
+}
+
+template <int WT>
+int launch(const ec_gemm_args &a, const void *const *aparts, const float *row_scale, int dev, cudaStream_t stream) {
+    constexpr int S = TcCfg<WT>::S, BN = TcCfg<WT>::BN, ELT = TcCfg<WT>::ELT;
+    {
+        const int e = set_attr<WT>(dev);
+        if (e) return e;
     }
     TcMaps maps;
     memset(&maps, 0, sizeof maps);
@@ -508,6 +517,23 @@ extern "C" int ec_launch_gemm_tc(const ec_gemm_args *args, cudaStream_t stream) 
     e = cudaGetLastError();
     if (e != cudaSuccess) return (int)e;
     return launch<EC_W_BF16>(a, parts, rscale, dev, stream);
+}
+
+extern "C" int ec_tc_init(void) {
+    pthread_once(&g_once, resolve_encode);
+    if (!g_encode) return (int)cudaErrorNotSupported;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= 64) return (int)cudaErrorNotSupported;
+    if (!g_sms[dev]) {
+        e = cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return (int)e;
+    }
+    int rc = set_attr<EC_W_I8>(dev);
+    if (!rc) rc = set_attr<EC_W_F16>(dev);
+    if (!rc) rc = set_attr<EC_W_BF16>(dev);
+    return rc;
 }
 
 extern "C" int ec_tc_error_take(int *code) {

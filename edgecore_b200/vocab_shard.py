@@ -40,8 +40,12 @@ def pack_keys(maxv, idx) -> np.ndarray:
         raise ValueError("maxv and idx must have the same shape")
     if np.any(i < 0) or np.any(i > 0x7FFFFFFF):
         raise ValueError("indices must be in [0, 2^31)")
+    # -0.0 and +0.0 are equal to the reference's '>' scan: encode both as +0.0
+    v = np.where(v == 0.0, np.float32(0.0), v).astype(np.float32)
     b = v.view(np.uint32).astype(np.uint64)
     b = np.where(b & np.uint64(0x80000000), ~b & np.uint64(0xFFFFFFFF), b | np.uint64(0x80000000))
+    # a NaN never wins a '>' comparison: below every number
+    b = np.where(np.isnan(v), np.uint64(0), b)
     key = (b << np.uint64(32)) | (np.uint64(0x7FFFFFFF) - i.astype(np.uint64))
     return (key ^ _SIGN).view(np.int64)
 

@@ -109,7 +109,9 @@ int ec_forward_shard_argmax(GPT2 *g, const int *tokens, const int *positions,
 
 /* Encode (max, idx) as a 64-bit key whose unsigned order is "larger logit,
  * then lower index": combining shards with an unsigned max gives the
- * reference tie rule.  Decode inverts it. */
+ * reference tie rule.  -0.0 is encoded as +0.0 (the reference's '>' scan
+ * treats them as equal) and NaN below every number (it never wins a '>').
+ * Decode inverts it (a NaN comes back as a NaN, -0.0 as +0.0). */
 uint64_t ec_argmax_key(float maxv, int idx);
 void ec_argmax_key_decode(uint64_t key, float *maxv, int *idx);
 
@@ -123,15 +125,25 @@ int ec_quantize_rows(int8_t *q, float *scale, const float *x, int M, int K);
 int ec_linear_int8(float *C, const float *X, const int8_t *W,
                    const float *w_scale, const float *bias, int M, int K, int N);
 
+/* Device-side error of the standalone ops: synchronises `stream`, then reads
+ * and clears the library's device error words into *code (0 none, 1 a
+ * bounded wait inside a kernel gave up, 2 an out-of-range index was
+ * skipped).  The entry points that return before their kernels finish
+ * (ec_linear_int8_noalloc, ec_forward_device) report such errors only here. */
+int ec_device_error_take(void *stream, int *code);
+
 /* ec_linear_int8 that allocates no device memory: no counterpart in the
  * reference (whose CPU op needs none).  For callers that cannot allocate on
  * the request path -- HBM handed to a caching allocator, or a decode loop
  * that must not be stalled by cudaMalloc's device synchronisation.  The
  * int8 activations and their scales live in a fixed 4 MiB per-device static
  * buffer: requires M*K + 4*M (rounded up to 256) <= 4 MiB, K % 16 == 0 and
- * device pointers only; larger sizes are rejected with an error.  The first
- * call on a device does the set-up (scratch address lookup, kernel
- * attributes and loading) and should come before any stream capture.  Work
+ * device pointers only; larger sizes are rejected with an error.  M <= 8
+ * uses the weight-streaming GEMV when a W row plus the M activation rows fit
+ * its shared memory (K up to about 113,000 at M = 1), else the GEMM kernels.
+ * The first call on a device does the set-up (scratch address lookup,
+ * kernel attributes, tensor-map encoder, loading) and should come before any
+ * stream capture.  Device-side errors: ec_device_error_take.  Work
  * is enqueued on `stream` (cudaStream_t, NULL = legacy default) without a
  * host wait.  Calls that can overlap on the device share the one buffer and
  * race: order them on one stream or with events.  Returns 0 or -1 (reason

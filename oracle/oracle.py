@@ -17,7 +17,8 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF_DIR = Path(os.environ.get("EDGECORE_REFERENCE", "/root/reference"))
+# The reference checkout: $EDGECORE_REFERENCE when set, else a sibling of the repo.
+REF_DIR = Path(os.environ.get("EDGECORE_REFERENCE", str(HERE.parent.parent / "reference")))
 
 _i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")

@@ -180,7 +180,8 @@ def gen_layout(ref_root: Path) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=str(orc.REF_DIR),
+                    help="reference checkout (default: $EDGECORE_REFERENCE, else a sibling of the repo)")
     args = ap.parse_args()
     ref_root = Path(args.reference)
     orc.build(reference=True)

@@ -40,11 +40,20 @@ def test_keys_order_and_roundtrip(built):
     for v, i, k in zip(vals, idx, keys):
         assert (ec.argmax_key(float(v), int(i)) ^ (1 << 63)) == int(np.int64(k).astype(np.uint64))
     v2, i2 = vs.unpack_keys(keys)
-    assert np.array_equal(v2.view(np.uint32), vals.view(np.uint32)) and np.array_equal(i2, idx)
+    want_v = np.where(vals == 0.0, np.float32(0.0), vals).astype(np.float32)   # -0.0 comes back as +0.0
+    assert np.array_equal(v2.view(np.uint32), want_v.view(np.uint32)) and np.array_equal(i2, idx)
     # signed max of keys == (largest value, then lowest index)
     order = sorted(range(len(vals)), key=lambda j: (vals[j], -idx[j]))
     assert int(np.argmax(keys)) == order[-1]
     assert keys[7] < keys[8]          # 1.0 at index 8 loses to 1.0 at index 2
+    # -0.0 and +0.0 tie, so the lower index wins, whichever sign it carries
+    assert keys[5] > keys[4]          # +0.0 at index 3 beats -0.0 at index 7
+    z = vs.pack_keys(np.array([-0.0, 0.0], np.float32), np.array([1, 2]))
+    assert z[0] > z[1]                # -0.0 at index 1 beats +0.0 at index 2
+    # NaN loses to every number, -inf included
+    n = vs.pack_keys(np.array([np.nan, -np.inf], np.float32), np.array([0, 1]))
+    assert n[0] < n[1]
+    assert (ec.argmax_key(float("nan"), 0) ^ (1 << 63)) == int(np.int64(n[0]).astype(np.uint64))
 
 
 def _rank_main(rank: int, world: int, port: int, seed: int, out_dir: str):
@@ -60,6 +69,9 @@ def _rank_main(rank: int, world: int, port: int, seed: int, out_dir: str):
         logits[0, half - 1] = logits[0, half] = 1e3        # tie straddling the shard boundary
         logits[1, :] = -np.inf                              # every row -inf: index 0 wins
         logits[2, V - 1] = 2e3                              # max in the last shard
+        logits[3, :] = -1.0                                 # +/-0 tie across the shard boundary:
+        logits[3, half - 1] = -0.0                          # the lower index wins although it
+        logits[3, half + 1] = 0.0                           # carries the minus sign
         v0, v1 = vs.shard_range(V, rank, world)
         mv, mi = _ref_argmax(logits[:, v0:v1])
         got_v, got_i = vs.combine_argmax(mv, mi + v0)

@@ -1,7 +1,9 @@
-"""ec_linear_int8_noalloc (fixed static scratch, no device allocation) against
-the allocating ec_linear_int8 entry point, both called through the C ABI.
-Named so that it is collected after every other test file; it also passes
-alone."""
+"""ec_linear_int8_noalloc -- the W8A8 linear for callers that cannot allocate
+device memory per call (HBM handed to a caching allocator, or a decode loop
+that must not wait on cudaMalloc's device synchronisation) -- checked
+bit-exactly against the CPU oracle and the allocating ec_linear_int8 entry
+point, through the C ABI.  Named so that it is collected after every other
+test file; it also passes alone."""
 from __future__ import annotations
 
 import ctypes
@@ -23,6 +25,8 @@ def _lib():
     lib.ec_linear_int8.argtypes = [vp, vp, vp, vp, vp, i, i, i]
     lib.ec_linear_int8.restype = i
     lib.ec_last_error.restype = ctypes.c_char_p
+    lib.ec_device_error_take.argtypes = [vp, ctypes.POINTER(ctypes.c_int)]
+    lib.ec_device_error_take.restype = i
     return lib
 
 
@@ -38,27 +42,47 @@ def _ptr(t):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else None
 
 
-def test_noalloc_matches_allocating_entry_point(built, cuda):
+def _check(lib, rng, M, K, N, with_bias):
+    """One call of the no-allocation entry point on device operands, bit-exact
+    against the CPU restatement of the reference's W8A8 linear and against
+    the allocating ec_linear_int8 entry point on the same inputs."""
     import torch
+    from oracle.oracle import Restatement
+    X, W, ws, b = _case(rng, M, K, N, with_bias)
+    dX, dW, dws = (torch.from_numpy(a).cuda() for a in (X, W, ws))
+    db = torch.from_numpy(b).cuda() if b is not None else None
+    out = torch.full((M, N), float("nan"), device="cuda")
+    rc = lib.ec_linear_int8_noalloc(_ptr(out), _ptr(dX), _ptr(dW), _ptr(dws), _ptr(db), M, K, N, None)
+    assert rc == 0, lib.ec_last_error()
+    torch.cuda.synchronize()
+    code = ctypes.c_int(-1)
+    assert lib.ec_device_error_take(None, ctypes.byref(code)) == 0 and code.value == 0
+    got = out.cpu().numpy()
+    alloc = np.zeros((M, N), np.float32)
+    rc = lib.ec_linear_int8(alloc.ctypes.data, X.ctypes.data, W.ctypes.data, ws.ctypes.data,
+                            b.ctypes.data if b is not None else None, M, K, N)
+    assert rc == 0
+    want = Restatement().linear_int8(X, W, ws, b)
+    # exact int32 dots and the same fp32 epilogue: bit-identical results
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"M={M} K={K} N={N} differs from the oracle"
+    assert np.array_equal(got.view(np.uint32), alloc.view(np.uint32))
+
+
+def test_noalloc_matches_oracle_and_allocating_entry_point(built, cuda):
     lib = _lib()
     rng = np.random.default_rng(7)
     # two calls in a row through the same static scratch: the GEMV path
     # (M <= 8) then the GEMM path, the second larger than the first
     for M, K, N, with_bias in ((5, 896, 1152, True), (40, 4864, 896, False)):
-        X, W, ws, b = _case(rng, M, K, N, with_bias)
-        dX, dW, dws = (torch.from_numpy(a).cuda() for a in (X, W, ws))
-        db = torch.from_numpy(b).cuda() if b is not None else None
-        out = torch.full((M, N), float("nan"), device="cuda")
-        rc = lib.ec_linear_int8_noalloc(_ptr(out), _ptr(dX), _ptr(dW), _ptr(dws), _ptr(db), M, K, N, None)
-        assert rc == 0, lib.ec_last_error()
-        torch.cuda.synchronize()
-        want = np.zeros((M, N), np.float32)
-        rc = lib.ec_linear_int8(want.ctypes.data, X.ctypes.data, W.ctypes.data, ws.ctypes.data,
-                                b.ctypes.data if b is not None else None, M, K, N)
-        assert rc == 0
-        got = out.cpu().numpy()
-        # same quantisation and the same exact int32 dots: tolerance 1e-6 of max
-        assert np.abs(got - want).max() <= 1e-6 * np.abs(want).max()
+        _check(lib, rng, M, K, N, with_bias)
+
+
+def test_noalloc_long_rows(built, cuda):
+    """Rows too long for the GEMV's shared memory at M <= 8 go to the GEMM."""
+    lib = _lib()
+    rng = np.random.default_rng(11)
+    for M, K, N in ((1, 262144, 48), (8, 32768, 40), (1, 110592, 24)):
+        _check(lib, rng, M, K, N, True)
 
 
 def test_noalloc_rejects_oversize_and_host_pointers(built, cuda):
