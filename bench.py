@@ -373,6 +373,7 @@ def ours_arm(args, rank: int, world: int, local: int) -> None:
                 "profile_us_per_step": {k: 1e3 * v["ms"] / prof["steps"] for k, v in classes.items() if v["launches"]},
                 "profile_method": f"{prof['steps']} more steps, one launch each, CUDA events around every launch"}
     launches = 1   # the timed region is one launch of the persistent decode kernel
+    gemv = gemv_lm_head(stream) if rank == 0 else None
     cpu = None
     if rank == 0 and world == 1:
         cpu = cpu_baseline_leg(args)
@@ -386,7 +387,7 @@ def ours_arm(args, rank: int, world: int, local: int) -> None:
                         "d2h_bytes_per_step": 4 * spec.vocab, "steps": e2e_steps,
                         "api": "gpt2_forward (host tokens/positions, host logits [1][151936])"},
                 "gpu_launches": launches,
-                "roofline": roofline, "cpu_baseline": cpu}
+                "roofline": roofline, "cpu_baseline": cpu, "gemv_lm_head": gemv}
         print(json.dumps(line), flush=True)
     m.close()
     if world > 1:
@@ -411,41 +412,120 @@ def cpu_baseline_leg(args) -> dict:
     return out
 
 
+SWEEP_SHAPES = ((1152, 896), (896, 896), (4864, 896), (896, 4864), (151936, 896))
+
+
+def time_op(launch, nbuf: int, reps: int, warmup: int, stream) -> float:
+    """Mean µs per launch of `launch(i)` (i selects one of `nbuf` rotating
+    operand sets whose total exceeds L2, so every launch reads HBM), CUDA
+    events on `stream` around `reps` back-to-back launches."""
+    import torch
+    with torch.cuda.stream(stream):
+        for i in range(warmup):
+            launch(i % nbuf)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        start.record(stream)
+        for i in range(reps):
+            launch(i % nbuf)
+        end.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) * 1e3 / reps
+
+
+def gemv_lm_head(stream, reps: int = 20, warmup: int = 3) -> dict:
+    """The metric's "GEMV % of HBM peak": gemm_fp16_fp32 at M = 1 on the
+    Qwen2.5-0.5B lm_head (151936 x 896 fp16, 272 MB, larger than L2) through
+    ec_gemm_async, CUDA events around back-to-back launches."""
+    import torch
+
+    import edgecore_b200 as ec
+    N, K, M = 151936, 896, 1
+    g = torch.Generator(device="cuda").manual_seed(0)
+    W = (torch.randn((N, K), device="cuda", generator=g) * 0.02).half()
+    X = torch.randn((M, K), device="cuda", generator=g)
+    out = torch.empty((M, N), device="cuda")
+    us = time_op(lambda i: ec.gemm_async(1, out, X, None, W.view(torch.int16), stream=stream.cuda_stream),
+                 1, reps, warmup, stream)
+    assert ec.device_error_take(stream.cuda_stream) == 0
+    peak, kind = measured_peaks()
+    algo = N * K * 2 + M * K * 4 + M * N * 4
+    del W
+    return {"op": "gemm_fp16_fp32", "M": M, "N": N, "K": K, "us": us, "achieved_gbs": algo / us / 1e3,
+            "frac": algo / us / 1e3 / peak, "peak": peak, "peak_source": kind,
+            "kernel": "k_gemv<fp16,M=1> (weight streaming)", "algorithmic_bytes": algo}
+
+
 def op_sweep(args) -> None:
-    """gemm_int8 through the C ABI with device operands: X int8 [M][K] (the
-    A2 quantisation output), W int8 [N][K], per-row scales.  Times include the
-    entry point's host work and its synchronisation per call; kernel-only
-    times come from ncu on the same command."""
+    """BASELINE config 1's int8 operator sweep plus the fp16 lm_head, through
+    ec_gemm_async with device operands: X int8 [M][K] (the A2 quantisation
+    output) with a_scale, W int8 [N][K] with per-row scales (or fp16 W and
+    fp32 X).  Kernel time = CUDA events around back-to-back launches that
+    rotate through weight copies totalling >= 256 MB (> 126 MB L2).  One
+    JSON line per shape, with the reference CPU gemm on a bounded sample."""
     import torch
 
     import edgecore_b200 as ec
     torch.manual_seed(0)
-    for M in (1, 8, 64, 512, 16384):
-        for N, K in ((1152, 896), (896, 896), (4864, 896), (896, 4864), (151936, 896)):
-            if M == 16384 and N == 151936:
-                continue   # fp16 in the model; 9.9 GB of fp32 output
-            if (args.sweep_m and M != args.sweep_m) or (args.sweep_n and N != args.sweep_n):
-                continue
+    stream = torch.cuda.Stream()
+    peak, peak_kind = measured_peaks()
+    ref = None
+    if args.cpu_seconds > 0:
+        try:
+            from oracle import oracle
+            ref = oracle.Reference(threads=host_cores())
+        except FileNotFoundError:
+            ref = None
+    cases = [("int8", M, N, K) for M in (1, 8, 64, 512) for N, K in SWEEP_SHAPES]
+    cases += [("fp16", M, 151936, 896) for M in (1, 8, 64, 512)]
+    for wt_name, M, N, K in cases:
+        if (args.sweep_m and M != args.sweep_m) or (args.sweep_n and N != args.sweep_n):
+            continue
+        wt = 0 if wt_name == "int8" else 1
+        elt = 1 if wt == 0 else 2
+        wbytes = N * K * elt
+        nbuf = max(1, -(-(256 << 20) // wbytes))
+        if wt == 0:
+            Ws = [torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda") for _ in range(nbuf)]
             A = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda")
-            W = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda")
             a_s = torch.rand(M, device="cuda") * 1e-2 + 1e-3
-            w_s = torch.rand(N, device="cuda") * 1.9e-2 + 1e-3
-            out = torch.empty((M, N), device="cuda")
-            for _ in range(max(args.warmup, 3)):
-                ec.gemm_int8(A, a_s, W, w_s, out=out)
-            torch.cuda.synchronize()
-            reps = 20
+        else:
+            Ws = [(torch.randn((N, K), device="cuda") * 0.02).half().view(torch.int16) for _ in range(nbuf)]
+            A = torch.randn((M, K), device="cuda")
+            a_s = None
+        w_s = torch.rand(N, device="cuda") * 1.9e-2 + 1e-3 if wt == 0 else None
+        out = torch.empty((M, N), device="cuda")
+        us = time_op(lambda i: ec.gemm_async(wt, out, A, a_s, Ws[i], w_s, stream=stream.cuda_stream),
+                     nbuf, max(10, 2 * nbuf), max(args.warmup, 3), stream)
+        assert ec.device_error_take(stream.cuda_stream) == 0
+        algo = wbytes + (4 * N if wt == 0 else 0) + M * K * (1 if wt == 0 else 4) + (4 * M if wt == 0 else 0) + 4 * M * N
+        flops = 2.0 * M * N * K
+        line = {"op_sweep": "gemm_int8" if wt == 0 else "gemm_fp16_fp32", "M": M, "N": N, "K": K,
+                "us_per_call": us, "algorithmic_bytes": algo, "achieved_gbs": algo / us / 1e3,
+                "hbm_frac": algo / us / 1e3 / peak, "hbm_peak_gbs": peak, "peak_source": peak_kind,
+                "tops" if wt == 0 else "tflops": flops / us / 1e6,
+                "path": "weight-streaming GEMV" if M <= 8 else ("tcgen05" if M >= 32 else "SIMT"),
+                "timing": f"CUDA events, {max(10, 2 * nbuf)} back-to-back launches rotating {nbuf} weight "
+                          f"copies ({nbuf * wbytes / 2**20:.0f} MiB > L2)"}
+        if ref is not None and M * N * K <= 2e10:
+            Ah = A.cpu().numpy()
+            Wh = Ws[0].cpu().numpy()
             t0 = time.perf_counter()
-            for _ in range(reps):
-                ec.gemm_int8(A, a_s, W, w_s, out=out)
-            torch.cuda.synchronize()
-            us = (time.perf_counter() - t0) / reps * 1e6
-            algo = N * K + 4 * N + M * K + 4 * M + 4 * M * N
-            print(json.dumps({"op_sweep": "gemm_int8", "M": M, "N": N, "K": K, "us_per_call": us,
-                              "int8_tops": 2.0 * M * N * K / us / 1e6, "algorithmic_gbs": algo / us / 1e3,
-                              "path": "tcgen05" if M >= 32 else "weight-streaming GEMV" if M <= 8 else "SIMT"}),
-                  flush=True)
-            del A, W, out
+            n = 0
+            while True:
+                if wt == 0:
+                    ref.gemm_int8(Ah, a_s.cpu().numpy(), Wh, w_s.cpu().numpy())
+                else:
+                    ref.gemm_fp16(Ah, Wh.view(np.uint16))
+                n += 1
+                if time.perf_counter() - t0 >= min(args.cpu_seconds, 2.0):
+                    break
+            cpu_us = (time.perf_counter() - t0) / n * 1e6
+            line["cpu_baseline"] = {"value": cpu_us, "unit": "us_per_call", "cores": host_cores(),
+                                    "kind": "reference", "sample": f"{n} calls of the reference "
+                                    f"{'gemm_int8' if wt == 0 else 'gemm_fp16_fp32'} on host operands"}
+        print(json.dumps(line), flush=True)
+        del Ws, A, out
 
 
 def main():

@@ -23,7 +23,8 @@ from typing import Any
 import numpy as np
 
 __all__ = ["load_library", "Model", "gemm_int8", "gemm_fp16_fp32", "gemm_bf16_fp32",
-           "quantize_rows", "linear_int8", "argmax_key", "argmax_key_decode", "LIB_PATH"]
+           "quantize_rows", "linear_int8", "gemm_async", "device_error_take", "argmax_key", "argmax_key_decode",
+           "LIB_PATH"]
 
 LIB_PATH = Path(__file__).resolve().parent / "libedgecore_b200.so"
 _LIB: C.CDLL | None = None
@@ -53,6 +54,8 @@ def _declare(lib: C.CDLL) -> None:
         "ec_argmax_key_decode": (None, [C.c_uint64, _vp, _vp]),
         "ec_quantize_rows": (_i, [_vp, _vp, _vp, _i, _i]),
         "ec_linear_int8": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i]),
+        "ec_gemm_async": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+        "ec_device_error_take": (_i, [_vp, _vp]),
         "gemm_fp16_fp32": (None, [_vp, _vp, _vp, _i, _i, _i]),
         "gemm_bf16_fp32": (None, [_vp, _vp, _vp, _i, _i, _i]),
         "gemm_int8": (None, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i]),
@@ -148,6 +151,27 @@ def gemm_fp16_fp32(A, B16, out=None):
 def gemm_bf16_fp32(A, B16, out=None):
     """Same as gemm_fp16_fp32 with bfloat16 weights (uint16 bit patterns)."""
     return _gemm16("gemm_bf16_fp32", A, B16, out)
+
+
+def gemm_async(wt: int, out, A, a_scale, B, b_scale=None, bias=None, stream=None) -> None:
+    """gemm_int8 (wt 0) / gemm_fp16_fp32 (1) / gemm_bf16_fp32 (2) on device
+    tensors, enqueued on `stream` (an int cudaStream_t or None) without a host
+    synchronisation; errors inside kernels surface in device_error_take()."""
+    lib = load_library()
+    M, K = A.shape
+    N = B.shape[0]
+    if lib.ec_gemm_async(int(wt), _ptr(out), _ptr(A), _ptr(a_scale), _ptr(B), _ptr(b_scale), _ptr(bias),
+                         M, K, N, stream):
+        raise RuntimeError(last_error())
+
+
+def device_error_take(stream=None) -> int:
+    """Synchronise `stream`, then read and clear the library's device error
+    code (0 none, 1 a bounded wait gave up, 2 an out-of-range index)."""
+    code = C.c_int(0)
+    if load_library().ec_device_error_take(stream, C.byref(code)):
+        raise RuntimeError(last_error())
+    return code.value
 
 
 def quantize_rows(X):
@@ -277,7 +301,8 @@ class Model:
                                                     int(n_steps), _ptr(d_out_ids)))
 
     TRACE_CODES = {1: "barrier", 2: "operand", 3: "tiles", 4: "attention", 5: "lm_head", 6: "argmax",
-                   7: "tile_in", 8: "tile_free", 9: "tile_done", 10: "issue"}
+                   7: "tile_in", 8: "tile_free", 9: "tile_done", 10: "issue", 11: "staged", 12: "stats",
+                   13: "scores", 14: "softmax"}
 
     def decode_trace(self, d_tokens, start_pos: int, n_steps: int, cap: int = 1 << 16):
         """Timeline of CTA 0 of the persistent decode kernel: list of (event, ns)

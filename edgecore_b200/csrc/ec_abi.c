@@ -177,6 +177,66 @@ static int run_linear(abi_ctx *c, int wt, float *C, const float *X, const int8_t
     return 0;
 }
 
+EC_EXPORT int ec_gemm_async(int wt, float *C, const void *A, const float *a_scale, const void *B,
+                            const float *b_scale, const float *bias, int M, int K, int N, void *stream)
+{
+    if (M <= 0 || N <= 0) return 0;
+    char msg[200];
+    if ((wt != EC_W_I8 && wt != EC_W_F16 && wt != EC_W_BF16) || K <= 0 || K % 16) {
+        snprintf(msg, sizeof msg, "ec_gemm_async: wt=%d K=%d (wt 0/1/2, K a positive multiple of 16)", wt, K);
+        ec_set_error_text(msg);
+        return -1;
+    }
+    if (!is_device_ptr(C) || !is_device_ptr(A) || !is_device_ptr(B) || (b_scale && !is_device_ptr(b_scale)) ||
+        (bias && !is_device_ptr(bias)) || (wt == EC_W_I8 && !is_device_ptr(a_scale))) {
+        ec_set_error_text("ec_gemm_async: all operands must be device memory");
+        return -1;
+    }
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= EC_MAX_DEV) {
+        cudaGetLastError();
+        ec_set_error_text("ec_gemm_async: no usable CUDA device");
+        return -1;
+    }
+    pthread_mutex_lock(&g_abi_mu);
+    if (!g_scr[dev].sms) cudaDeviceGetAttribute(&g_scr[dev].sms, cudaDevAttrMultiProcessorCount, dev);
+    const int sms = g_scr[dev].sms;
+    cudaStream_t st = (cudaStream_t)stream;
+    int e = 0;
+    ec_gemv_args v;
+    memset(&v, 0, sizeof v);
+    v.W = B; v.wscale = b_scale; v.bias = bias; v.wt = wt; v.N = N; v.K = K; v.Kp = K; v.ldw = K;
+    v.M = M; v.out = C; v.ldo = N; v.epi = EC_EPI_STORE;
+    if (wt == EC_W_I8) { v.Xq = (const int8_t *)A; v.xscale = a_scale; v.ldx = K; }
+    else { v.X = (const float *)A; v.ldx = K; }
+    if (M <= 8 && ec_gemv_fits(&v)) {
+        e = ec_launch_gemv(&v, sms, st);
+    } else {
+        ec_gemm_args g;
+        memset(&g, 0, sizeof g);
+        g.W = B; g.wscale = b_scale; g.bias = bias; g.wt = wt; g.N = N; g.K = K; g.Kp = K; g.ldw = K; g.M = M;
+        g.out = C; g.ldo = N; g.epi = EC_EPI_STORE;
+        if (wt == EC_W_I8) {
+            g.Aq = (const int8_t *)A; g.a_scale = a_scale;
+        } else {
+            g.X = (const float *)A; g.ldx = K;
+            if (M >= EC_TC_MIN_M) {   /* tensor cores: activation parts workspace (allocated once, cached) */
+                g.split_bytes = ec_gemm_tc_split_bytes(wt, M, K);
+                g.split = scratch(dev, S_SPLIT, g.split_bytes);
+                if (!g.split) g.split_bytes = 0;
+            }
+        }
+        e = ec_launch_gemm(&g, st);
+    }
+    pthread_mutex_unlock(&g_abi_mu);
+    if (e) {
+        snprintf(msg, sizeof msg, "ec_gemm_async: launch failed: CUDA error %d (%s)", e, cudaGetErrorString((cudaError_t)e));
+        ec_set_error_text(msg);
+        return -1;
+    }
+    return 0;
+}
+
 EC_EXPORT int ec_device_error_take(void *stream, int *code)
 {
     if (!code) { ec_set_error_text("ec_device_error_take: code must not be NULL"); return -1; }

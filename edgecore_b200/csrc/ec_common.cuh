@@ -42,6 +42,105 @@ EC_DEV void ec_bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *ba
         ::"r"(ec_smem_u32(dst)), "l"(src), "r"(bytes), "r"(ec_smem_u32(bar)) : "memory");
 }
 
+// L2 policy for data read once per pass (weight streams): evicted first, so
+// that the KV cache and the activations exchanged between SMs stay in L2.
+EC_DEV uint64_t ec_l2_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// ec_bulk_g2s with an L2 cache policy.
+EC_DEV void ec_bulk_g2s_hint(void *dst, const void *src, uint32_t bytes, uint64_t *bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+        ::"r"(ec_smem_u32(dst)), "l"(src), "r"(bytes), "r"(ec_smem_u32(bar)), "l"(pol) : "memory");
+}
+
+// 16 bytes of read-only data read once: no L1 allocation, 256-byte L2 fetch.
+EC_DEV uint4 ec_ldg_stream16(const void *p) {
+    uint4 v;
+    asm("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+
+// ec_ldg_stream16 under an L2 cache policy.
+EC_DEV uint4 ec_ldg_stream16_hint(const void *p, uint64_t pol) {
+    uint4 v;
+    asm("ld.global.nc.L1::no_allocate.L2::cache_hint.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p), "l"(pol));
+    return v;
+}
+
+// Transposed warp sum of each of the V per-lane values: values are halved
+// between lane pairs at offsets 16, 8, ... (each lane keeps one half and adds
+// its partner's copy of it), so V values cost V-1 shuffles plus one per
+// remaining offset.  Every value is summed by the same xor tree 16, 8, 4, 2, 1
+// (pair sums are commutative), so a value's total does not depend on the
+// slot it sits in.  Lane L ends with the total of value ec_tr_vidx<V>(L);
+// lanes differing only in their low log2(32/V) bits hold the same total.
+template <int V, typename T>
+EC_DEV T ec_tr_reduce(T (&a)[V], int lane) {
+    static_assert(V >= 1 && V <= 32 && (V & (V - 1)) == 0, "V must be a power of two <= 32");
+    int n = V;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        if (n > 1) {
+            const bool up = (lane & o) != 0;
+#pragma unroll
+            for (int v = 0; v < V / 2; ++v) {
+                if (v < n / 2) {
+                    const T send = up ? a[v] : a[v + n / 2];
+                    const T keep = up ? a[v + n / 2] : a[v];
+                    a[v] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                }
+            }
+            n >>= 1;
+        } else {
+            a[0] = a[0] + __shfl_xor_sync(0xffffffffu, a[0], o);
+        }
+    }
+    return a[0];
+}
+
+template <int V>
+EC_DEV int ec_tr_vidx(int lane) {
+    int idx = 0, w = V >> 1;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        if (w >= 1) {
+            if (lane & o) idx += w;
+            w >>= 1;
+        }
+    }
+    return idx;
+}
+
+// fp32 dot contribution of one 16-byte chunk of 16-bit weights (8 elements,
+// in element order) with its activations x0 (elements 0-3) and x1 (4-7).
+template <bool BF16>
+EC_DEV float ec_dot8(const uint4 w, const float4 x0, const float4 x1, float t) {
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+    float f[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if (BF16) {
+            f[2 * i] = __uint_as_float(u[i] << 16);
+            f[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+        } else {
+            const float2 h = __half22float2(*reinterpret_cast<const __half2 *>(&u[i]));
+            f[2 * i] = h.x;
+            f[2 * i + 1] = h.y;
+        }
+    }
+    t = fmaf(f[0], x0.x, t); t = fmaf(f[1], x0.y, t);
+    t = fmaf(f[2], x0.z, t); t = fmaf(f[3], x0.w, t);
+    t = fmaf(f[4], x1.x, t); t = fmaf(f[5], x1.y, t);
+    t = fmaf(f[6], x1.z, t); t = fmaf(f[7], x1.w, t);
+    return t;
+}
+
 EC_DEV bool ec_mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(

@@ -54,7 +54,7 @@ constexpr unsigned PRODUCER_BACKOFF_NS = 128;      // producer sleep between emp
 
 // Phase kinds of the shared tile loop, and the five matrix shapes whose
 // per-CTA row ranges are computed once per launch.
-enum { PK_QKV = 0, PK_RESID = 1, PK_UP = 2, PK_LM = 3 };
+enum { PK_QKV = 0, PK_RESID = 1, PK_UP = 2 };
 enum { MI_QKV = 0, MI_O = 1, MI_UP = 2, MI_DOWN = 3, MI_LM = 4, MI_N = 5 };
 
 // Loop over the token rows m < p.M with compile-time indices (bounded by the
@@ -239,6 +239,7 @@ __device__ __forceinline__ void tmark(const ec_mk_params &p, const Sm &S, int wh
 __device__ __noinline__ uint32_t mk_produce(const ec_mk_params &p, const ec_mk_mat &m, int wt, Rg rg, uint32_t t) {
     const Sm S = sm_of(p);
     const uint32_t row_bytes = (uint32_t)m.ldw * (uint32_t)elt_of(wt);
+    const uint64_t pol = ec_l2_evict_first();
     for (int r = rg.r0; r < rg.r1; r += m.tile_rows) {
         const int nr = min(m.tile_rows, rg.r1 - r);
         const int s = (int)(t % STAGES);
@@ -257,8 +258,8 @@ __device__ __noinline__ uint32_t mk_produce(const ec_mk_params &p, const ec_mk_m
         }
         const uint32_t bytes = (uint32_t)nr * row_bytes;
         ec_mbar_expect_tx(&S.full[s], bytes);
-        ec_bulk_g2s(S.ring + (size_t)s * TILE, static_cast<const unsigned char *>(m.w) + (size_t)r * row_bytes,
-                    bytes, &S.full[s]);
+        ec_bulk_g2s_hint(S.ring + (size_t)s * TILE, static_cast<const unsigned char *>(m.w) + (size_t)r * row_bytes,
+                         bytes, &S.full[s], pol);
         tmark(p, S, 1, EC_TR_ISSUE);
         ++t;
     }
@@ -492,6 +493,7 @@ __device__ __noinline__ void mk_prep(const ec_mk_params &p, const float *src, in
     else FOR_TOK(m) FOR_K(k, K) st[m * K + k] = mk_embed(p, S.ltok[m], S.lpos[m], k);
     cpa_wait_all();
     cons_sync();
+    if (ct == 0) tmark(p, S, 0, EC_TR_STAGED);
     float mx[MM];
     FOR_TOK(m) mx[m] = 0.0f;
     if (g) {
@@ -504,6 +506,7 @@ __device__ __noinline__ void mk_prep(const ec_mk_params &p, const float *src, in
             }
         }
         red_sum_d<MM>(p, S, s1, ct, 0);
+        if (ct == 0) tmark(p, S, 0, EC_TR_STATS);
         if (b) {
             double s2[MM];
             FOR_TOK(m) {
@@ -655,11 +658,10 @@ __device__ __noinline__ uint32_t mk_phase(const ec_mk_params &p, int kind, int l
     const int nM = p.M;
     const int cta = blockIdx.x;
     // layer: index of the layer (bit 16 set: the down projection of a
-    // PK_RESID phase, else its o projection); -1 for the lm_head
-    const ec_mk_layer &ly = S.lay[layer < 0 ? 0 : (layer & 0xffff)];
-    const int mi = kind == PK_QKV ? MI_QKV : kind == PK_UP ? MI_UP : kind == PK_LM ? MI_LM
-                 : (layer & 0x10000) ? MI_DOWN : MI_O;
-    const ec_mk_mat &m = mi == MI_QKV ? ly.qkv : mi == MI_UP ? ly.up : mi == MI_LM ? p.lm : mi == MI_DOWN ? ly.down : ly.o;
+    // PK_RESID phase, else its o projection)
+    const ec_mk_layer &ly = S.lay[layer & 0xffff];
+    const int mi = kind == PK_QKV ? MI_QKV : kind == PK_UP ? MI_UP : (layer & 0x10000) ? MI_DOWN : MI_O;
+    const ec_mk_mat &m = mi == MI_QKV ? ly.qkv : mi == MI_UP ? ly.up : mi == MI_DOWN ? ly.down : ly.o;
     const Rg rg = S.rg[mi];
     const int lane = ct & 31, cw = ct >> 5;
     const uint32_t row_bytes = (uint32_t)m.ldw * ELT;
@@ -670,8 +672,6 @@ __device__ __noinline__ uint32_t mk_phase(const ec_mk_params &p, int kind, int l
     const int my = vidx<V>(lane);               // this lane's (row slot, token) after the reduction
     const int my_i = my / MM, my_q = my % MM;
     const bool my_lane = (lane & (D - 1)) == 0 && my_q < nM && (unit == 1 || (my_i & 1) == 0);
-    float bv = -INFINITY;                         // running argmax of token my_q
-    int bi = 0x7fffffff;
 
     for (int row0 = rg.r0; row0 < rg.r1; row0 += tile_rows) {
         const int nr = min(tile_rows, rg.r1 - row0);
@@ -812,36 +812,121 @@ __device__ __noinline__ uint32_t mk_phase(const ec_mk_params &p, int kind, int l
             } else if (kind == PK_UP) {
                 if (p.arch == ARCH_Q2) p.act[(size_t)q * p.I + (n >> 1)] = __fmul_rn(ec_silu(v0), v1);
                 else p.act[(size_t)q * (4 * p.E) + n] = ec_gelu(v0);
-            } else {   // PK_LM
-                if (p.logits) p.logits[(size_t)q * mN + n] = v0;
-                am_merge(bv, bi, v0, p.v0 + n);
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&S.empty[s]);   // this warp no longer reads the slot
         if (ct == 0) tmark(p, S, 0, EC_TR_TILE_DONE);
     }
-    if (kind == PK_LM) {
-        // lanes holding the same token: every offset except the token bits
+    return t;
+}
+
+// ---------------------------------------------------------------------------
+// consumers: the lm_head, streamed straight from HBM into registers
+// ---------------------------------------------------------------------------
+
+// The lm_head rows of this CTA (its MI_LM range), 16-bit weights, streamed by
+// the consumer warps without the ring: each warp takes groups of R rows
+// (groups w, w+8, ...), every lane loads the 16-byte chunks lane, lane+32,
+// ... of each row into registers (R*J loads in flight), and the warp sums
+// its R*MM dots with one transposed reduction.  The per-row order (lane
+// chunks in increasing order, 8 elements each, then the xor tree) is that of
+// the standalone GEMV (ec_kernels.cu k_gemv), so the logits are the same bits
+// as gemm_fp16_fp32 on the same rows.  Weights are read once per step:
+// loaded with the L2 evict-first policy.  Each warp keeps a running argmax
+// per token; the CTA's partial goes to amax_v / amax_i.
+template <int WT, int MM>
+__device__ __noinline__ void mk_lm(const ec_mk_params &p, int ct) {
+    // rows per group and chunks per lane per row in flight: R * J = 16 loads
+    // of 16 bytes per lane (64 KB per CTA), inside the 168 registers a thread
+    // of a 9-warp CTA can have (4 sub-partitions of 16K registers, 3 warps on one)
+    constexpr int R = MM >= 8 ? 2 : 4;
+    constexpr int J = 4;
+    constexpr int V = R * MM;            // values reduced per group (<= 32)
+    constexpr int D = 32 / V;            // lanes ending with the same total
+    static_assert(WT != EC_W_I8, "the lm_head has 16-bit weights");
+    const Sm S = sm_of(p);
+    const int nM = p.M;
+    const int cta = blockIdx.x;
+    const ec_mk_mat &m = p.lm;
+    const Rg rg = S.rg[MI_LM];
+    const int lane = ct & 31, cw = ct >> 5;
+    const size_t row_bytes = (size_t)m.ldw * 2;
+    const int Kp = m.Kp, nch = Kp / 8, mN = m.N;
+    const int groups = (rg.r1 - rg.r0 + R - 1) / R;
+    const uint64_t pol = ec_l2_evict_first();
+    const unsigned char *W = static_cast<const unsigned char *>(m.w);
+    const float *xs = reinterpret_cast<const float *>(S.xbuf);   // fp32 planes per token (mk_operand)
+    const int my = ec_tr_vidx<V>(lane);
+    const int my_r = my / MM, my_q = my % MM;
+    const bool my_lane = (lane & (D - 1)) == 0 && my_q < nM;
+    float bv = -INFINITY;   // running argmax of token my_q
+    int bi = 0x7fffffff;
+    for (int g = cw; g < groups; g += NCW) {
+        if (S.flag[0]) break;
+        const int n0 = rg.r0 + g * R;
+        float acc[V];
 #pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) {
-            if (o <= 4 && o * MM > 4) continue;
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            am_merge(bv, bi, ov, oi);
+        for (int v = 0; v < V; ++v) acc[v] = 0.0f;
+        for (int c0 = 0; c0 < nch; c0 += 32 * J) {
+            uint4 w[R][J];
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const unsigned char *rowp = W + (size_t)(n0 + r) * row_bytes;
+#pragma unroll
+                for (int j = 0; j < J; ++j) {
+                    const int c = c0 + lane + 32 * j;
+                    w[r][j] = (n0 + r < rg.r1 && c < nch) ? ec_ldg_stream16_hint(rowp + (size_t)c * 16, pol)
+                                                          : make_uint4(0, 0, 0, 0);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < J; ++j) {
+                const int c = c0 + lane + 32 * j;
+                if (c >= nch) break;
+                float4 x0[MM], x1[MM];
+#pragma unroll
+                for (int q = 0; q < MM; ++q) {
+                    if (q >= nM) break;
+                    const float *xm = xs + (size_t)q * Kp;
+                    x0[q] = reinterpret_cast<const float4 *>(xm)[c];
+                    x1[q] = reinterpret_cast<const float4 *>(xm + (Kp >> 1))[c];
+                }
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+#pragma unroll
+                    for (int q = 0; q < MM; ++q) {
+                        if (q >= nM) break;
+                        acc[r * MM + q] = ec_dot8<WT == EC_W_BF16>(w[r][j], x0[q], x1[q], acc[r * MM + q]);
+                    }
+                }
+            }
         }
-        cons_sync();
-        if (my < MM && (lane & (D - 1)) == 0) { S.redf[cw * MT + my_q] = bv; S.redi[cw * MT + my_q] = bi; }
-        cons_sync();
-        if (ct < nM) {
-            float v = S.redf[ct];
-            int i = S.redi[ct];
-            for (int w = 1; w < NCW; ++w) am_merge(v, i, S.redf[w * MT + ct], S.redi[w * MT + ct]);
-            p.amax_v[(size_t)cta * MT + ct] = v;
-            p.amax_i[(size_t)cta * MT + ct] = i;
+        const float tot = ec_tr_reduce<V>(acc, lane);
+        const int n = n0 + my_r;
+        if (my_lane && n < rg.r1) {
+            if (p.logits) p.logits[(size_t)my_q * mN + n] = tot;
+            am_merge(bv, bi, tot, p.v0 + n);
         }
     }
-    return t;
+    // lanes holding the same token: every xor offset except the token bits [D, D*MM)
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        if (o >= D && o < D * MM) continue;
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        am_merge(bv, bi, ov, oi);
+    }
+    cons_sync();
+    if (my_r == 0 && (lane & (D - 1)) == 0) { S.redf[cw * MT + my_q] = bv; S.redi[cw * MT + my_q] = bi; }
+    cons_sync();
+    if (ct < nM) {
+        float v = S.redf[ct];
+        int i = S.redi[ct];
+        for (int w = 1; w < NCW; ++w) am_merge(v, i, S.redf[w * MT + ct], S.redi[w * MT + ct]);
+        p.amax_v[(size_t)cta * MT + ct] = v;
+        p.amax_i[(size_t)cta * MT + ct] = i;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -888,6 +973,7 @@ __device__ __noinline__ void mk_attention(const ec_mk_params &p, int layer, int 
         }
         cpa_wait_all();
         cons_sync();
+        if (ct == 0) tmark(p, S, 0, EC_TR_STAGED);
         // scores: sequential fp32 dot per position, scaled in double
         float mx = -FLT_MAX;
         for (int c0 = 0; c0 < len; c0 += CH) {
@@ -929,6 +1015,7 @@ __device__ __noinline__ void mk_attention(const ec_mk_params &p, int layer, int 
             for (int i = 1; i < NCW; ++i) t = ec_max_keep(t, S.redf[i * MT]);
             mx = t;
         }
+        if (ct == 0) tmark(p, S, 0, EC_TR_SCORES);
         double sum = 0.0;
         for (int i = ct; i < len; i += NCT) {
             const float e = ec_expf(__fsub_rn(sc[i], mx));
@@ -947,6 +1034,7 @@ __device__ __noinline__ void mk_attention(const ec_mk_params &p, int layer, int 
         const double isum = __ddiv_rn(1.0, sum);
         for (int i = ct; i < len; i += NCT) sc[i] = (float)__dmul_rn((double)sc[i], isum);
         cons_sync();
+        if (ct == 0) tmark(p, S, 0, EC_TR_SOFTMAX);
         // P.V: sequential over positions for each output dimension
         float o = 0.0f;
         for (int c0 = 0; c0 < len; c0 += CH) {
@@ -1095,7 +1183,8 @@ __global__ void __launch_bounds__(EC_MK_THREADS, 1) k_decode(const __grid_consta
                     if (t != T_ABORT) t = mk_produce(p, ly.up, LWT, S.rg[MI_UP], t);
                     if (t != T_ABORT) t = mk_produce(p, ly.down, LWT, S.rg[MI_DOWN], t);
                 }
-                if (t != T_ABORT) t = mk_produce(p, p.lm, HWT, S.rg[MI_LM], t);
+                // the lm_head is streamed by the consumers themselves (mk_lm);
+                // meanwhile this loop already fills the ring for the next step
             }
             if (t == T_ABORT) {
                 // give the copies already issued a bounded time to land
@@ -1182,7 +1271,7 @@ __global__ void __launch_bounds__(EC_MK_THREADS, 1) k_decode(const __grid_consta
         mk_norm<MM>(p, false, p.nfg, p.nfb, ct);
         mk_operand<MM>(p, nullptr, p.E, p.lm.Kp, HWT, ct);
         if (ct == 0) tmark(p, S, 0, EC_TR_PROLOGUE);
-        t = mk_phase<HWT, MM>(p, PK_LM, -1, t, ct);
+        mk_lm<HWT, MM>(p, ct);
         if (ct == 0) tmark(p, S, 0, EC_TR_LM);
         // G: merge the per-CTA partials (CTA order, lowest index on ties)
         SYNC_OR_RETURN();

@@ -86,7 +86,11 @@ typedef struct {
  * done; attention done; lm_head done; argmax merged; per weight tile: data
  * arrived, ring slot released, epilogue done; producer issued a tile copy. */
 enum { EC_TR_SYNC = 1, EC_TR_PROLOGUE = 2, EC_TR_TILES = 3, EC_TR_ATTN = 4, EC_TR_LM = 5, EC_TR_ARGMAX = 6,
-       EC_TR_TILE_IN = 7, EC_TR_TILE_FREE = 8, EC_TR_TILE_DONE = 9, EC_TR_ISSUE = 10 };
+       EC_TR_TILE_IN = 7, EC_TR_TILE_FREE = 8, EC_TR_TILE_DONE = 9, EC_TR_ISSUE = 10,
+       EC_TR_STAGED = 11,    /* a prologue's or attention item's inputs arrived in shared memory */
+       EC_TR_STATS = 12,     /* norm statistics reduced */
+       EC_TR_SCORES = 13,    /* attention scores and their max done */
+       EC_TR_SOFTMAX = 14 }; /* attention weights normalised */
 
 /* Dynamic shared memory of the kernel for these parameters. */
 size_t ec_mk_smem_bytes(const ec_mk_params *p);

@@ -25,55 +25,26 @@ __device__ int g_ec_err;
 #define GEMV_THREADS 256
 #define GEMV_WARPS (GEMV_THREADS / 32)
 #define GEMV_MT 8          // max token rows per GEMV launch
-#define GEMV_MAX_ROWS 128  // max staged rows per block (val[] size)
 
 // ---------------------------------------------------------------------------
-// GEMV
+// GEMV: weight streaming for M <= 8 token rows
+//
+// Every warp owns groups of R consecutive weight rows (group g, g + W, ... for
+// the W warps of the grid, so that the rows in flight at one time are close
+// together in HBM).  Lane l reads the 16-byte chunks l, l+32, l+64, l+96 of
+// each of the R rows straight into registers (up to 4R loads in flight per
+// lane, no shared-memory staging of weights), multiplies them with the
+// activation chunks held in shared memory, and the warp sums its R*MM
+// partial dots with one transposed shuffle reduction.  A row's result does not
+// depend on which warp or slot computes it: lane l always accumulates its
+// chunks in increasing order (8 elements per chunk in element order) and the
+// lane sum is the xor tree 16, 8, 4, 2, 1.
 // ---------------------------------------------------------------------------
 
-struct GemvSmem {
-    // Layout of the dynamic shared memory, computed identically on host and
-    // device: [stages][stage_bytes] | x region | val[GEMV_MAX_ROWS][MT] (4 B) |
-    // part[8][MT] | ascale[MT] | red[8][MT] | mbarriers[stages]
-    uint32_t stage_bytes, x_off, val_off, part_off, asc_off, red_off, bar_off, total;
-};
-
-__host__ __device__ inline uint32_t ec_align16(uint32_t v) { return (v + 15u) & ~15u; }
-
-__host__ __device__ inline GemvSmem gemv_layout(int wt, int M, int Kp, int ldw, int block_rows, int stages) {
-    GemvSmem s;
-    const uint32_t elt = wt == EC_W_I8 ? 1u : 2u;
-    s.stage_bytes = ec_align16((uint32_t)block_rows * (uint32_t)ldw * elt);
-    uint32_t off = s.stage_bytes * (uint32_t)stages;
-    s.x_off = off;
-    off += ec_align16((uint32_t)M * (uint32_t)Kp * (wt == EC_W_I8 ? 1u : 4u));
-    s.val_off = off;
-    off += GEMV_MAX_ROWS * GEMV_MT * 4;
-    s.part_off = off;
-    off += GEMV_WARPS * GEMV_MT * 4;
-    s.asc_off = off;
-    off += GEMV_MT * 4;
-    s.red_off = off;
-    off += GEMV_WARPS * GEMV_MT * 4;
-    s.bar_off = ec_align16(off);
-    s.total = s.bar_off + 8u * (uint32_t)stages;
-    return s;
-}
-
-template <int WT>
-struct GemvAcc;
+template <int WT> struct GemvAcc;
 template <> struct GemvAcc<EC_W_I8> { typedef int T; };
 template <> struct GemvAcc<EC_W_F16> { typedef float T; };
 template <> struct GemvAcc<EC_W_BF16> { typedef float T; };
-
-EC_DEV void ec_bf16x8_to_f32(const uint4 w, float f[8]) {
-    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        f[2 * i] = __uint_as_float(u[i] << 16);
-        f[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
-    }
-}
 
 EC_DEV void ec_f16x8_to_f32(const uint4 w, float f[8]) {
     const uint32_t u[4] = {w.x, w.y, w.z, w.w};
@@ -85,267 +56,164 @@ EC_DEV void ec_f16x8_to_f32(const uint4 w, float f[8]) {
     }
 }
 
-// Apply the epilogue of one (row value, token) pair set.  `v_lo` is the value
-// of staged row r (global row n_lo); for pair blocks `v_hi` is the partner row.
-EC_DEV void gemv_store_kv(const ec_kvgeo &g, uint16_t *cache, int slot, int pos, int col, float v) {
-    cache[((size_t)slot * g.C + pos) * g.kv + col] = ec_f2h(v);
+EC_DEV void prefetch_l2(const void *p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
+// Shared memory of one CTA: the activation operand, int8 [M][Kp] or fp32
+// planes [M][Kp] (elements 0-3 and 4-7 of every 8-element chunk in two
+// planes, so 16-byte reads by consecutive lanes are conflict-free).
+__host__ __device__ inline size_t gemv_smem_bytes(int wt, int M, int Kp) {
+    return (size_t)M * (size_t)Kp * (wt == EC_W_I8 ? 1u : 4u);
 }
 
-template <int WT>
-__global__ void __launch_bounds__(GEMV_THREADS)
-k_gemv(const ec_gemv_args a, const int stages) {
+template <int WT, int MM, int R, int J>
+__global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const ec_gemv_args a) {
     typedef typename GemvAcc<WT>::T Acc;
-    extern __shared__ __align__(128) unsigned char smem[];
-    const int M = a.M;
-    const int ldw = a.ldw ? a.ldw : a.Kp;
-    const GemvSmem L = gemv_layout(WT, M, a.Kp, ldw, a.block_rows, stages);
-    unsigned char *stage0 = smem;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bar_off);
-    Acc *val = reinterpret_cast<Acc *>(smem + L.val_off);
-    Acc *part = reinterpret_cast<Acc *>(smem + L.part_off);
-    float *asc = reinterpret_cast<float *>(smem + L.asc_off);
-    float *red = reinterpret_cast<float *>(smem + L.red_off);
+    constexpr int ELT = WT == EC_W_I8 ? 1 : 2;
+    constexpr int V = R * MM;   // values reduced per row group: [r][m]
+    constexpr int D = 32 / V;   // lanes ending with the same total
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ float asc[GEMV_MT];
+    __shared__ float red[GEMV_WARPS][GEMV_MT];
+    const int M = a.M, Kp = a.Kp, K = a.K, N = a.N;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t elt = WT == EC_W_I8 ? 1u : 2u;
-    const uint32_t row_bytes = (uint32_t)ldw * elt;   // staged row stride
-    const int nch = (int)((uint32_t)a.Kp * elt / 16u);  // 16-byte weight chunks per row
-    const int nmine = (a.nblocks - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
-    if (nmine <= 0) return;
+    const int ldw = a.ldw ? a.ldw : Kp;
+    const size_t row_bytes = (size_t)ldw * ELT;
+    const int nch = Kp * ELT / 16;
+    const int groups = (N + R - 1) / R;
+    const int nw = (int)gridDim.x * GEMV_WARPS;
+    const int gw = (int)blockIdx.x * GEMV_WARPS + warp;
+    const unsigned char *W = static_cast<const unsigned char *>(a.W);
 
-    auto desc = [&](int i) -> ec_block {
-        const int b = (int)blockIdx.x + i * (int)gridDim.x;
-        if (a.blocks) return a.blocks[b];
-        ec_block d;
-        d.row0 = b * a.block_rows;
-        d.nrows = min(a.block_rows, a.N - d.row0);
-        d.pair = 0;
-        d.kind = 0;
-        return d;
-    };
-    auto issue = [&](int i) {
-        const ec_block d = desc(i);
-        const int s = i % stages;
-        unsigned char *dst = stage0 + (size_t)s * L.stage_bytes;
-        const uint32_t b1 = (uint32_t)d.nrows * row_bytes;
-        const uint32_t tot = d.pair ? 2u * b1 : b1;
-        ec_mbar_expect_tx(&bars[s], tot);
-        const unsigned char *W = static_cast<const unsigned char *>(a.W);
-        ec_bulk_g2s(dst, W + (size_t)d.row0 * row_bytes, b1, &bars[s]);
-        if (d.pair) ec_bulk_g2s(dst + b1, W + (size_t)(d.row0 + d.pair) * row_bytes, b1, &bars[s]);
-    };
-
-    if (tid == 0) {
-        for (int s = 0; s < stages; ++s) ec_mbar_init(&bars[s], 1);
-        ec_fence_mbar_init();
-    }
-    __syncthreads();
-    if (tid == 0) {
-        const int pre = nmine < stages ? nmine : stages;
-        for (int i = 0; i < pre; ++i) issue(i);
+    // this warp's first row group into L2 while the activations are prepared
+    if (gw < groups) {
+        const int rows = min(R, N - gw * R);
+        const unsigned char *g0 = W + (size_t)gw * R * row_bytes;
+        const size_t bytes = (size_t)(rows - 1) * row_bytes + (size_t)Kp * ELT;
+        for (size_t o = (size_t)lane * 128; o < bytes; o += 32 * 128) prefetch_l2(g0 + o);
     }
 
-    // ---- activation prologue (overlaps the weight fetch) -------------------
-    if (WT == EC_W_I8 && a.Xq) {
-        int8_t *xs = reinterpret_cast<int8_t *>(smem + L.x_off);
-        if (tid < M) asc[tid] = a.xscale[tid];
-        for (int m = 0; m < M; ++m)
-            for (int k = tid; k < a.Kp; k += GEMV_THREADS)
-                xs[(size_t)m * a.Kp + k] = k < a.K ? a.Xq[(size_t)m * a.ldx + k] : (int8_t)0;
-    } else if (WT == EC_W_I8) {
-        int8_t *xs = reinterpret_cast<int8_t *>(smem + L.x_off);
-        float mx[GEMV_MT];
+    // ---- activation operand -------------------------------------------------
+    if (WT == EC_W_I8) {
+        int8_t *xs = reinterpret_cast<int8_t *>(smem);
+        if (a.Xq) {
+            if (tid < M) asc[tid] = a.xscale[tid];
+            for (int m = 0; m < M; ++m)
+                for (int k = tid; k < Kp; k += GEMV_THREADS)
+                    xs[(size_t)m * Kp + k] = k < K ? a.Xq[(size_t)m * a.ldx + k] : (int8_t)0;
+        } else {
+            // reference activation quantisation (src/gpt2.c:446-461), per CTA
+            float mx[MM];
 #pragma unroll
-        for (int m = 0; m < GEMV_MT; ++m) mx[m] = 0.0f;
-        for (int k = tid; k < a.K; k += GEMV_THREADS) {
+            for (int m = 0; m < MM; ++m) mx[m] = 0.0f;
+            for (int k = tid; k < K; k += GEMV_THREADS) {
 #pragma unroll
-            for (int m = 0; m < GEMV_MT; ++m)
-                if (m < M) mx[m] = ec_max_keep(mx[m], fabsf(a.X[(size_t)m * a.ldx + k]));
-        }
-#pragma unroll
-        for (int m = 0; m < GEMV_MT; ++m) {
-            float w = ec_warp_max(mx[m]);
-            if (lane == 0 && m < M) red[warp * GEMV_MT + m] = w;
-        }
-        __syncthreads();
-        if (tid < M) {
-            float w = 0.0f;
-            for (int i = 0; i < GEMV_WARPS; ++i) w = ec_max_keep(w, red[i * GEMV_MT + tid]);
-            asc[tid] = w > 0.0f ? __fdiv_rn(w, 127.0f) : 1.0f;
-        }
-        __syncthreads();
-        for (int m = 0; m < M; ++m) {
-            const float s = asc[m];
-            const float *xr = a.X + (size_t)m * a.ldx;
-            for (int k = tid; k < a.Kp; k += GEMV_THREADS)
-                xs[(size_t)m * a.Kp + k] = (int8_t)(k < a.K ? ec_quant1(xr[k], s) : 0);
-        }
-    } else {
-        // fp32 activations, stored as two planes per row (elements 0-3 and
-        // 4-7 of every 8-element chunk) so that 16-byte reads are conflict-free.
-        float *xs = reinterpret_cast<float *>(smem + L.x_off);
-        for (int m = 0; m < M; ++m) {
-            const float *xr = a.X + (size_t)m * a.ldx;
-            float *xm = xs + (size_t)m * a.Kp;
-            for (int k = tid; k < a.Kp; k += GEMV_THREADS) {
-                const float v = k < a.K ? xr[k] : 0.0f;
-                const int c = k >> 3, e = k & 7;
-                xm[(e >> 2) * (a.Kp >> 1) + c * 4 + (e & 3)] = v;
+                for (int m = 0; m < MM; ++m)
+                    if (m < M) mx[m] = ec_max_keep(mx[m], fabsf(a.X[(size_t)m * a.ldx + k]));
             }
-        }
-    }
-    __syncthreads();
-
-    for (int i = 0; i < nmine; ++i) {
-        const int s = i % stages;
-        const ec_block d = desc(i);
-        const int rows = d.pair ? 2 * d.nrows : d.nrows;
-        const bool ok = ec_mbar_wait(&bars[s], (uint32_t)((i / stages) & 1), &g_ec_err);
-        if (__syncthreads_or(!ok)) return;
-        const unsigned char *st = stage0 + (size_t)s * L.stage_bytes;
-
-        // warps per row: split a row's chunks across warps only when all rows
-        // of the block fit in one pass (rows * wpr <= 8), so part[] is
-        // written once per block
-        const int wpr = rows > 4 ? 1 : (rows > 2 ? 2 : (rows == 2 ? 4 : 8));
-        const int conc = GEMV_WARPS / wpr;
-        for (int r0 = 0; r0 < rows; r0 += conc) {
-            const int r = r0 + warp / wpr, sub = warp % wpr;
-            if (r < rows) {
-                Acc acc[GEMV_MT];
 #pragma unroll
-                for (int m = 0; m < GEMV_MT; ++m) acc[m] = 0;
-                const uint4 *wrow = reinterpret_cast<const uint4 *>(st + (size_t)r * row_bytes);
-                for (int c = sub * 32 + lane; c < nch; c += wpr * 32) {
-                    const uint4 w = wrow[c];
-                    if (WT == EC_W_I8) {
-                        const int8_t *xs = reinterpret_cast<const int8_t *>(smem + L.x_off);
-#pragma unroll
-                        for (int m = 0; m < GEMV_MT; ++m) {
-                            if (m < M) {
-                                const uint4 x = reinterpret_cast<const uint4 *>(xs + (size_t)m * a.Kp)[c];
-                                int t = (int)acc[m];
-                                t = __dp4a((int)w.x, (int)x.x, t);
-                                t = __dp4a((int)w.y, (int)x.y, t);
-                                t = __dp4a((int)w.z, (int)x.z, t);
-                                t = __dp4a((int)w.w, (int)x.w, t);
-                                acc[m] = t;
-                            }
-                        }
-                    } else {
-                        float f[8];
-                        if (WT == EC_W_F16) ec_f16x8_to_f32(w, f); else ec_bf16x8_to_f32(w, f);
-                        const float *xs = reinterpret_cast<const float *>(smem + L.x_off);
-#pragma unroll
-                        for (int m = 0; m < GEMV_MT; ++m) {
-                            if (m < M) {
-                                const float *xm = xs + (size_t)m * a.Kp;
-                                const float4 x0 = reinterpret_cast<const float4 *>(xm)[c];
-                                const float4 x1 = reinterpret_cast<const float4 *>(xm + (a.Kp >> 1))[c];
-                                float t = (float)acc[m];
-                                t = fmaf(f[0], x0.x, t); t = fmaf(f[1], x0.y, t);
-                                t = fmaf(f[2], x0.z, t); t = fmaf(f[3], x0.w, t);
-                                t = fmaf(f[4], x1.x, t); t = fmaf(f[5], x1.y, t);
-                                t = fmaf(f[6], x1.z, t); t = fmaf(f[7], x1.w, t);
-                                acc[m] = t;
-                            }
-                        }
-                    }
-                }
-#pragma unroll
-                for (int m = 0; m < GEMV_MT; ++m) {
-                    if (WT == EC_W_I8) acc[m] = ec_warp_sum_i((int)acc[m]);
-                    else acc[m] = ec_warp_sum((float)acc[m]);
-                }
-                if (lane == 0) {
-                    for (int m = 0; m < M; ++m) {
-                        if (wpr == 1) val[r * GEMV_MT + m] = acc[m];
-                        else part[warp * GEMV_MT + m] = acc[m];
-                    }
-                }
-            }
-        }
-        __syncthreads();
-        if (wpr > 1) {
-            for (int idx = tid; idx < rows * M; idx += GEMV_THREADS) {
-                const int r = idx / M, m = idx % M;
-                Acc t = 0;
-                for (int q = 0; q < wpr; ++q) t = t + part[(r * wpr + q) * GEMV_MT + m];
-                val[r * GEMV_MT + m] = t;
+            for (int m = 0; m < MM; ++m) {
+                const float w = ec_warp_max(mx[m]);
+                if (lane == 0) red[warp][m] = w;
             }
             __syncthreads();
+            if (tid < M) {
+                float w = 0.0f;
+                for (int i = 0; i < GEMV_WARPS; ++i) w = ec_max_keep(w, red[i][tid]);
+                asc[tid] = w > 0.0f ? __fdiv_rn(w, 127.0f) : 1.0f;
+            }
+            __syncthreads();
+            for (int m = 0; m < M; ++m) {
+                const float s = asc[m], r = __fdiv_rn(1.0f, s);
+                const float *xr = a.X + (size_t)m * a.ldx;
+                for (int k = tid; k < Kp; k += GEMV_THREADS)
+                    xs[(size_t)m * Kp + k] = (int8_t)(k < K ? ec_quant_fast(xr[k], s, r) : 0);
+            }
         }
-        // The stage has been consumed: refill it with block i + stages.
-        if (tid == 0 && i + stages < nmine) issue(i + stages);
+    } else {
+        float *xs = reinterpret_cast<float *>(smem);
+        for (int m = 0; m < M; ++m) {
+            const float *xr = a.X + (size_t)m * a.ldx;
+            float *xm = xs + (size_t)m * Kp;
+            for (int k = tid; k < Kp; k += GEMV_THREADS) {
+                const float v = k < K ? xr[k] : 0.0f;
+                const int c = k >> 3, e = k & 7;
+                xm[(e >> 2) * (Kp >> 1) + c * 4 + (e & 3)] = v;
+            }
+        }
+    }
+    __syncthreads();
 
-        // ---- epilogue ------------------------------------------------------
-        const int nout = d.nrows;
-        for (int idx = tid; idx < nout * M; idx += GEMV_THREADS) {
-            const int r = idx / M, m = idx % M;
-            const int n_lo = d.row0 + r;
-            float v_lo, v_hi = 0.0f;
-            int n_hi = n_lo + d.pair;
-            if (WT == EC_W_I8) {
-                const float as = asc[m];
-                float t = __fmul_rn(__fmul_rn(__int2float_rn((int)val[r * GEMV_MT + m]), as),
-                                    a.wscale ? a.wscale[n_lo] : 1.0f);
-                v_lo = __fadd_rn(a.bias ? a.bias[n_lo] : 0.0f, t);
-                if (d.pair) {
-                    float u = __fmul_rn(__fmul_rn(__int2float_rn((int)val[(d.nrows + r) * GEMV_MT + m]), as),
-                                        a.wscale ? a.wscale[n_hi] : 1.0f);
-                    v_hi = __fadd_rn(a.bias ? a.bias[n_hi] : 0.0f, u);
-                }
-            } else {
-                v_lo = (float)val[r * GEMV_MT + m];
-                if (a.bias) v_lo = __fadd_rn(v_lo, a.bias[n_lo]);
-                if (d.pair) {
-                    v_hi = (float)val[(d.nrows + r) * GEMV_MT + m];
-                    if (a.bias) v_hi = __fadd_rn(v_hi, a.bias[n_hi]);
+    // ---- row groups ---------------------------------------------------------
+    const int my = ec_tr_vidx<V>(lane);
+    const int my_r = my / MM, my_m = my % MM;
+    const bool my_lane = (lane & (D - 1)) == 0 && my_m < M;
+    for (int g = gw; g < groups; g += nw) {
+        const int n0 = g * R;
+        Acc acc[V];
+#pragma unroll
+        for (int v = 0; v < V; ++v) acc[v] = 0;
+        for (int c0 = 0; c0 < nch; c0 += 32 * J) {
+            uint4 w[R][J];
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const unsigned char *rowp = W + (size_t)(n0 + r) * row_bytes;
+#pragma unroll
+                for (int j = 0; j < J; ++j) {
+                    const int c = c0 + lane + 32 * j;
+                    w[r][j] = (n0 + r < N && c < nch) ? ec_ldg_stream16(rowp + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
                 }
             }
-            float *orow = a.out + (size_t)m * a.ldo;
-            switch (a.epi) {
-            case EC_EPI_STORE: orow[n_lo] = v_lo; if (d.pair) orow[n_hi] = v_hi; break;
-            case EC_EPI_RESID:
-                orow[n_lo] = __fadd_rn(orow[n_lo], v_lo);
-                if (d.pair) orow[n_hi] = __fadd_rn(orow[n_hi], v_hi);
-                break;
-            case EC_EPI_GELU:
-                orow[n_lo] = ec_gelu(v_lo);
-                if (d.pair) orow[n_hi] = ec_gelu(v_hi);
-                break;
-            case EC_EPI_SWIGLU: orow[n_lo] = __fmul_rn(ec_silu(v_lo), v_hi); break;
-            case EC_EPI_QKV: {
-                const ec_kvgeo &g = a.geo;
-                const int pos = a.tk.pos[m], slot = a.tk.slot[m];
-                if (pos < 0 || pos >= g.C || slot < 0 || slot >= g.B) {
-                    atomicCAS(&g_ec_err, 0, EC_KERR_BAD_INDEX);
-                    break;
+#pragma unroll
+            for (int j = 0; j < J; ++j) {
+                const int c = c0 + lane + 32 * j;
+                if (c >= nch) break;
+                if (WT == EC_W_I8) {
+                    const int8_t *xs = reinterpret_cast<const int8_t *>(smem);
+#pragma unroll
+                    for (int m = 0; m < MM; ++m) {
+                        if (m >= M) break;
+                        const uint4 x = reinterpret_cast<const uint4 *>(xs + (size_t)m * Kp)[c];
+#pragma unroll
+                        for (int r = 0; r < R; ++r) {
+                            int t = (int)acc[r * MM + m];
+                            t = __dp4a((int)w[r][j].x, (int)x.x, t);
+                            t = __dp4a((int)w[r][j].y, (int)x.y, t);
+                            t = __dp4a((int)w[r][j].z, (int)x.z, t);
+                            t = __dp4a((int)w[r][j].w, (int)x.w, t);
+                            acc[r * MM + m] = t;
+                        }
+                    }
+                } else {
+                    const float *xs = reinterpret_cast<const float *>(smem);
+#pragma unroll
+                    for (int m = 0; m < MM; ++m) {
+                        if (m >= M) break;
+                        const float *xm = xs + (size_t)m * Kp;
+                        const float4 x0 = reinterpret_cast<const float4 *>(xm)[c];
+                        const float4 x1 = reinterpret_cast<const float4 *>(xm + (Kp >> 1))[c];
+#pragma unroll
+                        for (int r = 0; r < R; ++r)
+                            acc[r * MM + m] = ec_dot8<WT == EC_W_BF16>(w[r][j], x0, x1, (float)acc[r * MM + m]);
+                    }
                 }
-                if (d.kind == EC_BK_ROPE) {
-                    const int half = g.hd >> 1;
-                    const int i2 = (n_lo % g.hd);   // < half by construction
-                    const double c = g.rope_cos[(size_t)pos * half + i2];
-                    const double sn = g.rope_sin[(size_t)pos * half + i2];
-                    const double av = (double)v_lo, bv = (double)v_hi;
-                    const float lo = (float)__dsub_rn(__dmul_rn(av, c), __dmul_rn(bv, sn));
-                    const float hi = (float)__dadd_rn(__dmul_rn(av, sn), __dmul_rn(bv, c));
-                    v_lo = lo;
-                    v_hi = hi;
-                }
-                const int nn[2] = {n_lo, n_hi};
-                const float vv[2] = {v_lo, v_hi};
-                for (int h = 0; h < (d.pair ? 2 : 1); ++h) {
-                    const int n = nn[h];
-                    if (n < g.E) orow[n] = vv[h];
-                    else if (n < g.E + g.kv) gemv_store_kv(g, g.kc, slot, pos, n - g.E, vv[h]);
-                    else gemv_store_kv(g, g.vc, slot, pos, n - g.E - g.kv, vv[h]);
-                }
-                break;
-            }
-            default: break;
             }
         }
-        __syncthreads();
+        const Acc tot = ec_tr_reduce<V>(acc, lane);
+        const int n = n0 + my_r;
+        if (!my_lane || n >= N) continue;
+        float v;
+        if (WT == EC_W_I8) {
+            // reference gemm_int8 epilogue: bias + ((float)dot * a_scale) * b_scale (src/kernels.c:153-168)
+            const float t = __fmul_rn(__fmul_rn(__int2float_rn((int)tot), asc[my_m]), a.wscale ? a.wscale[n] : 1.0f);
+            v = __fadd_rn(a.bias ? a.bias[n] : 0.0f, t);
+        } else {
+            v = (float)tot;
+            if (a.bias) v = __fadd_rn(v, a.bias[n]);
+        }
+        float *o = a.out + (size_t)my_m * a.ldo + n;
+        if (a.epi == EC_EPI_RESID) *o = __fadd_rn(*o, v);
+        else if (a.epi == EC_EPI_GELU) *o = ec_gelu(v);
+        else *o = v;
     }
 }
 
@@ -357,61 +225,85 @@ extern "C" int ec_kernels_init(void) {
     if (e != cudaSuccess) return (int)e;
     e = cudaDeviceGetAttribute(&g_ec_max_optin_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     if (e != cudaSuccess) return (int)e;
-    e = cudaFuncSetAttribute(k_gemv<EC_W_I8>, cudaFuncAttributeMaxDynamicSharedMemorySize, g_ec_max_optin_smem);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(k_gemv<EC_W_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, g_ec_max_optin_smem);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(k_gemv<EC_W_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, g_ec_max_optin_smem);
-    if (e == cudaSuccess) {
-        ec_attention_exact_fits(1, 1, 8, 1);   // sets the exact-attention smem attribute outside any capture
-        e = cudaGetLastError();
-    }
-    return (int)e;
+    ec_attention_exact_fits(1, 1, 8, 1);   // sets the exact-attention smem attribute outside any capture
+    return (int)cudaGetLastError();
 }
 
-// Shared memory of one GEMV launch with the fewest stages (1), or 0 when the
-// arguments are outside what the kernel takes.
-static size_t gemv_min_smem(const ec_gemv_args *a) {
-    if (a->M <= 0 || a->M > GEMV_MT || a->block_rows <= 0 || a->block_rows > GEMV_MAX_ROWS || (a->Kp % 16) != 0)
-        return 0;
+// The GEMV takes M <= 8 rows, plain / residual / GELU epilogues, no row
+// blocks, K a multiple of 16 and the activation operand in shared memory.
+static size_t gemv_need(const ec_gemv_args *a) {
+    if (a->M <= 0 || a->M > GEMV_MT || a->blocks || a->Kp % 16 || a->K > a->Kp) return 0;
+    if (a->epi != EC_EPI_STORE && a->epi != EC_EPI_RESID && a->epi != EC_EPI_GELU) return 0;
     const int ldw = a->ldw ? a->ldw : a->Kp;
     if (ldw < a->Kp || (ldw * (a->wt == EC_W_I8 ? 1 : 2)) % 16 != 0) return 0;
-    return gemv_layout(a->wt, a->M, a->Kp, ldw, a->block_rows, 1).total;
+    return gemv_smem_bytes(a->wt, a->M, a->Kp) + 16;
 }
 
 extern "C" int ec_gemv_fits(const ec_gemv_args *a) {
     if (g_ec_max_optin_smem == 0 && ec_kernels_init() != 0) return 0;
-    const size_t need = gemv_min_smem(a);
+    const size_t need = gemv_need(a);
     return need > 0 && need <= (size_t)g_ec_max_optin_smem;
 }
 
+template <int WT, int MM, int R, int J>
+static int gemv_launch(const ec_gemv_args *a, int num_sms, size_t smem, cudaStream_t stream) {
+    auto kern = k_gemv<WT, MM, R, J>;
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return (int)e;
+    }
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, GEMV_THREADS, smem) != cudaSuccess || occ < 1) {
+        cudaGetLastError();
+        occ = 1;
+    }
+    const long long groups = ((long long)a->N + R - 1) / R;
+    long long grid = (groups + GEMV_WARPS - 1) / GEMV_WARPS;
+    const long long cap = (long long)num_sms * occ;
+    if (grid > cap) grid = cap;
+    kern<<<(int)grid, GEMV_THREADS, smem, stream>>>(*a);
+    return (int)cudaGetLastError();
+}
+
+// R rows of J chunks per lane in flight (R * J = 16 loads of 16 bytes):
+// 8 rows of 2 chunks when a row has at most 64 chunks, else 4 rows of 4;
+// 8 token rows keep R * MM <= 32 values per reduction (and 16-bit weights
+// their registers) with fewer rows per group.
+template <int WT>
+static int gemv_launch_r(const ec_gemv_args *a, int num_sms, size_t smem, cudaStream_t stream) {
+    const int nch = a->Kp * (WT == EC_W_I8 ? 1 : 2) / 16;
+    const bool short_rows = nch <= 64;
+    if constexpr (WT == EC_W_I8) {
+        if (a->M <= 1) return short_rows ? gemv_launch<WT, 1, 8, 2>(a, num_sms, smem, stream)
+                                         : gemv_launch<WT, 1, 4, 4>(a, num_sms, smem, stream);
+        if (a->M <= 2) return short_rows ? gemv_launch<WT, 2, 8, 2>(a, num_sms, smem, stream)
+                                         : gemv_launch<WT, 2, 4, 4>(a, num_sms, smem, stream);
+        if (a->M <= 4) return short_rows ? gemv_launch<WT, 4, 8, 2>(a, num_sms, smem, stream)
+                                         : gemv_launch<WT, 4, 4, 4>(a, num_sms, smem, stream);
+        return gemv_launch<WT, 8, 4, 4>(a, num_sms, smem, stream);
+    } else {
+        if (a->M <= 1) return short_rows ? gemv_launch<WT, 1, 8, 2>(a, num_sms, smem, stream)
+                                         : gemv_launch<WT, 1, 4, 4>(a, num_sms, smem, stream);
+        if (a->M <= 2) return gemv_launch<WT, 2, 4, 4>(a, num_sms, smem, stream);
+        if (a->M <= 4) return gemv_launch<WT, 4, 4, 4>(a, num_sms, smem, stream);
+        return gemv_launch<WT, 8, 2, 4>(a, num_sms, smem, stream);
+    }
+}
+
 extern "C" int ec_launch_gemv(const ec_gemv_args *a, int num_sms, cudaStream_t stream) {
-    if (a->M <= 0 || a->nblocks <= 0) return 0;
-    if (a->M > GEMV_MT || a->block_rows > GEMV_MAX_ROWS || (a->Kp % 16) != 0) return (int)cudaErrorInvalidValue;
+    if (a->M <= 0 || a->N <= 0) return 0;
     if (g_ec_max_optin_smem == 0) {
         const int e = ec_kernels_init();
         if (e) return e;
     }
-    // A CTA owning several blocks keeps up to 3 of them in flight.
-    const int per_sm_target = 2;
-    int grid = a->nblocks;
-    const int cap = num_sms * per_sm_target;
-    int stages = 1;
-    if (grid > cap) { grid = cap; stages = 3; }
-    const int ldw = a->ldw ? a->ldw : a->Kp;
-    if (ldw < a->Kp || (ldw * (a->wt == EC_W_I8 ? 1 : 2)) % 16 != 0) return (int)cudaErrorInvalidValue;
-    GemvSmem L = gemv_layout(a->wt, a->M, a->Kp, ldw, a->block_rows, stages);
-    while (stages > 1 && (int)L.total > g_ec_max_optin_smem / per_sm_target) {
-        --stages;
-        L = gemv_layout(a->wt, a->M, a->Kp, ldw, a->block_rows, stages);
-    }
-    if ((int)L.total > g_ec_max_optin_smem) return (int)cudaErrorInvalidValue;
+    const size_t need = gemv_need(a);
+    if (need == 0 || need > (size_t)g_ec_max_optin_smem) return (int)cudaErrorInvalidValue;
+    const size_t smem = gemv_smem_bytes(a->wt, a->M, a->Kp);
     switch (a->wt) {
-    case EC_W_I8: k_gemv<EC_W_I8><<<grid, GEMV_THREADS, L.total, stream>>>(*a, stages); break;
-    case EC_W_F16: k_gemv<EC_W_F16><<<grid, GEMV_THREADS, L.total, stream>>>(*a, stages); break;
-    default: k_gemv<EC_W_BF16><<<grid, GEMV_THREADS, L.total, stream>>>(*a, stages); break;
+    case EC_W_I8: return gemv_launch_r<EC_W_I8>(a, num_sms, smem, stream);
+    case EC_W_F16: return gemv_launch_r<EC_W_F16>(a, num_sms, smem, stream);
+    default: return gemv_launch_r<EC_W_BF16>(a, num_sms, smem, stream);
     }
-    return (int)cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------

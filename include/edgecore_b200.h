@@ -87,7 +87,10 @@ int ec_decode_profile(GPT2 *g, int *d_tokens, int start_pos, int n_steps, double
  * globaltimer-ns, first those of one consumer thread (codes 1 barrier passed,
  * 2 operand built, 3 weight tiles done, 4 attention done, 5 lm_head done,
  * 6 argmax merged, 7 tile data arrived, 8 ring slot released, 9 tile epilogue
- * done), then those of the producer thread (10 tile copy issued), each part
+ * done, 11 a prologue's or attention item's inputs staged in shared memory,
+ * 12 norm statistics reduced, 13 attention scores and their max done,
+ * 14 attention weights normalised), then those of the producer thread
+ * (10 tile copy issued), each part
  * holding at most cap/2 entries.  Returns the number of entries, or -1. */
 int ec_decode_trace(GPT2 *g, int *d_tokens, int start_pos, int n_steps,
                     unsigned long long *out, int cap);
@@ -124,6 +127,17 @@ int ec_quantize_rows(int8_t *q, float *scale, const float *x, int M, int K);
 /* W8A8 linear: quantise X rows then gemm_int8 (reference src/gpt2.c:437-462). */
 int ec_linear_int8(float *C, const float *X, const int8_t *W,
                    const float *w_scale, const float *bias, int M, int K, int N);
+
+/* gemm_int8 (wt 0: A int8 [M][K] with a_scale[M]), gemm_fp16_fp32 (wt 1)
+ * or gemm_bf16_fp32 (wt 2: A fp32 [M][K]) on DEVICE operands of the current
+ * device, enqueued on `stream` with no host synchronisation: the
+ * reference's gemm_* (src/kernels.c:129-168) for GPU callers that keep their
+ * data resident.  K must be a multiple of 16 (rows are read in place).
+ * M <= 8 runs the weight-streaming GEMV, larger M the GEMM kernels (tcgen05
+ * from 32 rows; 16-bit weights there use a library workspace allocated on
+ * first use).  Device-side errors: ec_device_error_take. */
+int ec_gemm_async(int wt, float *C, const void *A, const float *a_scale, const void *B,
+                  const float *b_scale, const float *bias, int M, int K, int N, void *stream);
 
 /* Device-side error of the standalone ops: synchronises `stream`, then reads
  * and clears the library's device error words into *code (0 none, 1 a

@@ -120,3 +120,58 @@ def test_lm_head_fp16_sweep(eco, cuda, M):
     rows = np.unique(np.concatenate([[0, N - 1], rng.choice(N, 300, replace=False)]))
     want = eco.gemm_fp16(X, W[rows].view(np.uint16))
     assert rel_err(y[:, rows], want) < TOL_FP32_ACC
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 5, 8])
+@pytest.mark.parametrize("K", [160, 896, 4864])
+def test_gemm_async_device(eco, cuda, M, K):
+    """ec_gemm_async (device operands, no host sync) over the weight-streaming
+    GEMV shapes: int8 bit-exact with the restatement, fp16 / bf16 within the
+    fp32-accumulate bar; N = 1001 leaves a ragged last row group."""
+    torch = cuda
+    N = 1001
+    rng = np.random.default_rng(M * 31 + K)
+    A = rng.integers(-128, 128, (M, K), dtype=np.int64).astype(np.int8)
+    asc = rng.uniform(1e-3, 2e-2, M).astype(np.float32)
+    W = rng.integers(-127, 128, (N, K), dtype=np.int64).astype(np.int8)
+    ws = rng.uniform(1e-3, 2e-2, N).astype(np.float32)
+    b = rng.standard_normal(N).astype(np.float32)
+    dev = [torch.from_numpy(t).cuda() for t in (A, asc, W, ws, b)]
+    out = torch.full((M, N), float("nan"), device="cuda")
+    ec.gemm_async(0, out, dev[0], dev[1], dev[2], dev[3], dev[4])
+    assert ec.device_error_take() == 0
+    assert np.array_equal(bits(out.cpu().numpy()), bits(eco.gemm_int8(A, asc, W, ws, b)))
+    X = rng.standard_normal((M, K), dtype=np.float32)
+    W16 = (rng.standard_normal((N, K), dtype=np.float32) * 0.05).astype(np.float16)
+    o16 = torch.full((M, N), float("nan"), device="cuda")
+    ec.gemm_async(1, o16, torch.from_numpy(X).cuda(), None, torch.from_numpy(W16.view(np.int16)).cuda())
+    assert ec.device_error_take() == 0
+    assert rel_err(o16.cpu().numpy(), eco.gemm_fp16(X, W16.view(np.uint16))) < TOL_FP32_ACC
+    Wb = (rng.standard_normal((N, K), dtype=np.float32) * 0.05).view(np.uint32) >> 16
+    Wb = Wb.astype(np.uint16)
+    ob = torch.full((M, N), float("nan"), device="cuda")
+    ec.gemm_async(2, ob, torch.from_numpy(X).cuda(), None, torch.from_numpy(Wb.view(np.int16)).cuda())
+    assert ec.device_error_take() == 0
+    assert rel_err(ob.cpu().numpy(), eco.gemm_bf16(X, Wb)) < TOL_FP32_ACC
+
+
+@pytest.mark.parametrize("M", [1, 4])
+def test_gemv_row_result_independent_of_position(eco, cuda, M):
+    """A row's fp16 dot is the same bits whichever warp, group slot or launch
+    computes it: shifting the rows by one (a different slot of every row
+    group) or restricting them to a shard leaves every output bit unchanged."""
+    torch = cuda
+    N, K = 4099, 896
+    rng = np.random.default_rng(5 + M)
+    X = torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32)).cuda()
+    W = torch.from_numpy((rng.standard_normal((N, K), dtype=np.float32) * 0.05).astype(np.float16).view(np.int16)).cuda()
+    full = torch.empty((M, N), device="cuda")
+    ec.gemm_async(1, full, X, None, W)
+    shifted = torch.empty((M, N - 1), device="cuda")
+    ec.gemm_async(1, shifted, X, None, W[1:].contiguous())
+    shard = torch.empty((M, 1000), device="cuda")
+    ec.gemm_async(1, shard, X, None, W[2000:3000].contiguous())
+    assert ec.device_error_take() == 0
+    f = full.cpu().numpy()
+    assert np.array_equal(bits(f[:, 1:]), bits(shifted.cpu().numpy()))
+    assert np.array_equal(bits(f[:, 2000:3000]), bits(shard.cpu().numpy()))
