@@ -862,8 +862,21 @@ __device__ __noinline__ void mk_lm(const ec_mk_params &p, int ct) {
     const bool my_lane = (lane & (D - 1)) == 0 && my_q < nM;
     float bv = -INFINITY;   // running argmax of token my_q
     int bi = 0x7fffffff;
+    // L2 prefetch of the row group a warp loads LMPF iterations later: more
+    // bytes in flight than the registers of the loads hold
+    constexpr int LMPF = 2;
+    auto prefetch_group = [&](int gp) {
+        if (gp >= groups) return;
+        const int rows = min(R, rg.r1 - (rg.r0 + gp * R));
+        const unsigned char *base = W + (size_t)(rg.r0 + gp * R) * row_bytes;
+        const size_t bytes = (size_t)rows * row_bytes;
+        for (size_t o = (size_t)lane * 128; o < bytes; o += 32 * 128)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(base + o));
+    };
+    for (int i = 1; i < LMPF; ++i) prefetch_group(cw + i * NCW);
     for (int g = cw; g < groups; g += NCW) {
         if (S.flag[0]) break;
+        prefetch_group(g + LMPF * NCW);
         const int n0 = rg.r0 + g * R;
         float acc[V];
 #pragma unroll
