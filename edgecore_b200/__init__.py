@@ -47,6 +47,11 @@ def _declare(lib: C.CDLL) -> None:
         "ec_decode_profile": (_i, [_vp, _vp, _i, _i, _vp]),
         "ec_decode_greedy_cycle": (_i, [_vp, _vp, _i, _i, _i, _vp]),
         "ec_decode_trace": (_i, [_vp, _vp, _i, _i, _vp, _i]),
+        "ec_decode_batch": (_i, [_vp, _vp, _vp, _i, _vp]),
+        "ec_batch_hidden": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
+        "ec_lm_shard_keys": (_i, [_vp, _vp, _i, _vp]),
+        "ec_keys_advance": (_i, [_vp, _vp, _i, _vp, _vp]),
+        "ec_batch_graph_kernels": (_i, [_vp, _i]),
         "ec_model_set_taps": (_i, [_vp, _i]),
         "ec_model_get_taps": (_i, [_vp, _vp, _i]),
         "ec_model_set_vocab_shard": (_i, [_vp, _i, _i]),
@@ -299,6 +304,36 @@ class Model:
     def decode_greedy_cycle(self, d_tokens, start_pos: int, period: int, n_steps: int, d_out_ids=None) -> None:
         self._check(self.lib.ec_decode_greedy_cycle(self.h, _ptr(d_tokens), int(start_pos), int(period),
                                                     int(n_steps), _ptr(d_out_ids)))
+
+    def decode_batch(self, d_tokens, d_positions, n_steps: int, d_out_ids=None) -> None:
+        """Greedy decode of n_steps tokens for all batch_cap slots (device
+        int32 tokens / positions [batch_cap], updated in place; ids into
+        d_out_ids [n_steps][batch_cap] when given), one captured CUDA graph
+        per step on the model stream."""
+        self._check(self.lib.ec_decode_batch(self.h, _ptr(d_tokens), _ptr(d_positions), int(n_steps),
+                                             _ptr(d_out_ids)))
+
+    def batch_hidden(self, d_tokens, d_positions, M: int, max_pos_end: int, d_hidden) -> None:
+        """Rows m < M (slot m) through every layer and the final norm into
+        d_hidden [M][n_embd] fp32 (device); every position < max_pos_end."""
+        self._check(self.lib.ec_batch_hidden(self.h, _ptr(d_tokens), _ptr(d_positions), int(M), int(max_pos_end),
+                                             _ptr(d_hidden)))
+
+    def lm_shard_keys(self, d_hidden, rows: int, d_keys) -> None:
+        """lm_head of the vocab shard over `rows` hidden rows, per-row argmax
+        as signed int64 keys (signed max across shards = the global greedy id)."""
+        self._check(self.lib.ec_lm_shard_keys(self.h, _ptr(d_hidden), int(rows), _ptr(d_keys)))
+
+    def keys_advance(self, d_keys, M: int, d_tokens, d_positions) -> None:
+        """tokens[m] = index in keys[m], positions[m] += 1 (device arrays)."""
+        self._check(self.lib.ec_keys_advance(self.h, _ptr(d_keys), int(M), _ptr(d_tokens), _ptr(d_positions)))
+
+    def batch_graph_kernels(self, kind: int) -> int:
+        """Kernel launches in the captured step graph (0: decode_batch, 1: batch_hidden)."""
+        n = self.lib.ec_batch_graph_kernels(self.h, int(kind))
+        if n < 0:
+            raise RuntimeError(last_error())
+        return n
 
     TRACE_CODES = {1: "barrier", 2: "operand", 3: "tiles", 4: "attention", 5: "lm_head", 6: "argmax",
                    7: "tile_in", 8: "tile_free", 9: "tile_done", 10: "issue", 11: "staged", 12: "stats",

@@ -255,6 +255,12 @@ typedef struct ec_dev {
     float *h_max;
     float *h_logits;
     size_t h_logits_cap;
+    /* batched decode: one captured CUDA graph per step shape (0: full greedy
+     * step, 1: hidden rows only); ws_gen counts workspace reallocations and
+     * vocab-shard changes, which invalidate the graphs */
+    struct { cudaGraphExec_t exec; int M, maxlen, chunk, hist, kernels; unsigned gen; } bg[2];
+    unsigned ws_gen;
+    int *d_counter;
     /* taps */
     int taps_on;
     float *taps;
@@ -301,6 +307,8 @@ static void ec_unregister(GPT2 *g)
 }
 
 static int round16(int k) { return (k + 15) & ~15; }
+
+#define EC_MAX_TENSORS 4096   /* tensor entries of one .ecm file */
 
 /* ---- uploads ---- */
 
@@ -589,6 +597,7 @@ static int ec_ensure(ec_dev *d, int M)
     CK(cudaMallocHost((void **)&d->h_ids, (size_t)cap * 4));
     CK(cudaMallocHost((void **)&d->h_max, (size_t)cap * 4));
     d->cap = cap;
+    d->ws_gen++;
     return 0;
 }
 
@@ -620,6 +629,7 @@ static int ec_ensure_attn(ec_dev *d, int M, int maxlen)
     d->attn_part = NULL;
     CK(cudaMalloc((void **)&d->attn_part, need * 4));
     d->attn_part_floats = need;
+    d->ws_gen++;
     return 0;
 }
 
@@ -631,6 +641,7 @@ static int ec_ensure_logits(ec_dev *d, int rows)
     d->logits = NULL;
     CK(cudaMalloc((void **)&d->logits, (size_t)rows * (d->v1 - d->v0) * 4));
     d->logit_rows = rows;
+    d->ws_gen++;
     return 0;
 }
 
@@ -644,6 +655,7 @@ static int ec_ensure_amax(ec_dev *d, int M)
     d->amax_part = NULL;
     CK(cudaMalloc(&d->amax_part, (size_t)rows * chunks * 8));
     d->amax_chunks = chunks;
+    d->ws_gen++;
     return 0;
 }
 
@@ -669,7 +681,9 @@ static void ec_dev_free(ec_dev *d)
     cudaFree(d->d_mk_layers); cudaFree(d->d_bar); cudaFree(d->d_mk_err);
     cudaFree(d->amax_v); cudaFree(d->amax_i);
     cudaFree(d->attn_part); cudaFree(d->logits); cudaFree(d->amax_part);
-    cudaFree(d->d_hist); cudaFree(d->taps);
+    cudaFree(d->d_hist); cudaFree(d->taps); cudaFree(d->d_counter);
+    for (int k = 0; k < 2; k++)
+        if (d->bg[k].exec) cudaGraphExecDestroy(d->bg[k].exec);
     cudaFreeHost(d->h_logits);
     if (d->prof_ready)
         for (int i = 0; i < 2 * EC_PROF_MAX; i++) cudaEventDestroy(d->prof_ev[i]);
@@ -685,6 +699,7 @@ static int ec_set_lm_shard(ec_dev *d, int v0, int v1)
     d->logit_rows = 0;
     cudaFree(d->logits);
     d->logits = NULL;
+    d->ws_gen++;
     return 0;
 }
 
@@ -839,8 +854,12 @@ static int ec_load_host(GPT2 *g, const char *path, int batch_cap, int max_ctx)
     g->file_size = (size_t)st.st_size;
     g->file_mapped = 1;
 
-    EcmTensor *t = calloc(512, sizeof *t);
-    const int n = ecm_parse(g->file_data, g->file_size, t, 512, g);
+    /* The reference's table holds 512 entries (src/gpt2.c:180-181), too few
+     * for a 28-layer Qwen2 with q/k/v biases (534 tensors, BASELINE config
+     * 4's Qwen2.5-1.5B); this loader's holds EC_MAX_TENSORS. */
+    EcmTensor *t = calloc(EC_MAX_TENSORS, sizeof *t);
+    if (!t) { ec_seterr("out of host memory"); return -1; }
+    const int n = ecm_parse(g->file_data, g->file_size, t, EC_MAX_TENSORS, g);
     if (n < 0) return ec_load_fail(t, "ecm: parse failed%s", "");
     const char *base = g->file_data;
     for (int i = 0; i < n; i++)
@@ -1447,6 +1466,7 @@ EC_EXPORT int ec_decode_greedy_cycle(GPT2 *g, int *d_tokens, int start_pos, int 
         CK(cudaStreamSynchronize(d->stream));
         cudaFree(d->d_hist);
         d->d_hist = NULL;
+        d->ws_gen++;
         CK(cudaMalloc((void **)&d->d_hist, (size_t)n_steps * M * 4));
         d->hist_cap = n_steps * M;
     }
@@ -1467,6 +1487,208 @@ EC_EXPORT int ec_decode_greedy(GPT2 *g, int *d_tokens, int start_pos, int n_step
     return ec_decode_greedy_cycle(g, d_tokens, start_pos, 0, n_steps, d_out_ids);
 }
 
+/* ------------------------------------------------------------------ */
+/* batched decode: any number of token rows, per-layer kernels           */
+/* ------------------------------------------------------------------ */
+
+/* Rows of lm_head logits computed per chunk (<= 512 MB of logits). */
+static int ec_lm_chunk(const ec_dev *d, int M)
+{
+    const int Vs = d->v1 - d->v0;
+    int chunk = (int)((512u << 20) / ((size_t)Vs * 4));
+    if (chunk < EC_TC_MIN_M) chunk = EC_TC_MIN_M;
+    return chunk < M ? chunk : M;
+}
+
+/* lm_head of the vocab shard over rows [0, M) of d->h and the row argmax
+ * into d_ids / d_max (global vocab ids), chunk rows at a time. */
+static int ec_enqueue_lm_argmax(ec_dev *d, int M, int chunk)
+{
+    const int Vs = d->v1 - d->v0;
+    for (int r0 = 0; r0 < M; r0 += chunk) {
+        const int rows = M - r0 < chunk ? M - r0 : chunk;
+        if (ec_enqueue_lm(d, r0, rows)) return -1;
+        CK(ec_launch_argmax(d->d_ids + r0, d->d_max + r0, d->logits, Vs, Vs, rows, d->v0, d->amax_part,
+                            d->amax_chunks, d->stream));
+    }
+    return 0;
+}
+
+/* Workspaces of a batched call of M rows (slot m = row m) attending at most
+ * maxlen positions, with lm_head chunks of `chunk` rows; kernel set-up done
+ * here so that nothing allocates or sets attributes during graph capture. */
+static int ec_batch_prepare(ec_dev *d, int M, int maxlen, int chunk)
+{
+    if (ec_ensure(d, M) || ec_ensure_attn(d, M, maxlen)) return -1;
+    if (chunk > 0 && (ec_ensure_logits(d, chunk) || ec_ensure_amax(d, chunk))) return -1;
+    if (!d->d_counter) CK(cudaMalloc((void **)&d->d_counter, 16));
+    const int tc = ec_tc_init();
+    if (tc && tc != (int)cudaErrorNotSupported) { ec_seterr("tensor-core set-up failed: %s", cudaGetErrorString((cudaError_t)tc)); return -1; }
+    cudaGetLastError();
+    CK(cudaStreamSynchronize(d->stream));   /* h_in reuse */
+    for (int m = 0; m < M; m++) d->h_in[2 * M + m] = m;
+    CK(cudaMemcpyAsync(d->d_slot, d->h_in + 2 * M, (size_t)M * 4, cudaMemcpyHostToDevice, d->stream));
+    return 0;
+}
+
+/* The captured graph of kind k (0: body + lm_head argmax + token/position
+ * advance; 1: body only, normed rows left in d->h), rebuilt when the shape or
+ * a workspace changed. */
+static int ec_bgraph(ec_dev *d, int kind, int M, int maxlen, int chunk, int hist, cudaGraphExec_t *out)
+{
+    if (d->bg[kind].exec && d->bg[kind].M == M && d->bg[kind].maxlen == maxlen && d->bg[kind].chunk == chunk &&
+        d->bg[kind].hist == hist && d->bg[kind].gen == d->ws_gen) {
+        *out = d->bg[kind].exec;
+        return 0;
+    }
+    if (d->bg[kind].exec) {
+        cudaGraphExecDestroy(d->bg[kind].exec);
+        d->bg[kind].exec = NULL;
+    }
+    cudaGraph_t gr = NULL;
+    CK(cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = 0;
+    rc = ec_enqueue_body(d, M, maxlen);
+    if (!rc && kind == 0) rc = ec_enqueue_lm_argmax(d, M, chunk);
+    if (!rc && kind == 0 &&
+        ec_launch_step_advance(d->d_tok, d->d_pos, d->d_ids, M, hist ? d->d_hist : NULL, hist ? d->d_counter : NULL,
+                               0, 0, d->stream))
+        rc = -1;
+    const cudaError_t ee = cudaStreamEndCapture(d->stream, &gr);
+    if (rc || ee != cudaSuccess) {
+        if (gr) cudaGraphDestroy(gr);
+        cudaGetLastError();
+        if (!rc) ec_seterr("stream capture failed: %s", cudaGetErrorString(ee));
+        return -1;
+    }
+    size_t nn = 0;
+    int nk = 0;
+    if (cudaGraphGetNodes(gr, NULL, &nn) == cudaSuccess && nn > 0) {
+        cudaGraphNode_t *nodes = malloc(nn * sizeof *nodes);
+        if (nodes && cudaGraphGetNodes(gr, nodes, &nn) == cudaSuccess)
+            for (size_t i = 0; i < nn; i++) {
+                enum cudaGraphNodeType ty;
+                if (cudaGraphNodeGetType(nodes[i], &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) nk++;
+            }
+        free(nodes);
+    }
+    const cudaError_t ei = cudaGraphInstantiate(&d->bg[kind].exec, gr, 0);
+    cudaGraphDestroy(gr);
+    if (ei != cudaSuccess) {
+        d->bg[kind].exec = NULL;
+        ec_seterr("cudaGraphInstantiate: %s", cudaGetErrorString(ei));
+        return -1;
+    }
+    d->bg[kind].M = M;
+    d->bg[kind].maxlen = maxlen;
+    d->bg[kind].chunk = chunk;
+    d->bg[kind].hist = hist;
+    d->bg[kind].gen = d->ws_gen;
+    d->bg[kind].kernels = nk;
+    *out = d->bg[kind].exec;
+    return 0;
+}
+
+/* Attended-length bucket for rows whose positions are < max_pos_end. */
+static int ec_batch_len(const ec_dev *d, int max_pos_end)
+{
+    int len = max_pos_end;
+    if (d->window > 0 && len > d->window) len = d->window;
+    return ec_len_bucket(d, len);
+}
+
+EC_EXPORT int ec_decode_batch(GPT2 *g, int *d_tokens, int *d_positions, int n_steps, int *d_out_ids)
+{
+    ec_dev *d = ec_lookup(g);
+    if (!d) { ec_seterr("model not loaded"); return -1; }
+    if (n_steps < 0) { ec_seterr("n_steps must be >= 0"); return -1; }
+    if (n_steps == 0) return 0;
+    const int M = d->B;
+    if (ec_ensure(d, M)) return -1;
+    CK(cudaStreamSynchronize(d->stream));
+    CK(cudaMemcpy(d->h_in + M, d_positions, (size_t)M * 4, cudaMemcpyDeviceToHost));
+    int maxp = 0;
+    for (int m = 0; m < M; m++) {
+        const int p = d->h_in[M + m];
+        if (p < 0 || p + n_steps > d->C) {
+            ec_seterr("slot %d: positions [%d, %d) exceed eff_ctx %d", m, p, p + n_steps, d->C);
+            return -1;
+        }
+        if (p + n_steps > maxp) maxp = p + n_steps;
+    }
+    const int maxlen = ec_batch_len(d, maxp);
+    const int chunk = ec_lm_chunk(d, M);
+    if (d_out_ids && d->hist_cap < n_steps * M) {
+        cudaFree(d->d_hist);
+        d->d_hist = NULL;
+        CK(cudaMalloc((void **)&d->d_hist, (size_t)n_steps * M * 4));
+        d->hist_cap = n_steps * M;
+        d->ws_gen++;
+    }
+    if (ec_batch_prepare(d, M, maxlen, chunk)) return -1;
+    CK(cudaMemcpyAsync(d->d_tok, d_tokens, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
+    CK(cudaMemcpyAsync(d->d_pos, d_positions, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
+    if (d_out_ids) CK(cudaMemsetAsync(d->d_counter, 0, 4, d->stream));
+    cudaGraphExec_t ex;
+    if (ec_bgraph(d, 0, M, maxlen, chunk, d_out_ids != NULL, &ex)) return -1;
+    for (int s = 0; s < n_steps; s++) CK(cudaGraphLaunch(ex, d->stream));
+    CK(cudaMemcpyAsync(d_tokens, d->d_tok, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
+    CK(cudaMemcpyAsync(d_positions, d->d_pos, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
+    if (d_out_ids)
+        CK(cudaMemcpyAsync(d_out_ids, d->d_hist, (size_t)n_steps * M * 4, cudaMemcpyDeviceToDevice, d->stream));
+    return 0;
+}
+
+EC_EXPORT int ec_batch_hidden(GPT2 *g, const int *d_tokens, const int *d_positions, int M, int max_pos_end,
+                              float *d_hidden)
+{
+    ec_dev *d = ec_lookup(g);
+    if (!d) { ec_seterr("model not loaded"); return -1; }
+    if (M < 1 || M > d->B) { ec_seterr("ec_batch_hidden: 1 <= M <= batch_cap (%d), got %d", d->B, M); return -1; }
+    if (max_pos_end < 1 || max_pos_end > d->C) { ec_seterr("ec_batch_hidden: max_pos_end %d outside [1, %d]", max_pos_end, d->C); return -1; }
+    const int maxlen = ec_batch_len(d, max_pos_end);
+    if (ec_batch_prepare(d, M, maxlen, 0)) return -1;
+    CK(cudaMemcpyAsync(d->d_tok, d_tokens, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
+    CK(cudaMemcpyAsync(d->d_pos, d_positions, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
+    cudaGraphExec_t ex;
+    if (ec_bgraph(d, 1, M, maxlen, 0, 0, &ex)) return -1;
+    CK(cudaGraphLaunch(ex, d->stream));
+    CK(cudaMemcpyAsync(d_hidden, d->h, (size_t)M * d->E * 4, cudaMemcpyDeviceToDevice, d->stream));
+    return 0;
+}
+
+EC_EXPORT int ec_lm_shard_keys(GPT2 *g, const float *d_hidden, int rows, long long *d_keys)
+{
+    ec_dev *d = ec_lookup(g);
+    if (!d) { ec_seterr("model not loaded"); return -1; }
+    if (rows < 1) { ec_seterr("ec_lm_shard_keys: rows must be >= 1"); return -1; }
+    const int chunk = ec_lm_chunk(d, rows);
+    if (ec_ensure(d, rows) || ec_ensure_logits(d, chunk) || ec_ensure_amax(d, chunk)) return -1;
+    const int tc = ec_tc_init();
+    if (tc && tc != (int)cudaErrorNotSupported) { ec_seterr("tensor-core set-up failed"); return -1; }
+    cudaGetLastError();
+    CK(cudaMemcpyAsync(d->h, d_hidden, (size_t)rows * d->E * 4, cudaMemcpyDeviceToDevice, d->stream));
+    if (ec_enqueue_lm_argmax(d, rows, chunk)) return -1;
+    CK(ec_launch_pack_keys(d->d_ids, d->d_max, rows, d_keys, d->stream));
+    return 0;
+}
+
+EC_EXPORT int ec_batch_graph_kernels(GPT2 *g, int kind)
+{
+    ec_dev *d = ec_lookup(g);
+    if (!d || kind < 0 || kind > 1) { ec_seterr("ec_batch_graph_kernels: no model or bad kind"); return -1; }
+    return d->bg[kind].exec ? d->bg[kind].kernels : 0;
+}
+
+EC_EXPORT int ec_keys_advance(GPT2 *g, const long long *d_keys, int M, int *d_tokens, int *d_positions)
+{
+    ec_dev *d = ec_lookup(g);
+    if (!d) { ec_seterr("model not loaded"); return -1; }
+    if (M < 1) { ec_seterr("ec_keys_advance: M must be >= 1"); return -1; }
+    CK(ec_launch_keys_advance(d_keys, M, d_tokens, d_positions, NULL, d->stream));
+    return 0;
+}
+
 /* Instrumented decode: each step is one launch of the persistent kernel with
  * an event pair around it (class 0), so out[0..2] = {ms, algorithmic bytes,
  * launches} of that kernel.  Models the kernel cannot take fall back to the
@@ -1476,7 +1698,7 @@ EC_EXPORT int ec_decode_profile(GPT2 *g, int *d_tokens, int start_pos, int n_ste
     ec_dev *d = ec_lookup(g);
     if (!d) { ec_seterr("model not loaded"); return -1; }
     const int M = d->B;
-    if (M > EC_MK_MT || n_steps < 1 || start_pos < 0 || start_pos + n_steps > d->C) { ec_seterr("bad profile range"); return -1; }
+    if (n_steps < 1 || start_pos < 0 || start_pos + n_steps > d->C) { ec_seterr("bad profile range"); return -1; }
     if (!d->prof_ready) {
         for (int i = 0; i < 2 * EC_PROF_MAX; i++) CK(cudaEventCreate(&d->prof_ev[i]));
         d->prof_ready = 1;
@@ -1500,17 +1722,24 @@ EC_EXPORT int ec_decode_profile(GPT2 *g, int *d_tokens, int start_pos, int n_ste
             out[EC_PC_STEP * 3 + 2] += 1.0;
         }
     } else {
-        if (ec_decode_setup(d, d_tokens, start_pos, M) || ec_ensure_logits(d, 8) || ec_ensure_amax(d, 8) ||
+        const int chunk = ec_lm_chunk(d, M);
+        if (ec_decode_setup(d, d_tokens, start_pos, M) || ec_ensure_logits(d, chunk) || ec_ensure_amax(d, chunk) ||
             ec_ensure_attn(d, M, maxlen)) return -1;
         for (int st = 0; st < n_steps; st++) {
             d->prof_on = 1;
             d->prof_n = 0;
-            int rc = ec_enqueue_body(d, M, maxlen) || ec_enqueue_lm(d, 0, M);
+            int rc = ec_enqueue_body(d, M, maxlen);
+            for (int r0 = 0; !rc && r0 < M; r0 += chunk) {   /* lm_head (GEMM class) + argmax (other) */
+                const int rows = M - r0 < chunk ? M - r0 : chunk;
+                rc = ec_enqueue_lm(d, r0, rows);
+                const int pa = ec_prof_begin(d, EC_PC_OTHER, 0.0);
+                if (!rc && ec_launch_argmax(d->d_ids + r0, d->d_max + r0, d->logits, d->v1 - d->v0, d->v1 - d->v0,
+                                            rows, d->v0, d->amax_part, d->amax_chunks, d->stream))
+                    rc = -1;
+                ec_prof_end(d, pa);
+            }
             int pi = ec_prof_begin(d, EC_PC_OTHER, 0.0);
-            if (!rc && (ec_launch_argmax(d->d_ids, d->d_max, d->logits, d->v1 - d->v0, d->v1 - d->v0, M, d->v0,
-                                         d->amax_part, d->amax_chunks, d->stream) ||
-                        ec_launch_step_advance(d->d_tok, d->d_pos, d->d_ids, M, NULL, NULL, 0, 0, d->stream)))
-                rc = -1;
+            if (!rc && ec_launch_step_advance(d->d_tok, d->d_pos, d->d_ids, M, NULL, NULL, 0, 0, d->stream)) rc = -1;
             ec_prof_end(d, pi);
             d->prof_on = 0;
             if (rc) return -1;

@@ -969,6 +969,47 @@ extern "C" int ec_launch_step_advance(int *tok, int *pos, const int *ids, int M,
     return (int)cudaGetLastError();
 }
 
+// Signed 64-bit argmax keys: the order-preserving bits of the max logit
+// (-0 as +0, NaN below every number) above (0x7fffffff - index), top bit
+// flipped, so that the signed max over vocab shards is "larger logit, then
+// lower index" -- the reference's greedy tie rule (src/runtime_main.c:213-219).
+// Same encoding as ec_argmax_key (ec_host.c) with the sign bit flipped.
+__device__ __forceinline__ long long argmax_key(float v, int idx) {
+    if (v == 0.0f) v = 0.0f;
+    uint32_t b = __float_as_uint(v);
+    if (v != v) b = 0u;
+    else b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    const unsigned long long k = ((unsigned long long)b << 32) | (uint32_t)(0x7fffffff - idx);
+    return (long long)(k ^ 0x8000000000000000ull);
+}
+
+__global__ void k_pack_keys(const int *ids, const float *maxv, int M, long long *keys) {
+    const int m = blockIdx.x * blockDim.x + threadIdx.x;
+    if (m < M) keys[m] = argmax_key(maxv[m], ids[m]);
+}
+
+extern "C" int ec_launch_pack_keys(const int *ids, const float *maxv, int M, long long *keys, cudaStream_t stream) {
+    k_pack_keys<<<(M + 255) / 256, 256, 0, stream>>>(ids, maxv, M, keys);
+    return (int)cudaGetLastError();
+}
+
+// tok[m] = the index in keys[m], pos[m] += 1; optionally ids[m] = the index.
+__global__ void k_keys_advance(const long long *keys, int M, int *tok, int *pos, int *ids) {
+    const int m = blockIdx.x * blockDim.x + threadIdx.x;
+    if (m >= M) return;
+    const unsigned long long k = (unsigned long long)keys[m] ^ 0x8000000000000000ull;
+    const int id = 0x7fffffff - (int)(uint32_t)(k & 0xffffffffu);
+    tok[m] = id;
+    if (pos) pos[m] += 1;
+    if (ids) ids[m] = id;
+}
+
+extern "C" int ec_launch_keys_advance(const long long *keys, int M, int *tok, int *pos, int *ids,
+                                      cudaStream_t stream) {
+    k_keys_advance<<<(M + 255) / 256, 256, 0, stream>>>(keys, M, tok, pos, ids);
+    return (int)cudaGetLastError();
+}
+
 extern "C" int ec_kernel_error_take(cudaStream_t stream, int *code) {
     int zero = 0;
     cudaError_t e = cudaMemcpyFromSymbolAsync(code, g_ec_err, sizeof(int), 0, cudaMemcpyDeviceToHost, stream);

@@ -167,6 +167,14 @@ int ec_launch_argmax(int *ids, float *maxv, const float *logits, int ld, int N, 
 int ec_launch_step_advance(int *tok, int *pos, const int *ids, int M, int *hist, int *counter,
                            int wrap_lo, int wrap_hi, cudaStream_t stream);
 
+/* keys[m] = signed 64-bit argmax key of (maxv[m], ids[m]): larger logit,
+ * then lower index, wins a signed max (see ec_argmax_key). */
+int ec_launch_pack_keys(const int *ids, const float *maxv, int M, long long *keys, cudaStream_t stream);
+
+/* tok[m] = index of keys[m]; pos[m] += 1 (pos may be NULL); ids[m] = index
+ * (ids may be NULL). */
+int ec_launch_keys_advance(const long long *keys, int M, int *tok, int *pos, int *ids, cudaStream_t stream);
+
 /* The library-wide device error word (bounded waits that gave up, bad
  * indices skipped).  Read and cleared by ec_kernel_error_take. */
 int ec_kernel_error_take(cudaStream_t stream, int *code);

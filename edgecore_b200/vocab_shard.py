@@ -20,7 +20,7 @@ from __future__ import annotations
 
 import numpy as np
 
-__all__ = ["shard_range", "pack_keys", "unpack_keys", "combine_argmax", "ShardedGreedy"]
+__all__ = ["shard_range", "pack_keys", "unpack_keys", "combine_argmax", "ShardedGreedy", "ShardedBatchDecoder"]
 
 _SIGN = np.uint64(1 << 63)
 
@@ -97,3 +97,57 @@ class ShardedGreedy:
         ids, maxv = self.model.forward_argmax(tokens, positions, seqs, shard=True)
         _, gids = combine_argmax(maxv, ids, self.group, self.device)
         return gids
+
+
+class ShardedBatchDecoder:
+    """Batched greedy decode of many independent streams: the streams are
+    split data-parallel over the ranks of `group` (each rank runs its own
+    `m_local` slots through every layer), and the lm_head is column-split.
+
+    One step on every rank, all on the current CUDA stream:
+
+    1. ``batch_hidden``: this rank's slots through the layers and the final
+       norm (normed rows [m_local][n_embd]);
+    2. ``all_gather`` of those rows: every rank holds the rows of all
+       world * m_local streams;
+    3. ``lm_shard_keys``: this rank's vocab block of the lm_head over all the
+       rows, each row's argmax packed as a signed 64-bit key;
+    4. ``all_reduce(MAX)`` of the keys: every row's global greedy id, with the
+       reference's tie rule (src/runtime_main.c:213-219);
+    5. ``keys_advance``: this rank's slots take their ids, positions + 1.
+
+    Compared with a full lm_head per rank, every rank reads 1/world of the
+    lm_head weights, for the price of one all-gather of hidden rows and one
+    all-reduce of 8 bytes per stream.  `model` is an ``edgecore_b200.Model``
+    (or any object with those three methods, operating on torch tensors on
+    this rank's device for NCCL, or on CPU for gloo).
+    """
+
+    def __init__(self, model, rank: int, world: int, m_local: int, n_embd: int, vocab: int, group=None,
+                 device=None):
+        import torch
+        self.model, self.rank, self.world, self.m = model, rank, world, int(m_local)
+        self.group = group
+        self.v0, self.v1 = shard_range(vocab, rank, world)
+        model.set_vocab_shard(self.v0, self.v1)
+        dev = device if device is not None else "cpu"
+        self.hid = torch.empty((self.m, n_embd), dtype=torch.float32, device=dev)
+        self.hid_all = torch.empty((world * self.m, n_embd), dtype=torch.float32, device=dev)
+        self.keys = torch.empty(world * self.m, dtype=torch.int64, device=dev)
+
+    def step(self, d_tokens, d_positions, max_pos_end: int) -> None:
+        """One greedy step of this rank's slots: d_tokens / d_positions
+        (int32 [m_local]) are updated in place; every position must be below
+        max_pos_end."""
+        import torch.distributed as dist
+        m = self.model
+        m.batch_hidden(d_tokens, d_positions, self.m, int(max_pos_end), self.hid)
+        if self.world > 1:
+            dist.all_gather_into_tensor(self.hid_all, self.hid, group=self.group)
+        else:
+            self.hid_all.copy_(self.hid)
+        m.lm_shard_keys(self.hid_all, self.world * self.m, self.keys)
+        if self.world > 1:
+            dist.all_reduce(self.keys, op=dist.ReduceOp.MAX, group=self.group)
+        mine = self.keys[self.rank * self.m:(self.rank + 1) * self.m]
+        m.keys_advance(mine, self.m, d_tokens, d_positions)

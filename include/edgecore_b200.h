@@ -74,11 +74,50 @@ int ec_decode_greedy(GPT2 *g, int *d_tokens, int start_pos, int n_steps,
 int ec_decode_greedy_cycle(GPT2 *g, int *d_tokens, int start_pos, int period, int n_steps,
                            int *d_out_ids);
 
+/* ---- batched decode: any number of independent streams ------------------ */
+
+/* Device-resident greedy decode of n_steps tokens for every one of the
+ * batch_cap slots, each at its own position: DEVICE d_tokens[batch_cap] and
+ * d_positions[batch_cap] hold each slot's current token and position and are
+ * updated in place; the sampled ids go to DEVICE d_out_ids[n_steps][batch_cap]
+ * (may be NULL).  Every step runs the per-layer kernels (tcgen05 GEMMs from
+ * 32 rows, attention of each slot over its own KV rows, the lm_head and a row
+ * argmax with the lowest index on ties) captured once into a CUDA graph and
+ * replayed.  The call reads the positions once (synchronising the model
+ * stream) and returns with the steps enqueued.  Reference: the batched decode
+ * loop of src/runtime_main.c:336-352 with sample_token's greedy branch
+ * (:213-219). */
+int ec_decode_batch(GPT2 *g, int *d_tokens, int *d_positions, int n_steps, int *d_out_ids);
+
+/* The column-split lm_head across ranks, in three steps a caller interleaves
+ * with its own collectives (all on the model stream):
+ *   ec_batch_hidden  -- rows m < M (slot m, DEVICE tokens / positions, every
+ *                       position < max_pos_end) through every layer and the
+ *                       final norm; normed rows [M][n_embd] fp32 into DEVICE
+ *                       d_hidden (reference src/gpt2.c:797-798);
+ *   ec_lm_shard_keys -- the lm_head of this model's vocab shard
+ *                       (ec_model_set_vocab_shard) over `rows` DEVICE hidden
+ *                       rows, each row's argmax packed as a signed 64-bit key
+ *                       (ec_argmax_key with the top bit flipped) into DEVICE
+ *                       d_keys[rows]: the signed max over all shards is the
+ *                       reference's greedy pick (src/runtime_main.c:213-219);
+ *   ec_keys_advance  -- d_tokens[m] = the index in d_keys[m], d_positions[m]
+ *                       += 1 for m < M (DEVICE arrays). */
+int ec_batch_hidden(GPT2 *g, const int *d_tokens, const int *d_positions, int M, int max_pos_end,
+                    float *d_hidden);
+int ec_lm_shard_keys(GPT2 *g, const float *d_hidden, int rows, long long *d_keys);
+int ec_keys_advance(GPT2 *g, const long long *d_keys, int M, int *d_tokens, int *d_positions);
+
+/* Kernel launches in the last captured step graph of ec_decode_batch
+ * (kind 0) or ec_batch_hidden (kind 1); 0 if none was captured. */
+int ec_batch_graph_kernels(GPT2 *g, int kind);
+
 /* Instrumented greedy decode for measurement: n_steps steps, one kernel
  * launch per step, with a CUDA event pair around every kernel launch on the
  * model stream.  out[16]: for kernel class c in {0 persistent decode step,
- * 1 GEMM, 2 attention, 3 norms, 4 other} (classes 1-4 only when the
- * persistent kernel cannot take the model): out[3c] = total ms, out[3c+1] =
+ * 1 GEMM (activation quantisation included; the lm_head too), 2 attention,
+ * 3 norms, 4 other} (classes 1-4 when the persistent kernel cannot take the
+ * batch: batch_cap > 8 or shared memory): out[3c] = total ms, out[3c+1] =
  * total algorithmic HBM bytes, out[3c+2] = launches; out[15] = steps. */
 int ec_decode_profile(GPT2 *g, int *d_tokens, int start_pos, int n_steps, double *out16);
 

@@ -26,6 +26,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#define ECO_MAX_TENSORS 4096
+
 #define ECO_API __attribute__((visibility("default")))
 
 /* Transcendentals.  The default build calls the host libm exactly as the
@@ -331,7 +333,9 @@ ECO_API eco_model *eco_open(const char *path, int batch_cap, int max_ctx)
         else if (!strcmp(k, "tie_word_embeddings")) m->tie = atoi(v);
         else if (!strcmp(k, "arch")) m->arch = (!strcmp(v, "qwen2") || !strcmp(v, "olmo3")) ? ARCH_QWEN2 : ARCH_GPT2;
     }
-    eco_t *t = calloc(512, sizeof *t);
+    /* 512 entries in the reference (src/gpt2.c:180-181); more here so that the
+     * 28-layer config-4 model (534 tensors) can serve as a CPU baseline */
+    eco_t *t = calloc(ECO_MAX_TENSORS, sizeof *t);
     int nt = 0;
     while (1) {
         if (eco_line(&p, end, ln, sizeof ln)) { free(t); eco_close(m); return NULL; }
@@ -362,7 +366,7 @@ ECO_API eco_model *eco_open(const char *path, int batch_cap, int max_ctx)
         snprintf(t[nt].name, sizeof t[nt].name, "%s", name);
         t[nt].dt = dt;
         t[nt].bytes = ne * eco_dsize(dt);
-        if (++nt >= 512) { free(t); eco_close(m); return NULL; }
+        if (++nt >= ECO_MAX_TENSORS) { free(t); eco_close(m); return NULL; }
     }
     size_t off = (size_t)(p - m->file);
     for (int i = 0; i < nt; i++) { t[i].off = off; off += t[i].bytes; }

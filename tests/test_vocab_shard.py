@@ -90,3 +90,72 @@ def test_combine_across_gloo_ranks(world, tmp_path):
                        start_method="spawn", join=True)
     r = [np.load(tmp_path / f"r{k}.npy") for k in range(world)]
     assert all(np.array_equal(r[0], x) for x in r)   # every rank agrees
+
+
+class _NumpyModel:
+    """Stand-in for edgecore_b200.Model on CPU tensors: 'hidden' = a fixed
+    random embedding of (token, position), lm_head = a fixed random matrix."""
+
+    def __init__(self, V, E, seed=0):
+        rng = np.random.default_rng(seed)
+        self.emb = rng.standard_normal((V, E)).astype(np.float32)
+        self.W = rng.integers(-3, 4, (V, E)).astype(np.float32)   # integer logits: many exact ties
+        self.v0, self.v1 = 0, V
+
+    def set_vocab_shard(self, v0, v1):
+        self.v0, self.v1 = v0, v1
+
+    def hidden_np(self, tok, pos):
+        return self.emb[tok] + np.float32(0.0) * pos[:, None]
+
+    def batch_hidden(self, d_tok, d_pos, M, max_pos_end, out):
+        import torch
+        assert int(d_pos.max()) < max_pos_end
+        out.copy_(torch.from_numpy(self.hidden_np(d_tok.numpy()[:M], d_pos.numpy()[:M])))
+
+    def lm_shard_keys(self, hid, rows, keys):
+        import torch
+        lg = np.rint(hid.numpy()[:rows] @ self.W[self.v0:self.v1].T).astype(np.float32)
+        mv, mi = _ref_argmax(lg)
+        keys[:rows] = torch.from_numpy(vs.pack_keys(mv, mi + self.v0))
+
+    def keys_advance(self, keys, M, d_tok, d_pos):
+        import torch
+        _, idx = vs.unpack_keys(keys.numpy()[:M])
+        d_tok[:M] = torch.from_numpy(idx.astype(np.int32))
+        d_pos[:M] += 1
+
+
+def _batch_rank_main(rank: int, world: int, port: int, out_dir: str):
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        V, E, M = 97, 6, 5
+        model = _NumpyModel(V, E)
+        dec = vs.ShardedBatchDecoder(model, rank, world, M, E, V)
+        rng = np.random.default_rng(11)
+        tok_all = rng.integers(0, V, world * M).astype(np.int32)
+        tok = torch.from_numpy(tok_all[rank * M:(rank + 1) * M].copy())
+        pos = torch.arange(M, dtype=torch.int32)
+        ref = _NumpyModel(V, E)
+        ref_tok = tok_all.copy()
+        for _ in range(4):
+            dec.step(tok, pos, int(pos.max()) + 1)
+            lg = np.rint(ref.hidden_np(ref_tok, np.zeros(len(ref_tok))) @ ref.W.T).astype(np.float32)
+            ref_tok = np.argmax(lg, axis=1).astype(np.int32)   # lowest index on ties
+            assert np.array_equal(tok.numpy(), ref_tok[rank * M:(rank + 1) * M])
+        np.save(os.path.join(out_dir, f"b{rank}.npy"), tok.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_batch_decoder_gloo(tmp_path):
+    """Two ranks, each with its own streams and half of the vocab, agree with
+    the unsharded greedy continuation of all streams."""
+    import torch.multiprocessing as mp
+    mp.start_processes(_batch_rank_main, args=(2, _free_port(), str(tmp_path)), nprocs=2,
+                       start_method="spawn", join=True)
+    assert all((tmp_path / f"b{k}.npy").exists() for k in range(2))
