@@ -237,6 +237,12 @@ EC_EXPORT int ec_gemm_async(int wt, float *C, const void *A, const float *a_scal
     return 0;
 }
 
+EC_EXPORT int ec_attention_force_split(int on)
+{
+    ec_attention_set_force_split(on);
+    return 0;
+}
+
 EC_EXPORT int ec_device_error_take(void *stream, int *code)
 {
     if (!code) { ec_set_error_text("ec_device_error_take: code must not be NULL"); return -1; }

@@ -878,10 +878,14 @@ extern "C" int ec_attention_exact_fits(int H, int KVH, int hd, int maxlen) {
     return attx_smem_bytes(G, hd, maxlen) <= (size_t)g_attx_max_smem;
 }
 
+static int g_attn_force_split = 0;
+
+extern "C" void ec_attention_set_force_split(int on) { g_attn_force_split = on != 0; }
+
 extern "C" int ec_launch_attention(const ec_attn_args *a, cudaStream_t stream) {
     if (a->M <= 0) return 0;
     if (a->geo.hd > 256 || a->geo.hd % 8 || a->nsplit < 1) return (int)cudaErrorInvalidValue;
-    if (ec_attention_exact_fits(a->H, a->KVH, a->geo.hd, a->maxlen)) {
+    if (!g_attn_force_split && ec_attention_exact_fits(a->H, a->KVH, a->geo.hd, a->maxlen)) {
         const int G = a->H / a->KVH;
         dim3 g(a->KVH, a->M);
         k_attn_exact<<<g, ATTX_THREADS, attx_smem_bytes(G, a->geo.hd, a->maxlen), stream>>>(*a);

@@ -151,6 +151,8 @@ typedef struct {
  * (token, KV head) holding all scores in shared memory) when maxlen fits,
  * else the split kernel (flash-decoding order, within 1e-6 of the reference). */
 int ec_launch_attention(const ec_attn_args *a, cudaStream_t stream);
+/* 1: every ec_launch_attention uses the split kernels (tests, measurement). */
+void ec_attention_set_force_split(int on);
 size_t ec_attention_scratch_floats(int M, int H, int hd, int nsplit);
 /* 1 if the exact-order kernel handles rows of up to maxlen positions. */
 int ec_attention_exact_fits(int H, int KVH, int hd, int maxlen);

@@ -167,6 +167,15 @@ int ec_quantize_rows(int8_t *q, float *scale, const float *x, int M, int K);
 int ec_linear_int8(float *C, const float *X, const int8_t *W,
                    const float *w_scale, const float *bias, int M, int K, int N);
 
+/* Attention of the per-layer path (prefill, batched decode; the persistent
+ * decode kernel has its own): 1 = always the split kernels (flash-decoding
+ * partial sums over position blocks, then a combine), which otherwise run
+ * only when a row's scores do not fit the exact-order kernel's shared memory
+ * (tens of thousands of positions); 0 = the default choice.  Process-wide,
+ * for tests and measurement.  The reference's order is the exact kernel's;
+ * the split kernels agree with it to rounding of the partial sums. */
+int ec_attention_force_split(int on);
+
 /* gemm_int8 (wt 0: A int8 [M][K] with a_scale[M]), gemm_fp16_fp32 (wt 1)
  * or gemm_bf16_fp32 (wt 2: A fp32 [M][K]) on DEVICE operands of the current
  * device, enqueued on `stream` with no host synchronisation: the
