@@ -71,6 +71,8 @@ def parse():
     ap.add_argument("--streams", type=int, default=1024, help="--config c4: streams over all GPUs")
     ap.add_argument("--prompt", type=int, default=128, help="--config c4: prompt tokens per stream")
     ap.add_argument("--decode", type=int, default=128, help="--config c4: timed greedy steps per stream")
+    ap.add_argument("--no-c4", action="store_true",
+                    help="default run: skip the config-4 sub-measurement (\"c4\" in the JSON line)")
     ap.add_argument("--sweep-m", type=int, default=0, help="--op-sweep: only this M")
     ap.add_argument("--sweep-n", type=int, default=0, help="--op-sweep: only this N")
     return ap.parse_args()
@@ -272,10 +274,6 @@ def ours_arm(args, rank: int, world: int, local: int) -> None:
     import edgecore_b200 as ec
 
     torch.cuda.set_device(local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
-                                device_id=torch.device("cuda", local))
     spec = synth.CONFIGS[CONFIG_KEY]
     if rank == 0:
         path = synth.ensure_model(spec)
@@ -284,7 +282,12 @@ def ours_arm(args, rank: int, world: int, local: int) -> None:
     path = synth.ensure_model(spec)
 
     max_ctx = PROMPT + PERIOD
+    # cold start as the reference CLI reports it (load_time_ms,
+    # src/runtime_main.c:651-656): gpt2_load = parse + device upload + repack
+    t_load = time.perf_counter()
     m = ec.Model(path, batch_cap=1, max_ctx=max_ctx)
+    torch.cuda.synchronize()
+    load_ms = (time.perf_counter() - t_load) * 1e3
     stream = torch.cuda.Stream()
     m.set_stream(stream.cuda_stream)
     toks = synth.prompt_ids(spec.vocab, PROMPT)
@@ -384,6 +387,8 @@ def ours_arm(args, rank: int, world: int, local: int) -> None:
     cpu = None
     if rank == 0 and world == 1:
         cpu = cpu_baseline_leg(args)
+    m.close()
+    c4 = None if args.no_c4 else c4_arm(args, rank, world, local)
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
                 "warmup": max(args.warmup, 3), "ms_per_step": ms_max / args.steps, "higher_is_better": True,
@@ -394,11 +399,9 @@ def ours_arm(args, rank: int, world: int, local: int) -> None:
                         "d2h_bytes_per_step": 4 * spec.vocab, "steps": e2e_steps,
                         "api": "gpt2_forward (host tokens/positions, host logits [1][151936])"},
                 "gpu_launches": launches,
-                "roofline": roofline, "cpu_baseline": cpu, "gemv_lm_head": gemv}
+                "roofline": roofline, "cpu_baseline": cpu, "gemv_lm_head": gemv,
+                "load_time_ms": load_ms, "c4": c4}
         print(json.dumps(line), flush=True)
-    m.close()
-    if world > 1:
-        dist.destroy_process_group()
 
 
 def cpu_baseline_leg(args) -> dict:
@@ -541,10 +544,6 @@ def c4_arm(args, rank: int, world: int, local: int) -> None:
     from edgecore_b200.vocab_shard import ShardedBatchDecoder
 
     torch.cuda.set_device(local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
-                                device_id=torch.device("cuda", local))
     if args.streams % world:
         raise SystemExit(f"--streams {args.streams} must be a multiple of the GPU count {world}")
     spec = synth.CONFIGS[C4_KEY]
@@ -557,8 +556,7 @@ def c4_arm(args, rank: int, world: int, local: int) -> None:
     e2e_steps = 4
     ctx = args.prompt + args.decode + e2e_steps + 1
     m = ec.Model(path, batch_cap=mloc, max_ctx=ctx)
-    stream = torch.cuda.current_stream()
-    m.set_stream(stream.cuda_stream)
+    stream = torch.cuda.current_stream()   # the decoder runs on its own stream and orders itself with this one
 
     # untimed prefill of this rank's streams (full lm_head): first greedy ids
     g0 = rank * mloc
@@ -651,6 +649,7 @@ def c4_arm(args, rank: int, world: int, local: int) -> None:
     if rank == 0 and world == 1:
         tps, kind, sample = c4_reference_decode(args, host_cores())
         cpu = {"value": tps, "unit": "tok/s", "cores": host_cores(), "kind": kind, "sample": sample}
+    line = None
     if rank == 0:
         line = {"metric": C4_METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.decode,
                 "warmup": max(args.warmup, 3), "ms_per_step": ms / args.decode, "higher_is_better": True,
@@ -662,11 +661,9 @@ def c4_arm(args, rank: int, world: int, local: int) -> None:
                         "api": f"gpt2_forward per rank ({mloc} host token/position/slot rows, host logits "
                                f"[{mloc}][{spec.vocab}])"},
                 "gpu_launches": launches, "roofline": roofline, "cpu_baseline": cpu}
-        print(json.dumps(line), flush=True)
     del dec
     m.close()
-    if world > 1:
-        dist.destroy_process_group()
+    return line
 
 
 def op_sweep(args) -> None:
@@ -749,15 +746,29 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
-    if args.config == "c4":
-        if args.impl == "reference":
+    if args.impl == "reference":
+        if args.config == "c4":
             c4_reference_arm(args, rank, world)
         else:
-            c4_arm(args, rank, world, local)
-    elif args.impl == "reference":
-        reference_arm(args, rank, world)
-    else:
-        ours_arm(args, rank, world, local)
+            reference_arm(args, rank, world)
+        return
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
+                                device_id=torch.device("cuda", local))
+    try:
+        if args.config == "c4":
+            line = c4_arm(args, rank, world, local)
+            if rank == 0:
+                print(json.dumps(line), flush=True)
+        else:
+            ours_arm(args, rank, world, local)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
 
 
 if __name__ == "__main__":

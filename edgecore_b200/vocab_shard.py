@@ -121,6 +121,13 @@ class ShardedBatchDecoder:
     all-reduce of 8 bytes per stream.  `model` is an ``edgecore_b200.Model``
     (or any object with those three methods, operating on torch tensors on
     this rank's device for NCCL, or on CPU for gloo).
+
+    On a CUDA device the step runs on a stream of its own, to which the model
+    is bound: the library's kernels, the torch copies and the collectives are
+    then ordered on one stream (torch's default stream has the handle 0,
+    which the library reads as "the model's own stream", so binding the
+    model to it would not order anything).  The step waits for the caller's
+    current stream on entry and makes it wait on exit.
     """
 
     def __init__(self, model, rank: int, world: int, m_local: int, n_embd: int, vocab: int, group=None,
@@ -131,6 +138,10 @@ class ShardedBatchDecoder:
         self.v0, self.v1 = shard_range(vocab, rank, world)
         model.set_vocab_shard(self.v0, self.v1)
         dev = device if device is not None else "cpu"
+        self.cuda = torch.device(dev).type == "cuda"
+        self.stream = torch.cuda.Stream(device=dev) if self.cuda else None
+        if self.cuda:
+            model.set_stream(self.stream.cuda_stream)
         self.hid = torch.empty((self.m, n_embd), dtype=torch.float32, device=dev)
         self.hid_all = torch.empty((world * self.m, n_embd), dtype=torch.float32, device=dev)
         self.keys = torch.empty(world * self.m, dtype=torch.int64, device=dev)
@@ -139,15 +150,27 @@ class ShardedBatchDecoder:
         """One greedy step of this rank's slots: d_tokens / d_positions
         (int32 [m_local]) are updated in place; every position must be below
         max_pos_end."""
+        import contextlib
+
+        import torch
         import torch.distributed as dist
         m = self.model
-        m.batch_hidden(d_tokens, d_positions, self.m, int(max_pos_end), self.hid)
-        if self.world > 1:
-            dist.all_gather_into_tensor(self.hid_all, self.hid, group=self.group)
+        if self.cuda:
+            caller = torch.cuda.current_stream()
+            self.stream.wait_stream(caller)
+            ctx = torch.cuda.stream(self.stream)
         else:
-            self.hid_all.copy_(self.hid)
-        m.lm_shard_keys(self.hid_all, self.world * self.m, self.keys)
-        if self.world > 1:
-            dist.all_reduce(self.keys, op=dist.ReduceOp.MAX, group=self.group)
-        mine = self.keys[self.rank * self.m:(self.rank + 1) * self.m]
-        m.keys_advance(mine, self.m, d_tokens, d_positions)
+            ctx = contextlib.nullcontext()
+        with ctx:
+            m.batch_hidden(d_tokens, d_positions, self.m, int(max_pos_end), self.hid)
+            if self.world > 1:
+                dist.all_gather_into_tensor(self.hid_all, self.hid, group=self.group)
+            else:
+                self.hid_all.copy_(self.hid)
+            m.lm_shard_keys(self.hid_all, self.world * self.m, self.keys)
+            if self.world > 1:
+                dist.all_reduce(self.keys, op=dist.ReduceOp.MAX, group=self.group)
+            mine = self.keys[self.rank * self.m:(self.rank + 1) * self.m]
+            m.keys_advance(mine, self.m, d_tokens, d_positions)
+        if self.cuda:
+            caller.wait_stream(self.stream)

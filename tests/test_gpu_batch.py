@@ -108,7 +108,12 @@ def test_vocab_shard_keys_combine(int8_models, cuda):
         toks, lens = _prompts(spec, 7)
         V = spec.vocab
         models = [ec.Model(path, batch_cap=B) for _ in range(3)]
+        st = torch.cuda.Stream()   # library work and torch ops ordered on one stream
+        ctx = torch.cuda.stream(st)
+        ctx.__enter__()
         try:
+            for m in models:
+                m.set_stream(st.cuda_stream)
             models[1].set_vocab_shard(0, V // 2 + 3)
             models[2].set_vocab_shard(V // 2 + 3, V)
             # the same prompts into every model's KV cache; a shard's prefill
@@ -135,5 +140,68 @@ def test_vocab_shard_keys_combine(int8_models, cuda):
             assert np.array_equal(d_tok.cpu().numpy(), ids_ref), key
             assert np.array_equal(d_pos.cpu().numpy(), pos + 1)
         finally:
+            ctx.__exit__(None, None, None)
             for m in models:
                 m.close()
+
+
+def test_sharded_decode_emulated_two_ranks(int8_models, cuda):
+    """The ShardedBatchDecoder step with two 'ranks' in one process: two
+    models, each holding half of the streams in its slots 0..19 and half of
+    the vocab; hidden rows concatenated and keys combined with a max in
+    place of NCCL's all-gather and all-reduce.  Same ids as one model
+    decoding all streams with ec_decode_batch."""
+    torch = cuda
+    for key, (spec, path) in int8_models.items():
+        toks, lens = _prompts(spec, 9)
+        V, half = spec.vocab, B // 2
+        with ec.Model(path, batch_cap=B) as full:
+            cur, pos, _ = _prefill(full, toks, lens)
+            d_tok = torch.from_numpy(cur).cuda()
+            d_pos = torch.from_numpy(pos).cuda()
+            d_ids = torch.zeros((STEPS, B), dtype=torch.int32, device="cuda")
+            full.decode_batch(d_tok, d_pos, STEPS, d_ids)
+            torch.cuda.synchronize()
+            want = d_ids.cpu().numpy()
+        ranks = [ec.Model(path, batch_cap=half) for _ in range(2)]
+        # the library's work and the torch ops below on one (non-default) stream
+        st = torch.cuda.Stream()
+        ctx = torch.cuda.stream(st)
+        ctx.__enter__()
+        try:
+            for m in ranks:
+                m.set_stream(st.cuda_stream)
+            state = []
+            for r, m in enumerate(ranks):
+                c, p, _ = _prefill_slice(m, toks[r * half:(r + 1) * half], lens[r * half:(r + 1) * half])
+                m.set_vocab_shard(r * V // 2, (r + 1) * V // 2)
+                state.append((torch.from_numpy(c).cuda(), torch.from_numpy(p).cuda()))
+            hid = [torch.empty((half, spec.n_embd), device="cuda") for _ in ranks]
+            keys = [torch.empty(B, dtype=torch.int64, device="cuda") for _ in ranks]
+            got = []
+            for s in range(STEPS):
+                for r, m in enumerate(ranks):
+                    m.batch_hidden(state[r][0], state[r][1], half, int(lens.max()) + s + 1, hid[r])
+                allh = torch.cat(hid)
+                for r, m in enumerate(ranks):
+                    m.lm_shard_keys(allh, B, keys[r])
+                comb = torch.maximum(keys[0], keys[1])
+                for r, m in enumerate(ranks):
+                    m.keys_advance(comb[r * half:(r + 1) * half].contiguous(), half, state[r][0], state[r][1])
+                torch.cuda.synchronize()
+                got.append(torch.cat([state[0][0], state[1][0]]).cpu().numpy())
+            assert np.array_equal(np.stack(got), want), key
+        finally:
+            ctx.__exit__(None, None, None)
+            for m in ranks:
+                m.close()
+
+
+def _prefill_slice(model, toks, lens):
+    """_prefill for a subset of the streams, placed in slots 0.. of `model`."""
+    t = np.concatenate(toks).astype(np.int32)
+    p = np.concatenate([np.arange(n) for n in lens]).astype(np.int32)
+    s = np.concatenate([np.full(n, b) for b, n in enumerate(lens)]).astype(np.int32)
+    lg = model.forward(t, p, s)
+    last = np.cumsum(lens) - 1
+    return np.argmax(lg[last], axis=1).astype(np.int32), np.asarray(lens, np.int32), lg[last]
