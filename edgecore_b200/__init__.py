@@ -23,7 +23,7 @@ from typing import Any
 import numpy as np
 
 __all__ = ["load_library", "Model", "gemm_int8", "gemm_fp16_fp32", "gemm_bf16_fp32",
-           "quantize_rows", "linear_int8", "gemm_async", "device_error_take", "attention_force_split", "argmax_key", "argmax_key_decode",
+           "quantize_rows", "linear_int8", "gemm_async", "device_error_take", "attention_force_split", "reference_math", "argmax_key", "argmax_key_decode",
            "LIB_PATH"]
 
 LIB_PATH = Path(__file__).resolve().parent / "libedgecore_b200.so"
@@ -62,6 +62,7 @@ def _declare(lib: C.CDLL) -> None:
         "ec_gemm_async": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
         "ec_device_error_take": (_i, [_vp, _vp]),
         "ec_attention_force_split": (_i, [_i]),
+        "ec_reference_math": (_i, [_vp, _vp, _vp, _i, _vp]),
         "gemm_fp16_fp32": (None, [_vp, _vp, _vp, _i, _i, _i]),
         "gemm_bf16_fp32": (None, [_vp, _vp, _vp, _i, _i, _i]),
         "gemm_int8": (None, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i]),
@@ -168,6 +169,13 @@ def gemm_async(wt: int, out, A, a_scale, B, b_scale=None, bias=None, stream=None
     N = B.shape[0]
     if lib.ec_gemm_async(int(wt), _ptr(out), _ptr(A), _ptr(a_scale), _ptr(B), _ptr(b_scale), _ptr(bias),
                          M, K, N, stream):
+        raise RuntimeError(last_error())
+
+
+def reference_math(d_x, d_exp=None, d_tanh=None, stream=None) -> None:
+    """The library's device expf / tanhf (restated host libm) on a device float tensor."""
+    n = int(d_x.numel())
+    if load_library().ec_reference_math(_ptr(d_x), _ptr(d_exp), _ptr(d_tanh), n, stream):
         raise RuntimeError(last_error())
 
 

@@ -237,6 +237,16 @@ EC_EXPORT int ec_gemm_async(int wt, float *C, const void *A, const float *a_scal
     return 0;
 }
 
+EC_EXPORT int ec_reference_math(const float *d_x, float *d_exp, float *d_tanh, int n, void *stream)
+{
+    const int e = ec_launch_reference_math(d_x, d_exp, d_tanh, n, (cudaStream_t)stream);
+    if (e) {
+        ec_set_error_text("ec_reference_math: launch failed");
+        return -1;
+    }
+    return 0;
+}
+
 EC_EXPORT int ec_attention_force_split(int on)
 {
     ec_attention_set_force_split(on);

@@ -218,13 +218,141 @@ EC_DEV int ec_quant_fast(float x, float s, float r) {
     return (int)n;
 }
 
-// Correctly rounded fp32 exp and tanh: the fp64 function (error < 1 ulp of
-// fp64) rounded once to fp32.  The reference calls the host libm's expf /
-// tanhf, which are not correctly rounded; every int8 quantisation downstream
-// is discontinuous, so this library pins the rounding of these functions to
-// the one well-defined choice and the oracle has a matching build.
-EC_DEV float ec_expf(float x) { return __double2float_rn(exp((double)x)); }
-EC_DEV float ec_tanhf(float x) { return __double2float_rn(tanh((double)x)); }
+// The reference's exp and tanh.  The reference calls the host C library's
+// expf / tanhf (glibc 2.39 on the x86-64 build hosts of this project), which
+// are not correctly rounded; every int8 activation quantisation downstream is
+// discontinuous, so a last-bit difference in exp can move a W8A8 model's
+// residual stream by ~1e-2.  These are restatements of glibc's published
+// algorithms, checked bit for bit against the host library on all 2^32 float
+// inputs (oracle/libm_check.c):
+//  * expf: ARM optimized-routines (glibc sysdeps/ieee754/flt-32/e_expf.c):
+//    k = round(x * 32/ln2), exp(x) = 2^(k/32) * p(r) with a 32-entry table of
+//    2^(i/32) and a cubic in double; the fused multiply-adds are those of the
+//    FMA-capable x86-64 build the library dispatches to on AVX2/FMA hosts.
+//  * tanhf: fdlibm (s_tanhf.c): 1 - 2/(expm1(2|x|) + 2) for |x| >= 1,
+//    -expm1(-2|x|)/(expm1(-2|x|) + 2) below, with fdlibm's expm1f (reduction by
+//    ln2 in hi/lo parts and its 5-term rational correction), in float.
+// Every operation is written with an explicit-rounding intrinsic so that the
+// compiler contracts nothing the host build does not.
+
+// 2^(i/32) as the bits of the nearest double, minus i << 47 (the exponent
+// adjustment the reconstruction adds back).
+static __device__ const unsigned long long ec_exp2f_tab[32] = {
+    0x3ff0000000000000ULL, 0x3fefd9b0d3158574ULL, 0x3fefb5586cf9890fULL, 0x3fef9301d0125b51ULL, 0x3fef72b83c7d517bULL, 0x3fef54873168b9aaULL, 0x3fef387a6e756238ULL, 0x3fef1e9df51fdee1ULL, 0x3fef06fe0a31b715ULL, 0x3feef1a7373aa9cbULL, 0x3feedea64c123422ULL, 0x3feece086061892dULL, 0x3feebfdad5362a27ULL, 0x3feeb42b569d4f82ULL, 0x3feeab07dd485429ULL, 0x3feea47eb03a5585ULL, 0x3feea09e667f3bcdULL, 0x3fee9f75e8ec5f74ULL, 0x3feea11473eb0187ULL, 0x3feea589994cce13ULL, 0x3feeace5422aa0dbULL, 0x3feeb737b0cdc5e5ULL, 0x3feec49182a3f090ULL, 0x3feed503b23e255dULL, 0x3feee89f995ad3adULL, 0x3feeff76f2fb5e47ULL, 0x3fef199bdd85529cULL, 0x3fef3720dcef9069ULL, 0x3fef5818dcfba487ULL, 0x3fef7c97337b9b5fULL, 0x3fefa4afa2a490daULL, 0x3fefd0765b6e4540ULL};
+
+EC_DEV float ec_expf(float x) {
+    constexpr double C0 = 0x1.c6af84b912394p-5 / 32 / 32 / 32, C1 = 0x1.ebfce50fac4f3p-3 / 32 / 32,
+                     C2 = 0x1.62e42ff0c52d6p-1 / 32, INVLN2N = 0x1.71547652b82fep+0 * 32, SHIFT = 0x1.8p+52;
+    const uint32_t ux = __float_as_uint(x);
+    const uint32_t abstop = (ux >> 20) & 0x7ffu;
+    if (abstop >= 0x42bu) {                       // |x| >= 88, inf or nan
+        if (ux == 0xff800000u) return 0.0f;
+        if (abstop >= 0x7f8u) return __fadd_rn(x, x);
+        if (x > 0x1.62e42ep6f) return __int_as_float(0x7f800000);
+        if (x < -0x1.9fe368p6f) return 0.0f;
+    }
+    const double xd = (double)x;
+    const double z = __dmul_rn(INVLN2N, xd);
+    double kd = __dadd_rn(z, SHIFT);
+    const unsigned long long ki = (unsigned long long)__double_as_longlong(kd);
+    kd = __dsub_rn(kd, SHIFT);
+    const double r = __fma_rn(INVLN2N, xd, -kd);
+    const double s = __longlong_as_double((long long)(ec_exp2f_tab[ki % 32] + (ki << 47)));
+    const double p = __fma_rn(C0, r, C1);
+    const double r2 = __dmul_rn(r, r);
+    double y = __fma_rn(C2, r, 1.0);
+    y = __fma_rn(p, r2, y);
+    return __double2float_rn(__dmul_rn(y, s));
+}
+
+EC_DEV float ec_expm1f(float x) {
+    constexpr float ln2_hi = 6.9313812256e-01f, ln2_lo = 9.0580006145e-06f, invln2 = 1.4426950216e+00f;
+    constexpr float Q1 = -3.3333335072e-02f, Q2 = 1.5873016091e-03f, Q3 = -7.9365076090e-05f,
+                    Q4 = 4.0082177293e-06f, Q5 = -2.0109921195e-07f;
+    float hi, lo, c = 0.0f, t, e, y;
+    int k;
+    uint32_t hx = __float_as_uint(x);
+    const uint32_t xsb = hx & 0x80000000u;
+    hx &= 0x7fffffffu;
+    if (hx >= 0x4195b844u) {                      // |x| >= 27 ln2
+        if (hx >= 0x42b17218u) {
+            if (hx > 0x7f800000u) return __fadd_rn(x, x);
+            if (hx == 0x7f800000u) return xsb == 0 ? x : -1.0f;
+            if (x > 8.8721679688e+01f) return __int_as_float(0x7f800000);
+        }
+        if (xsb != 0) return -1.0f;
+    }
+    if (hx > 0x3eb17218u) {                       // |x| > 0.5 ln2
+        if (hx < 0x3f851592u) {                   // and < 1.5 ln2
+            if (xsb == 0) { hi = __fsub_rn(x, ln2_hi); lo = ln2_lo; k = 1; }
+            else { hi = __fadd_rn(x, ln2_hi); lo = -ln2_lo; k = -1; }
+        } else {
+            k = __float2int_rz(__fadd_rn(__fmul_rn(invln2, x), xsb == 0 ? 0.5f : -0.5f));
+            t = __int2float_rn(k);
+            hi = __fsub_rn(x, __fmul_rn(t, ln2_hi));
+            lo = __fmul_rn(t, ln2_lo);
+        }
+        x = __fsub_rn(hi, lo);
+        c = __fsub_rn(__fsub_rn(hi, x), lo);
+    } else if (hx < 0x33000000u) {                // |x| < 2^-25
+        return x;
+    } else {
+        k = 0;
+    }
+    const float hfx = __fmul_rn(0.5f, x);
+    const float hxs = __fmul_rn(x, hfx);
+    float q = __fadd_rn(Q4, __fmul_rn(hxs, Q5));
+    q = __fadd_rn(Q3, __fmul_rn(hxs, q));
+    q = __fadd_rn(Q2, __fmul_rn(hxs, q));
+    q = __fadd_rn(Q1, __fmul_rn(hxs, q));
+    const float r1 = __fadd_rn(1.0f, __fmul_rn(hxs, q));
+    t = __fsub_rn(3.0f, __fmul_rn(r1, hfx));
+    e = __fmul_rn(hxs, __fdiv_rn(__fsub_rn(r1, t), __fsub_rn(6.0f, __fmul_rn(x, t))));
+    if (k == 0) return __fsub_rn(x, __fsub_rn(__fmul_rn(x, e), hxs));
+    e = __fsub_rn(__fmul_rn(x, __fsub_rn(e, c)), c);
+    e = __fsub_rn(e, hxs);
+    if (k == -1) return __fsub_rn(__fmul_rn(0.5f, __fsub_rn(x, e)), 0.5f);
+    if (k == 1) {
+        if (x < -0.25f) return __fmul_rn(-2.0f, __fsub_rn(e, __fadd_rn(x, 0.5f)));
+        return __fadd_rn(1.0f, __fmul_rn(2.0f, __fsub_rn(x, e)));
+    }
+    if (k <= -2 || k > 56) {
+        y = __fsub_rn(1.0f, __fsub_rn(e, x));
+        if (k == 128) y = __fmul_rn(__fmul_rn(y, 2.0f), 0x1p127f);
+        else y = __uint_as_float(__float_as_uint(y) + ((uint32_t)k << 23));
+        return __fsub_rn(y, 1.0f);
+    }
+    if (k < 23) {
+        t = __uint_as_float(0x3f800000u - (0x1000000u >> k));
+        y = __fsub_rn(t, __fsub_rn(e, x));
+    } else {
+        t = __uint_as_float((uint32_t)(0x7f - k) << 23);
+        y = __fsub_rn(x, __fadd_rn(e, t));
+        y = __fadd_rn(y, 1.0f);
+    }
+    return __uint_as_float(__float_as_uint(y) + ((uint32_t)k << 23));
+}
+
+EC_DEV float ec_tanhf(float x) {
+    const uint32_t jx = __float_as_uint(x), ix = jx & 0x7fffffffu;
+    float t, z;
+    if (ix >= 0x7f800000u)                                   // inf or nan
+        return (int)jx >= 0 ? __fadd_rn(__fdiv_rn(1.0f, x), 1.0f) : __fsub_rn(__fdiv_rn(1.0f, x), 1.0f);
+    if (ix < 0x41b00000u) {                                  // |x| < 22
+        if (ix == 0) return x;
+        if (ix < 0x24000000u) return __fmul_rn(x, __fadd_rn(1.0f, x));
+        if (ix >= 0x3f800000u) {                             // |x| >= 1
+            t = ec_expm1f(__fmul_rn(2.0f, fabsf(x)));
+            z = __fsub_rn(1.0f, __fdiv_rn(2.0f, __fadd_rn(t, 2.0f)));
+        } else {
+            t = ec_expm1f(__fmul_rn(-2.0f, fabsf(x)));
+            z = __fdiv_rn(-t, __fadd_rn(t, 2.0f));
+        }
+    } else {
+        z = __fsub_rn(1.0f, 1.0e-30f);
+    }
+    return (int)jx >= 0 ? z : -z;
+}
 
 // Reference gelu_new (src/gpt2.c:393-396) with its evaluation order kept.
 EC_DEV float ec_gelu(float x) {

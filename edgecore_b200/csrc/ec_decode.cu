@@ -29,7 +29,7 @@
 // Numerics are those of the reference (src/gpt2.c, src/kernels.c): exact
 // int32 dots and the (bias + ((float)dot*as)*ws) epilogue, fp64 norm
 // statistics, fp64 RoPE, the exact-order attention of k_attn_exact, and
-// correctly rounded exp/tanh.  Every wait is bounded; a CTA that gives up
+// the host libm's exp/tanh (ec_expf / ec_tanhf).  Every wait is bounded; a CTA that gives up
 // raises the shared abort flag so the others leave instead of spinning.
 #include "ec_common.cuh"
 #include "ec_launch.h"

@@ -1014,6 +1014,20 @@ extern "C" int ec_launch_keys_advance(const long long *keys, int M, int *tok, in
     return (int)cudaGetLastError();
 }
 
+__global__ void k_reference_math(const float *x, float *e, float *t, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        if (e) e[i] = ec_expf(x[i]);
+        if (t) t[i] = ec_tanhf(x[i]);
+    }
+}
+
+extern "C" int ec_launch_reference_math(const float *x, float *e, float *t, int n, cudaStream_t stream) {
+    if (n <= 0) return 0;
+    const int grid = (n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096;
+    k_reference_math<<<grid, 256, 0, stream>>>(x, e, t, n);
+    return (int)cudaGetLastError();
+}
+
 extern "C" int ec_kernel_error_take(cudaStream_t stream, int *code) {
     int zero = 0;
     cudaError_t e = cudaMemcpyFromSymbolAsync(code, g_ec_err, sizeof(int), 0, cudaMemcpyDeviceToHost, stream);

@@ -177,6 +177,10 @@ int ec_launch_pack_keys(const int *ids, const float *maxv, int M, long long *key
  * (ids may be NULL). */
 int ec_launch_keys_advance(const long long *keys, int M, int *tok, int *pos, int *ids, cudaStream_t stream);
 
+/* e[i] = expf(x[i]), t[i] = tanhf(x[i]) with the device restatements of the
+ * reference's libm functions (ec_common.cuh); e or t may be NULL. */
+int ec_launch_reference_math(const float *x, float *e, float *t, int n, cudaStream_t stream);
+
 /* The library-wide device error word (bounded waits that gave up, bad
  * indices skipped).  Read and cleared by ec_kernel_error_take. */
 int ec_kernel_error_take(cudaStream_t stream, int *code);

@@ -167,6 +167,13 @@ int ec_quantize_rows(int8_t *q, float *scale, const float *x, int M, int K);
 int ec_linear_int8(float *C, const float *X, const int8_t *W,
                    const float *w_scale, const float *bias, int M, int K, int N);
 
+/* The device exp and tanh every kernel of this library uses: restatements
+ * of the reference's host libm expf / tanhf (glibc 2.39: ARM
+ * optimized-routines expf, fdlibm tanhf / expm1f) that round exactly as the
+ * host functions.  Applies them to n DEVICE floats (d_exp or d_tanh may be
+ * NULL), enqueued on `stream`; for checking against the host library. */
+int ec_reference_math(const float *d_x, float *d_exp, float *d_tanh, int n, void *stream);
+
 /* Attention of the per-layer path (prefill, batched decode; the persistent
  * decode kernel has its own): 1 = always the split kernels (flash-decoding
  * partial sums over position blocks, then a combine), which otherwise run

@@ -32,17 +32,23 @@
 
 /* Transcendentals.  The default build calls the host libm exactly as the
  * reference does (its results are libm-specific: glibc's expf and tanhf are
- * not correctly rounded).  Built with -DECO_CR_MATH (libecoracle_cr.so), the
- * restatement uses correctly rounded fp32 results, obtained from the fp64
- * functions, which is what the CUDA library computes; that build checks the
- * GPU path bit-for-bit, the default build checks it against the reference. */
-#ifdef ECO_CR_MATH
-static float eco_expf(float x) { return (float)exp((double)x); }
-static float eco_tanhf(float x) { return (float)tanh((double)x); }
-#else
+ * not correctly rounded).  The CUDA library computes exactly these host
+ * functions (its device expf / tanhf restate glibc's algorithms, checked
+ * against the host library by oracle/libm_check.c and the GPU tests), so the
+ * restatement is the GPU path's bit-level oracle as well as the
+ * reference's. */
 #define eco_expf expf
 #define eco_tanhf tanhf
-#endif
+
+/* The host libm's expf / tanhf on n values (the GPU's device restatements
+ * are checked against these). */
+ECO_API void eco_libm(const float *x, float *e, float *t, int n)
+{
+    for (int i = 0; i < n; i++) {
+        if (e) e[i] = expf(x[i]);
+        if (t) t[i] = tanhf(x[i]);
+    }
+}
 
 /* ------------------------------------------------------------------ */
 /* GEMM restatements                                                    */

@@ -49,12 +49,11 @@ class _Lib:
 
 
 class Restatement(_Lib):
-    """oracle/libecoracle.so (host libm, as the reference), or with cr=True
-    oracle/libecoracle_cr.so (correctly rounded expf/tanhf, as the GPU)."""
+    """oracle/libecoracle.so: the reference's algorithm in our own C, calling
+    the host libm's expf / tanhf as the reference does."""
 
-    def __init__(self, cr: bool = False):
-        super().__init__(HERE / ("libecoracle_cr.so" if cr else "libecoracle.so"))
-        self.cr = cr
+    def __init__(self):
+        super().__init__(HERE / "libecoracle.so")
         L = self.lib
         L.eco_open.restype = C.c_void_p
         L.eco_open.argtypes = [C.c_char_p, C.c_int, C.c_int]
@@ -73,8 +72,16 @@ class Restatement(_Lib):
         L.eco_rmsnorm.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_int, C.c_double]
         L.eco_rope_inv_freq.argtypes = [_f64p, C.c_int, C.c_double, C.c_int, C.c_double, C.c_double]
         L.eco_rope_cos_sin.argtypes = [_f64p, _f64p, _f64p, C.c_int, C.c_int, C.c_double]
+        L.eco_libm.argtypes = [_f32p, _f32p, _f32p, C.c_int]
 
     # ---- ops ----
+    def libm(self, x):
+        """(expf(x), tanhf(x)) from this library's libm, element-wise."""
+        x = _as(x, np.float32).ravel()
+        e, t = np.empty_like(x), np.empty_like(x)
+        self.lib.eco_libm(x, e, t, x.size)
+        return e, t
+
     def quantize_rows(self, x):
         x = _as(x, np.float32)
         M, K = x.shape

@@ -36,7 +36,7 @@ def split_on():
 @pytest.fixture(scope="module")
 def cro(built, cuda):
     from oracle.oracle import Restatement
-    return Restatement(cr=True)
+    return Restatement()
 
 
 @pytest.mark.parametrize("force_split", [False, True])

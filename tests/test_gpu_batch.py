@@ -88,7 +88,7 @@ def test_decode_batch_matches_stepwise_forward(int8_models, cuda):
 
 def test_batched_step_against_cpu_oracle(int8_models, cuda):
     from oracle.oracle import Restatement
-    ro = Restatement(cr=True)
+    ro = Restatement()
     for key, (spec, path) in int8_models.items():
         toks, lens = _prompts(spec, 5)
         r = ro.open(path, batch_cap=B, max_ctx=spec.n_ctx)

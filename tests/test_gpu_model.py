@@ -1,22 +1,19 @@
 """GPU parity of the model path (gpt2_load / gpt2_forward and extensions).
 
-Two oracles (oracle/ec_oracle.c), pinned bit-exact to the reference on CPU:
-  * glibc build -- the reference's own numerics, libm included;
-  * CR build    -- identical except expf/tanhf are correctly rounded, which is
-                   what this library computes on the GPU.
-W8A8 models quantise every activation row with a data-dependent scale, so a
-1-ulp difference anywhere upstream can flip one int8 rounding and move the
-residual stream by ~1e-2 of its max (tests/test_oracle.py measures this on the
-reference's own numpy mirror).  glibc's expf / tanhf are not correctly rounded
-(8.7e-5 / 5.4% of inputs differ by an ulp), so the reference itself is only
-defined up to its libm.  The bars:
-  * GPU vs CR oracle, int8 models: residual taps and logits within 1e-5 of
-    the tensor max (everything feeding an int8 quantisation follows the
-    reference order; only the fp16 lm_head sums in another order), identical
-    greedy ids; fp16/bf16 models (no quantisation, linears summed in another
-    order than the 8-lane AVX2 loop): 1e-3;
-  * GPU vs reference (golden / glibc oracle): 1e-3 on the tiny models, and
-    identical greedy ids except at near-ties.
+The oracle is the C restatement of the reference (oracle/ec_oracle.c),
+pinned bit-exact on CPU to the reference's own golden vectors and build.  It
+calls the host libm's expf / tanhf as the reference does, and the device
+kernels use restatements of those same algorithms (bit-exact on every float,
+tests/test_gpu_ops.py), so everything that feeds an int8 activation
+quantisation rounds as in the reference.  W8A8 models quantise every
+activation row with a data-dependent scale: one last-bit difference upstream
+can flip an int8 rounding and move the residual stream by ~1e-2 of its max,
+so these bars only hold because the arithmetic is the reference's.
+  * int8 models: residual taps and logits within 1e-5 of the tensor max (the
+    fp16 lm_head is the one product summed in another order than the
+    reference's 8-lane AVX2 loop), identical greedy ids except at near-ties
+    (top-2 margin below 1e-3 of the row max);
+  * fp16/bf16 models (every linear summed in another order): 1e-3.
 """
 from __future__ import annotations
 
@@ -28,8 +25,8 @@ from edgecore_b200 import synth
 
 pytestmark = pytest.mark.gpu
 
-TOL = 1e-3      # vs the reference (fp32-accumulate bar of the spec)
-TOL_CR = 1e-5   # vs the CR-math restatement
+TOL = 1e-3        # fp32-accumulate bar of the spec (fp16 / bf16 models)
+TOL_EXACT = 1e-5  # int8 models: only the lm_head's summation order differs
 
 
 def rel_err(a, b):
@@ -45,18 +42,12 @@ def assert_greedy(ids, ref_ids, ref_logits, tol=TOL):
 
 
 @pytest.fixture(scope="module")
-def cro(built, cuda):
+def eco(built, cuda):
     from oracle.oracle import Restatement
-    return Restatement(cr=True)
+    return Restatement()
 
 
-@pytest.fixture(scope="module")
-def glo(built, cuda):
-    from oracle.oracle import Restatement
-    return Restatement(cr=False)
-
-
-def test_tiny_models_prefill_taps(golden, tiny_models, cro, cuda):
+def test_tiny_models_prefill_taps(golden, tiny_models, eco, cuda):
     g = golden("models.npz")
     for key, (spec, path) in tiny_models.items():
         with ec.Model(path, batch_cap=2) as m:
@@ -66,12 +57,13 @@ def test_tiny_models_prefill_taps(golden, tiny_models, cro, cuda):
         assert rel_err(logits, g[f"{key}_logits"]) < TOL, key
         for l in range(taps.shape[0]):
             assert rel_err(taps[l], g[f"{key}_taps"][l]) < TOL, (key, l)
-        r = cro.open(path, batch_cap=2)
+        r = eco.open(path, batch_cap=2)
         lr, tr = r.forward_taps(toks, np.arange(n, dtype=np.int32), np.zeros(n, np.int32))
         r.close()
-        assert rel_err(logits, lr) < TOL_CR, key
+        # tiny dims: even the fp16 / bf16 sums agree to ~1e-7 here
+        assert rel_err(logits, lr) < TOL_EXACT, key
         for l in range(taps.shape[0]):
-            assert rel_err(taps[l], tr[l]) < TOL_CR, (key, l)
+            assert rel_err(taps[l], tr[l]) < TOL_EXACT, (key, l)
 
 
 def test_tiny_models_decode(golden, tiny_models, cuda):
@@ -149,7 +141,8 @@ MID = {
 
 
 def _compare_run(m, ref, toks, n_dec, tol, greedy_tol):
-    """Prefill (taps) + teacher-forced decode of n_dec steps; returns max errors."""
+    """Prefill (taps) + decode of n_dec steps teacher-forced with the
+    reference's greedy ids; returns those ids and their logits."""
     n = len(toks)
     pos = np.arange(n, dtype=np.int32)
     sq = np.zeros(n, np.int32)
@@ -169,50 +162,53 @@ def _compare_run(m, ref, toks, n_dec, tol, greedy_tol):
         ref_lg.append(b)
         cur = ref_ids[-1]
     assert_greedy(ids, ref_ids, ref_lg, greedy_tol)
+    return ref_ids, ref_lg
 
 
 @pytest.mark.parametrize("key", list(MID))
-def test_mid_models_real_shapes(key, cro, tmp_path_factory, cuda):
+def test_mid_models_real_shapes(key, eco, tmp_path_factory, cuda):
     """Real layer shapes (E, heads, GQA, intermediate, head_dim 64/128) with few
     layers: 40-token prefill (generic GEMM path) and 3 decode steps (GEMV path)."""
     spec = MID[key]
     path = synth.ensure_model(spec, tmp_path_factory.mktemp(key))
-    tol = TOL_CR if spec.precision == "int8" else TOL
-    ref = cro.open(path, batch_cap=2, max_ctx=128)
+    tol = TOL_EXACT if spec.precision == "int8" else TOL
+    ref = eco.open(path, batch_cap=2, max_ctx=128)
     with ec.Model(path, batch_cap=2, max_ctx=128) as m:
         _compare_run(m, ref, synth.prompt_ids(spec.vocab, 40, seed=2), 3, tol, tol)
     ref.close()
 
 
-@pytest.mark.parametrize("cfg", ["c3_qwen05b_int8", "c0_gpt2_small_int8", "c2_qwen05b_fp16"])
-def test_full_size_baseline_models(cfg, cro, glo, cuda):
-    """BASELINE configurations at full size: 16-token prefill and 6 teacher-forced
-    decode steps against the CR restatement; greedy ids against the reference
-    numerics (glibc restatement) up to near-ties."""
+FULL = [("c0_gpt2_small_int8", 128), ("c3_qwen05b_int8", 256), ("c2_qwen05b_fp16", 256)]
+
+
+@pytest.mark.parametrize("cfg,n_dec", FULL)
+def test_full_size_baseline_models(cfg, n_dec, eco, cuda):
+    """BASELINE configurations 0, 2 and 3 at full size against the
+    restatement of the reference: a 64-token prefill (every layer's residual
+    tap and the logits), then n_dec greedy decode steps at positions 64..
+    63+n_dec, teacher-forced with the reference's ids.  int8 models to 1e-5
+    of the row max, the fp16 model to 1e-3; greedy ids identical except where
+    the reference's own top-2 margin is below 1e-3 of the row max."""
     spec = synth.CONFIGS[cfg]
     path = synth.ensure_model(spec)
-    toks = synth.prompt_ids(spec.vocab, 16)
-    # fp16 linears sum in a different order than the reference's 8-lane AVX2
-    # loop: ~1e-7 per layer, ~2e-4 after 24 layers; the spec's 1e-3 bar applies
-    tol = TOL_CR if spec.precision == "int8" else TOL
-    ref = cro.open(path, batch_cap=1, max_ctx=128)
-    with ec.Model(path, batch_cap=1, max_ctx=128) as m:
-        _compare_run(m, ref, toks, 6, tol, tol)
+    toks = synth.prompt_ids(spec.vocab, 64)
+    tol = TOL_EXACT if spec.precision == "int8" else TOL
+    ctx = 64 + n_dec + 1
+    ref = eco.open(path, batch_cap=1, max_ctx=ctx)
+    with ec.Model(path, batch_cap=1, max_ctx=ctx) as m:
+        ref_ids, ref_lg = _compare_run(m, ref, toks, n_dec, tol, TOL)
+        # the device-resident greedy loop (the benchmarked path) generates the
+        # reference's sequence up to the first near-tie
+        torch = cuda
+        m.forward(toks, np.arange(64), np.zeros(64, np.int32))
+        d_tok = torch.tensor([int(toks[-1])], dtype=torch.int32, device="cuda")
+        d_out = torch.zeros(n_dec + 1, dtype=torch.int32, device="cuda")
+        m.decode_greedy(d_tok, 63, n_dec + 1, d_out)
+        torch.cuda.synchronize()
+        got = d_out.cpu().tolist()[1:]
     ref.close()
-    # the reference's own numerics: greedy decode from the same prompt
-    gl = glo.open(path, batch_cap=1, max_ctx=128)
-    gl.reset()
-    lr = gl.forward(toks, np.arange(16, dtype=np.int32), np.zeros(16, np.int32))
-    with ec.Model(path, batch_cap=1, max_ctx=128) as m:
-        m.forward(toks, np.arange(16), np.zeros(16, np.int32))
-        cur = int(np.argmax(lr[-1]))
-        ids, ref_ids, ref_lg = [], [], []
-        for i in range(6):
-            a = m.forward([cur], [16 + i])[0]
-            b = gl.forward(np.array([cur], np.int32), np.array([16 + i], np.int32))[0]
-            ids.append(int(np.argmax(a)))
-            ref_ids.append(int(np.argmax(b)))
-            ref_lg.append(b)
-            cur = ref_ids[-1]
-    gl.close()
-    assert_greedy(ids, ref_ids, ref_lg, tol=5e-2)
+    for i, (a, b) in enumerate(zip(got, ref_ids)):
+        top2 = np.sort(ref_lg[i])[-2:]
+        if (top2[1] - top2[0]) / np.abs(ref_lg[i]).max() < TOL:
+            break
+        assert a == b, f"free-running greedy id differs at step {i}"

@@ -175,3 +175,24 @@ def test_gemv_row_result_independent_of_position(eco, cuda, M):
     f = full.cpu().numpy()
     assert np.array_equal(bits(f[:, 1:]), bits(shifted.cpu().numpy()))
     assert np.array_equal(bits(f[:, 2000:3000]), bits(shard.cpu().numpy()))
+
+
+def test_device_expf_tanhf_match_host_libm(eco, cuda):
+    """The kernels' expf / tanhf (GELU, SiLU, softmax) round exactly as the
+    host C library the reference calls: every 256th float bit pattern
+    (2^24 inputs) plus the specials, compared bit for bit (NaN as NaN)."""
+    torch = cuda
+    pat = np.arange(0, 1 << 32, 256, dtype=np.uint64).astype(np.uint32) + np.uint32(77)
+    extra = np.array([0x00000000, 0x80000000, 0x7f800000, 0xff800000, 0x7fc00000, 0x42b17217, 0x42b17218,
+                      0xc2cff1b4, 0xc2cff1b5, 0x3f800000, 0xbf800000, 0x41b00000, 0x41b00001, 0x24000000,
+                      0x23ffffff, 0x3eb17218, 0x3f851592], np.uint32)
+    x = np.concatenate([pat, extra]).view(np.float32)
+    want_e, want_t = eco.libm(x)
+    d_x = torch.from_numpy(x).cuda()
+    d_e, d_t = torch.empty_like(d_x), torch.empty_like(d_x)
+    ec.reference_math(d_x, d_e, d_t)
+    torch.cuda.synchronize()
+    for got, want, name in ((d_e.cpu().numpy(), want_e, "expf"), (d_t.cpu().numpy(), want_t, "tanhf")):
+        same = (bits(got) == bits(want)) | (np.isnan(got) & np.isnan(want))
+        bad = np.flatnonzero(~same)
+        assert bad.size == 0, (name, [hex(int(v)) for v in x[bad[:5]].view(np.uint32)])

@@ -140,3 +140,17 @@ def test_live_against_reference_build(eco, built):
         la, lb = a.forward(toks[:3], np.array([10, 0, 10], np.int32)), b.forward(toks[:3], np.array([10, 0, 10], np.int32))
         assert np.array_equal(bits(la), bits(lb))
         a.close(); b.close()
+
+
+def test_libm_restatement_matches_host_libm(built):
+    """The C restatement of the host libm's expf / tanhf (the algorithms the
+    device kernels use) against the host library, every 64th float bit
+    pattern (oracle/_ref/libm_check; `--all` checks all 2^32)."""
+    import subprocess
+    from pathlib import Path
+    exe = Path(__file__).resolve().parent.parent / "oracle" / "_ref" / "libm_check"
+    if not exe.exists():
+        pytest.skip("oracle/_ref/libm_check not built")
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "0 differ" in r.stdout
