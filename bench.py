@@ -64,13 +64,16 @@ def parse():
                     help="instead of the decode benchmark: BASELINE config 1's int8 operator sweep "
                          "(M in 1/8/64/512 and the 16384 prefill rows of config 3, Qwen2.5-0.5B (N,K) shapes), "
                          "one JSON line per shape")
-    ap.add_argument("--config", default="c3", choices=["c3", "c4"],
+    ap.add_argument("--config", default="c3", choices=["c3", "c4", "c0", "c2", "c3b"],
                     help="c3 (default): the headline, Qwen2.5-0.5B-shape int8 batch-1 decode, one stream per GPU; "
                          "c4: BASELINE config 4, Qwen2.5-1.5B-shape int8, --streams independent streams split over "
                          "the GPUs, lm_head column-split with an NCCL argmax combine")
     ap.add_argument("--streams", type=int, default=1024, help="--config c4: streams over all GPUs")
     ap.add_argument("--prompt", type=int, default=128, help="--config c4: prompt tokens per stream")
     ap.add_argument("--decode", type=int, default=128, help="--config c4: timed greedy steps per stream")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="default line without the config 0/2 decode, operator sweep, batch sweep and config-3 "
+                         "batched sub-measurements")
     ap.add_argument("--no-c4", action="store_true",
                     help="default run: skip the config-4 sub-measurement (\"c4\" in the JSON line)")
     ap.add_argument("--sweep-m", type=int, default=0, help="--op-sweep: only this M")
@@ -197,7 +200,8 @@ class ClockSampler:
 
 # ---- CPU reference ------------------------------------------------------------
 
-def run_reference_decode(path: Path, steps: int, warmup: int, min_s: float, threads: int, cap_s: float = 120.0):
+def run_reference_decode(path: Path, steps: int, warmup: int, min_s: float, threads: int, cap_s: float = 120.0,
+                         key: str = CONFIG_KEY, prompt: int = PROMPT, period: int = PERIOD):
     """Reference CPU decode (oracle/_ref, built from the reference sources;
     the restatement if that is absent): `warmup` untimed steps, then timed
     steps until at least `steps` steps and `min_s` seconds are done (at most
@@ -209,13 +213,13 @@ def run_reference_decode(path: Path, steps: int, warmup: int, min_s: float, thre
     except FileNotFoundError:
         R = oracle.Restatement()
         kind = "port"
-    spec = synth.CONFIGS[CONFIG_KEY]
-    m = R.open(path, batch_cap=1, max_ctx=PROMPT + PERIOD)
+    spec = synth.CONFIGS[key]
+    m = R.open(path, batch_cap=1, max_ctx=prompt + period)
     m.reset()
-    toks = synth.prompt_ids(spec.vocab, PROMPT)
-    lg = m.forward(toks, np.arange(PROMPT, dtype=np.int32), np.zeros(PROMPT, np.int32))
+    toks = synth.prompt_ids(spec.vocab, prompt)
+    lg = m.forward(toks, np.arange(prompt, dtype=np.int32), np.zeros(prompt, np.int32))
     cur = int(np.argmax(lg[-1]))
-    pos = PROMPT
+    pos = prompt
     total, done = 0.0, 0
     i = 0
     while True:
@@ -223,7 +227,7 @@ def run_reference_decode(path: Path, steps: int, warmup: int, min_s: float, thre
         lg = m.forward(np.array([cur], np.int32), np.array([pos], np.int32))
         dt = time.perf_counter() - t0
         cur = int(np.argmax(lg[0]))
-        pos = pos + 1 if pos + 1 < PROMPT + PERIOD else PROMPT
+        pos = pos + 1 if pos + 1 < prompt + period else prompt
         if i >= warmup:
             total += dt
             done += 1
@@ -237,20 +241,44 @@ def run_reference_decode(path: Path, steps: int, warmup: int, min_s: float, thre
 def reference_arm(args, rank: int, world: int) -> None:
     if rank != 0:
         return
-    path = synth.ensure_model(synth.CONFIGS[CONFIG_KEY])
+    name = args.config if args.config in DECODE_CONFIGS else "c3"
+    key, prompt, period, metric = DECODE_CONFIGS[name]
+    spec = synth.CONFIGS[key]
+    path = synth.ensure_model(spec)
     threads = host_cores()
     warm = max(args.warmup, 3)
-    tps, done, kind = run_reference_decode(path, args.steps, warm, args.cpu_seconds, threads)
+    tps, done, kind = run_reference_decode(path, args.steps, warm, args.cpu_seconds, threads,
+                                           key=key, prompt=prompt, period=period)
     sample = (f"{done} timed decode steps (at least --steps {args.steps} and {args.cpu_seconds:.0f} s, at most "
-              f"120 s) after a {PROMPT}-token prefill and {warm} warm-up steps, {threads} threads, "
+              f"120 s) after a {prompt}-token prefill and {warm} warm-up steps, {threads} threads, "
               f"gpt2_forward per step as the reference runtime times it")
-    line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": world,
+    line = {"impl": "reference", "metric": metric, "value": tps, "unit": "tok/s", "n_gpus": world,
             "steps": done, "warmup": warm, "ms_per_step": 1000.0 / tps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded random-init weights)",
-            "config": config_dict(1),
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8" if spec.precision == "int8" else spec.precision,
+            "data": "synthetic (seeded random-init weights)",
+            "config": config_dict(1) if name == "c3" else decode_config(name),
             "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": kind, "sample": sample},
             "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+DECODE_CONFIGS = {   # BASELINE configs 0, 2 and 3 at batch 1: (model, prompt tokens, decode tokens, metric)
+    "c0": ("c0_gpt2_small_int8", 16, 128, "GPT-2-small-shape int8 batch-1 greedy decode tok/s"),
+    "c2": ("c2_qwen05b_fp16", 64, 256, "Qwen2.5-0.5B-shape fp16 batch-1 greedy decode tok/s"),
+    "c3": (CONFIG_KEY, PROMPT, PERIOD, METRIC),
+}
+
+
+def decode_config(name: str) -> dict:
+    key, prompt, period, _ = DECODE_CONFIGS[name]
+    spec = synth.CONFIGS[key]
+    return {"workload": f"{key}: batch-1 greedy decode, {prompt}-token prompt, positions cycling "
+                        f"{prompt}..{prompt + period - 1} ({period}-token continuations)",
+            "config": key, "arch": spec.arch, "precision": spec.precision, "n_layer": spec.n_layer,
+            "n_embd": spec.n_embd, "n_head": spec.n_head, "n_kv_head": spec.n_kv_head,
+            "intermediate": spec.intermediate, "vocab": spec.vocab, "prompt": prompt, "decode_period": period,
+            "streams_per_gpu": 1, "global_batch": 1, "parallelism": "replicas1",
+            "l2": "weights streamed per step larger than L2"}
 
 
 # ---- our arm ------------------------------------------------------------------
@@ -388,6 +416,13 @@ def ours_arm(args, rank: int, world: int, local: int) -> None:
     if rank == 0 and world == 1:
         cpu = cpu_baseline_leg(args)
     m.close()
+    extras = {}
+    if rank == 0 and world == 1 and not args.no_extras:
+        extras["batch_sweep"] = batch_sweep(args, stream, value)
+        extras["c3_batched"] = c3_batched(args, stream)
+        extras["c0"] = decode_line(args, "c0", stream)
+        extras["c2"] = decode_line(args, "c2", stream)
+        extras["op_sweep"] = list(op_sweep_results(args, cpu_seconds=0.25))
     c4 = None if args.no_c4 else c4_arm(args, rank, world, local)
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -400,7 +435,7 @@ def ours_arm(args, rank: int, world: int, local: int) -> None:
                         "api": "gpt2_forward (host tokens/positions, host logits [1][151936])"},
                 "gpu_launches": launches,
                 "roofline": roofline, "cpu_baseline": cpu, "gemv_lm_head": gemv,
-                "load_time_ms": load_ms, "c4": c4}
+                "load_time_ms": load_ms, **extras, "c4": c4}
         print(json.dumps(line), flush=True)
 
 
@@ -464,6 +499,239 @@ def gemv_lm_head(stream, reps: int = 20, warmup: int = 3) -> dict:
     return {"op": "gemm_fp16_fp32", "M": M, "N": N, "K": K, "us": us, "achieved_gbs": algo / us / 1e3,
             "frac": algo / us / 1e3 / peak, "peak": peak, "peak_source": kind,
             "kernel": "k_gemv<fp16,M=1> (weight streaming)", "algorithmic_bytes": algo}
+
+
+# ---- sub-measurements of the default line (1 GPU) ------------------------------
+
+def child_reference(args, config: str, cpu_seconds: float) -> dict | None:
+    """`bench.py --impl reference --config <config>` in a child process (no CUDA
+    context or torch threads in the process that times the CPU); its line."""
+    cmd = [sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--config", config, "--steps", "1",
+           "--warmup", str(max(args.warmup, 3)), "--cpu-seconds", str(cpu_seconds)]
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK")}
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=900)
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    if r.returncode != 0 or not lines:
+        return {"value": None, "cores": host_cores(), "kind": "reference",
+                "sample": f"reference arm failed: rc {r.returncode}: {r.stderr[-300:]}"}
+    return json.loads(lines[-1])
+
+
+def decode_line(args, name: str, stream, steps: int | None = None, cpu: bool = True) -> dict:
+    """Batch-1 greedy decode of BASELINE config 0 / 2 / 3: the device-resident
+    loop timed with CUDA events (value), the reference-facing gpt2_forward
+    with host arrays (e2e), the algorithmic bytes of the timed steps over the
+    measured time (roofline), and the reference CPU path on the host cores."""
+    import torch
+
+    import edgecore_b200 as ec
+    key, prompt, period, metric = DECODE_CONFIGS[name]
+    spec = synth.CONFIGS[key]
+    path = synth.ensure_model(spec)
+    steps = steps or 4 * period
+    t_load = time.perf_counter()
+    m = ec.Model(path, batch_cap=1, max_ctx=prompt + period)
+    torch.cuda.synchronize()
+    load_ms = (time.perf_counter() - t_load) * 1e3
+    m.set_stream(stream.cuda_stream)
+    toks = synth.prompt_ids(spec.vocab, prompt)
+    lg = m.forward(toks, np.arange(prompt), np.zeros(prompt, np.int32))
+    first = int(np.argmax(lg[-1]))
+    d_tok = torch.tensor([first], dtype=torch.int32, device="cuda")
+    m.decode_greedy_cycle(d_tok, prompt, period, max(args.warmup, 3))
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(torch.cuda.current_device())
+    start.record(stream)
+    m.decode_greedy_cycle(d_tok, prompt, period, steps)
+    end.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = start.elapsed_time(end)
+    prof = m.decode_profile(d_tok, prompt, 8)
+    torch.cuda.synchronize()
+    classes = {k: v for k, v in prof.items() if k != "steps"}
+    kv_per_pos = m.n_layer * 2 * m.n_kv_embd * 2
+    fixed = (sum(v["bytes"] for v in classes.values())
+             - sum(kv_per_pos * (prompt + i + 2) for i in range(prof["steps"]))) / prof["steps"]
+    timed_bytes = steps * fixed + sum(kv_per_pos * (prompt + (i % period) + 2) for i in range(steps))
+    peak, peak_kind = measured_peaks()
+    achieved = timed_bytes / (ms / 1e3) / 1e9
+    # e2e: gpt2_forward on host arrays, host logits
+    m.set_stream(None)
+    m.forward(toks, np.arange(prompt), np.zeros(prompt, np.int32))
+    tok_h, pos_h = np.empty(1, np.int32), np.empty(1, np.int32)
+    out = np.empty((1, spec.vocab), np.float32)
+    tok_p, pos_p, out_p = (ctypes.c_void_p(a.ctypes.data) for a in (tok_h, pos_h, out))
+    fwd = m.lib.gpt2_forward
+    cur, pos, e2e_s, n_e2e = first, prompt, 0.0, min(128, period)
+    for i in range(n_e2e + 3):
+        tok_h[0], pos_h[0] = cur, pos
+        t0 = time.perf_counter()
+        fwd(m.h, tok_p, pos_p, None, 1, out_p)
+        if i >= 3:
+            e2e_s += time.perf_counter() - t0
+        cur = int(np.argmax(out[0]))
+        pos = pos + 1 if pos + 1 < prompt + period else prompt
+    m.close()
+    line = {"metric": metric, "value": steps / (ms / 1e3), "unit": "tok/s", "n_gpus": 1, "steps": steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms / steps, "higher_is_better": True,
+            "dtype": spec.precision, "config": decode_config(name), "clocks": clk,
+            "e2e": {"value": n_e2e / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 8,
+                    "d2h_bytes_per_step": 4 * spec.vocab, "steps": n_e2e,
+                    "api": f"gpt2_forward (host tokens/positions, host logits [1][{spec.vocab}])"},
+            "gpu_launches": 1,
+            "roofline": {"bound": "hbm", "kernel": f"k_decode (persistent, 1 launch = {steps} steps)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": peak_kind, "bytes_per_step": timed_bytes / steps, "traffic": None,
+                         "method": "algorithmic bytes of the timed steps / CUDA-event time of the timed launch"},
+            "load_time_ms": load_ms, "cpu_baseline": None}
+    if cpu:
+        ref = child_reference(args, name, min(args.cpu_seconds, 5.0))
+        line["cpu_baseline"] = ref.get("cpu_baseline", ref) if ref else None
+    return line
+
+
+def batch_sweep(args, stream, m1_value: float) -> list:
+    """Batched greedy decode of the config-3 model over M independent streams
+    (each a distinct 64-token prompt in its own KV slot): M = 1 is the
+    headline loop; M = 8, 32, 128 run ec_decode_batch (one CUDA graph of the
+    per-layer kernels per step; tensor-core GEMMs from M = 32)."""
+    import torch
+
+    import edgecore_b200 as ec
+    spec = synth.CONFIGS[CONFIG_KEY]
+    path = synth.ensure_model(spec)
+    out = [{"M": 1, "tok_s": m1_value, "path": "k_decode (persistent)"}]
+    steps = 64
+    for M in (8, 32, 128):
+        m = ec.Model(path, batch_cap=M, max_ctx=PROMPT + 2 * steps + 8)
+        m.set_stream(stream.cuda_stream)
+        t = np.concatenate([synth.prompt_ids(spec.vocab, PROMPT, seed=100 + b) for b in range(M)]).astype(np.int32)
+        p = np.tile(np.arange(PROMPT, dtype=np.int32), M)
+        sl = np.repeat(np.arange(M, dtype=np.int32), PROMPT)
+        ids, _ = m.forward_argmax(t, p, sl)
+        d_tok = torch.from_numpy(ids.reshape(M, PROMPT)[:, -1].copy()).cuda()
+        d_pos = torch.full((M,), PROMPT, dtype=torch.int32, device="cuda")
+        wt, wp = d_tok.clone(), d_pos.clone()
+        torch.cuda.synchronize()       # the library's stream starts after torch's default stream
+        m.decode_batch(wt, wp, max(args.warmup, 3))
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        m.decode_batch(d_tok, d_pos, steps)
+        end.record(stream)
+        torch.cuda.synchronize()
+        assert ec.device_error_take(stream.cuda_stream) == 0
+        ms = start.elapsed_time(end)
+        out.append({"M": M, "tok_s": M * steps / (ms / 1e3), "ms_per_step": ms / steps, "steps": steps,
+                    "path": "ec_decode_batch (CUDA graph per step; " +
+                            ("tcgen05 GEMMs)" if M >= 32 else "weight-streaming GEMV)"),
+                    "graph_kernels_per_step": m.batch_graph_kernels(0)})
+        m.close()
+    return out
+
+
+C3B_SEQ, C3B_LEN, C3B_DEC = 32, 512, 128
+
+
+def c3_batched(args, stream) -> dict:
+    """32 sequences x 512 distinct uniform-random prompt
+    tokens prefilled in one gpt2_forward-shaped call (rows carry their own
+    positions and KV slots, reference src/edgecore.h:249-260), then 128
+    greedy decode steps of the 32 streams (ec_decode_batch).  The prefill's
+    tensor work is the int8 linears (2 * rows * int8 weights) plus the fp16
+    lm_head over every row, the counts BASELINE quotes (1.17e13 + 4.46e12)."""
+    import torch
+
+    import edgecore_b200 as ec
+    spec = synth.CONFIGS[CONFIG_KEY]
+    path = synth.ensure_model(spec)
+    S, P, D = C3B_SEQ, C3B_LEN, C3B_DEC
+    m = ec.Model(path, batch_cap=S, max_ctx=P + D + 8)
+    m.set_stream(stream.cuda_stream)
+    t = np.concatenate([synth.prompt_ids(spec.vocab, P, seed=300 + b) for b in range(S)]).astype(np.int32)
+    p = np.tile(np.arange(P, dtype=np.int32), S)
+    sl = np.repeat(np.arange(S, dtype=np.int32), P)
+    m.forward_argmax(t, p, sl)                      # workspaces and tensor maps for S*P rows
+    torch.cuda.synchronize()
+    reps, best = 3, 1e30
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        ids, _ = m.forward_argmax(t, p, sl)
+        torch.cuda.synchronize()
+        best = min(best, time.perf_counter() - t0)
+    rows = S * P
+    L, E, I, V, kv = spec.n_layer, spec.n_embd, spec.intermediate, spec.vocab, spec.kv_embd
+    w_int8 = L * ((E + 2 * kv) * E + E * E + 2 * I * E + E * I)
+    int8_ops = 2.0 * rows * w_int8
+    fp16_flops = 2.0 * rows * V * E
+    d_tok = torch.from_numpy(ids.reshape(S, P)[:, -1].copy()).cuda()
+    d_pos = torch.full((S,), P, dtype=torch.int32, device="cuda")
+    wt, wp = d_tok.clone(), d_pos.clone()
+    torch.cuda.synchronize()           # the library's stream starts after torch's default stream
+    m.decode_batch(wt, wp, max(args.warmup, 3))
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    m.decode_batch(d_tok, d_pos, D)
+    end.record(stream)
+    torch.cuda.synchronize()
+    assert ec.device_error_take(stream.cuda_stream) == 0
+    dms = start.elapsed_time(end)
+    m.close()
+    line = {"metric": "Qwen2.5-0.5B-shape int8: 32x512 distinct-prompt prefill, then 128 batched greedy steps",
+            "prefill_tok_s": rows / best, "prefill_ms": best * 1e3, "prefill_rows": rows,
+            "prefill_int8_tops": int8_ops / best / 1e12, "prefill_fp16_tflops": fp16_flops / best / 1e12,
+            "prefill_tensor_ops": {"int8": int8_ops, "fp16": fp16_flops},
+            "prefill_timing": f"best of {reps} host-timed forward_argmax calls of {rows} rows (synchronised)",
+            "decode_tok_s": S * D / (dms / 1e3), "decode_ms_per_step": dms / D, "decode_steps": D,
+            "decode_timing": "CUDA events around ec_decode_batch of 128 steps",
+            "kv": "contiguous arena [layer][slot][position] sized by max_ctx"}
+    ref = child_reference(args, "c3b", 0.0)
+    line["cpu_baseline"] = ref.get("cpu_baseline", ref) if ref else None
+    return line
+
+
+def c3b_reference_arm(args, rank: int) -> None:
+    """The reference's own C path on a bounded sample of config 3: a prefill of
+    2 x 128 distinct-prompt rows in one gpt2_forward call, then 3 batched
+    steps of 32 streams."""
+    if rank != 0:
+        return
+    from oracle import oracle
+    try:
+        R, kind = oracle.Reference(threads=host_cores()), "reference"
+    except FileNotFoundError:
+        R, kind = oracle.Restatement(), "port"
+    spec = synth.CONFIGS[CONFIG_KEY]
+    path = synth.ensure_model(spec)
+    n, plen = 2, 128
+    # the reference's workspaces hold max(max_ctx, batch_cap) rows per call (src/gpt2.c:319-351)
+    m = R.open(path, batch_cap=C3B_SEQ, max_ctx=n * plen + 8)
+    m.reset()
+    t = np.concatenate([synth.prompt_ids(spec.vocab, plen, seed=300 + b) for b in range(n)]).astype(np.int32)
+    t0 = time.perf_counter()
+    m.forward(t, np.tile(np.arange(plen, dtype=np.int32), n), np.repeat(np.arange(n, dtype=np.int32), plen))
+    pre = n * plen / (time.perf_counter() - t0)
+    cur = synth.prompt_ids(spec.vocab, C3B_SEQ, seed=7).astype(np.int32)
+    slots = np.arange(C3B_SEQ, dtype=np.int32)
+    pos = np.full(C3B_SEQ, plen, np.int32)
+    m.forward(cur, pos, slots)
+    t0 = time.perf_counter()
+    for s in range(3):
+        lg = m.forward(cur, pos + 1 + s, slots)
+        cur = np.argmax(lg, axis=1).astype(np.int32)
+    dec = 3 * C3B_SEQ / (time.perf_counter() - t0)
+    m.close()
+    sample = (f"prefill of {n} x {plen} rows in one gpt2_forward call ({pre:.1f} tok/s), then 3 batched steps "
+              f"of {C3B_SEQ} streams ({dec:.1f} tok/s), {host_cores()} threads")
+    line = {"impl": "reference", "metric": "config 3 batched decode tok/s (CPU sample)", "value": dec,
+            "unit": "tok/s", "prefill_tok_s": pre,
+            "cpu_baseline": {"value": dec, "unit": "tok/s", "prefill_tok_s": pre, "cores": host_cores(),
+                             "kind": kind, "sample": sample},
+            "e2e": {"value": dec, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
 
 
 # ---- config 4: many independent streams, column-split lm_head --------------
@@ -667,6 +935,11 @@ def c4_arm(args, rank: int, world: int, local: int) -> None:
 
 
 def op_sweep(args) -> None:
+    for line in op_sweep_results(args, cpu_seconds=min(args.cpu_seconds, 2.0)):
+        print(json.dumps(line), flush=True)
+
+
+def op_sweep_results(args, cpu_seconds: float):
     """BASELINE config 1's int8 operator sweep plus the fp16 lm_head, through
     ec_gemm_async with device operands: X int8 [M][K] (the A2 quantisation
     output) with a_scale, W int8 [N][K] with per-row scales (or fp16 W and
@@ -680,7 +953,7 @@ def op_sweep(args) -> None:
     stream = torch.cuda.Stream()
     peak, peak_kind = measured_peaks()
     ref = None
-    if args.cpu_seconds > 0:
+    if cpu_seconds > 0:
         try:
             from oracle import oracle
             ref = oracle.Reference(threads=host_cores())
@@ -728,14 +1001,16 @@ def op_sweep(args) -> None:
                 else:
                     ref.gemm_fp16(Ah, Wh.view(np.uint16))
                 n += 1
-                if time.perf_counter() - t0 >= min(args.cpu_seconds, 2.0):
+                if time.perf_counter() - t0 >= cpu_seconds:
                     break
             cpu_us = (time.perf_counter() - t0) / n * 1e6
             line["cpu_baseline"] = {"value": cpu_us, "unit": "us_per_call", "cores": host_cores(),
                                     "kind": "reference", "sample": f"{n} calls of the reference "
                                     f"{'gemm_int8' if wt == 0 else 'gemm_fp16_fp32'} on host operands"}
-        print(json.dumps(line), flush=True)
+        else:
+            line["cpu_baseline"] = None
         del Ws, A, out
+        yield line
 
 
 def main():
@@ -749,6 +1024,8 @@ def main():
     if args.impl == "reference":
         if args.config == "c4":
             c4_reference_arm(args, rank, world)
+        elif args.config == "c3b":
+            c3b_reference_arm(args, rank)
         else:
             reference_arm(args, rank, world)
         return
@@ -764,7 +1041,11 @@ def main():
             line = c4_arm(args, rank, world, local)
             if rank == 0:
                 print(json.dumps(line), flush=True)
-        else:
+        elif args.config in ("c0", "c2") and rank == 0:
+            print(json.dumps(decode_line(args, args.config, torch.cuda.Stream(), steps=args.steps)), flush=True)
+        elif args.config == "c3b" and rank == 0:
+            print(json.dumps(c3_batched(args, torch.cuda.Stream())), flush=True)
+        elif args.config in ("c3",):
             ours_arm(args, rank, world, local)
     finally:
         if world > 1:

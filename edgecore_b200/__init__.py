@@ -352,7 +352,7 @@ class Model:
 
     TRACE_CODES = {1: "barrier", 2: "operand", 3: "tiles", 4: "attention", 5: "lm_head", 6: "argmax",
                    7: "tile_in", 8: "tile_free", 9: "tile_done", 10: "issue", 11: "staged", 12: "stats",
-                   13: "scores", 14: "softmax"}
+                   13: "scores", 14: "softmax", 15: "phase_in"}
 
     def decode_trace(self, d_tokens, start_pos: int, n_steps: int, cap: int = 1 << 16):
         """Timeline of CTA 0 of the persistent decode kernel: list of (event, ns)

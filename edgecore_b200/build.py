@@ -5,7 +5,10 @@ for the host library, linked with the static CUDA runtime.
 
 Objects go to edgecore_b200/_build/; the shared library to
 edgecore_b200/libedgecore_b200.so.  Only the symbols of include/edgecore.h and
-include/edgecore_b200.h are exported.
+include/edgecore_b200.h are exported.  With EDGECORE_B200_TRACE=1 the same
+sources build the diagnostic variant libedgecore_b200_trace.so (objects in
+_build_trace/), whose decode kernel records the per-phase timeline that
+ec_decode_trace returns.
 """
 from __future__ import annotations
 
@@ -53,11 +56,14 @@ def _run(cmd: list[str]) -> None:
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
-    BUILD.mkdir(exist_ok=True)
+    trace = os.environ.get("EDGECORE_B200_TRACE") == "1"
+    bdir = PKG / "_build_trace" if trace else BUILD
+    lib = PKG / "libedgecore_b200_trace.so" if trace else LIB
+    bdir.mkdir(exist_ok=True)
     objs: list[Path] = []
-    inc = ["-I", str(ROOT / "include"), "-I", str(CSRC)]
+    inc = ["-I", str(ROOT / "include"), "-I", str(CSRC)] + (["-DEC_DECODE_TRACE"] if trace else [])
     for src in CU_SOURCES:
-        s, o = CSRC / src, BUILD / (Path(src).stem + ".o")
+        s, o = CSRC / src, bdir / (Path(src).stem + ".o")
         if force or _stale(o, [s, *HEADERS]):
             cmd = [_nvcc(), *ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden",
                    "--expt-relaxed-constexpr", *inc, "-c", str(s), "-o", str(o)]
@@ -66,17 +72,17 @@ def build(force: bool = False, verbose: bool = False) -> Path:
             _run(cmd)
         objs.append(o)
     for src in C_SOURCES:
-        s, o = CSRC / src, BUILD / (Path(src).stem + ".o")
+        s, o = CSRC / src, bdir / (Path(src).stem + ".o")
         if force or _stale(o, [s, *HEADERS]):
             _run([_cc(), "-std=c11", "-O2", "-fPIC", "-fvisibility=hidden", "-Wall", "-Wextra",
                   "-Wno-unused-parameter", *inc, "-I", str(CUDA / "include"), "-c", str(s), "-o", str(o)])
         objs.append(o)
-    if force or _stale(LIB, objs):
-        tmp = LIB.with_suffix(".so.tmp")
+    if force or _stale(lib, objs):
+        tmp = lib.with_suffix(".so.tmp")
         _run([_nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(tmp), *map(str, objs),
               "-Xlinker", "--exclude-libs=ALL", "-Xlinker", "-Bsymbolic", "-lpthread", "-lm", "-ldl", "-lrt"])
-        tmp.replace(LIB)
-    return LIB
+        tmp.replace(lib)
+    return lib
 
 
 if __name__ == "__main__":

@@ -214,9 +214,12 @@ __device__ __forceinline__ void stage_issue(float *dst, const float *src, int n,
     for (int i = done + ct; i < n; i += NCT) dst[i] = __ldcg(src + i);
 }
 
-// Timeline of CTA 0 when p.trace is set: consumer thread 0 writes the first
-// half of the buffer, the producer thread the second half, entries
+// Timeline of CTA 0 when p.trace is set, in builds with EC_DECODE_TRACE
+// defined (the product build has none: even a not-taken check of p.trace at
+// every mark cost ~5 % of the decode step): consumer thread 0 writes the
+// first half of the buffer, the producer thread the second half, entries
 // (code << 56) | globaltimer ns.  Each half has its own count in shared memory.
+#ifdef EC_DECODE_TRACE
 __device__ __noinline__ void tmark_rec(const ec_mk_params &p, int *tcount, int who, int code) {
     const int half = p.trace_cap / 2, cap = who ? p.trace_cap - half : half;
     int &n = tcount[who];
@@ -227,10 +230,13 @@ __device__ __noinline__ void tmark_rec(const ec_mk_params &p, int *tcount, int w
     }
 }
 
-// The check stays inline, the recording out of line (kept off the hot path).
+// The check stays inline, the recording out of line.
 __device__ __forceinline__ void tmark(const ec_mk_params &p, const Sm &S, int who, int code) {
     if (p.trace && blockIdx.x == 0) tmark_rec(p, S.tcount, who, code);
 }
+#else
+__device__ __forceinline__ void tmark(const ec_mk_params &, const Sm &, int, int) {}
+#endif
 
 // ---------------------------------------------------------------------------
 // producer
@@ -672,6 +678,7 @@ __device__ __noinline__ uint32_t mk_phase(const ec_mk_params &p, int kind, int l
     const int my = vidx<V>(lane);               // this lane's (row slot, token) after the reduction
     const int my_i = my / MM, my_q = my % MM;
     const bool my_lane = (lane & (D - 1)) == 0 && my_q < nM && (unit == 1 || (my_i & 1) == 0);
+    if (ct == 0) tmark(p, S, 0, EC_TR_PHASE_IN);
 
     for (int row0 = rg.r0; row0 < rg.r1; row0 += tile_rows) {
         const int nr = min(tile_rows, rg.r1 - row0);
@@ -1350,6 +1357,14 @@ int mk_launch_m(const ec_mk_params *p, int n_steps, int grid, cudaStream_t strea
 }
 
 }  // namespace
+
+extern "C" int ec_mk_traced(void) {
+#ifdef EC_DECODE_TRACE
+    return 1;
+#else
+    return 0;
+#endif
+}
 
 extern "C" size_t ec_mk_smem_bytes(const ec_mk_params *p) {
     return mk_layout(p->xbuf_bytes, p->stage_bytes, p->L, p->E, p->hd, p->own_rows).total;

@@ -90,7 +90,8 @@ enum { EC_TR_SYNC = 1, EC_TR_PROLOGUE = 2, EC_TR_TILES = 3, EC_TR_ATTN = 4, EC_T
        EC_TR_STAGED = 11,    /* a prologue's or attention item's inputs arrived in shared memory */
        EC_TR_STATS = 12,     /* norm statistics reduced */
        EC_TR_SCORES = 13,    /* attention scores and their max done */
-       EC_TR_SOFTMAX = 14 }; /* attention weights normalised */
+       EC_TR_SOFTMAX = 14,   /* attention weights normalised */
+       EC_TR_PHASE_IN = 15 }; /* a weight phase entered */
 
 /* Dynamic shared memory of the kernel for these parameters. */
 size_t ec_mk_smem_bytes(const ec_mk_params *p);
@@ -100,6 +101,8 @@ int ec_mk_smem_limit(void);
 
 /* Launch (cooperative, one CTA per SM).  The barrier counter must be zero. */
 int ec_mk_launch(const ec_mk_params *p, int n_steps, int grid, cudaStream_t stream);
+/* 1 when the decode kernel was compiled with its timeline (EC_DECODE_TRACE). */
+int ec_mk_traced(void);
 
 #ifdef __cplusplus
 }

@@ -1767,6 +1767,11 @@ EC_EXPORT int ec_decode_trace(GPT2 *g, int *d_tokens, int start_pos, int n_steps
 {
     ec_dev *d = ec_lookup(g);
     if (!d) { ec_seterr("model not loaded"); return -1; }
+    if (!ec_mk_traced()) {
+        ec_seterr("decode timeline not compiled in (build with EDGECORE_B200_TRACE=1: "
+                  "libedgecore_b200_trace.so)");
+        return -1;
+    }
     const int M = d->B;
     if (M > EC_MK_MT || n_steps < 1 || cap < 1 || start_pos < 0 || start_pos + n_steps > d->C) {
         ec_seterr("bad trace range");
