@@ -595,8 +595,9 @@ def decode_line(args, name: str, stream, steps: int | None = None, cpu: bool = T
 def batch_sweep(args, stream, m1_value: float) -> list:
     """Batched greedy decode of the config-3 model over M independent streams
     (each a distinct 64-token prompt in its own KV slot): M = 1 is the
-    headline loop; M = 8, 32, 128 run ec_decode_batch (one CUDA graph of the
-    per-layer kernels per step; tensor-core GEMMs from M = 32)."""
+    headline loop; M = 8, 32, 128 run ec_decode_batch (the persistent decode
+    kernel up to 8 streams; above, one CUDA graph of the per-layer kernels
+    per step with tensor-core GEMMs)."""
     import torch
 
     import edgecore_b200 as ec
@@ -625,9 +626,9 @@ def batch_sweep(args, stream, m1_value: float) -> list:
         assert ec.device_error_take(stream.cuda_stream) == 0
         ms = start.elapsed_time(end)
         out.append({"M": M, "tok_s": M * steps / (ms / 1e3), "ms_per_step": ms / steps, "steps": steps,
-                    "path": "ec_decode_batch (CUDA graph per step; " +
-                            ("tcgen05 GEMMs)" if M >= 32 else "weight-streaming GEMV)"),
-                    "graph_kernels_per_step": m.batch_graph_kernels(0)})
+                    "path": "ec_decode_batch: " + ("k_decode (persistent, one launch for all steps)" if M <= 8 else
+                                                   "one CUDA graph of per-layer kernels per step, tcgen05 GEMMs"),
+                    "graph_kernels_per_step": m.batch_graph_kernels(0) if M > 8 else 0})
         m.close()
     return out
 

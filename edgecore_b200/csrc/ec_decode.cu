@@ -477,6 +477,136 @@ __device__ __noinline__ void mk_operand(const ec_mk_params &p, const float *src,
     cons_sync();
 }
 
+// mk_prep for 4 or 8 token rows: the same arithmetic in the same order, but
+// the element loops run over one token row at a time and the per-row
+// statistics, scales and reciprocals pass through shared memory, so that no
+// per-row array lives in registers across an element loop (with 8 rows
+// unrolled the register form spilled to local memory inside those loops,
+// ~20-70 us per phase).
+template <int MM>
+__device__ __noinline__ void mk_prep_rows(const ec_mk_params &p, const float *src, int K, int Kp, bool from_embed,
+                                          const float *g, const float *b, int ct) {
+    const Sm S = sm_of(p);
+    const int nM = p.M;
+    const int lane = ct & 31, w = ct >> 5;
+    float *st = S.stage;
+    float *gs = S.nrm, *bs = S.nrm + ((K + 3) & ~3);
+    if (g) {
+        stage_issue(gs, g, K, ct);
+        if (b) stage_issue(bs, b, K, ct);
+    }
+    if (!from_embed) stage_issue(st, src, nM * K, ct);
+    else FOR_TOK(m) FOR_K(k, K) st[m * K + k] = mk_embed(p, S.ltok[m], S.lpos[m], k);
+    cpa_wait_all();
+    cons_sync();
+    double *part = S.redd;                      // [NCW][MT] per-warp partial sums
+    double *mean = S.redd + NCW * MT, *rstd = mean + MT;
+    float *pmax = S.redf;                       // [NCW][MT] per-warp maxima
+    float *rcp = S.redf + NCW * MT;
+    if (g) {
+#pragma unroll 1
+        for (int m = 0; m < nM; ++m) {
+            double s1 = 0.0;
+            FOR_K(k, K) {
+                const double d = (double)st[m * K + k];
+                s1 = b ? __dadd_rn(s1, d) : __dadd_rn(s1, __dmul_rn(d, d));
+            }
+            s1 = ec_warp_sum_d(s1);
+            if (lane == 0) part[w * MT + m] = s1;
+        }
+        cons_sync();
+        if (ct < nM) {
+            double t = 0.0;
+            for (int i = 0; i < NCW; ++i) t = __dadd_rn(t, part[i * MT + ct]);
+            if (b) mean[ct] = __ddiv_rn(t, (double)K);
+            else {
+                mean[ct] = 0.0;
+                rstd[ct] = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(t, (double)K), p.eps)));
+            }
+        }
+        cons_sync();
+        if (b) {
+#pragma unroll 1
+            for (int m = 0; m < nM; ++m) {
+                const double mu = mean[m];
+                double s2 = 0.0;
+                FOR_K(k, K) {
+                    const double d = __dsub_rn((double)st[m * K + k], mu);
+                    s2 = __dadd_rn(s2, __dmul_rn(d, d));
+                }
+                s2 = ec_warp_sum_d(s2);
+                if (lane == 0) part[w * MT + m] = s2;
+            }
+            cons_sync();
+            if (ct < nM) {
+                double t = 0.0;
+                for (int i = 0; i < NCW; ++i) t = __dadd_rn(t, part[i * MT + ct]);
+                rstd[ct] = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(t, (double)K), p.eps)));
+            }
+            cons_sync();
+        }
+#pragma unroll 1
+        for (int m = 0; m < nM; ++m) {
+            const double mu = mean[m], rs = rstd[m];
+            float mx = 0.0f;
+            float4 *r4 = reinterpret_cast<float4 *>(st + (size_t)m * K);
+            FOR_K(c, K >> 2) {
+                float e[4];
+                *reinterpret_cast<float4 *>(e) = r4[c];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int k = 4 * c + j;
+                    const double d = b ? __dsub_rn((double)e[j], mu) : (double)e[j];
+                    const float t = (float)__dmul_rn(d, rs);
+                    e[j] = b ? __fadd_rn(__fmul_rn(t, gs[k]), bs[k]) : __fmul_rn(t, gs[k]);
+                    mx = ec_max_keep(mx, fabsf(e[j]));
+                }
+                r4[c] = *reinterpret_cast<const float4 *>(e);
+            }
+            mx = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(mx)));
+            if (lane == 0) pmax[w * MT + m] = mx;
+        }
+    } else {
+#pragma unroll 1
+        for (int m = 0; m < nM; ++m) {
+            float mx = 0.0f;
+            const float4 *r4 = reinterpret_cast<const float4 *>(st + (size_t)m * K);
+            FOR_K(c, K >> 2) {
+                const float4 v = r4[c];
+                mx = ec_max_keep(ec_max_keep(ec_max_keep(ec_max_keep(mx, fabsf(v.x)), fabsf(v.y)), fabsf(v.z)), fabsf(v.w));
+            }
+            mx = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(mx)));
+            if (lane == 0) pmax[w * MT + m] = mx;
+        }
+    }
+    cons_sync();
+    if (ct < nM) {
+        float t = pmax[ct];
+        for (int i = 1; i < NCW; ++i) t = ec_max_keep(t, pmax[i * MT + ct]);
+        const float sc = t > 0.0f ? __fdiv_rn(t, 127.0f) : 1.0f;
+        S.asc[ct] = sc;
+        rcp[ct] = __fdiv_rn(1.0f, sc);
+    }
+    cons_sync();
+    int8_t *xq = reinterpret_cast<int8_t *>(S.xbuf);
+#pragma unroll 1
+    for (int m = 0; m < nM; ++m) {
+        const float sc = S.asc[m], r = rcp[m];
+        const float4 *r4 = reinterpret_cast<const float4 *>(st + (size_t)m * K);
+        char4 *q4 = reinterpret_cast<char4 *>(xq + (size_t)m * Kp);
+        FOR_K(c, Kp >> 2) {
+            char4 o = make_char4(0, 0, 0, 0);
+            if (4 * c < K) {
+                const float4 v = r4[c];
+                o = make_char4((signed char)ec_quant_fast(v.x, sc, r), (signed char)ec_quant_fast(v.y, sc, r),
+                               (signed char)ec_quant_fast(v.z, sc, r), (signed char)ec_quant_fast(v.w, sc, r));
+            }
+            q4[c] = o;
+        }
+    }
+    cons_sync();
+}
+
 // Int8 operand of one phase in a single pass, shared by the four per-layer
 // call sites so that one copy of the code serves them all: the K-wide rows
 // come from `src` (o / down inputs) or are the norm of the residual rows
@@ -487,6 +617,10 @@ __device__ __noinline__ void mk_operand(const ec_mk_params &p, const float *src,
 template <int MM>
 __device__ __noinline__ void mk_prep(const ec_mk_params &p, const float *src, int K, int Kp, bool from_embed,
                                      const float *g, const float *b, int ct) {
+    if constexpr (MM >= 4) {
+        mk_prep_rows<MM>(p, src, K, Kp, from_embed, g, b, ct);
+        return;
+    }
     const Sm S = sm_of(p);
     const int nM = p.M;
     float *st = S.stage;

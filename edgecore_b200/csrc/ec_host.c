@@ -240,6 +240,9 @@ typedef struct ec_dev {
     float *as;
     void *split;          /* 16-bit activation parts for the tensor-core GEMMs */
     size_t split_bytes;
+    int *acc32;           /* split-K int8 GEMMs: int32 tile sums and tile counters, kept zero */
+    size_t acc32_elems;
+    unsigned *tile_cnt;
     float *attn_part;
     size_t attn_part_floats;
     float *logits;
@@ -541,6 +544,8 @@ static int ec_mk_build(ec_dev *d)
     return 0;
 }
 
+#define EC_TILE_CNT 256
+
 /* ---- workspaces ---- */
 
 static void ec_free_work(ec_dev *d)
@@ -587,6 +592,14 @@ static int ec_ensure(ec_dev *d, int M)
     if (cap >= EC_TC_MIN_M) {   /* the lm_head is always 16-bit; bf16 needs three parts */
         d->split_bytes = ec_gemm_tc_split_bytes(d->prec == 2 ? EC_W_BF16 : EC_W_F16, cap, kmax);
         CK(cudaMalloc(&d->split, d->split_bytes));
+    }
+    if (cap >= EC_TC_MIN_M && !d->acc32) {
+        /* split-K happens for outputs of at most num_sms/2 tiles of 128 x 256 */
+        d->acc32_elems = (size_t)(d->num_sms / 2) * 128 * 256;
+        CK(cudaMalloc((void **)&d->acc32, d->acc32_elems * 4));
+        CK(cudaMemset(d->acc32, 0, d->acc32_elems * 4));
+        CK(cudaMalloc((void **)&d->tile_cnt, EC_TILE_CNT * 4));
+        CK(cudaMemset(d->tile_cnt, 0, EC_TILE_CNT * 4));
     }
     CK(cudaMalloc((void **)&d->d_tok, (size_t)cap * 4));
     CK(cudaMalloc((void **)&d->d_pos, (size_t)cap * 4));
@@ -682,6 +695,7 @@ static void ec_dev_free(ec_dev *d)
     cudaFree(d->amax_v); cudaFree(d->amax_i);
     cudaFree(d->attn_part); cudaFree(d->logits); cudaFree(d->amax_part);
     cudaFree(d->d_hist); cudaFree(d->taps); cudaFree(d->d_counter);
+    cudaFree(d->acc32); cudaFree(d->tile_cnt);
     for (int k = 0; k < 2; k++)
         if (d->bg[k].exec) cudaGraphExecDestroy(d->bg[k].exec);
     cudaFreeHost(d->h_logits);
@@ -1074,6 +1088,7 @@ static int ec_linear(ec_dev *d, const ec_lin *l, const float *X, int ldx, int M,
     }
     g.out = out; g.ldo = ldo; g.epi = epi;
     g.split = d->split; g.split_bytes = d->split_bytes;
+    g.acc32 = d->acc32; g.acc32_elems = d->acc32_elems; g.tile_cnt = d->tile_cnt; g.cnt_elems = EC_TILE_CNT;
     CK(ec_launch_gemm(&g, st));
     ec_prof_end(d, pi);
     return 0;
@@ -1615,6 +1630,33 @@ EC_EXPORT int ec_decode_batch(GPT2 *g, int *d_tokens, int *d_positions, int n_st
             return -1;
         }
         if (p + n_steps > maxp) maxp = p + n_steps;
+    }
+    if (M <= EC_MK_MT) {   /* up to 8 streams: the persistent decode kernel, one launch for all steps */
+        int max_len = maxp;
+        if (d->window > 0 && max_len > d->window) max_len = d->window;
+        ec_mk_params mp;
+        if (ec_mk_plan(d, M, ec_len_bucket(d, max_len), &mp) == 0) {
+            if (d_out_ids && d->hist_cap < n_steps * M) {
+                cudaFree(d->d_hist);
+                d->d_hist = NULL;
+                d->ws_gen++;
+                CK(cudaMalloc((void **)&d->d_hist, (size_t)n_steps * M * 4));
+                d->hist_cap = n_steps * M;
+            }
+            for (int m = 0; m < M; m++) d->h_in[2 * M + m] = m;
+            CK(cudaMemcpyAsync(d->d_tok, d_tokens, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
+            CK(cudaMemcpyAsync(d->d_pos, d->h_in + M, (size_t)M * 4, cudaMemcpyHostToDevice, d->stream));
+            CK(cudaMemcpyAsync(d->d_slot, d->h_in + 2 * M, (size_t)M * 4, cudaMemcpyHostToDevice, d->stream));
+            mp.hist = d_out_ids ? d->d_hist : NULL;
+            mp.advance = 1;
+            if (ec_mk_run(d, &mp, n_steps)) return -1;
+            CK(cudaMemcpyAsync(d_tokens, d->d_tok, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
+            CK(cudaMemcpyAsync(d_positions, d->d_pos, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
+            if (d_out_ids)
+                CK(cudaMemcpyAsync(d_out_ids, d->d_hist, (size_t)n_steps * M * 4, cudaMemcpyDeviceToDevice,
+                                   d->stream));
+            return 0;
+        }
     }
     const int maxlen = ec_batch_len(d, maxp);
     const int chunk = ec_lm_chunk(d, M);

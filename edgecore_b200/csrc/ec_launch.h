@@ -93,6 +93,10 @@ typedef struct {
     void *split; size_t split_bytes;          /* 16-bit weights on tensor cores: workspace
                                                  of ec_gemm_tc_split_bytes() bytes,
                                                  256-byte aligned (NULL: SIMT kernel) */
+    int *acc32; size_t acc32_elems;           /* int8 on tensor cores, split over K when the
+                                                 output has few tiles: int32 [M][N] sums, all
+                                                 zero between calls (NULL: no split) */
+    unsigned *tile_cnt; int cnt_elems;        /* per-tile split counters, zero between calls */
 } ec_gemm_args;
 int ec_launch_gemm(const ec_gemm_args *a, cudaStream_t stream);
 

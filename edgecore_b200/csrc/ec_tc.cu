@@ -32,6 +32,11 @@
 //              split the columns), scale and bias per element, transpose
 //              through shared memory, coalesced 16-byte stores (store,
 //              residual add or GELU)
+// int8 GEMMs whose output has few tiles (decode-sized M) split K over
+// `ksplit` CTAs per tile: each adds its int32 partial tile into a zeroed
+// int32 workspace with atomics (integer sums: exact, in any order), and the
+// CTA that finishes a tile last (a per-tile counter) applies the epilogue to
+// the total and zeroes the workspace and the counter again.
 // Loads never use cluster multicast; every wait is bounded and TMEM is freed
 // on every path.
 #include "ec_common.cuh"
@@ -148,11 +153,94 @@ struct TcMaps {
     CUtensorMap b;      // weights
 };
 
+// AND of `v` over the 256 epilogue threads (named barrier 1): every
+// epilogue warp takes the same decision, so that none of them waits at a
+// later named barrier for a warp that has left.
+__device__ __forceinline__ bool epi_all(bool v) {
+    int r;
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.s32 p, %1, 0;\n\tbar.red.and.pred p, 1, 256, p;\n\t"
+                 "selp.s32 %0, 1, 0, p;\n\t}" : "=r"(r) : "r"((int)v) : "memory");
+    return r != 0;
+}
+
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// Split-K, part 1: this warp's rows (TMEM lane group lg) and column half ch
+// of the int32 partial tile at `taddr`, transposed through `st`, added into
+// a.acc32 [M][N] with coalesced atomics.
+template <int BN>
+__device__ __forceinline__ void split_tile_add(const ec_gemm_args &a, uint32_t taddr, int m0, int n0, int lg, int ch,
+                                               int lane, float *st) {
+    constexpr int HALF = BN / 2;
+    int *sti = reinterpret_cast<int *>(st);
+    for (int c0 = ch * HALF; c0 < (ch + 1) * HALF && n0 + c0 < a.N; c0 += EPI_COLS) {
+        uint32_t r[16];
+        tmem_ld16(taddr + (uint32_t)c0, r);
+#pragma unroll
+        for (int j = 0; j < EPI_COLS; j += 4)
+            *reinterpret_cast<int4 *>(sti + lane * EPI_LD + j) = make_int4((int)r[j], (int)r[j + 1], (int)r[j + 2], (int)r[j + 3]);
+        __syncwarp();
+#pragma unroll
+        for (int pass = 0; pass < 4; ++pass) {
+            const int row = pass * 8 + (lane >> 2), c4 = (lane & 3) * 4;
+            const int m = m0 + lg * 32 + row, n = n0 + c0 + c4;
+            if (m >= a.M) continue;
+            int *dst = a.acc32 + (size_t)m * a.N + n;
+            for (int e = 0; e < 4 && n + e < a.N; ++e)
+                asm volatile("red.relaxed.gpu.global.add.s32 [%0], %1;" ::"l"(dst + e), "r"(sti[row * EPI_LD + c4 + e]) : "memory");
+        }
+        __syncwarp();
+    }
+    __threadfence();   // this thread's additions before the tile counter below
+}
+
+// Split-K, part 2 (all 256 epilogue threads, et = 0..255): count this CTA's
+// part of the tile; the CTA that completes it applies the int8 epilogue of
+// the non-split path to the int32 totals, bit for bit, and zeroes the
+// workspace and the counter for the next call.
+__device__ __forceinline__ void split_tile_finish(const ec_gemm_args &a, const float *row_scale, int tile, int m0,
+                                                  int n0, int bn, int ksplit, volatile int *flag_last, int et) {
+    epi_sync();
+    if (et == 0) *flag_last = atomicAdd(a.tile_cnt + tile, 1u) == (unsigned)(ksplit - 1);
+    epi_sync();
+    if (!*flag_last) return;
+    __threadfence();
+    // thread et: column et % bn of the tile, rows et / bn, + 256 / bn, ...;
+    // eight rows' loads in flight per thread
+    const int rows = min(BM, a.M - m0);
+    const int c = et % bn, r0 = et / bn, rstep = 256 / bn, n = n0 + c;
+    if (n < a.N) {
+        const float ws = a.wscale ? __ldg(a.wscale + n) : 1.0f;
+        const float bs = a.bias ? __ldg(a.bias + n) : 0.0f;
+        for (int rb = r0; rb < rows; rb += 8 * rstep) {
+            int acc[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int r = rb + i * rstep;
+                acc[i] = r < rows ? __ldcg(a.acc32 + (size_t)(m0 + r) * a.N + n) : 0;
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int r = rb + i * rstep;
+                if (r >= rows) break;
+                const int m = m0 + r;
+                __stcg(a.acc32 + (size_t)m * a.N + n, 0);
+                const float v = __fadd_rn(bs, __fmul_rn(__fmul_rn(__int2float_rn(acc[i]), __ldg(row_scale + m)), ws));
+                float *o = a.out + (size_t)m * a.ldo + n;
+                *o = epi_apply(a.epi, a.epi == EC_EPI_RESID ? *o : 0.0f, v);
+            }
+        }
+    }
+    epi_sync();
+    if (et == 0) a.tile_cnt[tile] = 0u;
+}
+
 // row_scale: a_scale (int8) or the power-of-two row scale of the split (16-bit)
 template <int WT>
 __global__ void __launch_bounds__(THREADS, 1)
 k_gemm_tc(const __grid_constant__ TcMaps maps, const ec_gemm_args a, const float *row_scale,
-          int flags) {   // bit 0: 16-byte aligned output rows
+          int flags,     // bit 0: 16-byte aligned output rows
+          int ksplit) {  // CTAs per output tile over K (int8 only; 1: no split)
     constexpr int S = TcCfg<WT>::S, BN = TcCfg<WT>::BN, STAGES = TcCfg<WT>::STAGES;
     constexpr int SB = stage_bytes<WT>();
     constexpr int KSTEP = 32;                                      // bytes of K per MMA instruction (both kinds)
@@ -171,13 +259,14 @@ k_gemm_tc(const __grid_constant__ TcMaps maps, const ec_gemm_args a, const float
     volatile int *stop = reinterpret_cast<volatile int *>(tmem_slot + 1);
     int *issued = const_cast<int *>(stop) + 1;   // k-blocks whose TMA loads were issued ...
     int *consumed = issued + 1;                  // ... and whose loads the MMA thread waited for
+    volatile int *flag_last = consumed + 1;      // split-K: this CTA completed the tile
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kbytes = a.Kp * TcCfg<WT>::ELT;
     const int nk = (kbytes + BKB - 1) / BKB;
     const int kel = BKB / TcCfg<WT>::ELT;                          // K elements per stage
     const int mt = (a.M + BM - 1) / BM, nt = (a.N + BN - 1) / BN;
-    const int tiles = mt * nt;
+    const int tiles = mt * nt, items = tiles * ksplit;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -206,9 +295,11 @@ k_gemm_tc(const __grid_constant__ TcMaps maps, const ec_gemm_args a, const float
     if (warp == 0) {
         if (lane == 0) {   // TMA producer, one ring across all tiles of this CTA
             int g = 0;
-            for (int tile = blockIdx.x; tile < tiles && !*stop; tile += gridDim.x) {
+            for (int it = blockIdx.x; it < items && !*stop; it += gridDim.x) {
+                const int tile = it / ksplit, sp = it - tile * ksplit;
                 const int m0 = (tile / nt) * BM, n0 = (tile % nt) * BN;
-                for (int kb = 0; kb < nk; ++kb, ++g) {
+                const int kb0 = sp * nk / ksplit, kb1 = (sp + 1) * nk / ksplit;
+                for (int kb = kb0; kb < kb1; ++kb, ++g) {
                     const int s = g % STAGES;
                     if (g >= STAGES && !tc_wait(&empty[s], (uint32_t)((g / STAGES - 1) & 1), stop)) break;
                     const uint32_t st = base + (uint32_t)(s * SB);
@@ -223,13 +314,15 @@ k_gemm_tc(const __grid_constant__ TcMaps maps, const ec_gemm_args a, const float
     } else if (warp == 1) {
         if (lane == 0) {   // MMA issuer
             int g = 0, tc = 0;
-            for (int tile = blockIdx.x; tile < tiles && !*stop; tile += gridDim.x, ++tc) {
+            for (int it = blockIdx.x; it < items && !*stop; it += gridDim.x, ++tc) {
+                const int sp = it % ksplit;
+                const int kb0 = sp * nk / ksplit, kb1 = (sp + 1) * nk / ksplit;
                 const int b = tc & 1;
                 if (tc >= 2 && !tc_wait(&acce[b], (uint32_t)((tc / 2 - 1) & 1), stop)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + (uint32_t)(b * BN);
                 bool ok = true;
-                for (int kb = 0; kb < nk; ++kb, ++g) {
+                for (int kb = kb0; kb < kb1; ++kb, ++g) {
                     const int s = g % STAGES;
                     if (!tc_wait(&full[s], (uint32_t)((g / STAGES) & 1), stop)) { ok = false; break; }
                     tc_fence_after();
@@ -239,7 +332,7 @@ k_gemm_tc(const __grid_constant__ TcMaps maps, const ec_gemm_args a, const float
                     for (int k = 0; k < BKB / KSTEP; ++k)     // +2 in 16-byte units per 32 bytes of K
 #pragma unroll
                         for (int p = 0; p < S; ++p)
-                            mma<WT>(d, sw128_desc(st + p * A_BYTES) + 2 * k, db + 2 * k, (kb | k | p) != 0);
+                            mma<WT>(d, sw128_desc(st + p * A_BYTES) + 2 * k, db + 2 * k, ((kb - kb0) | k | p) != 0);
                     mma_commit(ec_smem_u32(&empty[s]));   // stage reusable once these MMAs have read it
                     *consumed = g + 1;
                 }
@@ -258,9 +351,24 @@ k_gemm_tc(const __grid_constant__ TcMaps maps, const ec_gemm_args a, const float
         float *cws = cst + (size_t)(warp - 2) * BN, *cb = cws + HALF;   // this warp's columns
         const bool vec_out = flags & 1;
         int tc = 0;
-        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++tc) {
+        for (int it = blockIdx.x; it < items; it += gridDim.x, ++tc) {
+            const int tile = it / ksplit;
             const int m0 = (tile / nt) * BM, n0 = (tile % nt) * BN;
             const int b = tc & 1;
+            if (WT == EC_W_I8 && ksplit > 1) {
+                int ready = 0;
+                if (lane == 0) ready = tc_wait(&accf[b], (uint32_t)((tc / 2) & 1), stop) && !*stop;
+                ready = __shfl_sync(0xffffffffu, ready, 0);
+                if (!epi_all(ready != 0)) break;
+                tc_fence_after();
+                split_tile_add<BN>(a, tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)(b * BN), m0, n0, lg, ch, lane, st);
+                // this warp is done with accumulator b
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(ec_smem_u32(&acce[b])) : "memory");
+                split_tile_finish(a, row_scale, tile, m0, n0, BN, ksplit, flag_last, (int)threadIdx.x - 64);
+                continue;
+            }
             // Issue the tile's constants before waiting for its accumulator, so
             // their latency hides behind the MMAs: the row scale of this lane
             // and w_scale / bias of the warp's columns (lane j: j, j+32, ...).
@@ -454,9 +562,26 @@ int launch(const ec_gemm_args &a, const void *const *aparts, const float *row_sc
     if (rc) return rc;
     const long long tiles = (long long)((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
     if (tiles > 0x7fffffffLL) return (int)cudaErrorInvalidValue;
-    const int grid = (int)(tiles < (long long)g_sms[dev] ? tiles : g_sms[dev]);
+    const int sms = g_sms[dev];
+    // split K when the output is one row of tiles (M <= 64) and has fewer
+    // tiles than half the SMs: at least 4 k-blocks of 128 bytes per split, at
+    // most 8 splits and one CTA per SM in total.  Every split adds its whole
+    // partial tile with atomics, so more rows or splits cost more than they
+    // save (measured: decode of 32 streams 2.93 -> 2.76 ms per step, of 128
+    // streams 3.03 -> 3.83 ms).
+    int ksplit = 1;
+    const int nk = (a.Kp * ELT + BKB - 1) / BKB;
+    if (WT == EC_W_I8 && a.M <= 64 && a.acc32 && a.tile_cnt && 2 * tiles <= sms && tiles <= a.cnt_elems &&
+        (size_t)a.M * a.N <= a.acc32_elems) {
+        ksplit = sms / (int)tiles;
+        if (ksplit > nk / 4) ksplit = nk / 4;
+        if (ksplit > 8) ksplit = 8;
+        if (ksplit < 1) ksplit = 1;
+    }
+    const long long items = tiles * ksplit;
+    const int grid = (int)(items < (long long)sms ? items : sms);
     const int flags = (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 && (a.ldo & 3) == 0 ? 1 : 0;
-    k_gemm_tc<WT><<<grid, THREADS, smem_bytes<WT>(), stream>>>(maps, a, row_scale, flags);
+    k_gemm_tc<WT><<<grid, THREADS, smem_bytes<WT>(), stream>>>(maps, a, row_scale, flags, ksplit);
     return (int)cudaGetLastError();
 }
 
