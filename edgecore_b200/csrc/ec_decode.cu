@@ -491,6 +491,44 @@ __device__ __noinline__ void mk_prep_rows(const ec_mk_params &p, const float *sr
     const int lane = ct & 31, w = ct >> 5;
     float *st = S.stage;
     float *gs = S.nrm, *bs = S.nrm + ((K + 3) & ~3);
+    float *pmax = S.redf;                       // [NCW][MT] per-warp maxima
+    if (!g && !from_embed && (size_t)nM * K * 4 > (size_t)p.stage_bytes) {
+        // rows wider than the staging area holds together (the down
+        // projection's input): one row at a time
+        int8_t *xq = reinterpret_cast<int8_t *>(S.xbuf);
+#pragma unroll 1
+        for (int m = 0; m < nM; ++m) {
+            stage_issue(st, src + (size_t)m * K, K, ct);
+            cpa_wait_all();
+            cons_sync();
+            float mx = 0.0f;
+            const float4 *r4 = reinterpret_cast<const float4 *>(st);
+            FOR_K(c, K >> 2) {
+                const float4 v = r4[c];
+                mx = ec_max_keep(ec_max_keep(ec_max_keep(ec_max_keep(mx, fabsf(v.x)), fabsf(v.y)), fabsf(v.z)), fabsf(v.w));
+            }
+            mx = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(mx)));
+            if (lane == 0) pmax[w * MT + m] = mx;
+            cons_sync();
+            float t = pmax[m];
+            for (int i = 1; i < NCW; ++i) t = ec_max_keep(t, pmax[i * MT + m]);
+            const float sc = t > 0.0f ? __fdiv_rn(t, 127.0f) : 1.0f;
+            const float r = __fdiv_rn(1.0f, sc);
+            if (ct == 0) S.asc[m] = sc;
+            char4 *q4 = reinterpret_cast<char4 *>(xq + (size_t)m * Kp);
+            FOR_K(c, Kp >> 2) {
+                char4 o = make_char4(0, 0, 0, 0);
+                if (4 * c < K) {
+                    const float4 v = r4[c];
+                    o = make_char4((signed char)ec_quant_fast(v.x, sc, r), (signed char)ec_quant_fast(v.y, sc, r),
+                                   (signed char)ec_quant_fast(v.z, sc, r), (signed char)ec_quant_fast(v.w, sc, r));
+                }
+                q4[c] = o;
+            }
+            cons_sync();   // the staging area takes the next row
+        }
+        return;
+    }
     if (g) {
         stage_issue(gs, g, K, ct);
         if (b) stage_issue(bs, b, K, ct);
@@ -501,7 +539,6 @@ __device__ __noinline__ void mk_prep_rows(const ec_mk_params &p, const float *sr
     cons_sync();
     double *part = S.redd;                      // [NCW][MT] per-warp partial sums
     double *mean = S.redd + NCW * MT, *rstd = mean + MT;
-    float *pmax = S.redf;                       // [NCW][MT] per-warp maxima
     float *rcp = S.redf + NCW * MT;
     if (g) {
 #pragma unroll 1
@@ -1355,7 +1392,9 @@ __global__ void __launch_bounds__(EC_MK_THREADS, 1) k_decode(const __grid_consta
     uint32_t t = 0;
     unsigned target = 0;
     // int8 layers: the single-pass operand builder (its inputs must fit the staging area)
-    const bool I8P = LWT == EC_W_I8 && (size_t)M * (size_t)S.lay[0].down.K * 4 <= (size_t)p.stage_bytes &&
+    // (4-8 rows: mk_prep_rows stages the down-projection input one row at a time)
+    const bool I8P = LWT == EC_W_I8 &&
+                     (size_t)(MM >= 4 ? 1 : M) * (size_t)S.lay[0].down.K * 4 <= (size_t)p.stage_bytes &&
                      (size_t)M * (size_t)p.E * 4 <= (size_t)p.stage_bytes && (p.E & 3) == 0 && (S.lay[0].down.K & 3) == 0;
     const Rg xr = S.rg[MI_O];   // residual rows owned by this CTA
     const int xn = xr.r1 - xr.r0;

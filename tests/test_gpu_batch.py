@@ -205,3 +205,41 @@ def _prefill_slice(model, toks, lens):
     lg = model.forward(t, p, s)
     last = np.cumsum(lens) - 1
     return np.argmax(lg[last], axis=1).astype(np.int32), np.asarray(lens, np.int32), lg[last]
+
+
+@pytest.mark.parametrize("B", [3, 8])
+def test_decode_batch_small_against_cpu_oracle(int8_models, cuda, B):
+    """Up to 8 streams ec_decode_batch runs the persistent decode kernel with
+    each slot at its own position: greedy ids of STEPS steps against the CPU
+    restatement (identical except where the restatement's top-2 margin is
+    below 1e-3 of the row max)."""
+    torch = cuda
+    from oracle.oracle import Restatement
+    ro = Restatement()
+    for key, (spec, path) in int8_models.items():
+        rng = np.random.default_rng(11)
+        lens = rng.integers(3, 12, B)
+        toks = [synth.prompt_ids(spec.vocab, int(n), seed=500 + b) for b, n in enumerate(lens)]
+        r = ro.open(path, batch_cap=B, max_ctx=spec.n_ctx)
+        cur_r, pos_r, _ = _prefill(r, toks, lens)
+        with ec.Model(path, batch_cap=B) as m:
+            cur, pos, _ = _prefill(m, toks, lens)
+            assert np.array_equal(cur, cur_r), key
+            d_tok = torch.from_numpy(cur).cuda()
+            d_pos = torch.from_numpy(pos).cuda()
+            d_ids = torch.zeros((STEPS, B), dtype=torch.int32, device="cuda")
+            torch.cuda.synchronize()
+            m.decode_batch(d_tok, d_pos, STEPS, d_ids)
+            torch.cuda.synchronize()
+            assert ec.device_error_take() == 0
+            got = d_ids.cpu().numpy()
+            assert np.array_equal(d_pos.cpu().numpy(), pos + STEPS)
+        for s in range(STEPS):
+            lg = r.forward(cur_r, pos_r, np.arange(B, dtype=np.int32))
+            want = np.argmax(lg, axis=1).astype(np.int32)
+            for b in range(B):
+                if got[s, b] != want[b]:
+                    top2 = np.sort(lg[b])[-2:]
+                    assert (top2[1] - top2[0]) / np.abs(lg[b]).max() < 1e-3, (key, s, b)
+            cur_r, pos_r = got[s].astype(np.int32), pos_r + 1
+        r.close()
