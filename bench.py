@@ -460,16 +460,34 @@ def cpu_baseline_leg(args) -> dict:
 SWEEP_SHAPES = ((1152, 896), (896, 896), (4864, 896), (896, 4864), (151936, 896))
 
 
-def time_op(launch, nbuf: int, reps: int, warmup: int, stream) -> float:
+def time_op(launch, nbuf: int, reps: int, warmup: int, stream, graph: bool = True) -> float:
     """Mean µs per launch of `launch(i)` (i selects one of `nbuf` rotating
     operand sets whose total exceeds L2, so every launch reads HBM), CUDA
-    events on `stream` around `reps` back-to-back launches."""
+    events on `stream` around `reps` back-to-back launches.  With `graph`
+    the launches are captured once into a CUDA graph and the graph replay is
+    timed, so the figure is device time (kernels back to back) rather than
+    the host cost of `reps` library calls."""
     import torch
     with torch.cuda.stream(stream):
         for i in range(warmup):
             launch(i % nbuf)
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream, capture_error_mode="relaxed"):
+            for i in range(reps):
+                launch(i % nbuf)
+        with torch.cuda.stream(stream):   # a graph replays on the current stream
+            g.replay()
+            torch.cuda.synchronize()
+            start.record(stream)
+            g.replay()
+            end.record(stream)
         torch.cuda.synchronize()
+        del g
+        return start.elapsed_time(end) * 1e3 / reps
+    with torch.cuda.stream(stream):
         start.record(stream)
         for i in range(reps):
             launch(i % nbuf)
@@ -989,8 +1007,8 @@ def op_sweep_results(args, cpu_seconds: float):
                 "hbm_frac": algo / us / 1e3 / peak, "hbm_peak_gbs": peak, "peak_source": peak_kind,
                 "tops" if wt == 0 else "tflops": flops / us / 1e6,
                 "path": "weight-streaming GEMV" if M <= 8 else ("tcgen05" if M >= 32 else "SIMT"),
-                "timing": f"CUDA events, {max(10, 2 * nbuf)} back-to-back launches rotating {nbuf} weight "
-                          f"copies ({nbuf * wbytes / 2**20:.0f} MiB > L2)"}
+                "timing": f"CUDA events around one replay of a CUDA graph of {max(10, 2 * nbuf)} back-to-back "
+                          f"launches rotating {nbuf} weight copies ({nbuf * wbytes / 2**20:.0f} MiB > L2)"}
         if ref is not None and M * N * K <= 2e10:
             Ah = A.cpu().numpy()
             Wh = Ws[0].cpu().numpy()

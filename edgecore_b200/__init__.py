@@ -52,6 +52,9 @@ def _declare(lib: C.CDLL) -> None:
         "ec_lm_shard_keys": (_i, [_vp, _vp, _i, _vp]),
         "ec_keys_advance": (_i, [_vp, _vp, _i, _vp, _vp]),
         "ec_batch_graph_kernels": (_i, [_vp, _i]),
+        "ec_model_packed": (C.c_longlong, [_vp, _i, _i, _vp, C.c_size_t, _vp]),
+        "ec_kv_release": (_i, [_vp, _i]),
+        "ec_kv_info": (_i, [_vp, _vp]),
         "ec_model_set_taps": (_i, [_vp, _i]),
         "ec_model_get_taps": (_i, [_vp, _vp, _i]),
         "ec_model_set_vocab_shard": (_i, [_vp, _i, _i]),
@@ -342,6 +345,32 @@ class Model:
     def keys_advance(self, d_keys, M: int, d_tokens, d_positions) -> None:
         """tokens[m] = index in keys[m], positions[m] += 1 (device arrays)."""
         self._check(self.lib.ec_keys_advance(self.h, _ptr(d_keys), int(M), _ptr(d_tokens), _ptr(d_positions)))
+
+    def kv_release(self, slot: int = -1) -> None:
+        """Return the KV pages of `slot` (all slots when < 0) to the arena."""
+        self._check(self.lib.ec_kv_release(self.h, int(slot)))
+
+    def kv_info(self) -> dict:
+        """{pages, free, page_positions, pages_per_slot} of the paged KV arena."""
+        info = np.zeros(4, np.int32)
+        self._check(self.lib.ec_kv_info(self.h, _ptr(info)))
+        return dict(zip(("pages", "free", "page_positions", "pages_per_slot"), (int(v) for v in info)))
+
+    PACKED = {"qkv": 0, "o": 1, "up": 2, "down": 3, "lm_head": 4}
+
+    def packed(self, layer: int, which: str) -> tuple[np.ndarray, dict]:
+        """The device-packed rows of one linear (ec_model_packed): uint8
+        [N][ldw * element bytes] and {N, K, Kp, ldw, elt}."""
+        info = np.zeros(5, np.int32)
+        w = self.PACKED[which]
+        n = self.lib.ec_model_packed(self.h, int(layer), w, None, 0, _ptr(info))
+        if n < 0:
+            raise RuntimeError(last_error())
+        out = np.empty(int(n), np.uint8)
+        if self.lib.ec_model_packed(self.h, int(layer), w, _ptr(out), out.size, _ptr(info)) < 0:
+            raise RuntimeError(last_error())
+        N, K, Kp, ldw, elt = (int(v) for v in info)
+        return out.reshape(N, ldw * elt), {"N": N, "K": K, "Kp": Kp, "ldw": ldw, "elt": elt}
 
     def batch_graph_kernels(self, kind: int) -> int:
         """Kernel launches in the captured step graph (0: decode_batch, 1: batch_hidden)."""

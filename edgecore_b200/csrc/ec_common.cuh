@@ -8,6 +8,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include "ec_launch.h"
+
 #define EC_DEV __device__ __forceinline__
 
 // Error codes written to the library error word (first error wins).
@@ -139,6 +141,16 @@ EC_DEV float ec_dot8(const uint4 w, const float4 x0, const float4 x1, float t) {
     t = fmaf(f[4], x1.x, t); t = fmaf(f[5], x1.y, t);
     t = fmaf(f[6], x1.z, t); t = fmaf(f[7], x1.w, t);
     return t;
+}
+
+// Paged KV arena: a layer's K (or V) cache is [pages][EC_KV_PAGE][kv] fp16,
+// and pt[slot * mp + pos / EC_KV_PAGE] is the physical page holding
+// positions [64 j, 64 j + 64) of a slot (the host maps pages before every
+// launch that touches them; EC_KV_PAGE is 64, ec_launch.h).  Row of (slot,
+// pos) in the arena:
+EC_DEV size_t ec_kv_row(const int *pt, int mp, int slot, int pos) {
+    const int pg = __ldg(pt + (size_t)slot * mp + (pos >> 6));
+    return (size_t)(pg < 0 ? 0 : pg) * EC_KV_PAGE + (size_t)(pos & (EC_KV_PAGE - 1));
 }
 
 EC_DEV bool ec_mbar_try_wait(uint64_t *bar, uint32_t parity) {

@@ -69,8 +69,13 @@ enum { MI_QKV = 0, MI_O = 1, MI_UP = 2, MI_DOWN = 3, MI_LM = 4, MI_N = 5 };
 #define FOR_K(k, n) _Pragma("unroll 1") for (int k = ct; k < (n); k += NCT)
 
 struct Lay {
-    uint32_t ring, xbuf, stage, nrm, rope, xown, redd, redf, redi, asc, ints, bars, lays, par, total;
+    uint32_t ring, xbuf, stage, nrm, rope, xown, redd, redf, redi, asc, ints, lpt, bars, lays, par, total;
 };
+
+// KV page-table rows of the token rows' slots kept in shared memory (fixed
+// for a launch: the host maps every page a launch touches beforehand) when a
+// slot has at most PT_SMEM pages; else read from global memory.
+constexpr int PT_SMEM = 64;
 
 __host__ __device__ inline uint32_t al16(uint32_t v) { return (v + 15u) & ~15u; }
 
@@ -80,6 +85,7 @@ __host__ __device__ inline Lay mk_layout(int xbuf_bytes, int stage_bytes, int n_
     // in the helpers), then the regions sized by the model
     uint32_t o = 0;
     L.ints = o;  o += al16((3 * MT + 4 + 2 * MI_N) * 4);
+    L.lpt = o;   o += MT * PT_SMEM * 4;
     L.bars = o;  o += 2 * STAGES * 8;
     L.redd = o;  o += 2 * NCW * MT * 8;
     L.redf = o;  o += 2 * NCW * MT * 4;
@@ -113,6 +119,7 @@ struct Sm {
     int *redi;
     float *asc;
     int *ltok, *lpos, *lslot;
+    int *lpt;                 // [MT][PT_SMEM] page-table rows of the token rows' slots
     volatile int *flag;       // [0]: abort
     int *tcount;              // [2]: trace entries written (consumer, producer)
     Rg *rg;                   // [MI_N]: this CTA's row range of each matrix shape
@@ -138,6 +145,7 @@ __device__ __forceinline__ Sm sm_of(const ec_mk_params &p) {
     S.ltok = ints;
     S.lpos = ints + MT;
     S.lslot = ints + 2 * MT;
+    S.lpt = reinterpret_cast<int *>(g_smem + L.lpt);
     S.flag = ints + 3 * MT;
     S.tcount = ints + 3 * MT + 1;
     S.rg = reinterpret_cast<Rg *>(ints + 3 * MT + 4);
@@ -146,6 +154,12 @@ __device__ __forceinline__ Sm sm_of(const ec_mk_params &p) {
     S.lay = reinterpret_cast<const ec_mk_layer *>(g_smem + L.lays);
     S.par = reinterpret_cast<ec_mk_params *>(g_smem + L.par);
     return S;
+}
+
+// Arena row of position `pos` of token row q (slot `slot`).
+__device__ __forceinline__ size_t kv_row_q(const ec_mk_params &p, const Sm &S, int q, int slot, int pos) {
+    const int pg = p.mp <= PT_SMEM ? S.lpt[q * PT_SMEM + (pos >> 6)] : __ldg(p.pt + (size_t)slot * p.mp + (pos >> 6));
+    return (size_t)(pg < 0 ? 0 : pg) * EC_KV_PAGE + (size_t)(pos & (EC_KV_PAGE - 1));
 }
 
 __device__ __forceinline__ Rg mk_range(const ec_mk_mat &m, int c, int G) {
@@ -956,7 +970,7 @@ __device__ __noinline__ uint32_t mk_phase(const ec_mk_params &p, int kind, int l
             const int n = row0 + r0;   // matrix row of this lane's slot
             if (kind == PK_QKV) {
                 const int pos = S.lpos[q], slot = S.lslot[q];
-                const size_t kvo = ((size_t)slot * p.C + pos) * p.kv;
+                const size_t kvo = kv_row_q(p, S, q, slot, pos) * p.kv;
                 if (p.arch == ARCH_Q2) {
                     if (n < p.E + p.kv) {   // rotated pair (i, i + hd/2) of a q or k head
                         const int head = n / p.hd, i2 = (n % p.hd) >> 1;
@@ -1150,16 +1164,17 @@ __device__ __noinline__ void mk_attention(const ec_mk_params &p, int layer, int 
             if (ct == 0) atomicCAS(p.err, 0, ERR_INDEX);
             continue;
         }
-        const uint16_t *kb = kc + ((size_t)slot * p.C + lo) * kv + (size_t)kvh * hd;
-        const uint16_t *vb = vc + ((size_t)slot * p.C + lo) * kv + (size_t)kvh * hd;
+        // cached row of position lo + i: its page, then the row in the page
+        const uint16_t *kb = kc + (size_t)kvh * hd, *vb = vc + (size_t)kvh * hd;
         // the q row and the first K and V chunks in flight together
         for (int d = ct; d < (hd >> 2); d += NCT) cpa16(qs + 4 * d, p.q + (size_t)m * E + (size_t)h * hd + 4 * d);
         {
             const int n0 = min(CH, len);
             for (int e = ct; e < n0 * per; e += NCT) {
                 const int i = e / per, j = e - (e / per) * per;
-                cpa16(kch + (size_t)i * ks + 8 * j, kb + (size_t)i * kv + 8 * j);
-                cpa16(vch + (size_t)i * hd + 8 * j, vb + (size_t)i * kv + 8 * j);
+                const size_t r = kv_row_q(p, S, m, slot, lo + i) * kv;
+                cpa16(kch + (size_t)i * ks + 8 * j, kb + r + 8 * j);
+                cpa16(vch + (size_t)i * hd + 8 * j, vb + r + 8 * j);
             }
         }
         cpa_wait_all();
@@ -1173,7 +1188,7 @@ __device__ __noinline__ void mk_attention(const ec_mk_params &p, int layer, int 
                 cons_sync();   // previous K chunk consumed
                 for (int e = ct; e < n * per; e += NCT) {
                     const int i = e / per, j = e - (e / per) * per;
-                    cpa16(kch + (size_t)i * ks + 8 * j, kb + (size_t)(c0 + i) * kv + 8 * j);
+                    cpa16(kch + (size_t)i * ks + 8 * j, kb + kv_row_q(p, S, m, slot, lo + c0 + i) * kv + 8 * j);
                 }
                 cpa_wait_all();
                 cons_sync();
@@ -1234,7 +1249,7 @@ __device__ __noinline__ void mk_attention(const ec_mk_params &p, int layer, int 
                 cons_sync();   // previous V chunk consumed
                 for (int e = ct; e < n * per; e += NCT) {
                     const int i = e / per, j = e - (e / per) * per;
-                    cpa16(vch + (size_t)i * hd + 8 * j, vb + (size_t)(c0 + i) * kv + 8 * j);
+                    cpa16(vch + (size_t)i * hd + 8 * j, vb + kv_row_q(p, S, m, slot, lo + c0 + i) * kv + 8 * j);
                 }
                 cpa_wait_all();
                 cons_sync();
@@ -1342,6 +1357,13 @@ __global__ void __launch_bounds__(EC_MK_THREADS, 1) k_decode(const __grid_consta
         const uint32_t *src = reinterpret_cast<const uint32_t *>(pg.layers);
         const int words = (int)((size_t)pg.L * sizeof(ec_mk_layer) / 4);
         for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
+    }
+    __syncthreads();
+    if (pg.mp <= PT_SMEM) {   // page-table rows of the rows' slots (slots are fixed for the launch)
+        for (int i = threadIdx.x; i < M * pg.mp; i += blockDim.x) {
+            const int q = i / pg.mp, jj = i - q * pg.mp;
+            S.lpt[q * PT_SMEM + jj] = pg.pt[(size_t)S.lslot[q] * pg.mp + jj];
+        }
     }
     __syncthreads();
     if (threadIdx.x == 0) {   // row ranges: every layer has the same shapes

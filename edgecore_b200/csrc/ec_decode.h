@@ -43,7 +43,7 @@ typedef struct {
 typedef struct {
     ec_mk_mat qkv, o, up, down;
     const float *n1g, *n1b, *n2g, *n2b;
-    uint16_t *kc, *vc;          /* this layer's [B][C][kv] fp16 caches     */
+    uint16_t *kc, *vc;          /* this layer's paged fp16 caches          */
 } ec_mk_layer;
 
 typedef struct {
@@ -62,6 +62,8 @@ typedef struct {
     float *amax_v;              /* [grid][M] per-CTA argmax partials       */
     int *amax_i;
     int *tok, *pos, *slot;      /* [M] token state                         */
+    const int *pt;              /* KV page table [B][mp] (ec_kv_row)       */
+    int mp;
     int *ids;                   /* [M] argmax ids of the last step or NULL */
     float *maxv;                /* [M] their logits or NULL                */
     int *hist;                  /* [n_steps][M] or NULL                    */

@@ -222,9 +222,15 @@ typedef struct ec_dev {
     float *nfg, *nfb;
     ec_dlayer *lw;
     int v0, v1;                /* vocab shard [v0, v1) */
-    /* KV arena */
+    /* KV arena: per layer [kv_pages][EC_KV_PAGE][kv] fp16 for K and for V;
+     * slot s holds positions [64 j, 64 j + 64) in page pt[s][j] */
     uint16_t *kc, *vc;
-    size_t layer_kv;           /* elements per layer: B*C*kv */
+    size_t layer_kv;           /* elements per layer: kv_pages * EC_KV_PAGE * kv */
+    int kv_pages, mp;          /* pages per layer, pages per slot (ceil(C / 64)) */
+    int *h_pt, *d_pt;          /* page table [B][mp], -1 = unmapped (h_pt pinned) */
+    int *free_pages, nfree;    /* stack of unmapped pages */
+    int *kv_undo, nundo;       /* entries mapped by the current call (rolled back if it fails) */
+    int pt_dirty;
     double *rope_cos, *rope_sin;
     /* persistent decode kernel */
     ec_mk_layer *d_mk_layers;
@@ -691,6 +697,7 @@ static void ec_dev_free(ec_dev *d)
     if (d->lm != d->wte) cudaFree(d->lm);
     cudaFree(d->wte); cudaFree(d->wpe); cudaFree(d->nfg); cudaFree(d->nfb);
     cudaFree(d->kc); cudaFree(d->vc); cudaFree(d->rope_cos); cudaFree(d->rope_sin);
+    cudaFreeHost(d->h_pt); cudaFree(d->d_pt); free(d->free_pages); free(d->kv_undo);
     cudaFree(d->d_mk_layers); cudaFree(d->d_bar); cudaFree(d->d_mk_err);
     cudaFree(d->amax_v); cudaFree(d->amax_i);
     cudaFree(d->attn_part); cudaFree(d->logits); cudaFree(d->amax_part);
@@ -790,11 +797,28 @@ static int ec_dev_build(GPT2 *g, ec_dev *d)
     }
     ec_set_lm_shard(d, 0, d->V);
 
-    d->layer_kv = (size_t)d->B * d->C * d->kv;
+    /* paged KV arena: every slot's full context by default; EDGECORE_KV_PAGES
+     * sets a smaller pool that slots draw from as their positions grow */
+    d->mp = (d->C + EC_KV_PAGE - 1) / EC_KV_PAGE;
+    d->kv_pages = d->B * d->mp;
+    {
+        const char *env = getenv("EDGECORE_KV_PAGES");
+        if (env && atoi(env) > 0 && atoi(env) < d->kv_pages) d->kv_pages = atoi(env);
+    }
+    d->layer_kv = (size_t)d->kv_pages * EC_KV_PAGE * d->kv;
     CK(cudaMalloc((void **)&d->kc, d->layer_kv * d->L * 2));
     CK(cudaMalloc((void **)&d->vc, d->layer_kv * d->L * 2));
     CK(cudaMemset(d->kc, 0, d->layer_kv * d->L * 2));
     CK(cudaMemset(d->vc, 0, d->layer_kv * d->L * 2));
+    CK(cudaMallocHost((void **)&d->h_pt, (size_t)d->B * d->mp * 4));
+    CK(cudaMalloc((void **)&d->d_pt, (size_t)d->B * d->mp * 4));
+    d->free_pages = malloc((size_t)d->kv_pages * sizeof(int));
+    d->kv_undo = malloc((size_t)d->B * d->mp * sizeof(int));
+    if (!d->free_pages || !d->kv_undo) { ec_seterr("out of host memory"); return -1; }
+    for (int i = 0; i < d->B * d->mp; i++) d->h_pt[i] = -1;
+    for (int i = 0; i < d->kv_pages; i++) d->free_pages[i] = d->kv_pages - 1 - i;   /* pop 0, 1, 2, ... */
+    d->nfree = d->kv_pages;
+    CK(cudaMemcpy(d->d_pt, d->h_pt, (size_t)d->B * d->mp * 4, cudaMemcpyHostToDevice));
     if (d->arch == ARCH_QWEN2 && ec_rope_tables(d, g)) return -1;
     if (ec_mk_build(d)) return -1;
     if (ec_ensure(d, d->B > 8 ? d->B : 8)) return -1;
@@ -1016,6 +1040,8 @@ static ec_kvgeo ec_geo(const ec_dev *d, int l)
     ec_kvgeo g;
     g.kc = d->kc + d->layer_kv * l;
     g.vc = d->vc + d->layer_kv * l;
+    g.pt = d->d_pt;
+    g.mp = d->mp;
     g.B = d->B;
     g.C = d->C;
     g.kv = d->kv;
@@ -1151,6 +1177,64 @@ static int ec_enqueue_lm(ec_dev *d, int r0, int rows)
     return ec_linear(d, &lm, d->h + (size_t)r0 * d->E, d->E, rows, d->logits, d->v1 - d->v0, EC_EPI_STORE);
 }
 
+/* Map KV pages for positions [0, end) of slot s (pages come off the free
+ * stack in order); the table reaches the device with ec_kv_flush on the
+ * model stream, ahead of the launches that use it.  Entries only go from
+ * unmapped to mapped between releases, so a flush that runs later than it
+ * was enqueued copies a superset of what that launch needs. */
+static void ec_kv_begin(ec_dev *d) { d->nundo = 0; }
+
+/* A call that fails maps none of its pages. */
+static void ec_kv_undo(ec_dev *d)
+{
+    while (d->nundo > 0) {
+        int *e = &d->h_pt[d->kv_undo[--d->nundo]];
+        d->free_pages[d->nfree++] = *e;
+        *e = -1;
+    }
+}
+
+static int ec_kv_fail(ec_dev *d)
+{
+    ec_kv_undo(d);
+    ec_seterr("KV arena full: all %d pages of %d positions are mapped (ec_kv_release frees a slot)",
+              d->kv_pages, EC_KV_PAGE);
+    return -1;
+}
+
+static int ec_kv_map(ec_dev *d, int s, int end)
+{
+    if (end > d->C) end = d->C;
+    const int need = (end + EC_KV_PAGE - 1) / EC_KV_PAGE;
+    for (int j = 0; j < need; j++) {
+        const int idx = s * d->mp + j;
+        int *e = &d->h_pt[idx];
+        if (*e >= 0) continue;
+        if (d->nfree == 0) return ec_kv_fail(d);
+        *e = d->free_pages[--d->nfree];
+        d->kv_undo[d->nundo++] = idx;
+        d->pt_dirty = 1;
+    }
+    return 0;
+}
+
+static int ec_kv_flush(ec_dev *d)
+{
+    if (!d->pt_dirty) return 0;
+    CK(cudaMemcpyAsync(d->d_pt, d->h_pt, (size_t)d->B * d->mp * 4, cudaMemcpyHostToDevice, d->stream));
+    d->pt_dirty = 0;
+    return 0;
+}
+
+/* Slots [0, M) mapped for positions [0, end). */
+static int ec_kv_map_slots(ec_dev *d, int M, int end)
+{
+    ec_kv_begin(d);
+    for (int s = 0; s < M && s < d->B; s++)
+        if (ec_kv_map(d, s, end)) return -1;
+    return ec_kv_flush(d);
+}
+
 /* Validate host inputs and stage tok/pos/slot into the pinned buffer. */
 static int ec_stage_inputs(ec_dev *d, const int *tokens, const int *positions, const int *seqs, int M)
 {
@@ -1159,16 +1243,22 @@ static int ec_stage_inputs(ec_dev *d, const int *tokens, const int *positions, c
     if (ec_ensure(d, M)) return -1;
     CK(cudaStreamSynchronize(d->stream));   /* h_in may still feed a previous async copy */
     int *ht = d->h_in, *hp = d->h_in + M, *hs = d->h_in + 2 * M;
+    ec_kv_begin(d);
     for (int m = 0; m < M; m++) {
         const int t = tokens[m], p = positions[m];
         int s = seqs ? seqs[m] : m;
         if (s >= d->B) s = d->B - 1;   /* reference clamp, src/gpt2.c:512-513 */
-        if (t < 0 || t >= d->V) { ec_seterr("token id %d out of range [0,%d)", t, d->V); return -1; }
-        if (p < 0 || p >= d->C) { ec_seterr("position %d out of range [0,%d)", p, d->C); return -1; }
-        if (s < 0) { ec_seterr("slot %d is negative", s); return -1; }
+        if (t < 0 || t >= d->V || p < 0 || p >= d->C || s < 0) {
+            ec_kv_fail(d);
+            if (t < 0 || t >= d->V) ec_seterr("token id %d out of range [0,%d)", t, d->V);
+            else if (p < 0 || p >= d->C) ec_seterr("position %d out of range [0,%d)", p, d->C);
+            else ec_seterr("slot %d is negative", s);
+            return -1;
+        }
         ht[m] = t; hp[m] = p; hs[m] = s;
+        if (ec_kv_map(d, s, p + 1)) return -1;
     }
-    return 0;
+    return ec_kv_flush(d);
 }
 
 static int ec_copy_inputs(ec_dev *d, int M)
@@ -1261,6 +1351,7 @@ static int ec_mk_plan(ec_dev *d, int M, int maxlen, ec_mk_params *p)
     p->x = d->x; p->q = d->q; p->att = d->att; p->act = d->act;
     p->amax_v = d->amax_v; p->amax_i = d->amax_i;
     p->tok = d->d_tok; p->pos = d->d_pos; p->slot = d->d_slot;
+    p->pt = d->d_pt; p->mp = d->mp;
     p->bar = d->d_bar; p->abort_flag = d->d_abort; p->err = d->d_mk_err;
     p->maxlen = maxlen;
     p->taps = (d->taps_on && d->taps && M <= d->taps_rows) ? d->taps : NULL;
@@ -1413,6 +1504,8 @@ EC_EXPORT int ec_forward_device(GPT2 *g, const int *d_tokens, const int *d_posit
     if (!d) { ec_seterr("model not loaded"); return -1; }
     if (M < 1 || M > EC_MK_MT) { ec_seterr("ec_forward_device: 1 <= M <= %d", EC_MK_MT); return -1; }
     if (ec_ensure(d, M)) return -1;
+    /* device-resident slots and positions: every slot fully mapped */
+    if (ec_kv_map_slots(d, d->B, d->C)) return -1;
     ec_mk_params mp;
     if (ec_mk_plan(d, M, d->C, &mp)) { ec_seterr("ec_forward_device: eff_ctx too long for the decode kernel"); return -1; }
     CK(cudaStreamSynchronize(d->stream));   /* h_in reuse */
@@ -1443,9 +1536,11 @@ EC_EXPORT int ec_forward_shard_argmax(GPT2 *g, const int *tokens, const int *pos
 }
 
 /* Stage a decode run: tokens from device, positions start_pos, slots 0..M-1. */
-static int ec_decode_setup(ec_dev *d, int *d_tokens, int start_pos, int M)
+/* Rows m < M decode from slot m at start_pos on; positions up to end - 1. */
+static int ec_decode_setup(ec_dev *d, int *d_tokens, int start_pos, int M, int end)
 {
     if (ec_ensure(d, M)) return -1;
+    if (ec_kv_map_slots(d, M, end)) return -1;
     CK(cudaStreamSynchronize(d->stream));   /* h_in reuse */
     for (int m = 0; m < M; m++) {
         d->h_in[M + m] = start_pos;
@@ -1485,7 +1580,7 @@ EC_EXPORT int ec_decode_greedy_cycle(GPT2 *g, int *d_tokens, int start_pos, int 
         CK(cudaMalloc((void **)&d->d_hist, (size_t)n_steps * M * 4));
         d->hist_cap = n_steps * M;
     }
-    if (ec_decode_setup(d, d_tokens, start_pos, M)) return -1;
+    if (ec_decode_setup(d, d_tokens, start_pos, M, start_pos + span)) return -1;
     mp.hist = d_out_ids ? d->d_hist : NULL;
     mp.advance = 1;
     mp.wrap_lo = period > 0 ? start_pos : 0;
@@ -1623,14 +1718,18 @@ EC_EXPORT int ec_decode_batch(GPT2 *g, int *d_tokens, int *d_positions, int n_st
     CK(cudaStreamSynchronize(d->stream));
     CK(cudaMemcpy(d->h_in + M, d_positions, (size_t)M * 4, cudaMemcpyDeviceToHost));
     int maxp = 0;
+    ec_kv_begin(d);
     for (int m = 0; m < M; m++) {
         const int p = d->h_in[M + m];
         if (p < 0 || p + n_steps > d->C) {
+            ec_kv_undo(d);
             ec_seterr("slot %d: positions [%d, %d) exceed eff_ctx %d", m, p, p + n_steps, d->C);
             return -1;
         }
         if (p + n_steps > maxp) maxp = p + n_steps;
+        if (ec_kv_map(d, m, p + n_steps)) return -1;
     }
+    if (ec_kv_flush(d)) return -1;
     if (M <= EC_MK_MT) {   /* up to 8 streams: the persistent decode kernel, one launch for all steps */
         int max_len = maxp;
         if (d->window > 0 && max_len > d->window) max_len = d->window;
@@ -1689,6 +1788,7 @@ EC_EXPORT int ec_batch_hidden(GPT2 *g, const int *d_tokens, const int *d_positio
     if (M < 1 || M > d->B) { ec_seterr("ec_batch_hidden: 1 <= M <= batch_cap (%d), got %d", d->B, M); return -1; }
     if (max_pos_end < 1 || max_pos_end > d->C) { ec_seterr("ec_batch_hidden: max_pos_end %d outside [1, %d]", max_pos_end, d->C); return -1; }
     const int maxlen = ec_batch_len(d, max_pos_end);
+    if (ec_kv_map_slots(d, M, max_pos_end)) return -1;
     if (ec_batch_prepare(d, M, maxlen, 0)) return -1;
     CK(cudaMemcpyAsync(d->d_tok, d_tokens, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
     CK(cudaMemcpyAsync(d->d_pos, d_positions, (size_t)M * 4, cudaMemcpyDeviceToDevice, d->stream));
@@ -1713,6 +1813,61 @@ EC_EXPORT int ec_lm_shard_keys(GPT2 *g, const float *d_hidden, int rows, long lo
     if (ec_enqueue_lm_argmax(d, rows, chunk)) return -1;
     CK(ec_launch_pack_keys(d->d_ids, d->d_max, rows, d_keys, d->stream));
     return 0;
+}
+
+EC_EXPORT int ec_kv_release(GPT2 *g, int slot)
+{
+    ec_dev *d = ec_lookup(g);
+    if (!d) { ec_seterr("model not loaded"); return -1; }
+    if (slot >= d->B) { ec_seterr("ec_kv_release: slot %d >= batch_cap %d", slot, d->B); return -1; }
+    CK(cudaStreamSynchronize(d->stream));   /* no launch in flight still reads the pages */
+    for (int s = slot < 0 ? 0 : slot; s < (slot < 0 ? d->B : slot + 1); s++)
+        for (int j = 0; j < d->mp; j++) {
+            int *e = &d->h_pt[(size_t)s * d->mp + j];
+            if (*e < 0) continue;
+            d->free_pages[d->nfree++] = *e;
+            *e = -1;
+            d->pt_dirty = 1;
+        }
+    return ec_kv_flush(d);
+}
+
+EC_EXPORT int ec_kv_info(const GPT2 *g, int *info4)
+{
+    ec_dev *d = ec_lookup(g);
+    if (!d || !info4) { ec_seterr("ec_kv_info: no model or NULL info"); return -1; }
+    info4[0] = d->kv_pages;
+    info4[1] = d->nfree;
+    info4[2] = EC_KV_PAGE;
+    info4[3] = d->mp;
+    return 0;
+}
+
+EC_EXPORT long long ec_model_packed(const GPT2 *g, int layer, int which, void *out, size_t cap, int *info5)
+{
+    ec_dev *d = ec_lookup(g);
+    if (!d) { ec_seterr("model not loaded"); return -1; }
+    if (which < 0 || which > 4 || (which < 4 && (layer < 0 || layer >= d->L))) {
+        ec_seterr("ec_model_packed: bad layer %d / which %d", layer, which);
+        return -1;
+    }
+    ec_lin lm;
+    const ec_lin *l;
+    if (which == 4) {
+        lm = ec_lm_lin(d);
+        l = &lm;
+    } else {
+        const ec_dlayer *W = &d->lw[layer];
+        l = which == 0 ? &W->qkv : which == 1 ? &W->o : which == 2 ? &W->up : &W->down;
+    }
+    const int elt = l->wt == EC_W_I8 ? 1 : 2;
+    if (info5) { info5[0] = l->N; info5[1] = l->K; info5[2] = l->Kp; info5[3] = l->ldw; info5[4] = elt; }
+    const size_t bytes = (size_t)l->N * l->ldw * elt;
+    if (!out) return (long long)bytes;
+    if (cap < bytes) { ec_seterr("ec_model_packed: %zu bytes needed", bytes); return -1; }
+    CK(cudaStreamSynchronize(d->stream));
+    CK(cudaMemcpy(out, l->w, bytes, cudaMemcpyDeviceToHost));
+    return (long long)bytes;
 }
 
 EC_EXPORT int ec_batch_graph_kernels(GPT2 *g, int kind)
@@ -1749,7 +1904,7 @@ EC_EXPORT int ec_decode_profile(GPT2 *g, int *d_tokens, int start_pos, int n_ste
     const int maxlen = ec_len_bucket(d, start_pos + n_steps);
     ec_mk_params mp;
     if (ec_mk_plan(d, M, maxlen, &mp) == 0) {
-        if (ec_decode_setup(d, d_tokens, start_pos, M)) return -1;
+        if (ec_decode_setup(d, d_tokens, start_pos, M, start_pos + n_steps)) return -1;
         mp.advance = 1;
         for (int st = 0; st < n_steps; st++) {
             CK(cudaMemsetAsync(d->d_bar, 0, 32, d->stream));   /* counter and abort flag */
@@ -1765,7 +1920,8 @@ EC_EXPORT int ec_decode_profile(GPT2 *g, int *d_tokens, int start_pos, int n_ste
         }
     } else {
         const int chunk = ec_lm_chunk(d, M);
-        if (ec_decode_setup(d, d_tokens, start_pos, M) || ec_ensure_logits(d, chunk) || ec_ensure_amax(d, chunk) ||
+        if (ec_decode_setup(d, d_tokens, start_pos, M, start_pos + n_steps) || ec_ensure_logits(d, chunk) ||
+            ec_ensure_amax(d, chunk) ||
             ec_ensure_attn(d, M, maxlen)) return -1;
         for (int st = 0; st < n_steps; st++) {
             d->prof_on = 1;
@@ -1824,7 +1980,7 @@ EC_EXPORT int ec_decode_trace(GPT2 *g, int *d_tokens, int start_pos, int n_steps
     unsigned long long *dt = NULL;
     CK(cudaMalloc((void **)&dt, (size_t)cap * 8));
     CK(cudaMemsetAsync(dt, 0, (size_t)cap * 8, d->stream));
-    if (ec_decode_setup(d, d_tokens, start_pos, M)) { cudaFree(dt); return -1; }
+    if (ec_decode_setup(d, d_tokens, start_pos, M, start_pos + n_steps)) { cudaFree(dt); return -1; }
     mp.advance = 1;
     mp.trace = dt;
     mp.trace_cap = cap;

@@ -566,8 +566,9 @@ __global__ void __launch_bounds__(256) k_qkv_split(float *q_out, const float *qk
     }
     const float *row = qkv + (size_t)m * ldq;
     float *qo = q_out + (size_t)m * g.E;
-    uint16_t *kr = g.kc + ((size_t)slot * g.C + pos) * g.kv;
-    uint16_t *vr = g.vc + ((size_t)slot * g.C + pos) * g.kv;
+    const size_t kvo = ec_kv_row(g.pt, g.mp, slot, pos) * g.kv;
+    uint16_t *kr = g.kc + kvo;
+    uint16_t *vr = g.vc + kvo;
     if (packed) {
         const int half = g.hd >> 1;
         const int npairs = (H + KVH) * half;
@@ -672,8 +673,8 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const ec_attn_args a)
         return;
     }
     const int kvh = h * a.KVH / a.H;
-    const uint16_t *kb = g.kc + (size_t)slot * g.C * g.kv + (size_t)kvh * hd;
-    const uint16_t *vb = g.vc + (size_t)slot * g.C * g.kv + (size_t)kvh * hd;
+    const uint16_t *kb = g.kc + (size_t)kvh * hd;   // + the arena row of each position
+    const uint16_t *vb = g.vc + (size_t)kvh * hd;
     const float *q = a.q + (size_t)m * a.ldq + (size_t)h * hd;
     for (int d = threadIdx.x; d < hd; d += blockDim.x) qs[d] = q[d];
     __syncthreads();
@@ -681,7 +682,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const ec_attn_args a)
     // scores: one position per thread, the reference's sequential fp32 dot
     float mx = -FLT_MAX;
     for (int p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
-        const uint16_t *kp = kb + (size_t)p * g.kv;
+        const uint16_t *kp = kb + ec_kv_row(g.pt, g.mp, slot, p) * g.kv;
         float acc = 0.0f;
         for (int d = 0; d < hd; d += 8) {
             const uint4 w = *reinterpret_cast<const uint4 *>(kp + d);
@@ -722,7 +723,8 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const ec_attn_args a)
     for (int d = threadIdx.x; d < hd; d += blockDim.x) {
         float o = 0.0f;
         for (int p = p0; p < p1; ++p)
-            o = __fadd_rn(o, __fmul_rn(sc[p - p0], __half2float(__ushort_as_half(vb[(size_t)p * g.kv + d]))));
+            o = __fadd_rn(o, __fmul_rn(sc[p - p0],
+                                       __half2float(__ushort_as_half(vb[ec_kv_row(g.pt, g.mp, slot, p) * g.kv + d]))));
         part[d] = o;
     }
     if (threadIdx.x == 0) { part[hd] = mx; part[hd + 1] = (float)sum; }
@@ -787,8 +789,8 @@ __global__ void __launch_bounds__(ATTX_THREADS) k_attn_exact(const ec_attn_args 
     }
     float *qs = attx_smem;                 // [G][hd]
     float *sc = attx_smem + G * hd;        // [G][maxlen]
-    const uint16_t *kb = geo.kc + (size_t)slot * geo.C * geo.kv + (size_t)g * hd;
-    const uint16_t *vb = geo.vc + (size_t)slot * geo.C * geo.kv + (size_t)g * hd;
+    const uint16_t *kb = geo.kc + (size_t)g * hd;   // + the arena row of each position
+    const uint16_t *vb = geo.vc + (size_t)g * hd;
     for (int i = threadIdx.x; i < G * hd; i += blockDim.x)
         qs[i] = a.q[(size_t)m * a.ldq + (size_t)(h0 + i / hd) * hd + (i % hd)];
     __syncthreads();
@@ -796,7 +798,7 @@ __global__ void __launch_bounds__(ATTX_THREADS) k_attn_exact(const ec_attn_args 
 
     // scores, one position per thread, all heads of the group
     for (int p = lo + (int)threadIdx.x; p <= pos; p += blockDim.x) {
-        const uint16_t *kp = kb + (size_t)p * geo.kv;
+        const uint16_t *kp = kb + ec_kv_row(geo.pt, geo.mp, slot, p) * geo.kv;
         float acc[ATTX_MAX_GROUP];
 #pragma unroll
         for (int hh = 0; hh < ATTX_MAX_GROUP; ++hh) acc[hh] = 0.0f;
@@ -848,17 +850,17 @@ __global__ void __launch_bounds__(ATTX_THREADS) k_attn_exact(const ec_attn_args 
         float o = 0.0f;
         int i = 0;
         for (; i + 4 <= len; i += 4) {
-            const float v0 = __half2float(__ushort_as_half(vp[(size_t)(lo + i) * geo.kv]));
-            const float v1 = __half2float(__ushort_as_half(vp[(size_t)(lo + i + 1) * geo.kv]));
-            const float v2 = __half2float(__ushort_as_half(vp[(size_t)(lo + i + 2) * geo.kv]));
-            const float v3 = __half2float(__ushort_as_half(vp[(size_t)(lo + i + 3) * geo.kv]));
+            const float v0 = __half2float(__ushort_as_half(vp[ec_kv_row(geo.pt, geo.mp, slot, lo + i) * geo.kv]));
+            const float v1 = __half2float(__ushort_as_half(vp[ec_kv_row(geo.pt, geo.mp, slot, lo + i + 1) * geo.kv]));
+            const float v2 = __half2float(__ushort_as_half(vp[ec_kv_row(geo.pt, geo.mp, slot, lo + i + 2) * geo.kv]));
+            const float v3 = __half2float(__ushort_as_half(vp[ec_kv_row(geo.pt, geo.mp, slot, lo + i + 3) * geo.kv]));
             o = __fadd_rn(o, __fmul_rn(w[i], v0));
             o = __fadd_rn(o, __fmul_rn(w[i + 1], v1));
             o = __fadd_rn(o, __fmul_rn(w[i + 2], v2));
             o = __fadd_rn(o, __fmul_rn(w[i + 3], v3));
         }
         for (; i < len; ++i)
-            o = __fadd_rn(o, __fmul_rn(w[i], __half2float(__ushort_as_half(vp[(size_t)(lo + i) * geo.kv]))));
+            o = __fadd_rn(o, __fmul_rn(w[i], __half2float(__ushort_as_half(vp[ec_kv_row(geo.pt, geo.mp, slot, lo + i) * geo.kv]))));
         a.out[(size_t)m * a.ldo + (size_t)(h0 + hh) * hd + d] = o;
     }
 }

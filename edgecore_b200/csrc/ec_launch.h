@@ -40,9 +40,14 @@ typedef struct {
     const int *slot;    /* KV slot (already clamped)      */
 } ec_tokens;
 
+/* Positions per page of the paged KV arena (ec_kv_row in ec_common.cuh). */
+#define EC_KV_PAGE 64
+
 /* KV-cache / attention geometry for the QKV epilogue and attention. */
 typedef struct {
-    uint16_t *kc, *vc;        /* this layer's [B][C][kv] fp16 caches          */
+    uint16_t *kc, *vc;        /* this layer's paged fp16 caches [pages][64][kv] */
+    const int *pt;            /* page table [B][mp] (see ec_kv_row)            */
+    int mp;                   /* pages per slot                                */
     int B;                    /* batch_cap (slots)                             */
     int C;                    /* eff_ctx                                       */
     int kv;                   /* n_kv_embd                                     */

@@ -112,6 +112,34 @@ int ec_keys_advance(GPT2 *g, const long long *d_keys, int M, int *d_tokens, int 
  * (kind 0) or ec_batch_hidden (kind 1); 0 if none was captured. */
 int ec_batch_graph_kernels(GPT2 *g, int kind);
 
+/* Paged KV arena.  Each layer's K and V caches are pools of pages of 64
+ * positions; slot s keeps positions [64 j, 64 j + 64) in the page its table
+ * entry j names.  Pages are mapped as calls reach new positions of a slot
+ * (host-visible positions: the rows of gpt2_forward / ec_forward_argmax,
+ * start_pos + n_steps of the decode loops, max_pos_end of
+ * ec_batch_hidden; ec_forward_device maps every slot fully) and stay mapped
+ * until ec_kv_release(slot) (slot < 0: every slot) returns them.  The pool
+ * holds batch_cap * ceil(eff_ctx / 64) pages by default, so no call can run
+ * out; the environment variable EDGECORE_KV_PAGES at gpt2_load sets a
+ * smaller pool, and a call that needs more pages than are free fails with
+ * "KV arena full".  ec_kv_info: {pages, free pages, positions per page,
+ * pages per slot}. */
+int ec_kv_release(GPT2 *g, int slot);
+int ec_kv_info(const GPT2 *g, int *info4);
+
+/* The device copy of one linear as gpt2_load packed it (replaces reading the
+ * reference's host LayerW arrays, src/edgecore.h:119-136, for a check of the
+ * load-time repack).  which: 0 q|k|v, 1 o, 2 gate|up (Qwen2) / fc (GPT-2),
+ * 3 down / fc2, 4 lm_head (layer ignored).  info5 = {N rows, K, Kp, ldw,
+ * element bytes}; a packed row is Kp weights (K..Kp-1 zero) then, except for
+ * the lm_head, a 16-byte fp32 tail {scale, bias, 0, 0} (scale 1 / bias 0
+ * where the model has none).  Row order: Qwen2 q|k|v puts the RoPE partners
+ * i and i + head_dim/2 of every q and k head at rows 2i, 2i+1 (then the v
+ * rows in file order); Qwen2 gate|up interleaves gate j and up j at rows 2j,
+ * 2j+1; everything else is in file order.  out == NULL returns the byte
+ * count only; otherwise out must hold N * ldw * element bytes (cap). */
+long long ec_model_packed(const GPT2 *g, int layer, int which, void *out, size_t cap, int *info5);
+
 /* Instrumented greedy decode for measurement: n_steps steps, one kernel
  * launch per step, with a CUDA event pair around every kernel launch on the
  * model stream.  out[16]: for kernel class c in {0 persistent decode step,
