@@ -706,7 +706,7 @@ def c3_batched(args, stream) -> dict:
             "prefill_timing": f"best of {reps} host-timed forward_argmax calls of {rows} rows (synchronised)",
             "decode_tok_s": S * D / (dms / 1e3), "decode_ms_per_step": dms / D, "decode_steps": D,
             "decode_timing": "CUDA events around ec_decode_batch of 128 steps",
-            "kv": "contiguous arena [layer][slot][position] sized by max_ctx"}
+            "kv": "paged arena: 64-position pages per slot, mapped as the prefill and the decode steps reach them"}
     ref = child_reference(args, "c3b", 0.0)
     line["cpu_baseline"] = ref.get("cpu_baseline", ref) if ref else None
     return line

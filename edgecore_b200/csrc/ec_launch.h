@@ -1,5 +1,5 @@
 /*
- * ec_launch.h -- internal C interface between the host code (ec_model.c,
+ * ec_launch.h -- internal C interface between the host code (ec_host.c,
  * ec_abi.c; plain C11) and the sm_100a kernels (*.cu).  Every launcher
  * enqueues on `stream` and returns a cudaError_t-compatible int (0 = ok).
  */
