@@ -760,12 +760,19 @@ __global__ void k_attn_combine(const ec_attn_args a) {
 // sequential fp32 sum over positions of w * v, in position order.  Only the
 // fp64 sums are reassociated (they round to the same fp32 weights except in
 // ~2^-29 of cases).  One CTA per (KV head, token); scores live in shared
-// memory: maxlen * heads_per_group floats.
+// memory (maxlen * heads_per_group floats), and V comes through shared memory
+// ATTX_VCH positions at a time with coalesced 16-byte loads.
 #define ATTX_THREADS 256
 #define ATTX_MAX_GROUP 16
+#define ATTX_VCH 64
+#define ATTX_OPT 16   // (head, d) output pairs per thread at most: G * hd <= 16 * 256
+
+__host__ __device__ inline size_t attx_v_offset(int G, int hd, int maxlen) {
+    return (((size_t)G * hd + (size_t)G * maxlen) * sizeof(float) + 15) & ~(size_t)15;
+}
 
 __host__ __device__ inline size_t attx_smem_bytes(int G, int hd, int maxlen) {
-    return ((size_t)G * hd + (size_t)G * maxlen) * sizeof(float);
+    return attx_v_offset(G, hd, maxlen) + (size_t)ATTX_VCH * hd * 2;
 }
 
 __global__ void __launch_bounds__(ATTX_THREADS) k_attn_exact(const ec_attn_args a) {
@@ -842,26 +849,42 @@ __global__ void __launch_bounds__(ATTX_THREADS) k_attn_exact(const ec_attn_args 
     }
     __syncthreads();
 
-    // output: sequential fp32 accumulation over positions for every (head, d)
-    for (int idx = threadIdx.x; idx < G * hd; idx += blockDim.x) {
-        const int hh = idx / hd, d = idx % hd;
-        const float *w = sc + hh * a.maxlen;
-        const uint16_t *vp = vb + d;
-        float o = 0.0f;
-        int i = 0;
-        for (; i + 4 <= len; i += 4) {
-            const float v0 = __half2float(__ushort_as_half(vp[ec_kv_row(geo.pt, geo.mp, slot, lo + i) * geo.kv]));
-            const float v1 = __half2float(__ushort_as_half(vp[ec_kv_row(geo.pt, geo.mp, slot, lo + i + 1) * geo.kv]));
-            const float v2 = __half2float(__ushort_as_half(vp[ec_kv_row(geo.pt, geo.mp, slot, lo + i + 2) * geo.kv]));
-            const float v3 = __half2float(__ushort_as_half(vp[ec_kv_row(geo.pt, geo.mp, slot, lo + i + 3) * geo.kv]));
-            o = __fadd_rn(o, __fmul_rn(w[i], v0));
-            o = __fadd_rn(o, __fmul_rn(w[i + 1], v1));
-            o = __fadd_rn(o, __fmul_rn(w[i + 2], v2));
-            o = __fadd_rn(o, __fmul_rn(w[i + 3], v3));
+    // output: sequential fp32 accumulation over positions for every (head, d),
+    // V staged ATTX_VCH positions at a time; each pair keeps its running sum
+    // across chunks, so the order is the reference's
+    uint16_t *vs = reinterpret_cast<uint16_t *>(reinterpret_cast<unsigned char *>(attx_smem) +
+                                                attx_v_offset(G, hd, a.maxlen));
+    const int npair = G * hd, per = hd >> 3;
+    float o[ATTX_OPT];
+#pragma unroll
+    for (int k = 0; k < ATTX_OPT; ++k) o[k] = 0.0f;
+    for (int c0 = 0; c0 < len; c0 += ATTX_VCH) {
+        const int n = min(ATTX_VCH, len - c0);
+        __syncthreads();   // the previous chunk is consumed
+        for (int e = threadIdx.x; e < n * per; e += blockDim.x) {
+            const int i = e / per, j = e - i * per;
+            const uint16_t *src = vb + ec_kv_row(geo.pt, geo.mp, slot, lo + c0 + i) * geo.kv + 8 * j;
+            *reinterpret_cast<uint4 *>(vs + (size_t)i * hd + 8 * j) = __ldg(reinterpret_cast<const uint4 *>(src));
         }
-        for (; i < len; ++i)
-            o = __fadd_rn(o, __fmul_rn(w[i], __half2float(__ushort_as_half(vp[ec_kv_row(geo.pt, geo.mp, slot, lo + i) * geo.kv]))));
-        a.out[(size_t)m * a.ldo + (size_t)(h0 + hh) * hd + d] = o;
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < ATTX_OPT; ++k) {
+            const int idx = (int)threadIdx.x + k * ATTX_THREADS;
+            if (idx >= npair) break;
+            const int hh = idx / hd, d = idx - hh * hd;
+            const float *w = sc + hh * a.maxlen + c0;
+            float acc = o[k];
+            for (int i = 0; i < n; ++i)
+                acc = __fadd_rn(acc, __fmul_rn(w[i], __half2float(__ushort_as_half(vs[(size_t)i * hd + d]))));
+            o[k] = acc;
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < ATTX_OPT; ++k) {
+        const int idx = (int)threadIdx.x + k * ATTX_THREADS;
+        if (idx >= npair) break;
+        const int hh = idx / hd, d = idx - hh * hd;
+        a.out[(size_t)m * a.ldo + (size_t)(h0 + hh) * hd + d] = o[k];
     }
 }
 
@@ -870,7 +893,7 @@ static int g_attx_max_smem = 0;
 extern "C" int ec_attention_exact_fits(int H, int KVH, int hd, int maxlen) {
     if (KVH <= 0 || H % KVH) return 0;
     const int G = H / KVH;
-    if (G > ATTX_MAX_GROUP || maxlen < 1) return 0;
+    if (G > ATTX_MAX_GROUP || maxlen < 1 || G * hd > ATTX_OPT * ATTX_THREADS) return 0;
     if (g_attx_max_smem == 0) {
         int dev = 0;
         cudaGetDevice(&dev);
