@@ -1095,7 +1095,9 @@ static double ec_step_bytes(const ec_dev *d, int M, double kv_positions)
     return b;
 }
 
-/* One linear on the generic GEMM path (any M): out = X . W^T with epilogue. */
+/* One linear on the generic GEMM path (any M): out = X . W^T with epilogue.
+ * X == NULL for int8 weights: the operand is already quantised in d->aq /
+ * d->as (by a fused norm or SwiGLU kernel). */
 static int ec_linear(ec_dev *d, const ec_lin *l, const float *X, int ldx, int M, float *out, int ldo, int epi)
 {
     cudaStream_t st = d->stream;
@@ -1105,7 +1107,7 @@ static int ec_linear(ec_dev *d, const ec_lin *l, const float *X, int ldx, int M,
     g.wt = l->wt; g.N = l->N; g.K = l->K; g.Kp = l->Kp; g.ldw = l->ldw; g.M = M;
     int pi = ec_prof_begin(d, EC_PC_GEMM, ec_lin_bytes(l, M));
     if (l->wt == EC_W_I8) {
-        CK(ec_launch_quant(d->aq, d->as, X, ldx, M, l->K, l->Kp, st));
+        if (X) CK(ec_launch_quant(d->aq, d->as, X, ldx, M, l->K, l->Kp, st));
         g.Aq = d->aq;
         g.a_scale = d->as;
     } else {
@@ -1137,12 +1139,16 @@ static int ec_enqueue_body(ec_dev *d, int M, int maxlen)
     at.tk = ec_tk(d); at.H = d->H; at.KVH = d->KVH; at.M = M; at.window = d->window;
     at.part = d->attn_part; at.maxlen = maxlen; at.nsplit = ec_pick_nsplit(maxlen);
     const int wact = d->arch == ARCH_QWEN2 ? d->I : 4 * E;
+    /* int8 layers: the norms and SwiGLU write the int8 operand themselves */
+    const int fuse_norm = d->wt == EC_W_I8 && (size_t)E * 4 <= 48 * 1024;
+    const int fuse_swiglu = fuse_norm && d->arch == ARCH_QWEN2 && (size_t)d->I * 4 <= 48 * 1024;
     for (int l = 0; l < d->L; l++) {
         ec_dlayer *W = &d->lw[l];
         pi = ec_prof_begin(d, EC_PC_NORM, 8.0 * M * E);
-        CK(ec_launch_norm(d->h, d->x, W->n1g, W->n1b, M, E, d->eps, st));
+        if (fuse_norm) CK(ec_launch_norm_quant(d->aq, d->as, W->qkv.Kp, d->x, W->n1g, W->n1b, M, E, d->eps, st));
+        else CK(ec_launch_norm(d->h, d->x, W->n1g, W->n1b, M, E, d->eps, st));
         ec_prof_end(d, pi);
-        if (ec_linear(d, &W->qkv, d->h, E, M, d->qkv, ldqkv, EC_EPI_STORE)) return -1;
+        if (ec_linear(d, &W->qkv, fuse_norm ? NULL : d->h, E, M, d->qkv, ldqkv, EC_EPI_STORE)) return -1;
         pi = ec_prof_begin(d, EC_PC_OTHER, 0.0);
         CK(ec_launch_qkv_split(d->q, d->qkv, ldqkv, ec_tk(d), ec_geo(d, l), d->H, d->KVH, d->arch == ARCH_QWEN2, M, st));
         ec_prof_end(d, pi);
@@ -1152,15 +1158,17 @@ static int ec_enqueue_body(ec_dev *d, int M, int maxlen)
         ec_prof_end(d, pi);
         if (ec_linear(d, &W->o, d->att, E, M, d->x, E, EC_EPI_RESID)) return -1;
         pi = ec_prof_begin(d, EC_PC_NORM, 8.0 * M * E);
-        CK(ec_launch_norm(d->h, d->x, W->n2g, W->n2b, M, E, d->eps, st));
+        if (fuse_norm) CK(ec_launch_norm_quant(d->aq, d->as, W->up.Kp, d->x, W->n2g, W->n2b, M, E, d->eps, st));
+        else CK(ec_launch_norm(d->h, d->x, W->n2g, W->n2b, M, E, d->eps, st));
         ec_prof_end(d, pi);
         if (d->arch == ARCH_QWEN2) {
-            if (ec_linear(d, &W->up, d->h, E, M, d->big, 2 * d->I, EC_EPI_STORE)) return -1;
-            CK(ec_launch_swiglu(d->act, d->I, d->big, 2 * d->I, d->I, M, st));
+            if (ec_linear(d, &W->up, fuse_norm ? NULL : d->h, E, M, d->big, 2 * d->I, EC_EPI_STORE)) return -1;
+            if (fuse_swiglu) CK(ec_launch_swiglu_quant(d->aq, d->as, W->down.Kp, d->big, 2 * d->I, d->I, M, st));
+            else CK(ec_launch_swiglu(d->act, d->I, d->big, 2 * d->I, d->I, M, st));
         } else {
-            if (ec_linear(d, &W->up, d->h, E, M, d->act, wact, EC_EPI_GELU)) return -1;
+            if (ec_linear(d, &W->up, fuse_norm ? NULL : d->h, E, M, d->act, wact, EC_EPI_GELU)) return -1;
         }
-        if (ec_linear(d, &W->down, d->act, wact, M, d->x, E, EC_EPI_RESID)) return -1;
+        if (ec_linear(d, &W->down, fuse_swiglu ? NULL : d->act, wact, M, d->x, E, EC_EPI_RESID)) return -1;
         if (d->taps_on && d->taps && M <= d->taps_rows)
             CK(cudaMemcpyAsync(d->taps + (size_t)(l + 1) * M * E, d->x, (size_t)M * E * 4, cudaMemcpyDeviceToDevice, st));
     }

@@ -552,6 +552,69 @@ extern "C" int ec_launch_norm(float *out, const float *x, const float *gamma, co
     return (int)cudaGetLastError();
 }
 
+// The row's int8 quantisation (k_quant) of `row` [K] held in shared memory,
+// with this thread's running max |value|: q[Kp] (zero past K) and *scale.
+__device__ __forceinline__ void quant_smem_row(int8_t *q, float *scale, const float *row, int K, int Kp, float mx,
+                                               float *sh) {
+    mx = block_reduce_max(mx, sh);   // its barriers also publish the row
+    const float s = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 1.0f;
+    if (threadIdx.x == 0) *scale = s;
+    for (int k = threadIdx.x; k < Kp; k += blockDim.x) q[k] = (int8_t)(k < K ? ec_quant1(row[k], s) : 0);
+}
+
+// k_norm then k_quant in one pass, the same arithmetic in the same order: the
+// int8 operand of the q|k|v and gate|up linears (the fp32 normed rows are not
+// needed there).  Dynamic shared memory: E floats.
+__global__ void __launch_bounds__(256) k_norm_quant(int8_t *q, float *scale, int Kp, const float *x, const float *g,
+                                                    const float *b, int E, double eps) {
+    extern __shared__ float nq_row[];
+    __shared__ double sh[32];
+    __shared__ float shf[32];
+    const int m = blockIdx.x;
+    const float *xr = x + (size_t)m * E;
+    float mx = 0.0f;
+    if (b) {
+        double s = 0.0;
+        for (int i = threadIdx.x; i < E; i += blockDim.x) s = __dadd_rn(s, (double)xr[i]);
+        const double mean = __ddiv_rn(block_reduce_sum(s, sh), (double)E);
+        double v = 0.0;
+        for (int i = threadIdx.x; i < E; i += blockDim.x) {
+            const double d = __dsub_rn((double)xr[i], mean);
+            v = __dadd_rn(v, __dmul_rn(d, d));
+        }
+        const double var = __ddiv_rn(block_reduce_sum(v, sh), (double)E);
+        const double rstd = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(var, eps)));
+        for (int i = threadIdx.x; i < E; i += blockDim.x) {
+            const float t = (float)__dmul_rn(__dsub_rn((double)xr[i], mean), rstd);
+            const float o = __fadd_rn(__fmul_rn(t, g[i]), b[i]);
+            nq_row[i] = o;
+            mx = ec_max_keep(mx, fabsf(o));
+        }
+    } else {
+        double s = 0.0;
+        for (int i = threadIdx.x; i < E; i += blockDim.x) {
+            const double d = (double)xr[i];
+            s = __dadd_rn(s, __dmul_rn(d, d));
+        }
+        const double ms = block_reduce_sum(s, sh);
+        const double rstd = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ms, (double)E), eps)));
+        for (int i = threadIdx.x; i < E; i += blockDim.x) {
+            const float o = __fmul_rn((float)__dmul_rn((double)xr[i], rstd), g[i]);
+            nq_row[i] = o;
+            mx = ec_max_keep(mx, fabsf(o));
+        }
+    }
+    quant_smem_row(q + (size_t)m * Kp, scale + m, nq_row, E, Kp, mx, shf);
+}
+
+extern "C" int ec_launch_norm_quant(int8_t *q, float *scale, int Kp, const float *x, const float *gamma,
+                                    const float *beta, int M, int E, double eps, cudaStream_t stream) {
+    if (M <= 0) return 0;
+    if ((size_t)E * 4 > 48 * 1024) return (int)cudaErrorNotSupported;
+    k_norm_quant<<<M, 256, (size_t)E * 4, stream>>>(q, scale, Kp, x, gamma, beta, E, eps);
+    return (int)cudaGetLastError();
+}
+
 // Split the q|k|v rows of a GEMM output [M][ldq] (packed layout: RoPE
 // partners adjacent for Qwen2 when packed != 0, file order for GPT-2): RoPE
 // q and k (fp64, reference src/gpt2.c:656-665), q -> q_out [M][E] in head
@@ -619,6 +682,30 @@ extern "C" int ec_launch_swiglu(float *out, int ldo, const float *gu, int ldg, i
     const size_t n = (size_t)M * I;
     const int grid = (int)((n + 255) / 256 > 65535 ? 65535 : (n + 255) / 256);
     k_swiglu<<<grid, 256, 0, stream>>>(out, ldo, gu, ldg, I, M);
+    return (int)cudaGetLastError();
+}
+
+// k_swiglu then k_quant in one pass (one CTA per row): the int8 operand of
+// the down projection.  Dynamic shared memory: I floats.
+__global__ void __launch_bounds__(256) k_swiglu_quant(int8_t *q, float *scale, int Kp, const float *gu, int ldg, int I) {
+    extern __shared__ float sq_row[];
+    __shared__ float shf[32];
+    const int m = blockIdx.x;
+    const float *row = gu + (size_t)m * ldg;
+    float mx = 0.0f;
+    for (int j = threadIdx.x; j < I; j += blockDim.x) {
+        const float a = __fmul_rn(ec_silu(row[2 * j]), row[2 * j + 1]);
+        sq_row[j] = a;
+        mx = ec_max_keep(mx, fabsf(a));
+    }
+    quant_smem_row(q + (size_t)m * Kp, scale + m, sq_row, I, Kp, mx, shf);
+}
+
+extern "C" int ec_launch_swiglu_quant(int8_t *q, float *scale, int Kp, const float *gu, int ldg, int I, int M,
+                                      cudaStream_t stream) {
+    if (M <= 0) return 0;
+    if ((size_t)I * 4 > 48 * 1024) return (int)cudaErrorNotSupported;
+    k_swiglu_quant<<<M, 256, (size_t)I * 4, stream>>>(q, scale, Kp, gu, ldg, I);
     return (int)cudaGetLastError();
 }
 

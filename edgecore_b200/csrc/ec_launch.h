@@ -129,6 +129,16 @@ int ec_launch_quant(int8_t *q, float *scale, const float *X, int ldx, int M, int
 int ec_launch_embed(float *x, const uint16_t *wte, const uint16_t *wpe, int ld, int is_bf16,
                     ec_tokens tk, int M, int E, int V, int C, cudaStream_t stream);
 
+/* Norm rows then their int8 quantisation (k_norm + k_quant in one pass):
+ * q [M][Kp], scale [M]; cudaErrorNotSupported when E floats exceed 48 KB. */
+int ec_launch_norm_quant(int8_t *q, float *scale, int Kp, const float *x, const float *gamma, const float *beta,
+                         int M, int E, double eps, cudaStream_t stream);
+
+/* SwiGLU of interleaved gate|up rows then their int8 quantisation: q [M][Kp],
+ * scale [M]; cudaErrorNotSupported when I floats exceed 48 KB. */
+int ec_launch_swiglu_quant(int8_t *q, float *scale, int Kp, const float *gu, int ldg, int I, int M,
+                           cudaStream_t stream);
+
 /* LayerNorm (beta != NULL) or RMSNorm (beta == NULL) rows, fp64 statistics. */
 int ec_launch_norm(float *out, const float *x, const float *gamma, const float *beta,
                    int M, int E, double eps, cudaStream_t stream);
