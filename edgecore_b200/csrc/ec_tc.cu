@@ -56,32 +56,38 @@ constexpr int EPI_LD = 20;                             // staging row stride (fl
 constexpr int EPI_BYTES = EPI_WARPS * 32 * EPI_LD * 4;
 constexpr int A_BYTES = BM * BKB;                      // one A part per stage: 16 KB
 
-// Per weight type: A parts, tile columns, ring depth, instruction descriptor.
+// Per configuration (the weight type, and for int8 a narrow variant): weight
+// type, A parts, tile columns, ring depth, instruction descriptor.
 // Instruction descriptor fields: [4,6) D format (1 f32, 2 s32), [7,10) A and
 // [10,13) B format (i8: 1 = signed; f16 kind: 0 = f16, 1 = bf16), bits 15/16
 // K-major (0), [17,23) N >> 3, [24,29) M >> 4.
-template <int WT> struct TcCfg;
+constexpr int TC_I8_NARROW = 3;   // int8 with 64-column tiles: 4x the CTAs for one row of tiles
+template <int CF> struct TcCfg;
 template <> struct TcCfg<EC_W_I8> {
-    static constexpr int S = 1, BN = 256, STAGES = 4, ELT = 1;
+    static constexpr int WT = EC_W_I8, S = 1, BN = 256, STAGES = 4, ELT = 1;
     static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 };
 template <> struct TcCfg<EC_W_F16> {
-    static constexpr int S = 2, BN = 256, STAGES = 3, ELT = 2;
+    static constexpr int WT = EC_W_F16, S = 2, BN = 256, STAGES = 3, ELT = 2;
     static constexpr uint32_t IDESC = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 };
 template <> struct TcCfg<EC_W_BF16> {
-    static constexpr int S = 3, BN = 128, STAGES = 3, ELT = 2;
+    static constexpr int WT = EC_W_BF16, S = 3, BN = 128, STAGES = 3, ELT = 2;
     static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 };
+template <> struct TcCfg<TC_I8_NARROW> {
+    static constexpr int WT = EC_W_I8, S = 1, BN = 64, STAGES = 8, ELT = 1;
+    static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+};
 
-template <int WT> __host__ __device__ constexpr int b_bytes() { return TcCfg<WT>::BN * BKB; }
-template <int WT> __host__ __device__ constexpr int stage_bytes() { return TcCfg<WT>::S * A_BYTES + b_bytes<WT>(); }
-template <int WT> __host__ __device__ constexpr int cst_bytes() { return EPI_WARPS * 2 * (TcCfg<WT>::BN / 2) * 4; }
-template <int WT> __host__ __device__ constexpr int smem_bytes() {
-    return 1024 /* alignment slack */ + TcCfg<WT>::STAGES * stage_bytes<WT>() + EPI_BYTES + cst_bytes<WT>() + 256;
+template <int CF> __host__ __device__ constexpr int b_bytes() { return TcCfg<CF>::BN * BKB; }
+template <int CF> __host__ __device__ constexpr int stage_bytes() { return TcCfg<CF>::S * A_BYTES + b_bytes<CF>(); }
+template <int CF> __host__ __device__ constexpr int cst_bytes() { return EPI_WARPS * 2 * (TcCfg<CF>::BN / 2) * 4; }
+template <int CF> __host__ __device__ constexpr int smem_bytes() {
+    return 1024 /* alignment slack */ + TcCfg<CF>::STAGES * stage_bytes<CF>() + EPI_BYTES + cst_bytes<CF>() + 256;
 }
-static_assert(smem_bytes<EC_W_I8>() <= 232448 && smem_bytes<EC_W_F16>() <= 232448 && smem_bytes<EC_W_BF16>() <= 232448,
-              "shared memory per CTA");
+static_assert(smem_bytes<EC_W_I8>() <= 232448 && smem_bytes<EC_W_F16>() <= 232448 && smem_bytes<EC_W_BF16>() <= 232448 &&
+              smem_bytes<TC_I8_NARROW>() <= 232448, "shared memory per CTA");
 
 __device__ int g_tc_err;
 
@@ -100,20 +106,20 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
         ::"r"(dst), "l"(map), "r"(bar), "r"(x), "r"(y) : "memory");
 }
 
-template <int WT>
+template <int CF>
 __device__ __forceinline__ void mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
-    if (WT == EC_W_I8)
+    if (TcCfg<CF>::WT == EC_W_I8)
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
             "setp.ne.b32 p, %4, 0;\n\t"
             "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-            ::"r"(tmem_d), "l"(da), "l"(db), "r"(TcCfg<WT>::IDESC), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+            ::"r"(tmem_d), "l"(da), "l"(db), "r"(TcCfg<CF>::IDESC), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
     else
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
             "setp.ne.b32 p, %4, 0;\n\t"
             "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-            ::"r"(tmem_d), "l"(da), "l"(db), "r"(TcCfg<WT>::IDESC), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+            ::"r"(tmem_d), "l"(da), "l"(db), "r"(TcCfg<CF>::IDESC), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
 }
 
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
@@ -236,13 +242,14 @@ __device__ __forceinline__ void split_tile_finish(const ec_gemm_args &a, const f
 }
 
 // row_scale: a_scale (int8) or the power-of-two row scale of the split (16-bit)
-template <int WT>
+template <int CF>
 __global__ void __launch_bounds__(THREADS, 1)
 k_gemm_tc(const __grid_constant__ TcMaps maps, const ec_gemm_args a, const float *row_scale,
           int flags,     // bit 0: 16-byte aligned output rows
           int ksplit) {  // CTAs per output tile over K (int8 only; 1: no split)
-    constexpr int S = TcCfg<WT>::S, BN = TcCfg<WT>::BN, STAGES = TcCfg<WT>::STAGES;
-    constexpr int SB = stage_bytes<WT>();
+    constexpr int WT = TcCfg<CF>::WT;
+    constexpr int S = TcCfg<CF>::S, BN = TcCfg<CF>::BN, STAGES = TcCfg<CF>::STAGES;
+    constexpr int SB = stage_bytes<CF>();
     constexpr int KSTEP = 32;                                      // bytes of K per MMA instruction (both kinds)
     constexpr int TMEM_COLS = 2 * BN;                              // two accumulators
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -252,7 +259,7 @@ k_gemm_tc(const __grid_constant__ TcMaps maps, const ec_gemm_args a, const float
     // stage s: A parts at base + s*SB + p*A_BYTES, W at base + s*SB + S*A_BYTES
     float *stage_out = reinterpret_cast<float *>(gbase + STAGES * SB);
     float *cst = reinterpret_cast<float *>(gbase + STAGES * SB + EPI_BYTES);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(gbase + STAGES * SB + EPI_BYTES + cst_bytes<WT>());
+    uint64_t *bars = reinterpret_cast<uint64_t *>(gbase + STAGES * SB + EPI_BYTES + cst_bytes<CF>());
     uint64_t *full = bars, *empty = bars + STAGES;
     uint64_t *accf = bars + 2 * STAGES, *acce = accf + 2, *drain = acce + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
@@ -262,9 +269,9 @@ k_gemm_tc(const __grid_constant__ TcMaps maps, const ec_gemm_args a, const float
     volatile int *flag_last = consumed + 1;      // split-K: this CTA completed the tile
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int kbytes = a.Kp * TcCfg<WT>::ELT;
+    const int kbytes = a.Kp * TcCfg<CF>::ELT;
     const int nk = (kbytes + BKB - 1) / BKB;
-    const int kel = BKB / TcCfg<WT>::ELT;                          // K elements per stage
+    const int kel = BKB / TcCfg<CF>::ELT;                          // K elements per stage
     const int mt = (a.M + BM - 1) / BM, nt = (a.N + BN - 1) / BN;
     const int tiles = mt * nt, items = tiles * ksplit;
 
@@ -332,7 +339,7 @@ k_gemm_tc(const __grid_constant__ TcMaps maps, const ec_gemm_args a, const float
                     for (int k = 0; k < BKB / KSTEP; ++k)     // +2 in 16-byte units per 32 bytes of K
 #pragma unroll
                         for (int p = 0; p < S; ++p)
-                            mma<WT>(d, sw128_desc(st + p * A_BYTES) + 2 * k, db + 2 * k, ((kb - kb0) | k | p) != 0);
+                            mma<CF>(d, sw128_desc(st + p * A_BYTES) + 2 * k, db + 2 * k, ((kb - kb0) | k | p) != 0);
                     mma_commit(ec_smem_u32(&empty[s]));   // stage reusable once these MMAs have read it
                     *consumed = g + 1;
                 }
@@ -511,7 +518,7 @@ __global__ void __launch_bounds__(256) k_split16(uint16_t *parts, float *rscale,
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 pthread_once_t g_once = PTHREAD_ONCE_INIT;
-int g_attr_set[3][64];
+int g_attr_set[4][64];
 int g_sms[64];
 
 void resolve_encode() {
@@ -537,21 +544,22 @@ int make_map(CUtensorMap *map, const void *ptr, int elt, int inner, int rows, in
     return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
 }
 
-template <int WT>
+template <int CF>
 int set_attr(int dev) {
-    if (!g_attr_set[WT][dev]) {
-        const cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes<WT>());
+    if (!g_attr_set[CF][dev]) {
+        const cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<CF>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes<CF>());
         if (e != cudaSuccess) return (int)e;
-        g_attr_set[WT][dev] = 1;
+        g_attr_set[CF][dev] = 1;
     }
     return 0;
 }
 
-template <int WT>
+template <int CF>
 int launch(const ec_gemm_args &a, const void *const *aparts, const float *row_scale, int dev, cudaStream_t stream) {
-    constexpr int S = TcCfg<WT>::S, BN = TcCfg<WT>::BN, ELT = TcCfg<WT>::ELT;
+    constexpr int WT = TcCfg<CF>::WT;
+    constexpr int S = TcCfg<CF>::S, BN = TcCfg<CF>::BN, ELT = TcCfg<CF>::ELT;
     {
-        const int e = set_attr<WT>(dev);
+        const int e = set_attr<CF>(dev);
         if (e) return e;
     }
     TcMaps maps;
@@ -581,7 +589,7 @@ int launch(const ec_gemm_args &a, const void *const *aparts, const float *row_sc
     const long long items = tiles * ksplit;
     const int grid = (int)(items < (long long)sms ? items : sms);
     const int flags = (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 && (a.ldo & 3) == 0 ? 1 : 0;
-    k_gemm_tc<WT><<<grid, THREADS, smem_bytes<WT>(), stream>>>(maps, a, row_scale, flags, ksplit);
+    k_gemm_tc<CF><<<grid, THREADS, smem_bytes<CF>(), stream>>>(maps, a, row_scale, flags, ksplit);
     return (int)cudaGetLastError();
 }
 
@@ -623,6 +631,10 @@ extern "C" int ec_launch_gemm_tc(const ec_gemm_args *args, cudaStream_t stream) 
     }
     if (a.wt == EC_W_I8) {
         const void *parts[1] = {a.Aq};
+        // one row of tiles (M <= 128) whose 256-column tiles would occupy
+        // fewer than half the SMs: 64-column tiles, four times the CTAs
+        const int wide_tiles = (a.N + TcCfg<EC_W_I8>::BN - 1) / TcCfg<EC_W_I8>::BN;
+        if (a.M <= BM && 2 * wide_tiles <= g_sms[dev]) return launch<TC_I8_NARROW>(a, parts, a.a_scale, dev, stream);
         return launch<EC_W_I8>(a, parts, a.a_scale, dev, stream);
     }
     // 16-bit weights: split the activations first (Kp % 16 == 0 keeps every
@@ -656,6 +668,7 @@ extern "C" int ec_tc_init(void) {
         if (e != cudaSuccess) return (int)e;
     }
     int rc = set_attr<EC_W_I8>(dev);
+    if (!rc) rc = set_attr<TC_I8_NARROW>(dev);
     if (!rc) rc = set_attr<EC_W_F16>(dev);
     if (!rc) rc = set_attr<EC_W_BF16>(dev);
     return rc;
