@@ -631,10 +631,10 @@ extern "C" int ec_launch_gemm_tc(const ec_gemm_args *args, cudaStream_t stream) 
     }
     if (a.wt == EC_W_I8) {
         const void *parts[1] = {a.Aq};
-        // one row of tiles (M <= 128) whose 256-column tiles would occupy
-        // fewer than half the SMs: 64-column tiles, four times the CTAs
-        const int wide_tiles = (a.N + TcCfg<EC_W_I8>::BN - 1) / TcCfg<EC_W_I8>::BN;
-        if (a.M <= BM && 2 * wide_tiles <= g_sms[dev]) return launch<TC_I8_NARROW>(a, parts, a.a_scale, dev, stream);
+        // 256-column tiles that would occupy fewer than half the SMs:
+        // 64-column tiles, four times the CTAs
+        const long long wide_tiles = (long long)((a.M + BM - 1) / BM) * ((a.N + TcCfg<EC_W_I8>::BN - 1) / TcCfg<EC_W_I8>::BN);
+        if (2 * wide_tiles <= g_sms[dev]) return launch<TC_I8_NARROW>(a, parts, a.a_scale, dev, stream);
         return launch<EC_W_I8>(a, parts, a.a_scale, dev, stream);
     }
     // 16-bit weights: split the activations first (Kp % 16 == 0 keeps every
