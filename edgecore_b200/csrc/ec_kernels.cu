@@ -902,7 +902,10 @@ __global__ void __launch_bounds__(ATTX_THREADS) k_attn_exact(const ec_attn_args 
 #pragma unroll
             for (int hh = 0; hh < ATTX_MAX_GROUP; ++hh) {
                 if (hh < G) {
-                    const float *q = qs + hh * hd + d;
+                    // q in two 16-byte broadcast loads (qs rows are 32-byte aligned: hd % 8 == 0)
+                    const float4 q0 = *reinterpret_cast<const float4 *>(qs + hh * hd + d);
+                    const float4 q1 = *reinterpret_cast<const float4 *>(qs + hh * hd + d + 4);
+                    const float q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
                     float t = acc[hh];
 #pragma unroll
                     for (int e = 0; e < 8; ++e) t = __fadd_rn(t, __fmul_rn(q[e], f[e]));
@@ -960,9 +963,19 @@ __global__ void __launch_bounds__(ATTX_THREADS) k_attn_exact(const ec_attn_args 
             if (idx >= npair) break;
             const int hh = idx / hd, d = idx - hh * hd;
             const float *w = sc + hh * a.maxlen + c0;
+            const uint16_t *vd = vs + d;
             float acc = o[k];
-            for (int i = 0; i < n; ++i)
-                acc = __fadd_rn(acc, __fmul_rn(w[i], __half2float(__ushort_as_half(vs[(size_t)i * hd + d]))));
+            int i = 0;
+            if (((a.maxlen | c0) & 3) == 0)   // weights 16-byte aligned: four per broadcast load
+                for (; i + 4 <= n; i += 4) {
+                    const float4 w4 = *reinterpret_cast<const float4 *>(w + i);
+                    acc = __fadd_rn(acc, __fmul_rn(w4.x, __half2float(__ushort_as_half(vd[(size_t)i * hd]))));
+                    acc = __fadd_rn(acc, __fmul_rn(w4.y, __half2float(__ushort_as_half(vd[(size_t)(i + 1) * hd]))));
+                    acc = __fadd_rn(acc, __fmul_rn(w4.z, __half2float(__ushort_as_half(vd[(size_t)(i + 2) * hd]))));
+                    acc = __fadd_rn(acc, __fmul_rn(w4.w, __half2float(__ushort_as_half(vd[(size_t)(i + 3) * hd]))));
+                }
+            for (; i < n; ++i)
+                acc = __fadd_rn(acc, __fmul_rn(w[i], __half2float(__ushort_as_half(vd[(size_t)i * hd]))));
             o[k] = acc;
         }
     }
