@@ -1,15 +1,16 @@
 // ec_kernels.cu -- the sm_100a kernels of the decode/prefill path.
 //
-//   k_gemv        weight-streaming GEMV for M <= 8 token rows.  Each CTA owns
-//                 row blocks of the [N][Kp] weight matrix and stages them into
-//                 shared memory with bulk TMA copies (cp.async.bulk) issued
-//                 before it quantises the activations, so HBM streaming and the
-//                 activation prologue overlap.  int8 weights: exact int32 dp4a
-//                 dot + the reference epilogue (bias + ((float)dot*as)*ws).
-//   k_gemm_simt   generic tiled GEMM for any M (prefill until the tcgen05 path
-//                 takes over), same numerics.
+//   k_gemv        weight-streaming GEMV for M <= 8 token rows: every lane keeps
+//                 R rows x J 16-byte chunks of the [N][ldw] weight matrix in
+//                 flight with L1-bypassing loads, the activations sit in shared
+//                 memory, and a transposed shuffle reduction finishes each row.
+//                 int8 weights: exact int32 dp4a dot + the reference epilogue
+//                 (bias + ((float)dot*as)*ws).
+//   k_gemm_i8, k_gemm_f  SIMT tiled GEMMs for 8 < M < 32 and for operands the
+//                 tcgen05 path (ec_tc.cu) cannot take, same numerics.
 //   k_quant       per-row activation quantisation (reference gpt2.c:446-461).
-//   k_embed, k_norm, k_qkv_split, k_swiglu, k_gelu, k_attn_exact, k_attn_part/combine,
+//   k_embed, k_norm, k_norm_quant, k_qkv_split, k_swiglu, k_swiglu_quant, k_gelu,
+//   k_attn_exact, k_attn_part/combine,
 //   k_argmax*, k_step_advance.
 //
 // Every index that comes from the caller (token ids, positions, slots) is
