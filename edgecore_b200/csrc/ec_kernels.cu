@@ -865,10 +865,13 @@ __host__ __device__ inline size_t attx_smem_bytes(int G, int hd, int maxlen) {
 
 __global__ void __launch_bounds__(ATTX_THREADS) k_attn_exact(const ec_attn_args a) {
     extern __shared__ __align__(16) float attx_smem[];
-    const int g = blockIdx.x, m = blockIdx.y;
+    const int m = blockIdx.y;
     const ec_kvgeo &geo = a.geo;
     const int hd = geo.hd;
-    const int h0 = (g * a.H + a.KVH - 1) / a.KVH, h1 = ((g + 1) * a.H + a.KVH - 1) / a.KVH;
+    // the query heads of this CTA: one (per_head) or all of KV head g's
+    const int g = a.per_head ? (int)blockIdx.x * a.KVH / a.H : (int)blockIdx.x;
+    const int h0 = a.per_head ? (int)blockIdx.x : (g * a.H + a.KVH - 1) / a.KVH;
+    const int h1 = a.per_head ? h0 + 1 : ((g + 1) * a.H + a.KVH - 1) / a.KVH;
     const int G = h1 - h0;
     const int pos = a.tk.pos[m], slot = a.tk.slot[m];
     if (pos < 0 || pos >= geo.C || slot < 0 || slot >= geo.B || G <= 0 || G > ATTX_MAX_GROUP) {
@@ -1012,9 +1015,19 @@ extern "C" int ec_launch_attention(const ec_attn_args *a, cudaStream_t stream) {
     if (a->M <= 0) return 0;
     if (a->geo.hd > 256 || a->geo.hd % 8 || a->nsplit < 1) return (int)cudaErrorInvalidValue;
     if (!g_attn_force_split && ec_attention_exact_fits(a->H, a->KVH, a->geo.hd, a->maxlen)) {
-        const int G = a->H / a->KVH;
-        dim3 g(a->KVH, a->M);
-        k_attn_exact<<<g, ATTX_THREADS, attx_smem_bytes(G, a->geo.hd, a->maxlen), stream>>>(*a);
+        // few rows: one CTA per query head (its KV rows are read once per
+        // head instead of once per group) so that the grid fills the GPU
+        static int sms = 0;
+        if (!sms) {
+            int dev = 0;
+            cudaGetDevice(&dev);
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        }
+        ec_attn_args b = *a;
+        b.per_head = a->M * a->KVH < sms && a->H > a->KVH;   // measured: 32 rows 0.47 -> 0.39 ms per step; 128 rows slower
+        const int G = b.per_head ? 1 : a->H / a->KVH;
+        dim3 g(b.per_head ? a->H : a->KVH, a->M);
+        k_attn_exact<<<g, ATTX_THREADS, attx_smem_bytes(G, a->geo.hd, a->maxlen), stream>>>(b);
         return (int)cudaGetLastError();
     }
     dim3 g1(a->nsplit, a->H, a->M);

@@ -165,6 +165,8 @@ typedef struct {
     float *part;                  /* scratch: [M][H][nsplit][hd + 2] */
     int nsplit;
     int maxlen;                   /* upper bound on attended positions per row */
+    int per_head;                 /* set by the launcher: one CTA per (head, row)
+                                     instead of per (KV head, row) */
 } ec_attn_args;
 /* Chooses the exact-order kernel (reference summation order; one CTA per
  * (token, KV head) holding all scores in shared memory) when maxlen fits,
