@@ -1006,7 +1006,7 @@ def op_sweep_results(args, cpu_seconds: float):
                 "us_per_call": us, "algorithmic_bytes": algo, "achieved_gbs": algo / us / 1e3,
                 "hbm_frac": algo / us / 1e3 / peak, "hbm_peak_gbs": peak, "peak_source": peak_kind,
                 "tops" if wt == 0 else "tflops": flops / us / 1e6,
-                "path": "weight-streaming GEMV" if M <= 8 else ("tcgen05" if M >= 32 else "SIMT"),
+                "path": "weight-streaming GEMV" if M < 8 else "tcgen05",
                 "timing": f"CUDA events around one replay of a CUDA graph of {max(10, 2 * nbuf)} back-to-back "
                           f"launches rotating {nbuf} weight copies ({nbuf * wbytes / 2**20:.0f} MiB > L2)"}
         if ref is not None and M * N * K <= 2e10:

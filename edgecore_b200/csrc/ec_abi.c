@@ -92,7 +92,7 @@ static int dev_view(abi_ctx *c, int slot, const void *src, int rows, int cols, i
     return 0;
 }
 
-/* Weight-side linear over [N][Kp] with the GEMV (M <= 8) or GEMM kernels. */
+/* Weight-side linear over [N][Kp] with the GEMV (M < EC_TC_MIN_M) or GEMM kernels. */
 static int run_linear(abi_ctx *c, int wt, float *C, const float *X, const int8_t *Aq, const float *a_scale,
                       const void *B, const float *b_scale, const float *bias, int M, int K, int N, int quantise)
 {
@@ -110,7 +110,7 @@ static int run_linear(abi_ctx *c, int wt, float *C, const float *X, const int8_t
     }
     for (int m0 = 0; m0 < M;) {
         int rows = M - m0;
-        if (M <= 8) {
+        if (M < EC_TC_MIN_M) {
             ec_gemv_args g;
             memset(&g, 0, sizeof g);
             g.W = dB; g.wscale = dbs; g.bias = dbias; g.wt = wt; g.N = N; g.K = K; g.Kp = Kp;
@@ -209,7 +209,7 @@ EC_EXPORT int ec_gemm_async(int wt, float *C, const void *A, const float *a_scal
     v.M = M; v.out = C; v.ldo = N; v.epi = EC_EPI_STORE;
     if (wt == EC_W_I8) { v.Xq = (const int8_t *)A; v.xscale = a_scale; v.ldx = K; }
     else { v.X = (const float *)A; v.ldx = K; }
-    if (M <= 8 && ec_gemv_fits(&v)) {
+    if (M < EC_TC_MIN_M && ec_gemv_fits(&v)) {   /* from EC_TC_MIN_M rows the tensor cores are faster */
         e = ec_launch_gemv(&v, sms, st);
     } else {
         ec_gemm_args g;

@@ -110,7 +110,7 @@ int ec_launch_gemm(const ec_gemm_args *a, cudaStream_t stream);
  * activations split into 16-bit parts in the `split` workspace;
  * cudaErrorNotSupported when the operands miss its alignment rules.
  * ec_tc_error_take reads and clears its error word. */
-#define EC_TC_MIN_M 32
+#define EC_TC_MIN_M 8
 int ec_launch_gemm_tc(const ec_gemm_args *a, cudaStream_t stream);
 
 /* One-time set-up of the tensor-core GEMMs on the current device (driver

@@ -24,10 +24,10 @@
 //    the GEMV and of the tensor-core GEMMs and resolves the driver's
 //    tensor-map encoder, and the CUDA runtime loads the kernels it launches.
 //    Make that first call before starting any stream capture on that device.
-//  * M <= 8 runs the weight-streaming GEMV when one staged W row plus the M
+//  * M < 8 runs the weight-streaming GEMV when one staged W row plus the M
 //    int8 activation rows fit the GEMV's shared memory (K up to about
-//    113,000 at M = 1, 25,000 at M = 8); otherwise, and for M > 8, the GEMM
-//    kernels run.
+//    113,000 at M = 1, 28,000 at M = 7); otherwise, and for M >= 8, the
+//    GEMM kernels run (tcgen05 tensor cores from 8 rows).
 //  * Device-side failures (a bounded wait that gave up inside a kernel) are
 //    not visible in the return code, which only covers the checks and the
 //    launches: after synchronising the stream, ec_device_error_take() reads
@@ -140,7 +140,7 @@ extern "C" __attribute__((visibility("default"))) int ec_linear_int8_noalloc(
         ec_gemv_args g;
         memset(&g, 0, sizeof g);
         bool gemv = false;
-        if (M <= 8) {
+        if (M < EC_TC_MIN_M) {
             g.W = W; g.wscale = w_scale; g.bias = bias;
             g.wt = EC_W_I8; g.N = N; g.K = K; g.Kp = K; g.ldw = K;
             int R = (N + 2 * sms - 1) / (2 * sms);   // about two row blocks per SM

@@ -1,4 +1,4 @@
-// ec_tc.cu -- GEMMs on the 5th-generation tensor cores (tcgen05) for M >= 32
+// ec_tc.cu -- GEMMs on the 5th-generation tensor cores (tcgen05) for M >= EC_TC_MIN_M (8)
 // rows (prefill, batched decode):
 //
 //   int8 weights (kind::i8):

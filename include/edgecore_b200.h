@@ -216,9 +216,8 @@ int ec_attention_force_split(int on);
  * device, enqueued on `stream` with no host synchronisation: the
  * reference's gemm_* (src/kernels.c:129-168) for GPU callers that keep their
  * data resident.  K must be a multiple of 16 (rows are read in place).
- * M <= 8 runs the weight-streaming GEMV, larger M the GEMM kernels (tcgen05
- * from 32 rows; 16-bit weights there use a library workspace allocated on
- * first use).  Device-side errors: ec_device_error_take. */
+ * M < 8 runs the weight-streaming GEMV, larger M the tcgen05 GEMM kernels
+ * (16-bit weights there use a library workspace allocated on first use).  Device-side errors: ec_device_error_take. */
 int ec_gemm_async(int wt, float *C, const void *A, const float *a_scale, const void *B,
                   const float *b_scale, const float *bias, int M, int K, int N, void *stream);
 
@@ -235,7 +234,7 @@ int ec_device_error_take(void *stream, int *code);
  * that must not be stalled by cudaMalloc's device synchronisation.  The
  * int8 activations and their scales live in a fixed 4 MiB per-device static
  * buffer: requires M*K + 4*M (rounded up to 256) <= 4 MiB, K % 16 == 0 and
- * device pointers only; larger sizes are rejected with an error.  M <= 8
+ * device pointers only; larger sizes are rejected with an error.  M < 8
  * uses the weight-streaming GEMV when a W row plus the M activation rows fit
  * its shared memory (K up to about 113,000 at M = 1), else the GEMM kernels.
  * The first call on a device does the set-up (scratch address lookup,
