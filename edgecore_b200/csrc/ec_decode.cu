@@ -1346,11 +1346,13 @@ __global__ void __launch_bounds__(EC_MK_THREADS, 1) k_decode(const __grid_consta
         ec_fence_mbar_init();
         S.flag[0] = 0;
         S.tcount[0] = S.tcount[1] = 0;
+        // the paired counter is unused by this launch; the next one starts on it
+        if (cta == 0 && pg.bar_next) *pg.bar_next = 0u;
     }
     if (threadIdx.x < M) {
-        S.ltok[threadIdx.x] = pg.tok[threadIdx.x];
-        S.lpos[threadIdx.x] = pg.pos[threadIdx.x];
-        S.lslot[threadIdx.x] = pg.slot[threadIdx.x];
+        S.ltok[threadIdx.x] = pg.inline_in ? pg.in_tok[threadIdx.x] : pg.tok[threadIdx.x];
+        S.lpos[threadIdx.x] = pg.inline_in ? pg.in_pos[threadIdx.x] : pg.pos[threadIdx.x];
+        S.lslot[threadIdx.x] = pg.inline_in ? pg.in_slot[threadIdx.x] : pg.slot[threadIdx.x];
     }
     {   // layer descriptors -> shared memory (read on every phase and tile)
         uint32_t *dst = reinterpret_cast<uint32_t *>(g_smem + L.lays);
@@ -1514,6 +1516,9 @@ __global__ void __launch_bounds__(EC_MK_THREADS, 1) k_decode(const __grid_consta
         }
         cons_sync();
     }
+    // clean end: errors recorded by any CTA before the last grid barrier
+    // are visible here through that barrier's acquire
+    if (p.done && cta == 0 && ct == 0) *(volatile int *)p.done = ld_relaxed_i(p.err) ? -1 : p.seq;
 #undef SYNC_OR_RETURN
 }
 

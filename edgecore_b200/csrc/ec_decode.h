@@ -71,8 +71,17 @@ typedef struct {
     int wrap_lo, wrap_hi;       /* position cycle (wrap_hi <= 0: none)     */
     float *taps;                /* [L+1][M][E] or NULL                     */
     unsigned *bar;              /* grid barrier counter, zero at launch    */
+    unsigned *bar_next;         /* the other counter of a pair: CTA 0 zeroes
+                                   it for the next launch (or NULL)        */
     int *abort_flag;            /* set by any CTA that gives up            */
     int *err;
+    int in_tok[EC_MK_MT];       /* inline_in: the rows' token, position and */
+    int in_pos[EC_MK_MT];       /* slot passed by value (tok / pos / slot   */
+    int in_slot[EC_MK_MT];      /* are then not read)                       */
+    int inline_in;
+    int *done;                  /* host-mapped word or NULL: CTA 0 writes seq
+                                   at a clean end, -1 if an error was recorded */
+    int seq;
     int maxlen;                 /* max attended positions per row          */
     int own_rows;               /* >= residual rows owned by one CTA       */
     int kvchunk;                /* cached positions staged per attention

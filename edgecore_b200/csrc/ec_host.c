@@ -235,8 +235,11 @@ typedef struct ec_dev {
     /* persistent decode kernel */
     ec_mk_layer *d_mk_layers;
     int mk_grid;
-    unsigned *d_bar;
+    unsigned *d_bar;           /* two barrier counters (128 B apart) and the abort flag */
     int *d_abort, *d_mk_err;
+    int bar_par, bar_reset;    /* counter of the next launch; 1: clear all three first */
+    int *h_res, *h_res_dev;    /* pinned, mapped: completion word | ids [8] | max [8] */
+    int res_seq;
     float *amax_v;
     int *amax_i;
     /* workspaces */
@@ -540,9 +543,20 @@ static int ec_mk_build(ec_dev *d)
     free(h);
     if (rc) return -1;
     d->mk_grid = ok ? d->num_sms : 0;   /* 0: the persistent kernel is not usable */
-    /* barrier counter and abort flag side by side: one reset per launch */
-    CK(cudaMalloc((void **)&d->d_bar, 32));
-    d->d_abort = (int *)(d->d_bar + 4);
+    /* a pair of barrier counters used alternately (each launch zeroes the
+     * other one for its successor) and the abort flag, on separate lines */
+    CK(cudaMalloc((void **)&d->d_bar, 512));
+    d->d_abort = (int *)(d->d_bar + 64);
+    d->bar_par = 0;
+    d->bar_reset = 1;
+    /* small results of host-array decode calls, written by the kernel
+     * straight into pinned host memory */
+    CK(cudaHostAlloc((void **)&d->h_res, 256, cudaHostAllocMapped));
+    memset(d->h_res, 0, 256);
+    if (cudaHostGetDevicePointer((void **)&d->h_res_dev, d->h_res, 0) != cudaSuccess) {
+        cudaGetLastError();
+        d->h_res_dev = NULL;
+    }
     CK(cudaMalloc((void **)&d->d_mk_err, 16));
     CK(cudaMemset(d->d_mk_err, 0, 16));
     CK(cudaMalloc((void **)&d->amax_v, (size_t)d->num_sms * EC_MK_MT * 4));
@@ -699,6 +713,7 @@ static void ec_dev_free(ec_dev *d)
     cudaFree(d->kc); cudaFree(d->vc); cudaFree(d->rope_cos); cudaFree(d->rope_sin);
     cudaFreeHost(d->h_pt); cudaFree(d->d_pt); free(d->free_pages); free(d->kv_undo);
     cudaFree(d->d_mk_layers); cudaFree(d->d_bar); cudaFree(d->d_mk_err);
+    cudaFreeHost(d->h_res);
     cudaFree(d->amax_v); cudaFree(d->amax_i);
     cudaFree(d->attn_part); cudaFree(d->logits); cudaFree(d->amax_part);
     cudaFree(d->d_hist); cudaFree(d->taps); cudaFree(d->d_counter);
@@ -708,6 +723,7 @@ static void ec_dev_free(ec_dev *d)
     cudaFreeHost(d->h_logits);
     if (d->prof_ready)
         for (int i = 0; i < 2 * EC_PROF_MAX; i++) cudaEventDestroy(d->prof_ev[i]);
+
     if (d->own_stream) cudaStreamDestroy(d->own_stream);
     free(d);
     cudaSetDevice(cur);
@@ -1289,12 +1305,27 @@ static int ec_max_len(const ec_dev *d, int M)
     return mx;
 }
 
+/* Pinned host staging of at least `bytes` for logits copies. */
+static int ec_host_logits(ec_dev *d, size_t bytes)
+{
+    if (bytes <= d->h_logits_cap) return 0;
+    cudaFreeHost(d->h_logits);
+    d->h_logits = NULL;
+    d->h_logits_cap = 0;
+    CK(cudaMallocHost((void **)&d->h_logits, bytes));
+    d->h_logits_cap = bytes;
+    return 0;
+}
+
 static int ec_check_kernel_error(ec_dev *d)
 {
     int code = 0, mk = 0;
     CK(ec_kernel_error_take(d->stream, &code));
     CK(cudaMemcpy(&mk, d->d_mk_err, 4, cudaMemcpyDeviceToHost));
-    if (mk) CK(cudaMemset(d->d_mk_err, 0, 4));
+    if (mk) {
+        CK(cudaMemset(d->d_mk_err, 0, 4));
+        d->bar_reset = 1;   /* the abort flag may be set */
+    }
     if (code || mk) {
         ec_seterr("device kernel reported error code %d/%d (bad index or bounded wait gave up)", code, mk);
         return -1;
@@ -1366,10 +1397,20 @@ static int ec_mk_plan(ec_dev *d, int M, int maxlen, ec_mk_params *p)
     return 0;
 }
 
+/* Launch the decode kernel on the counter of this launch; it zeroes the
+ * other one for the next launch, so no reset is enqueued unless an error
+ * was seen (bar_reset). */
 static int ec_mk_run(ec_dev *d, const ec_mk_params *p, int n_steps)
 {
-    CK(cudaMemsetAsync(d->d_bar, 0, 32, d->stream));   /* counter and abort flag */
-    CK(ec_mk_launch(p, n_steps, d->mk_grid, d->stream));
+    ec_mk_params q = *p;
+    if (d->bar_reset) {
+        CK(cudaMemsetAsync(d->d_bar, 0, 512, d->stream));   /* both counters and the abort flag */
+        d->bar_reset = 0;
+    }
+    q.bar = d->d_bar + 32 * d->bar_par;
+    q.bar_next = d->d_bar + 32 * (1 - d->bar_par);
+    d->bar_par ^= 1;
+    CK(ec_mk_launch(&q, n_steps, d->mk_grid, d->stream));
     return 0;
 }
 
@@ -1386,15 +1427,54 @@ static int ec_forward_impl(GPT2 *g, const int *tokens, const int *positions, con
     if (ec_stage_inputs(d, tokens, positions, seqs, M)) return -1;
     const int maxlen = ec_len_bucket(d, ec_max_len(d, M));
     const int Vs = d->v1 - d->v0;
-    if (ec_copy_inputs(d, M)) return -1;
     ec_mk_params mp;
     if (ec_mk_plan(d, M, maxlen, &mp) == 0) {
-        if (!ids && ec_ensure_logits(d, M)) return -1;
-        mp.logits = ids ? NULL : d->logits;
-        mp.ids = d->d_ids;
-        mp.maxv = d->d_max;
+        const size_t bytes = (size_t)M * Vs * 4;
+        if (!ids && (ec_host_logits(d, bytes) || ec_ensure_logits(d, M))) return -1;
+        const int mapped = d->h_res_dev != NULL;
+        if (mapped) {
+            /* inputs by value in the launch parameters; ids and the completion
+             * word written by the kernel into pinned host memory; logits in
+             * device memory and one copy (written in place by the kernel over
+             * PCIe they cost more: its stores are scattered 16-byte pieces) */
+            for (int m = 0; m < M; m++) {
+                mp.in_tok[m] = d->h_in[m];
+                mp.in_pos[m] = d->h_in[M + m];
+                mp.in_slot[m] = d->h_in[2 * M + m];
+            }
+            mp.inline_in = 1;
+            mp.logits = ids ? NULL : d->logits;
+            mp.ids = d->h_res_dev + 1;
+            mp.maxv = (float *)(d->h_res_dev + 1 + EC_MK_MT);
+            d->res_seq = d->res_seq >= 0x3fffffff ? 1 : d->res_seq + 1;
+            mp.done = d->h_res_dev;
+            mp.seq = d->res_seq;
+            ((volatile int *)d->h_res)[0] = 0;
+        } else {
+            if (ec_copy_inputs(d, M)) return -1;
+            mp.logits = ids ? NULL : d->logits;
+            mp.ids = d->d_ids;
+            mp.maxv = d->d_max;
+        }
         mp.advance = 0;
         if (ec_mk_run(d, &mp, 1)) return -1;
+        if (mapped) {
+            if (!ids) CK(cudaMemcpyAsync(d->h_logits, d->logits, bytes, cudaMemcpyDeviceToHost, d->stream));
+            CK(cudaStreamSynchronize(d->stream));
+            if (((volatile int *)d->h_res)[0] != mp.seq) {   /* aborted or an error recorded */
+                if (ec_check_kernel_error(d)) return -1;
+                d->bar_reset = 1;
+                ec_seterr("decode kernel did not complete");
+                return -1;
+            }
+            if (ids) {
+                memcpy(ids, d->h_res + 1, (size_t)M * 4);
+                if (maxv) memcpy(maxv, d->h_res + 1 + EC_MK_MT, (size_t)M * 4);
+            } else {
+                memcpy(logits, d->h_logits, bytes);
+            }
+            return 0;
+        }
         if (ids) {
             CK(cudaMemcpyAsync(d->h_ids, d->d_ids, (size_t)M * 4, cudaMemcpyDeviceToHost, d->stream));
             CK(cudaMemcpyAsync(d->h_max, d->d_max, (size_t)M * 4, cudaMemcpyDeviceToHost, d->stream));
@@ -1402,13 +1482,6 @@ static int ec_forward_impl(GPT2 *g, const int *tokens, const int *positions, con
             memcpy(ids, d->h_ids, (size_t)M * 4);
             if (maxv) memcpy(maxv, d->h_max, (size_t)M * 4);
         } else {
-            const size_t bytes = (size_t)M * Vs * 4;
-            if (bytes > d->h_logits_cap) {
-                cudaFreeHost(d->h_logits);
-                d->h_logits = NULL;
-                CK(cudaMallocHost((void **)&d->h_logits, bytes));
-                d->h_logits_cap = bytes;
-            }
             CK(cudaMemcpyAsync(d->h_logits, d->logits, bytes, cudaMemcpyDeviceToHost, d->stream));
             CK(cudaStreamSynchronize(d->stream));
             memcpy(logits, d->h_logits, bytes);
@@ -1416,6 +1489,7 @@ static int ec_forward_impl(GPT2 *g, const int *tokens, const int *positions, con
         return ec_check_kernel_error(d);
     }
     /* prefill path: per-layer kernels, lm_head in row chunks */
+    if (ec_copy_inputs(d, M)) return -1;
     if (ec_ensure_attn(d, M, maxlen)) return -1;
     if (ec_enqueue_body(d, M, maxlen)) return -1;
     int chunk = (int)((256u << 20) / ((size_t)Vs * 4));
@@ -1423,12 +1497,7 @@ static int ec_forward_impl(GPT2 *g, const int *tokens, const int *positions, con
     if (chunk > M) chunk = M;
     if (ec_ensure_logits(d, chunk) || ec_ensure_amax(d, chunk)) return -1;
     const size_t hbytes = (size_t)chunk * Vs * 4;
-    if (!ids && hbytes > d->h_logits_cap) {
-        cudaFreeHost(d->h_logits);
-        d->h_logits = NULL;
-        CK(cudaMallocHost((void **)&d->h_logits, hbytes));
-        d->h_logits_cap = hbytes;
-    }
+    if (!ids && ec_host_logits(d, hbytes)) return -1;
     for (int r0 = 0; r0 < M; r0 += chunk) {
         const int rows = M - r0 < chunk ? M - r0 : chunk;
         if (ec_enqueue_lm(d, r0, rows)) return -1;
@@ -1915,9 +1984,12 @@ EC_EXPORT int ec_decode_profile(GPT2 *g, int *d_tokens, int start_pos, int n_ste
         if (ec_decode_setup(d, d_tokens, start_pos, M, start_pos + n_steps)) return -1;
         mp.advance = 1;
         for (int st = 0; st < n_steps; st++) {
-            CK(cudaMemsetAsync(d->d_bar, 0, 32, d->stream));   /* counter and abort flag */
+            if (d->bar_reset) {   /* outside the timed interval */
+                CK(cudaMemsetAsync(d->d_bar, 0, 512, d->stream));
+                d->bar_reset = 0;
+            }
             CK(cudaEventRecord(d->prof_ev[0], d->stream));
-            CK(ec_mk_launch(&mp, 1, d->mk_grid, d->stream));
+            if (ec_mk_run(d, &mp, 1)) return -1;
             CK(cudaEventRecord(d->prof_ev[1], d->stream));
             CK(cudaStreamSynchronize(d->stream));
             float ms = 0.0f;
