@@ -12,6 +12,39 @@
 
 #define EC_DEV __device__ __forceinline__
 
+// Programmatic dependent launch.  The tensor-core GEMMs (ec_launch_k) may
+// start while their predecessor on the stream is still finishing, so that
+// their set-up and first weight tiles overlap its tail.  EC_PDL_ENTER()
+// waits (griddepcontrol.wait) until the predecessor has completed and its
+// writes are visible -- a no-op for a kernel launched without the attribute
+// -- and lets the next kernel start early (griddepcontrol.launch_dependents,
+// which only matters when that kernel is launched with the attribute).  It
+// comes before the kernel's first global-memory access.  Every kernel of the
+// library enters through it; only the GEMMs are launched with the attribute
+// (per-step batched decode: 1.94 -> 1.84 ms at 32 streams; launching every
+// kernel so was slower than launching none).
+#define EC_PDL_WAIT() asm volatile("griddepcontrol.wait;" ::: "memory")
+#define EC_PDL_NEXT() asm volatile("griddepcontrol.launch_dependents;" ::: "memory")
+#define EC_PDL_ENTER() do { EC_PDL_WAIT(); EC_PDL_NEXT(); } while (0)
+
+// Launch with programmatic stream serialisation (see EC_PDL_ENTER); the
+// kernel must begin with EC_PDL_ENTER() or EC_PDL_WAIT().
+template <typename... KArgs, typename... Args>
+static inline cudaError_t ec_launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                      cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // Error codes written to the library error word (first error wins).
 enum { EC_KERR_NONE = 0, EC_KERR_WAIT_TIMEOUT = 1, EC_KERR_BAD_INDEX = 2 };
 

@@ -68,6 +68,7 @@ __host__ __device__ inline size_t gemv_smem_bytes(int wt, int M, int Kp) {
 
 template <int WT, int MM, int R, int J>
 __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const ec_gemv_args a) {
+    EC_PDL_ENTER();
     typedef typename GemvAcc<WT>::T Acc;
     constexpr int ELT = WT == EC_W_I8 ? 1 : 2;
     constexpr int V = R * MM;   // values reduced per row group: [r][m]
@@ -337,6 +338,7 @@ EC_DEV void gemm_apply(const ec_gemm_args &a, int m, int n, float v) {
 }
 
 __global__ void __launch_bounds__(256) k_gemm_i8(const ec_gemm_args a) {
+    EC_PDL_ENTER();
     __shared__ __align__(16) int8_t As[GT_BM][GT_BK + 16];
     __shared__ __align__(16) int8_t Ws[GT_BN][GT_BK + 16];
     const int tid = threadIdx.x;
@@ -381,6 +383,7 @@ __global__ void __launch_bounds__(256) k_gemm_i8(const ec_gemm_args a) {
 
 template <int WT>
 __global__ void __launch_bounds__(256) k_gemm_f(const ec_gemm_args a) {
+    EC_PDL_ENTER();
     __shared__ float As[GT_BK / 2][GT_BM + 4];   // [k][m]
     __shared__ float Ws[GT_BK / 2][GT_BN + 4];   // [k][n]
     const int tid = threadIdx.x;
@@ -468,6 +471,7 @@ EC_DEV float block_reduce_max(float v, float *sh) {
 
 // Per-row activation quantisation: q[m][k] (k < Kp, zero padding), scale[m].
 __global__ void __launch_bounds__(256) k_quant(int8_t *q, float *scale, const float *X, int ldx, int K, int Kp) {
+    EC_PDL_ENTER();
     __shared__ float sh[32];
     const int m = blockIdx.x;
     const float *xr = X + (size_t)m * ldx;
@@ -489,6 +493,7 @@ extern "C" int ec_launch_quant(int8_t *q, float *scale, const float *X, int ldx,
 
 __global__ void __launch_bounds__(256) k_embed(float *x, const uint16_t *wte, const uint16_t *wpe, int ld,
                                                int bf16, ec_tokens tk, int E, int V, int C) {
+    EC_PDL_ENTER();
     const int m = blockIdx.x;
     const int t = tk.tok[m];
     const int p = tk.pos ? tk.pos[m] : 0;
@@ -514,6 +519,7 @@ extern "C" int ec_launch_embed(float *x, const uint16_t *wte, const uint16_t *wp
 // products rounded separately as in the reference's -ffp-contract=off build.
 __global__ void __launch_bounds__(256) k_norm(float *out, const float *x, const float *g, const float *b,
                                               int E, double eps) {
+    EC_PDL_ENTER();
     __shared__ double sh[32];
     const int m = blockIdx.x;
     const float *xr = x + (size_t)m * E;
@@ -568,6 +574,7 @@ __device__ __forceinline__ void quant_smem_row(int8_t *q, float *scale, const fl
 // needed there).  Dynamic shared memory: E floats.
 __global__ void __launch_bounds__(256) k_norm_quant(int8_t *q, float *scale, int Kp, const float *x, const float *g,
                                                     const float *b, int E, double eps) {
+    EC_PDL_ENTER();
     extern __shared__ float nq_row[];
     __shared__ double sh[32];
     __shared__ float shf[32];
@@ -622,6 +629,7 @@ extern "C" int ec_launch_norm_quant(int8_t *q, float *scale, int Kp, const float
 // order, k and v -> fp16 KV cache at (slot, pos).
 __global__ void __launch_bounds__(256) k_qkv_split(float *q_out, const float *qkv, int ldq, ec_tokens tk,
                                                    ec_kvgeo g, int H, int KVH, int packed) {
+    EC_PDL_ENTER();
     const int m = blockIdx.x;
     const int pos = tk.pos[m], slot = tk.slot[m];
     if (pos < 0 || pos >= g.C || slot < 0 || slot >= g.B) {
@@ -670,6 +678,7 @@ extern "C" int ec_launch_qkv_split(float *q_out, const float *qkv, int ldq, ec_t
 
 // out[m][j] = silu(gate) * up with gate|up interleaved: gu[m][2j], gu[m][2j+1].
 __global__ void k_swiglu(float *out, int ldo, const float *gu, int ldg, int I, int M) {
+    EC_PDL_ENTER();
     const size_t n = (size_t)M * I;
     for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < n; idx += (size_t)gridDim.x * blockDim.x) {
         const size_t m = idx / I, j = idx % I;
@@ -689,6 +698,7 @@ extern "C" int ec_launch_swiglu(float *out, int ldo, const float *gu, int ldg, i
 // k_swiglu then k_quant in one pass (one CTA per row): the int8 operand of
 // the down projection.  Dynamic shared memory: I floats.
 __global__ void __launch_bounds__(256) k_swiglu_quant(int8_t *q, float *scale, int Kp, const float *gu, int ldg, int I) {
+    EC_PDL_ENTER();
     extern __shared__ float sq_row[];
     __shared__ float shf[32];
     const int m = blockIdx.x;
@@ -711,6 +721,7 @@ extern "C" int ec_launch_swiglu_quant(int8_t *q, float *scale, int Kp, const flo
 }
 
 __global__ void k_gelu(float *x, size_t n) {
+    EC_PDL_ENTER();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         x[i] = ec_gelu(x[i]);
 }
@@ -735,6 +746,7 @@ extern "C" size_t ec_attention_scratch_floats(int M, int H, int hd, int nsplit) 
 }
 
 __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const ec_attn_args a) {
+    EC_PDL_ENTER();
     __shared__ float qs[256];
     __shared__ float sc[ATT_MAX_CHUNK];
     __shared__ float red[ATT_THREADS / 32];
@@ -819,6 +831,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const ec_attn_args a)
 }
 
 __global__ void k_attn_combine(const ec_attn_args a) {
+    EC_PDL_ENTER();
     const int h = blockIdx.x, m = blockIdx.y;
     const int hd = a.geo.hd;
     const float *part = a.part + ((size_t)m * a.H + h) * a.nsplit * (hd + 2);
@@ -864,6 +877,7 @@ __host__ __device__ inline size_t attx_smem_bytes(int G, int hd, int maxlen) {
 }
 
 __global__ void __launch_bounds__(ATTX_THREADS) k_attn_exact(const ec_attn_args a) {
+    EC_PDL_ENTER();
     extern __shared__ __align__(16) float attx_smem[];
     const int m = blockIdx.y;
     const ec_kvgeo &geo = a.geo;
@@ -1046,6 +1060,7 @@ EC_DEV void argmax_merge(float &bv, int &bi, float v, int i) {
 }
 
 __global__ void __launch_bounds__(256) k_argmax_part(const float *logits, int ld, int N, int nchunk, float2 *part) {
+    EC_PDL_ENTER();
     __shared__ float sv[8];
     __shared__ int si[8];
     const int c = blockIdx.x, m = blockIdx.y;
@@ -1071,6 +1086,7 @@ __global__ void __launch_bounds__(256) k_argmax_part(const float *logits, int ld
 }
 
 __global__ void k_argmax_final(const float2 *part, int nchunk, int M, int id_base, int *ids, float *maxv) {
+    EC_PDL_ENTER();
     const int m = blockIdx.x * blockDim.x + threadIdx.x;
     if (m >= M) return;
     float bv = -INFINITY;
@@ -1095,6 +1111,7 @@ extern "C" int ec_launch_argmax(int *ids, float *maxv, const float *logits, int 
 
 __global__ void k_step_advance(int *tok, int *pos, const int *ids, int M, int *hist, int *counter,
                                int wrap_lo, int wrap_hi) {
+    EC_PDL_ENTER();
     const int step = counter ? *counter : 0;
     for (int m = threadIdx.x; m < M; m += blockDim.x) {
         tok[m] = ids[m];
@@ -1127,6 +1144,7 @@ __device__ __forceinline__ long long argmax_key(float v, int idx) {
 }
 
 __global__ void k_pack_keys(const int *ids, const float *maxv, int M, long long *keys) {
+    EC_PDL_ENTER();
     const int m = blockIdx.x * blockDim.x + threadIdx.x;
     if (m < M) keys[m] = argmax_key(maxv[m], ids[m]);
 }
@@ -1138,6 +1156,7 @@ extern "C" int ec_launch_pack_keys(const int *ids, const float *maxv, int M, lon
 
 // tok[m] = the index in keys[m], pos[m] += 1; optionally ids[m] = the index.
 __global__ void k_keys_advance(const long long *keys, int M, int *tok, int *pos, int *ids) {
+    EC_PDL_ENTER();
     const int m = blockIdx.x * blockDim.x + threadIdx.x;
     if (m >= M) return;
     const unsigned long long k = (unsigned long long)keys[m] ^ 0x8000000000000000ull;
@@ -1154,6 +1173,7 @@ extern "C" int ec_launch_keys_advance(const long long *keys, int M, int *tok, in
 }
 
 __global__ void k_reference_math(const float *x, float *e, float *t, int n) {
+    EC_PDL_ENTER();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         if (e) e[i] = ec_expf(x[i]);
         if (t) t[i] = ec_tanhf(x[i]);

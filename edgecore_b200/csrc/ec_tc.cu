@@ -299,6 +299,34 @@ k_gemm_tc(const __grid_constant__ TcMaps maps, const ec_gemm_args a, const float
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // The weights do not depend on the previous kernel on the stream, which
+    // may still be finishing (programmatic dependent launch): the producer
+    // issues the weight tiles of the first ring stages before waiting for it,
+    // their activation tiles right after; every other global access follows
+    // the wait.
+    int pre = 0;
+    if (warp == 0 && lane == 0 && (int)blockIdx.x < items) {
+        const int tile = blockIdx.x / ksplit, sp = blockIdx.x - tile * ksplit;
+        const int kb0 = sp * nk / ksplit, kb1 = (sp + 1) * nk / ksplit;
+        pre = kb1 - kb0 < STAGES ? kb1 - kb0 : STAGES;
+        for (int j = 0; j < pre; ++j) {
+            ec_mbar_expect_tx(&full[j], (uint32_t)SB);
+            tma_load_2d(base + (uint32_t)(j * SB) + S * A_BYTES, &maps.b, ec_smem_u32(&full[j]), (kb0 + j) * kel,
+                        (tile % nt) * BN);
+        }
+    }
+    EC_PDL_ENTER();
+    if (pre > 0) {
+        const int tile = blockIdx.x / ksplit, sp = blockIdx.x - tile * ksplit;
+        const int kb0 = sp * nk / ksplit;
+        for (int j = 0; j < pre; ++j)
+#pragma unroll
+            for (int p = 0; p < S; ++p)
+                tma_load_2d(base + (uint32_t)(j * SB) + p * A_BYTES, &maps.a[p], ec_smem_u32(&full[j]), (kb0 + j) * kel,
+                            (tile / nt) * BM);
+        *issued = pre;
+    }
+
     if (warp == 0) {
         if (lane == 0) {   // TMA producer, one ring across all tiles of this CTA
             int g = 0;
@@ -307,6 +335,7 @@ k_gemm_tc(const __grid_constant__ TcMaps maps, const ec_gemm_args a, const float
                 const int m0 = (tile / nt) * BM, n0 = (tile % nt) * BN;
                 const int kb0 = sp * nk / ksplit, kb1 = (sp + 1) * nk / ksplit;
                 for (int kb = kb0; kb < kb1; ++kb, ++g) {
+                    if (g < pre) continue;   // issued above
                     const int s = g % STAGES;
                     if (g >= STAGES && !tc_wait(&empty[s], (uint32_t)((g / STAGES - 1) & 1), stop)) break;
                     const uint32_t st = base + (uint32_t)(s * SB);
@@ -475,6 +504,7 @@ k_gemm_tc(const __grid_constant__ TcMaps maps, const ec_gemm_args a, const float
 template <int WT>
 __global__ void __launch_bounds__(256) k_split16(uint16_t *parts, float *rscale, const float *X, int ldx, int M, int K,
                                                  int Kp) {
+    EC_PDL_ENTER();
     const int m = blockIdx.x;
     const float *x = X + (size_t)m * ldx;
     __shared__ float red[8];
@@ -589,7 +619,8 @@ int launch(const ec_gemm_args &a, const void *const *aparts, const float *row_sc
     const long long items = tiles * ksplit;
     const int grid = (int)(items < (long long)sms ? items : sms);
     const int flags = (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 && (a.ldo & 3) == 0 ? 1 : 0;
-    k_gemm_tc<CF><<<grid, THREADS, smem_bytes<CF>(), stream>>>(maps, a, row_scale, flags, ksplit);
+    ec_launch_k(k_gemm_tc<CF>, dim3(grid), dim3(THREADS), (size_t)smem_bytes<CF>(), stream, maps, a, row_scale, flags,
+                ksplit);
     return (int)cudaGetLastError();
 }
 
@@ -645,12 +676,12 @@ extern "C" int ec_launch_gemm_tc(const ec_gemm_args *args, cudaStream_t stream) 
                                               ((a.wt == EC_W_F16 ? 2 : 3) * plane * 2 + 255) / 256 * 256);
     const void *parts[3] = {parts16, parts16 + plane, parts16 + 2 * plane};
     if (a.wt == EC_W_F16) {
-        k_split16<EC_W_F16><<<a.M, 256, 0, stream>>>(parts16, rscale, a.X, a.ldx, a.M, a.K, a.Kp);
+        ec_launch_k(k_split16<EC_W_F16>, dim3(a.M), dim3(256), 0, stream, parts16, rscale, a.X, a.ldx, a.M, a.K, a.Kp);
         e = cudaGetLastError();
         if (e != cudaSuccess) return (int)e;
         return launch<EC_W_F16>(a, parts, rscale, dev, stream);
     }
-    k_split16<EC_W_BF16><<<a.M, 256, 0, stream>>>(parts16, rscale, a.X, a.ldx, a.M, a.K, a.Kp);
+    ec_launch_k(k_split16<EC_W_BF16>, dim3(a.M), dim3(256), 0, stream, parts16, rscale, a.X, a.ldx, a.M, a.K, a.Kp);
     e = cudaGetLastError();
     if (e != cudaSuccess) return (int)e;
     return launch<EC_W_BF16>(a, parts, rscale, dev, stream);
