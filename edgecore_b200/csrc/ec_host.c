@@ -238,6 +238,7 @@ typedef struct ec_dev {
     unsigned *d_bar;           /* two barrier counters (128 B apart) and the abort flag */
     int *d_abort, *d_mk_err;
     int bar_par, bar_reset;    /* counter of the next launch; 1: clear all three first */
+    int rows_run;              /* the staged rows come in runs (ec_attn_args.runs) */
     int *h_res, *h_res_dev;    /* pinned, mapped: completion word | ids [8] | max [8] */
     int res_seq;
     float *amax_v;
@@ -1154,6 +1155,7 @@ static int ec_enqueue_body(ec_dev *d, int M, int maxlen)
     at.q = d->q; at.ldq = E; at.out = d->att; at.ldo = E;
     at.tk = ec_tk(d); at.H = d->H; at.KVH = d->KVH; at.M = M; at.window = d->window;
     at.part = d->attn_part; at.maxlen = maxlen; at.nsplit = ec_pick_nsplit(maxlen);
+    at.runs = d->rows_run;
     const int wact = d->arch == ARCH_QWEN2 ? d->I : 4 * E;
     /* int8 layers: the norms and SwiGLU write the int8 operand themselves */
     const int fuse_norm = d->wt == EC_W_I8 && (size_t)E * 4 <= 48 * 1024;
@@ -1491,7 +1493,16 @@ static int ec_forward_impl(GPT2 *g, const int *tokens, const int *positions, con
     /* prefill path: per-layer kernels, lm_head in row chunks */
     if (ec_copy_inputs(d, M)) return -1;
     if (ec_ensure_attn(d, M, maxlen)) return -1;
-    if (ec_enqueue_body(d, M, maxlen)) return -1;
+    /* rows in runs (every aligned block of EC_ATTN_RUN rows one slot at
+     * consecutive positions): the block attention kernel may take them */
+    int runs = 1;
+    for (int m = 0; m < M && runs; m++)
+        if (m % EC_ATTN_RUN && (d->h_in[2 * M + m] != d->h_in[2 * M + m - 1] || d->h_in[M + m] != d->h_in[M + m - 1] + 1))
+            runs = 0;
+    d->rows_run = runs;
+    const int body = ec_enqueue_body(d, M, maxlen);
+    d->rows_run = 0;
+    if (body) return -1;
     int chunk = (int)((256u << 20) / ((size_t)Vs * 4));
     if (chunk < 8) chunk = 8;
     if (chunk > M) chunk = M;

@@ -1006,6 +1006,179 @@ __global__ void __launch_bounds__(ATTX_THREADS) k_attn_exact(const ec_attn_args 
     }
 }
 
+// Exact-order attention for runs of query rows (prefill): the arithmetic of
+// k_attn_exact, value for value, for ATTP_QB consecutive rows of one slot at
+// consecutive positions and one query head, so that every cached K and V row
+// is brought into shared memory once per block instead of once per row.
+// Scores are kept transposed, scT[t - lo0][r] (row stride ATTP_QBP floats:
+// 16-byte aligned, and the score writes of a warp fall on distinct banks).
+// Per (row, d) the output is the sequential fp32 sum over positions t in
+// [lo_r, pos_r], ascending, as in the reference (src/gpt2.c:757-775).
+#define ATTP_QB EC_ATTN_RUN
+#define ATTP_QBP 36
+#define ATTP_THREADS 256
+#define ATTP_KCH 64
+
+__host__ __device__ inline int attp_span_cap(int maxlen) { return (maxlen + ATTP_QB - 1 + 3) & ~3; }
+
+__host__ __device__ inline size_t attp_smem_bytes(int hd, int span_cap) {
+    return (size_t)ATTP_QB * hd * 4 + (size_t)span_cap * ATTP_QBP * 4 + (size_t)ATTP_KCH * (hd + 8) * 2 +
+           (size_t)ATTP_KCH * hd * 2;
+}
+
+__global__ void __launch_bounds__(ATTP_THREADS) k_attn_prefill(const ec_attn_args a) {
+    EC_PDL_ENTER();
+    extern __shared__ __align__(16) float attp_smem[];
+    const ec_kvgeo &geo = a.geo;
+    const int hd = geo.hd, h = blockIdx.x, r0 = blockIdx.y * ATTP_QB;
+    const int nr = min(ATTP_QB, a.M - r0);
+    const int g = h * a.KVH / a.H;   // the KV head of query head h
+    const int pos0 = a.tk.pos[r0], slot = a.tk.slot[r0];
+    const int pend = pos0 + nr - 1;
+    int lo0 = 0;
+    if (a.window > 0) { lo0 = pos0 - a.window + 1; if (lo0 < 0) lo0 = 0; }
+    const int span = pend + 1 - lo0, cap = attp_span_cap(a.maxlen);
+    if (pos0 < 0 || pend >= geo.C || slot < 0 || slot >= geo.B || span > cap || hd > 128) {
+        if (threadIdx.x == 0) atomicCAS(&g_ec_err, 0, EC_KERR_BAD_INDEX);
+        return;
+    }
+    float *qs = attp_smem;                                   // [QB][hd]
+    float *scT = qs + ATTP_QB * hd;                          // [cap][QBP]
+    uint16_t *kch = reinterpret_cast<uint16_t *>(scT + (size_t)cap * ATTP_QBP);   // [KCH][hd + 8]
+    uint16_t *vch = kch + (size_t)ATTP_KCH * (hd + 8);                            // [KCH][hd]
+    const uint16_t *kb = geo.kc + (size_t)g * hd, *vb = geo.vc + (size_t)g * hd;
+    const int per = hd >> 3;   // 16-byte pieces of a cached row
+    for (int i = threadIdx.x; i < nr * hd; i += blockDim.x)
+        qs[i] = a.q[(size_t)(r0 + i / hd) * a.ldq + (size_t)h * hd + (i % hd)];
+    const double inv_hd = 1.0 / sqrt((double)hd);
+
+    // scores: thread (r, ib) takes positions ib, ib + 8, ... of each K chunk
+    {
+        const int r = threadIdx.x >> 3, ib = threadIdx.x & 7;
+        for (int c0 = lo0; c0 <= pend; c0 += ATTP_KCH) {
+            const int n = min(ATTP_KCH, pend + 1 - c0);
+            __syncthreads();   // q staged / the previous chunk consumed
+            for (int e = threadIdx.x; e < n * per; e += blockDim.x) {
+                const int i = e / per, j = e - i * per;
+                const uint16_t *src = kb + ec_kv_row(geo.pt, geo.mp, slot, c0 + i) * geo.kv + 8 * j;
+                *reinterpret_cast<uint4 *>(kch + (size_t)i * (hd + 8) + 8 * j) = __ldg(reinterpret_cast<const uint4 *>(src));
+            }
+            __syncthreads();
+            if (r < nr) {
+                float acc[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+                for (int d = 0; d < hd; d += 8) {
+                    const float4 q0 = *reinterpret_cast<const float4 *>(qs + r * hd + d);
+                    const float4 q1 = *reinterpret_cast<const float4 *>(qs + r * hd + d + 4);
+                    const float q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const int i = ib + 8 * j;
+                        if (i < n) {
+                            float f[8];
+                            ec_f16x8_to_f32(*reinterpret_cast<const uint4 *>(kch + (size_t)i * (hd + 8) + d), f);
+                            float t = acc[j];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) t = __fadd_rn(t, __fmul_rn(q[e], f[e]));
+                            acc[j] = t;
+                        }
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int i = ib + 8 * j;
+                    if (i < n) scT[(size_t)(c0 - lo0 + i) * ATTP_QBP + r] = (float)__dmul_rn((double)acc[j], inv_hd);
+                }
+            }
+        }
+    }
+    __syncthreads();
+
+    // softmax weights, one warp per row (the order of k_attn_exact)
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int r = warp; r < nr; r += ATTP_THREADS / 32) {
+        const int pr = pos0 + r;
+        int lr = 0;
+        if (a.window > 0) { lr = pr - a.window + 1; if (lr < 0) lr = 0; }
+        const int len = pr + 1 - lr;
+        float *s = scT + (size_t)(lr - lo0) * ATTP_QBP + r;
+        float mx = -FLT_MAX;
+        for (int i = lane; i < len; i += 32) mx = ec_max_keep(mx, s[(size_t)i * ATTP_QBP]);
+        mx = ec_warp_max(mx);
+        double sum = 0.0;
+        for (int i = lane; i < len; i += 32) {
+            const float e = ec_expf(__fsub_rn(s[(size_t)i * ATTP_QBP], mx));
+            s[(size_t)i * ATTP_QBP] = e;
+            sum = __dadd_rn(sum, (double)e);
+        }
+        sum = ec_warp_sum_d(sum);
+        const double isum = __ddiv_rn(1.0, sum);
+        __syncwarp();
+        for (int i = lane; i < len; i += 32) s[(size_t)i * ATTP_QBP] = (float)__dmul_rn((double)s[(size_t)i * ATTP_QBP], isum);
+    }
+
+    // P.V: thread (rows 8*rq .. 8*rq + 7; dimensions d0 and d0 + 64), positions ascending
+    const int rq = threadIdx.x >> 6, d0 = threadIdx.x & 63;
+    int lor[8], hir[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int r = 8 * rq + j, pr = pos0 + r;
+        int lr = 0;
+        if (a.window > 0) { lr = pr - a.window + 1; if (lr < 0) lr = 0; }
+        lor[j] = lr;
+        hir[j] = r < nr ? pr : -1;
+    }
+    const int tfull = a.window > 0 ? -1 : pos0 + 8 * rq;   // every row of the thread active up to here
+    float o[2][8];
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[u][j] = 0.0f;
+    for (int c0 = lo0; c0 <= pend; c0 += ATTP_KCH) {
+        const int n = min(ATTP_KCH, pend + 1 - c0);
+        __syncthreads();   // weights final / the previous chunk consumed
+        for (int e = threadIdx.x; e < n * per; e += blockDim.x) {
+            const int i = e / per, j = e - i * per;
+            const uint16_t *src = vb + ec_kv_row(geo.pt, geo.mp, slot, c0 + i) * geo.kv + 8 * j;
+            *reinterpret_cast<uint4 *>(vch + (size_t)i * hd + 8 * j) = __ldg(reinterpret_cast<const uint4 *>(src));
+        }
+        __syncthreads();
+        if (8 * rq >= nr) continue;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int d = d0 + 64 * u;
+            if (d >= hd) break;
+            for (int i = 0; i < n; ++i) {
+                const int t = c0 + i;
+                const float *wp = scT + (size_t)(t - lo0) * ATTP_QBP + 8 * rq;
+                const float4 w0 = *reinterpret_cast<const float4 *>(wp);
+                const float4 w1 = *reinterpret_cast<const float4 *>(wp + 4);
+                const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                const float v = __half2float(__ushort_as_half(vch[(size_t)i * hd + d]));
+                if (t <= tfull) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) o[u][j] = __fadd_rn(o[u][j], __fmul_rn(w[j], v));
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (t >= lor[j] && t <= hir[j]) o[u][j] = __fadd_rn(o[u][j], __fmul_rn(w[j], v));
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const int d = d0 + 64 * u;
+        if (d >= hd) break;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int r = 8 * rq + j;
+            if (r < nr) a.out[(size_t)(r0 + r) * a.ldo + (size_t)h * hd + d] = o[u][j];
+        }
+    }
+}
+
 static int g_attx_max_smem = 0;
 
 extern "C" int ec_attention_exact_fits(int H, int KVH, int hd, int maxlen) {
@@ -1021,6 +1194,24 @@ extern "C" int ec_attention_exact_fits(int H, int KVH, int hd, int maxlen) {
     return attx_smem_bytes(G, hd, maxlen) <= (size_t)g_attx_max_smem;
 }
 
+static int g_attp_max_smem = 0;
+
+// 1 if k_attn_prefill takes this geometry (hd % 8 == 0 checked by the caller).
+static int attp_fits(const ec_attn_args *a) {
+    if (a->geo.hd > 128 || a->KVH <= 0 || a->H % a->KVH || a->maxlen < 1) return 0;
+    if (g_attp_max_smem == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_attp_max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        if (cudaFuncSetAttribute(k_attn_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, g_attp_max_smem) !=
+            cudaSuccess) {
+            cudaGetLastError();
+            g_attp_max_smem = 48 * 1024;   // the default limit stays
+        }
+    }
+    return attp_smem_bytes(a->geo.hd, attp_span_cap(a->maxlen)) <= (size_t)g_attp_max_smem;
+}
+
 static int g_attn_force_split = 0;
 
 extern "C" void ec_attention_set_force_split(int on) { g_attn_force_split = on != 0; }
@@ -1028,6 +1219,11 @@ extern "C" void ec_attention_set_force_split(int on) { g_attn_force_split = on !
 extern "C" int ec_launch_attention(const ec_attn_args *a, cudaStream_t stream) {
     if (a->M <= 0) return 0;
     if (a->geo.hd > 256 || a->geo.hd % 8 || a->nsplit < 1) return (int)cudaErrorInvalidValue;
+    if (!g_attn_force_split && a->runs && attp_fits(a)) {
+        dim3 g(a->H, (a->M + ATTP_QB - 1) / ATTP_QB);
+        k_attn_prefill<<<g, ATTP_THREADS, attp_smem_bytes(a->geo.hd, attp_span_cap(a->maxlen)), stream>>>(*a);
+        return (int)cudaGetLastError();
+    }
     if (!g_attn_force_split && ec_attention_exact_fits(a->H, a->KVH, a->geo.hd, a->maxlen)) {
         // few rows: one CTA per query head (its KV rows are read once per
         // head instead of once per group) so that the grid fills the GPU

@@ -167,10 +167,16 @@ typedef struct {
     int maxlen;                   /* upper bound on attended positions per row */
     int per_head;                 /* set by the launcher: one CTA per (head, row)
                                      instead of per (KV head, row) */
+    int runs;                     /* 1: rows come in runs -- every aligned block of
+                                     32 rows is one slot at consecutive positions
+                                     (prefill): the block kernel may be used */
 } ec_attn_args;
-/* Chooses the exact-order kernel (reference summation order; one CTA per
- * (token, KV head) holding all scores in shared memory) when maxlen fits,
- * else the split kernel (flash-decoding order, within 1e-6 of the reference). */
+#define EC_ATTN_RUN 32            /* rows per block of the run kernel */
+/* Chooses the exact-order kernels (reference summation order): the block
+ * kernel for rows in runs (one CTA per query head and 32 rows, each cached
+ * K / V row staged once per block), else one CTA per (token, KV head) holding
+ * all scores in shared memory when maxlen fits, else the split kernel
+ * (flash-decoding order, within 1e-6 of the reference). */
 int ec_launch_attention(const ec_attn_args *a, cudaStream_t stream);
 /* 1: every ec_launch_attention uses the split kernels (tests, measurement). */
 void ec_attention_set_force_split(int on);
