@@ -259,6 +259,8 @@ typedef struct ec_dev {
     int logit_rows;
     void *amax_part;
     int amax_chunks;
+    void *lm_part;             /* argmax partials of the fused lm_head (EC_EPI_ARGMAX) */
+    size_t lm_part_bytes;
     int *d_tok, *d_pos, *d_slot, *d_ids;
     float *d_max;
     int *d_hist;
@@ -689,6 +691,11 @@ static int ec_ensure_amax(ec_dev *d, int M)
     d->amax_part = NULL;
     CK(cudaMalloc(&d->amax_part, (size_t)rows * chunks * 8));
     d->amax_chunks = chunks;
+    /* fused lm_head argmax: two partials per column tile of 64 or more */
+    cudaFree(d->lm_part);
+    d->lm_part = NULL;
+    d->lm_part_bytes = (size_t)rows * 2 * ((d->V + 63) / 64) * 8;
+    CK(cudaMalloc(&d->lm_part, d->lm_part_bytes));
     d->ws_gen++;
     return 0;
 }
@@ -716,7 +723,7 @@ static void ec_dev_free(ec_dev *d)
     cudaFree(d->d_mk_layers); cudaFree(d->d_bar); cudaFree(d->d_mk_err);
     cudaFreeHost(d->h_res);
     cudaFree(d->amax_v); cudaFree(d->amax_i);
-    cudaFree(d->attn_part); cudaFree(d->logits); cudaFree(d->amax_part);
+    cudaFree(d->attn_part); cudaFree(d->logits); cudaFree(d->amax_part); cudaFree(d->lm_part);
     cudaFree(d->d_hist); cudaFree(d->taps); cudaFree(d->d_counter);
     cudaFree(d->acc32); cudaFree(d->tile_cnt);
     for (int k = 0; k < 2; k++)
@@ -1115,7 +1122,8 @@ static double ec_step_bytes(const ec_dev *d, int M, double kv_positions)
 /* One linear on the generic GEMM path (any M): out = X . W^T with epilogue.
  * X == NULL for int8 weights: the operand is already quantised in d->aq /
  * d->as (by a fused norm or SwiGLU kernel). */
-static int ec_linear(ec_dev *d, const ec_lin *l, const float *X, int ldx, int M, float *out, int ldo, int epi)
+/* The launch of ec_linear, its CUDA status returned (0: enqueued). */
+static int ec_linear_rc(ec_dev *d, const ec_lin *l, const float *X, int ldx, int M, float *out, int ldo, int epi)
 {
     cudaStream_t st = d->stream;
     ec_gemm_args g;
@@ -1134,8 +1142,14 @@ static int ec_linear(ec_dev *d, const ec_lin *l, const float *X, int ldx, int M,
     g.out = out; g.ldo = ldo; g.epi = epi;
     g.split = d->split; g.split_bytes = d->split_bytes;
     g.acc32 = d->acc32; g.acc32_elems = d->acc32_elems; g.tile_cnt = d->tile_cnt; g.cnt_elems = EC_TILE_CNT;
-    CK(ec_launch_gemm(&g, st));
+    const int rc = ec_launch_gemm(&g, st);
     ec_prof_end(d, pi);
+    return rc;
+}
+
+static int ec_linear(ec_dev *d, const ec_lin *l, const float *X, int ldx, int M, float *out, int ldo, int epi)
+{
+    CK(ec_linear_rc(d, l, X, ldx, M, out, ldo, epi));
     return 0;
 }
 
@@ -1201,6 +1215,35 @@ static int ec_enqueue_lm(ec_dev *d, int r0, int rows)
 {
     const ec_lin lm = ec_lm_lin(d);
     return ec_linear(d, &lm, d->h + (size_t)r0 * d->E, d->E, rows, d->logits, d->v1 - d->v0, EC_EPI_STORE);
+}
+
+/* lm_head rows [r0, r0+rows) of h and their row argmax into d_ids / d_max
+ * (ids offset by v0).  When the tensor-core GEMM takes the call, the argmax
+ * runs in its epilogue (per-tile partials, then k_argmax_final) and no
+ * logits are written; otherwise (fewer than 64 rows, or operands the
+ * tensor-core path does not take) the logits, then the argmax kernels. */
+static int ec_lm_argmax_rows(ec_dev *d, int r0, int rows)
+{
+    const int Vs = d->v1 - d->v0;
+    /* from 64 rows (measured: 128 streams 2.17 -> 2.14 ms per step; 16 and 32
+     * streams 1-3 % slower fused, the epilogue's compare chains being longer
+     * than the stores and the argmax pass they replace) */
+    const int nch = rows >= 64 ? ec_gemm_tc_argmax_chunks(d->hwt, rows, Vs) : 0;
+    if (nch > 0 && d->lm_part && (size_t)rows * nch * 8 <= d->lm_part_bytes) {
+        const ec_lin lm = ec_lm_lin(d);
+        const int rc = ec_linear_rc(d, &lm, d->h + (size_t)r0 * d->E, d->E, rows, (float *)d->lm_part, nch,
+                                    EC_EPI_ARGMAX);
+        if (rc == 0) {
+            CK(ec_launch_argmax_final(d->d_ids + r0, d->d_max + r0, d->lm_part, nch, rows, d->v0, d->stream));
+            return 0;
+        }
+        if (rc != (int)cudaErrorNotSupported) CK(rc);
+        cudaGetLastError();
+    }
+    if (ec_enqueue_lm(d, r0, rows)) return -1;
+    CK(ec_launch_argmax(d->d_ids + r0, d->d_max + r0, d->logits, Vs, Vs, rows, d->v0, d->amax_part,
+                        d->amax_chunks, d->stream));
+    return 0;
 }
 
 /* Map KV pages for positions [0, end) of slot s (pages come off the free
@@ -1511,11 +1554,10 @@ static int ec_forward_impl(GPT2 *g, const int *tokens, const int *positions, con
     if (!ids && ec_host_logits(d, hbytes)) return -1;
     for (int r0 = 0; r0 < M; r0 += chunk) {
         const int rows = M - r0 < chunk ? M - r0 : chunk;
-        if (ec_enqueue_lm(d, r0, rows)) return -1;
         if (ids) {
-            CK(ec_launch_argmax(d->d_ids + r0, d->d_max + r0, d->logits, Vs, Vs, rows, d->v0, d->amax_part,
-                                d->amax_chunks, d->stream));
+            if (ec_lm_argmax_rows(d, r0, rows)) return -1;
         } else {
+            if (ec_enqueue_lm(d, r0, rows)) return -1;
             CK(cudaMemcpyAsync(d->h_logits, d->logits, (size_t)rows * Vs * 4, cudaMemcpyDeviceToHost, d->stream));
             CK(cudaStreamSynchronize(d->stream));
             memcpy(logits + (size_t)r0 * Vs, d->h_logits, (size_t)rows * Vs * 4);
@@ -1705,9 +1747,7 @@ static int ec_enqueue_lm_argmax(ec_dev *d, int M, int chunk)
     const int Vs = d->v1 - d->v0;
     for (int r0 = 0; r0 < M; r0 += chunk) {
         const int rows = M - r0 < chunk ? M - r0 : chunk;
-        if (ec_enqueue_lm(d, r0, rows)) return -1;
-        CK(ec_launch_argmax(d->d_ids + r0, d->d_max + r0, d->logits, Vs, Vs, rows, d->v0, d->amax_part,
-                            d->amax_chunks, d->stream));
+        if (ec_lm_argmax_rows(d, r0, rows)) return -1;
     }
     return 0;
 }

@@ -430,9 +430,10 @@ extern "C" int ec_launch_gemm(const ec_gemm_args *args, cudaStream_t stream) {
     if (a.Kp % 16 || a.ldw < a.Kp || (a.ldw * (a.wt == EC_W_I8 ? 1 : 2)) % 16) return (int)cudaErrorInvalidValue;
     if (a.M >= EC_TC_MIN_M) {   // tensor cores unless the operands miss their alignment rules
         const int rc = ec_launch_gemm_tc(&a, stream);
-        if (rc != (int)cudaErrorNotSupported) return rc;
+        if (rc != (int)cudaErrorNotSupported || a.epi == EC_EPI_ARGMAX) return rc;
         cudaGetLastError();
     }
+    if (a.epi == EC_EPI_ARGMAX) return (int)cudaErrorNotSupported;   // tensor cores only
     dim3 grid((a.N + GT_BN - 1) / GT_BN, (a.M + GT_BM - 1) / GT_BM);
     if (grid.y > 65535) return (int)cudaErrorInvalidValue;
     if (a.wt == EC_W_I8) k_gemm_i8<<<grid, 256, 0, stream>>>(a);
@@ -1301,6 +1302,13 @@ extern "C" int ec_launch_argmax(int *ids, float *maxv, const float *logits, int 
     if (M <= 0) return 0;
     dim3 g(nchunk, M);
     k_argmax_part<<<g, 256, 0, stream>>>(logits, ld, N, nchunk, static_cast<float2 *>(part));
+    k_argmax_final<<<(M + 127) / 128, 128, 0, stream>>>(static_cast<const float2 *>(part), nchunk, M, id_base, ids, maxv);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int ec_launch_argmax_final(int *ids, float *maxv, const void *part, int nchunk, int M, int id_base,
+                                      cudaStream_t stream) {
+    if (M <= 0) return 0;
     k_argmax_final<<<(M + 127) / 128, 128, 0, stream>>>(static_cast<const float2 *>(part), nchunk, M, id_base, ids, maxv);
     return (int)cudaGetLastError();
 }

@@ -23,7 +23,11 @@ enum {
     EC_EPI_RESID = 1,   /* out[m][n] = out[m][n] + v   (residual add)        */
     EC_EPI_GELU = 2,    /* out[m][n] = gelu_new(v)                           */
     EC_EPI_SWIGLU = 3,  /* pair blocks: out[m][j] = silu(v_j) * v_{j+P}      */
-    EC_EPI_QKV = 4      /* q -> out, k/v -> fp16 KV cache (+RoPE on pairs)   */
+    EC_EPI_QKV = 4,     /* q -> out, k/v -> fp16 KV cache (+RoPE on pairs)   */
+    EC_EPI_ARGMAX = 5   /* tensor-core GEMMs only: out is float2 [M][ldo],
+                           per (row, column tile, half) {max of v, first
+                           column index} for k_argmax_final; ldo >=
+                           ec_gemm_tc_argmax_chunks(wt, M, N)              */
 };
 
 /* One row block of a weight matrix: rows [row0, row0+nrows) and, when pair>0,
@@ -119,6 +123,10 @@ int ec_launch_gemm_tc(const ec_gemm_args *a, cudaStream_t stream);
  * driver has no tensor-map encoder (ec_launch_gemm then uses the SIMT kernels). */
 int ec_tc_init(void);
 size_t ec_gemm_tc_split_bytes(int wt, int M, int Kp);
+/* Partials per row that the tensor-core GEMM writes for EC_EPI_ARGMAX (two
+ * per column tile of the configuration it picks for M x N); 0 below
+ * EC_TC_MIN_M rows. */
+int ec_gemm_tc_argmax_chunks(int wt, int M, int N);
 int ec_tc_error_take(int *code);
 
 /* Per-row symmetric int8 quantisation of X [M][ldx] (K used, Kp written). */
@@ -188,6 +196,9 @@ int ec_attention_exact_fits(int H, int KVH, int hd, int maxlen);
  * reporting ids offset by id_base.  part is scratch of 2*M*nchunk words. */
 int ec_launch_argmax(int *ids, float *maxv, const float *logits, int ld, int N, int M,
                      int id_base, void *part, int nchunk, cudaStream_t stream);
+/* The merge step alone, over partials float2 [M][nchunk] (EC_EPI_ARGMAX). */
+int ec_launch_argmax_final(int *ids, float *maxv, const void *part, int nchunk, int M, int id_base,
+                           cudaStream_t stream);
 
 /* Device-side decode bookkeeping for a captured step: tok[m] = ids[m];
  * pos[m] += 1, wrapping to wrap_lo when it reaches wrap_hi (wrap_hi <= 0: no

@@ -428,6 +428,11 @@ k_gemm_tc(const __grid_constant__ TcMaps maps, const ec_gemm_args a, const float
                 cb[lane + 32 * q] = cbv[q];
             }
             __syncwarp();
+            // EC_EPI_ARGMAX: this lane's row, max and first index over the
+            // warp's columns, in four independent chains (columns e mod 4)
+            const bool amx = a.epi == EC_EPI_ARGMAX;
+            float bv[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+            int bi[4] = {0x7fffffff, 0x7fffffff, 0x7fffffff, 0x7fffffff};
             for (int c0 = ch * HALF; c0 < (ch + 1) * HALF && n0 + c0 < a.N; c0 += EPI_COLS) {
                 uint32_t r[16];
                 tmem_ld16(tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)(b * BN + c0), r);
@@ -449,8 +454,17 @@ k_gemm_tc(const __grid_constant__ TcMaps maps, const ec_gemm_args a, const float
                             vv[e] = a.bias ? __fadd_rn(dot, bs[e]) : dot;
                         }
                     }
-                    *reinterpret_cast<float4 *>(st + lane * EPI_LD + j) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+                    if (amx) {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int n = n0 + c0 + j + e;
+                            if (n < a.N && (vv[e] > bv[e] || (vv[e] == bv[e] && n < bi[e]))) { bv[e] = vv[e]; bi[e] = n; }
+                        }
+                    } else {
+                        *reinterpret_cast<float4 *>(st + lane * EPI_LD + j) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+                    }
                 }
+                if (amx) continue;
                 __syncwarp();
                 // coalesced: 4 lanes per row (16 bytes each), 8 rows per pass
 #pragma unroll
@@ -475,6 +489,13 @@ k_gemm_tc(const __grid_constant__ TcMaps maps, const ec_gemm_args a, const float
                     }
                 }
                 __syncwarp();
+            }
+            if (amx && mrow < a.M) {   // partial (row, column tile, half) in the layout k_argmax_final merges
+#pragma unroll
+                for (int e = 1; e < 4; ++e)
+                    if (bv[e] > bv[0] || (bv[e] == bv[0] && bi[e] < bi[0])) { bv[0] = bv[e]; bi[0] = bi[e]; }
+                reinterpret_cast<float2 *>(a.out)[(size_t)mrow * a.ldo + (size_t)(n0 / BN) * 2 + ch] =
+                    make_float2(bv[0], __int_as_float(bi[0]));
             }
             // this warp is done with accumulator b (and with its constants)
             tc_fence_before();
@@ -609,7 +630,8 @@ int launch(const ec_gemm_args &a, const void *const *aparts, const float *row_sc
     // streams 3.03 -> 3.83 ms).
     int ksplit = 1;
     const int nk = (a.Kp * ELT + BKB - 1) / BKB;
-    if (WT == EC_W_I8 && a.M <= 64 && a.acc32 && a.tile_cnt && 2 * tiles <= sms && tiles <= a.cnt_elems &&
+    if (WT == EC_W_I8 && a.epi != EC_EPI_ARGMAX && a.M <= 64 && a.acc32 && a.tile_cnt && 2 * tiles <= sms &&
+        tiles <= a.cnt_elems &&
         (size_t)a.M * a.N <= a.acc32_elems) {
         ksplit = sms / (int)tiles;
         if (ksplit > nk / 4) ksplit = nk / 4;
@@ -626,6 +648,19 @@ int launch(const ec_gemm_args &a, const void *const *aparts, const float *row_sc
 
 }  // namespace
 
+extern "C" int ec_gemm_tc_argmax_chunks(int wt, int M, int N) {
+    if (M < EC_TC_MIN_M || N <= 0) return 0;
+    int BN = wt == EC_W_F16 ? TcCfg<EC_W_F16>::BN : wt == EC_W_BF16 ? TcCfg<EC_W_BF16>::BN : TcCfg<EC_W_I8>::BN;
+    if (wt == EC_W_I8) {   // the launcher's narrow-tile rule
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+        if (!g_sms[dev] && cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+        const long long wide_tiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+        if (2 * wide_tiles <= g_sms[dev]) BN = TcCfg<TC_I8_NARROW>::BN;
+    }
+    return 2 * ((N + BN - 1) / BN);
+}
+
 extern "C" size_t ec_gemm_tc_split_bytes(int wt, int M, int Kp) {
     if (wt == EC_W_I8) return 0;
     const size_t S = wt == EC_W_F16 ? 2 : 3;
@@ -641,8 +676,9 @@ extern "C" int ec_launch_gemm_tc(const ec_gemm_args *args, cudaStream_t stream) 
     if (a.ldw == 0) a.ldw = a.Kp;
     const int elt = a.wt == EC_W_I8 ? 1 : 2;
     if (a.Kp % 16 || (a.ldw * elt) % 16 || a.ldw < a.Kp || (reinterpret_cast<uintptr_t>(a.W) & 15) ||
-        (a.epi != EC_EPI_STORE && a.epi != EC_EPI_RESID && a.epi != EC_EPI_GELU))
+        (a.epi != EC_EPI_STORE && a.epi != EC_EPI_RESID && a.epi != EC_EPI_GELU && a.epi != EC_EPI_ARGMAX))
         return (int)cudaErrorNotSupported;
+    if (a.epi == EC_EPI_ARGMAX && a.ldo < ec_gemm_tc_argmax_chunks(a.wt, a.M, a.N)) return (int)cudaErrorInvalidValue;
     if (a.wt == EC_W_I8) {
         if (!a.Aq || !a.a_scale || (reinterpret_cast<uintptr_t>(a.Aq) & 15)) return (int)cudaErrorNotSupported;
     } else {
