@@ -614,7 +614,7 @@ def batch_sweep(args, stream, m1_value: float) -> list:
     """Batched greedy decode of the config-3 model over M independent streams
     (each a distinct 64-token prompt in its own KV slot): M = 1 is the
     headline loop; M = 8, 32, 128 run ec_decode_batch (the persistent decode
-    kernel up to 8 streams; above, one CUDA graph of the per-layer kernels
+    kernel up to 7 streams; from 8, one CUDA graph of the per-layer kernels
     per step with tensor-core GEMMs)."""
     import torch
 
@@ -644,7 +644,7 @@ def batch_sweep(args, stream, m1_value: float) -> list:
         assert ec.device_error_take(stream.cuda_stream) == 0
         ms = start.elapsed_time(end)
         out.append({"M": M, "tok_s": M * steps / (ms / 1e3), "ms_per_step": ms / steps, "steps": steps,
-                    "path": "ec_decode_batch: " + ("k_decode (persistent, one launch for all steps)" if M <= 8 else
+                    "path": "ec_decode_batch: " + ("k_decode (persistent, one launch for all steps)" if M < 8 else
                                                    "one CUDA graph of per-layer kernels per step, tcgen05 GEMMs"),
                     "graph_kernels_per_step": m.batch_graph_kernels(0) if M > 8 else 0})
         m.close()

@@ -1858,7 +1858,8 @@ EC_EXPORT int ec_decode_batch(GPT2 *g, int *d_tokens, int *d_positions, int n_st
         if (ec_kv_map(d, m, p + n_steps)) return -1;
     }
     if (ec_kv_flush(d)) return -1;
-    if (M <= EC_MK_MT) {   /* up to 8 streams: the persistent decode kernel, one launch for all steps */
+    if (M < EC_TC_MIN_M) {   /* up to 7 streams: the persistent decode kernel, one launch for all steps;
+                               from 8 the per-layer graph with tensor-core GEMMs is faster */
         int max_len = maxp;
         if (d->window > 0 && max_len > d->window) max_len = d->window;
         ec_mk_params mp;

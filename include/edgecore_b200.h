@@ -80,10 +80,11 @@ int ec_decode_greedy_cycle(GPT2 *g, int *d_tokens, int start_pos, int period, in
  * batch_cap slots, each at its own position: DEVICE d_tokens[batch_cap] and
  * d_positions[batch_cap] hold each slot's current token and position and are
  * updated in place; the sampled ids go to DEVICE d_out_ids[n_steps][batch_cap]
- * (may be NULL).  Every step runs the per-layer kernels (tcgen05 GEMMs from
- * 32 rows, attention of each slot over its own KV rows, the lm_head and a row
- * argmax with the lowest index on ties) captured once into a CUDA graph and
- * replayed.  The call reads the positions once (synchronising the model
+ * (may be NULL).  Up to 7 slots run the persistent decode kernel, one
+ * launch for all steps; from 8, every step runs the per-layer kernels
+ * (tcgen05 GEMMs, attention of each slot over its own KV rows, the lm_head
+ * and a row argmax with the lowest index on ties) captured once into a CUDA
+ * graph and replayed.  The call reads the positions once (synchronising the model
  * stream) and returns with the steps enqueued.  Reference: the batched decode
  * loop of src/runtime_main.c:336-352 with sample_token's greedy branch
  * (:213-219). */

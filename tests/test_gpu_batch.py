@@ -209,8 +209,9 @@ def _prefill_slice(model, toks, lens):
 
 @pytest.mark.parametrize("B", [3, 8])
 def test_decode_batch_small_against_cpu_oracle(int8_models, cuda, B):
-    """Up to 8 streams ec_decode_batch runs the persistent decode kernel with
-    each slot at its own position: greedy ids of STEPS steps against the CPU
+    """3 streams run the persistent decode kernel (up to 7 do), 8 the graph
+    of per-layer kernels, each slot at its own position: greedy ids of STEPS
+    steps against the CPU
     restatement (identical except where the restatement's top-2 margin is
     below 1e-3 of the row max)."""
     torch = cuda
