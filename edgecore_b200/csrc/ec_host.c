@@ -238,7 +238,8 @@ typedef struct ec_dev {
     unsigned *d_bar;           /* two barrier counters (128 B apart) and the abort flag */
     int *d_abort, *d_mk_err;
     int bar_par, bar_reset;    /* counter of the next launch; 1: clear all three first */
-    int rows_run;              /* the staged rows come in runs (ec_attn_args.runs) */
+    int *h_blk, *d_blk;        /* attention block table of the staged rows (ec_attn_args.blocks) */
+    int nblk;                  /* 0: no table for the current call */
     int *h_res, *h_res_dev;    /* pinned, mapped: completion word | ids [8] | max [8] */
     int res_seq;
     float *amax_v;
@@ -577,6 +578,9 @@ static void ec_free_work(ec_dev *d)
     cudaFree(d->big); cudaFree(d->aq); cudaFree(d->as); cudaFree(d->d_tok); cudaFree(d->d_pos); cudaFree(d->d_slot);
     cudaFree(d->d_ids); cudaFree(d->d_max);
     cudaFreeHost(d->h_in); cudaFreeHost(d->h_ids); cudaFreeHost(d->h_max);
+    cudaFreeHost(d->h_blk); cudaFree(d->d_blk);
+    d->h_blk = NULL;
+    d->d_blk = NULL;
     d->x = d->h = d->qkv = d->q = d->att = d->act = d->big = NULL;
     d->aq = NULL;
     cudaFree(d->split);
@@ -630,6 +634,8 @@ static int ec_ensure(ec_dev *d, int M)
     CK(cudaMalloc((void **)&d->d_ids, (size_t)cap * 4));
     CK(cudaMalloc((void **)&d->d_max, (size_t)cap * 4));
     CK(cudaMallocHost((void **)&d->h_in, (size_t)cap * 3 * 4));
+    CK(cudaMallocHost((void **)&d->h_blk, (size_t)cap * 2 * 4));
+    CK(cudaMalloc((void **)&d->d_blk, (size_t)cap * 2 * 4));
     CK(cudaMallocHost((void **)&d->h_ids, (size_t)cap * 4));
     CK(cudaMallocHost((void **)&d->h_max, (size_t)cap * 4));
     d->cap = cap;
@@ -1169,7 +1175,8 @@ static int ec_enqueue_body(ec_dev *d, int M, int maxlen)
     at.q = d->q; at.ldq = E; at.out = d->att; at.ldo = E;
     at.tk = ec_tk(d); at.H = d->H; at.KVH = d->KVH; at.M = M; at.window = d->window;
     at.part = d->attn_part; at.maxlen = maxlen; at.nsplit = ec_pick_nsplit(maxlen);
-    at.runs = d->rows_run;
+    at.blocks = d->nblk > 0 ? d->d_blk : NULL;
+    at.nblocks = d->nblk;
     const int wact = d->arch == ARCH_QWEN2 ? d->I : 4 * E;
     /* int8 layers: the norms and SwiGLU write the int8 operand themselves */
     const int fuse_norm = d->wt == EC_W_I8 && (size_t)E * 4 <= 48 * 1024;
@@ -1536,15 +1543,27 @@ static int ec_forward_impl(GPT2 *g, const int *tokens, const int *positions, con
     /* prefill path: per-layer kernels, lm_head in row chunks */
     if (ec_copy_inputs(d, M)) return -1;
     if (ec_ensure_attn(d, M, maxlen)) return -1;
-    /* rows in runs (every aligned block of EC_ATTN_RUN rows one slot at
-     * consecutive positions): the block attention kernel may take them */
-    int runs = 1;
-    for (int m = 0; m < M && runs; m++)
-        if (m % EC_ATTN_RUN && (d->h_in[2 * M + m] != d->h_in[2 * M + m - 1] || d->h_in[M + m] != d->h_in[M + m - 1] + 1))
-            runs = 0;
-    d->rows_run = runs;
+    /* blocks of up to EC_ATTN_RUN consecutive rows of one slot at consecutive
+     * positions; when they average 8 rows or more (prefill), the block
+     * attention kernel takes them (the copy is complete before h_blk is
+     * written again: every host-array call synchronises the stream first) */
+    int nb = 0;
+    for (int m = 0; m < M;) {
+        int n = 1;
+        while (m + n < M && n < EC_ATTN_RUN && d->h_in[2 * M + m + n] == d->h_in[2 * M + m] &&
+               d->h_in[M + m + n] == d->h_in[M + m] + n)
+            n++;
+        d->h_blk[2 * nb] = m;
+        d->h_blk[2 * nb + 1] = n;
+        nb++;
+        m += n;
+    }
+    if (8 * nb <= M) {
+        CK(cudaMemcpyAsync(d->d_blk, d->h_blk, (size_t)nb * 8, cudaMemcpyHostToDevice, d->stream));
+        d->nblk = nb;
+    }
     const int body = ec_enqueue_body(d, M, maxlen);
-    d->rows_run = 0;
+    d->nblk = 0;
     if (body) return -1;
     int chunk = (int)((256u << 20) / ((size_t)Vs * 4));
     if (chunk < 8) chunk = 8;

@@ -1008,9 +1008,10 @@ __global__ void __launch_bounds__(ATTX_THREADS) k_attn_exact(const ec_attn_args 
 }
 
 // Exact-order attention for runs of query rows (prefill): the arithmetic of
-// k_attn_exact, value for value, for ATTP_QB consecutive rows of one slot at
-// consecutive positions and one query head, so that every cached K and V row
-// is brought into shared memory once per block instead of once per row.
+// k_attn_exact, value for value, for a block of up to ATTP_QB consecutive
+// rows of one slot at consecutive positions (the host's block table) and
+// one query head, so that every cached K and V row is brought into shared
+// memory once per block instead of once per row.
 // Scores are kept transposed, scT[t - lo0][r] (row stride ATTP_QBP floats:
 // 16-byte aligned, and the score writes of a warp fall on distinct banks).
 // Per (row, d) the output is the sequential fp32 sum over positions t in
@@ -1031,8 +1032,12 @@ __global__ void __launch_bounds__(ATTP_THREADS) k_attn_prefill(const ec_attn_arg
     EC_PDL_ENTER();
     extern __shared__ __align__(16) float attp_smem[];
     const ec_kvgeo &geo = a.geo;
-    const int hd = geo.hd, h = blockIdx.x, r0 = blockIdx.y * ATTP_QB;
-    const int nr = min(ATTP_QB, a.M - r0);
+    const int hd = geo.hd, h = blockIdx.x;
+    const int r0 = a.blocks[2 * blockIdx.y], nr = a.blocks[2 * blockIdx.y + 1];
+    if (r0 < 0 || nr < 1 || nr > ATTP_QB || r0 + nr > a.M) {
+        if (threadIdx.x == 0) atomicCAS(&g_ec_err, 0, EC_KERR_BAD_INDEX);
+        return;
+    }
     const int g = h * a.KVH / a.H;   // the KV head of query head h
     const int pos0 = a.tk.pos[r0], slot = a.tk.slot[r0];
     const int pend = pos0 + nr - 1;
@@ -1220,8 +1225,8 @@ extern "C" void ec_attention_set_force_split(int on) { g_attn_force_split = on !
 extern "C" int ec_launch_attention(const ec_attn_args *a, cudaStream_t stream) {
     if (a->M <= 0) return 0;
     if (a->geo.hd > 256 || a->geo.hd % 8 || a->nsplit < 1) return (int)cudaErrorInvalidValue;
-    if (!g_attn_force_split && a->runs && attp_fits(a)) {
-        dim3 g(a->H, (a->M + ATTP_QB - 1) / ATTP_QB);
+    if (!g_attn_force_split && a->blocks && a->nblocks > 0 && attp_fits(a)) {
+        dim3 g(a->H, a->nblocks);
         k_attn_prefill<<<g, ATTP_THREADS, attp_smem_bytes(a->geo.hd, attp_span_cap(a->maxlen)), stream>>>(*a);
         return (int)cudaGetLastError();
     }

@@ -175,11 +175,13 @@ typedef struct {
     int maxlen;                   /* upper bound on attended positions per row */
     int per_head;                 /* set by the launcher: one CTA per (head, row)
                                      instead of per (KV head, row) */
-    int runs;                     /* 1: rows come in runs -- every aligned block of
-                                     32 rows is one slot at consecutive positions
-                                     (prefill): the block kernel may be used */
+    const int *blocks;            /* or NULL: nblocks pairs {first row, rows}, each
+                                     up to EC_ATTN_RUN consecutive rows of one slot
+                                     at consecutive positions (prefill): the block
+                                     kernel may be used */
+    int nblocks;
 } ec_attn_args;
-#define EC_ATTN_RUN 32            /* rows per block of the run kernel */
+#define EC_ATTN_RUN 32            /* rows per block of the block kernel at most */
 /* Chooses the exact-order kernels (reference summation order): the block
  * kernel for rows in runs (one CTA per query head and 32 rows, each cached
  * K / V row staged once per block), else one CTA per (token, KV head) holding

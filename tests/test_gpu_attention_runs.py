@@ -1,13 +1,15 @@
 """The block attention kernel for rows in runs (prefill).
 
-When every aligned block of 32 rows of a call is one slot at consecutive
-positions, the attention runs one CTA per (query head, block) and stages each
-cached K / V row once per block.  Its arithmetic is the per-row exact-order
+The host cuts a call's rows into blocks of up to 32 consecutive rows of one
+slot at consecutive positions; when they average 8 rows or more (prefill),
+the attention runs one CTA per (query head, block) and stages each cached
+K / V row once per block.  Its arithmetic is the per-row exact-order
 kernel's, value for value (reference src/gpt2.c:526-557, :743-777: the fp32
 dot over head_dim, the fp64-scaled scores, exp(s - max) / sum, the fp32 sum
 over positions in order), so the same rows given in an order that is not a
 run (interleaved slots: the per-row kernel) must give identical logits, bit
-for bit.  Runs of 45 and 40 rows leave partial blocks and cross the 64-row
+for bit.  Runs of 45 and 40 rows (blocks of 32 + 13 and 32 + 8 rows, the
+second sequence starting mid-way through a 32-row stretch) cross the 64-row
 K / V chunks; the sliding-window model (window 5, shorter than a block)
 takes the per-row windows inside a block.
 """
