@@ -15,8 +15,9 @@
  *   - RoPE cos/sin tables in fp64 from the host libm with the reference
  *     formula (src/gpt2.c:608-654), so the rotation is bit-exact;
  *   - workspaces.
- * Calls of M <= 8 token rows run the persistent decode kernel (one launch per
- * step, ec_decode.cu); larger calls (prefill) run per-layer kernels.
+ * Forward calls of up to 8 token rows and batched decode of up to 7 streams
+ * run the persistent decode kernel (ec_decode.cu); larger calls (prefill,
+ * batched decode from 8 streams) run per-layer kernels.
  */
 #define _GNU_SOURCE
 #include "edgecore.h"

@@ -183,8 +183,9 @@ typedef struct {
 } ec_attn_args;
 #define EC_ATTN_RUN 32            /* rows per block of the block kernel at most */
 /* Chooses the exact-order kernels (reference summation order): the block
- * kernel for rows in runs (one CTA per query head and 32 rows, each cached
- * K / V row staged once per block), else one CTA per (token, KV head) holding
+ * kernel when the caller passes a block table (one CTA per query head and
+ * block of up to 32 rows, each cached K / V row staged once per block), else
+ * one CTA per (token, KV head) holding
  * all scores in shared memory when maxlen fits, else the split kernel
  * (flash-decoding order, within 1e-6 of the reference). */
 int ec_launch_attention(const ec_attn_args *a, cudaStream_t stream);
