@@ -738,7 +738,6 @@ static void ec_dev_free(ec_dev *d)
     cudaFreeHost(d->h_logits);
     if (d->prof_ready)
         for (int i = 0; i < 2 * EC_PROF_MAX; i++) cudaEventDestroy(d->prof_ev[i]);
-
     if (d->own_stream) cudaStreamDestroy(d->own_stream);
     free(d);
     cudaSetDevice(cur);
@@ -1463,7 +1462,9 @@ static int ec_mk_run(ec_dev *d, const ec_mk_params *p, int n_steps)
     q.bar = d->d_bar + 32 * d->bar_par;
     q.bar_next = d->d_bar + 32 * (1 - d->bar_par);
     d->bar_par ^= 1;
-    CK(ec_mk_launch(&q, n_steps, d->mk_grid, d->stream));
+    const int e = ec_mk_launch(&q, n_steps, d->mk_grid, d->stream);
+    if (e) d->bar_reset = 1;   /* the next counter was not zeroed by a kernel */
+    CK(e);
     return 0;
 }
 
